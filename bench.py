@@ -1,0 +1,368 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the token loop on B200.
+
+Workload: the Llama-2-7B-shaped block-quantized random model (dim 4096, 32
+layers, 32 heads x 128, SwiGLU 11008, vocab 32000, ctx 4096), a 128-token
+seeded uniform-random prompt, then greedy decode at batch 1. A step is one
+decode token (one pass of the whole token loop). Weights are N(0, 0.02)
+from the seeded generator, quantized with the reference's block quantizer;
+there is no dataset (data: synthetic).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Ours: W untimed device-resident decode steps, then exactly K timed steps
+(CUDA events on the model's stream, barrier + synchronize on both sides, max
+over ranks). Under torchrun each rank runs an independent replica on its
+own GPU (weak scaling; the decode path of one sequence is not sharded yet).
+The line also carries the end-to-end rate through the reference-facing
+call (transformer_forward semantics: host token in, host logits out, host
+argmax), the roofline of the dequant-GEMV kernels from CUDA events, the SM
+clocks sampled during the timed region and the CPU baseline (the oracle
+restatement on the host cores, rank 0 only).
+
+Reference arm (--impl reference): the reference's CPU token loop cannot run
+end to end (src/transformer.cpp:156 overflows a static buffer), so the arm
+times the CPU restatement of that loop (oracle/, built with the reference's
+own flags) on all host threads, on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "project-aaedn_b200"))
+
+METRIC = "decode tok/s (7B-shape, bs1, 1 GPU) + dequant-GEMV GB/s vs HBM peak"
+SEED = 1234
+PROMPT = 128
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--profile-steps", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def model_cfg():
+    import aaedn_b200 as ab
+    return dict(ab.LLAMA2_7B)
+
+
+def gemv_shapes(cfg):
+    D, H, hd, KV, F = cfg["dim"], cfg["n_heads"], cfg["head_dim"], cfg["n_kv_heads"], cfg["ffn_dim"]
+    # (rows, cols) of the four dequant-GEMVs of one layer, in launch order
+    return {"qkv": ((H + 2 * KV) * hd, D), "o": (D, H * hd), "gate_up": (2 * F, D), "down": (D, F)}
+
+
+def gemv_bytes(n, k, m=1):
+    """Algorithmic bytes of one M-row dequant-GEMV: codes + fp16 scales
+    (0.5625 B/weight) + fp32 activations in and out."""
+    return n * k * 0.5625 + 4 * (m * k + m * n)
+
+
+def step_bytes(cfg, pos):
+    """Algorithmic bytes of one decode step at position pos: every weight
+    once, the fp32 lm_head, and the K/V rows of positions 0..pos."""
+    w = sum(gemv_bytes(n, k) for n, k in gemv_shapes(cfg).values()) * cfg["n_layers"]
+    lm = cfg["vocab"] * cfg["dim"] * 4
+    kv = cfg["n_layers"] * 2 * (pos + 1) * cfg["n_kv_heads"] * cfg["head_dim"] * 4
+    return w + lm + kv
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per GEMV launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4_decode_7b.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch_avg:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons of one GPU while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(gpu_id)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in out.strip().splitlines():
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_identity(dev_index):
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(dev_index)
+        bus = getattr(p, "pci_bus_id", None)
+        dom = getattr(p, "pci_domain_id", 0)
+        dv = getattr(p, "pci_device_id", 0)
+        if bus is not None:
+            return f"{dom:08x}:{bus:02x}:{dv:02x}.0"
+    except Exception:
+        pass
+    return str(dev_index)
+
+
+def host_weights(cfg):
+    import aaedn_b200 as ab
+    return ab.synthetic_weights(cfg, SEED)
+
+
+def cpu_decode_sample(cfg, w, seconds, steps_cap=None):
+    """Times greedy decode steps of the CPU restatement (oracle/, reference
+    flags, all host threads) after a 2-token prompt; returns (tok/s, steps,
+    threads, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    import aaedn_b200 as ab
+    orc = pyoracle.Oracle(fast=True)
+    c = dict(cfg, max_seq=256)
+    om = pyoracle.OracleModel(orc, c, w)
+    prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], 2)
+    logits = None
+    for t in prompt:
+        logits = om.step(t)
+    t0 = time.perf_counter()
+    tok = int(np.argmax(logits))
+    logits = om.step(tok)
+    first = time.perf_counter() - t0
+    n = max(1, min(int(seconds / max(first, 1e-3)), steps_cap or 10 ** 9, 256 - 10))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        tok = int(np.argmax(logits))
+        logits = om.step(tok)
+    dt = time.perf_counter() - t0
+    desc = (f"{n} greedy decode steps of the full 7B-shape model at positions 3..{2 + n} after a 2-token prompt "
+            f"(oracle built -O3 -mavx2 -mfma -ffast-math, OpenMP over GEMV rows and heads)")
+    return n / dt, n, orc.threads(), desc
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = model_cfg()
+    if not os.path.exists(os.path.join(ROOT, "oracle", "build", "liboracle_fast.so")):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=True, capture_output=True)
+    w = host_weights(cfg)
+    # each step is one decode token; the count is bounded so the run stays
+    # within a few minutes of CPU time
+    cap = max(1, args.steps)
+    value, n, threads, desc = cpu_decode_sample(cfg, w, seconds=max(5.0, args.cpu_seconds), steps_cap=cap)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": n, "warmup": 1, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "llama2-7b-shape q4 greedy decode bs1 (CPU restatement of the reference loop)",
+                   "dim": cfg["dim"], "n_layers": cfg["n_layers"], "vocab": cfg["vocab"]},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import aaedn_b200 as ab
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = model_cfg()
+    K, W = args.steps, max(3, args.warmup)
+    E, P = args.e2e_steps, args.profile_steps
+    if PROMPT + W + K + E + P + 2 > cfg["max_seq"]:
+        raise SystemExit(f"steps+warmup too large for ctx {cfg['max_seq']}")
+
+    w = host_weights(cfg)
+    model = ab.Model(cfg)
+    model.set_weights(w)
+    stream = torch.cuda.ExternalStream(model.stream)
+    prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], PROMPT)
+
+    # prefill (one graph replay per prompt token), then W warm-up decode steps
+    model.forward(prompt, want_logits=False)
+    model.decode_steps(W)
+    torch.cuda.synchronize()
+    pos0 = model.pos
+
+    # ---- timed region: exactly K device-resident greedy steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(gpu_identity(local))
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = ab.kernel_launches()
+    ev0.record(stream)
+    model.decode_steps(K)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = ab.kernel_launches() - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * K / (ms_max / 1000.0)
+    pos1 = model.pos
+
+    # ---- end to end through the reference-facing call (host token in, host
+    # logits out, host argmax), E steps
+    logits = model.logits()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    tok = np.empty(1, np.uint32)
+    for _ in range(E):
+        tok[0] = int(np.argmax(logits))
+        logits = model.forward(tok)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    te = torch.tensor([e2e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * E / (float(te.item()) / 1000.0)
+
+    # ---- per-kernel device times of P steps (CUDA events between kernels,
+    # one graph replay per step)
+    prof = np.stack([model.profile_step() for _ in range(P)])  # [P][5L+1]
+    L = cfg["n_layers"]
+    per = prof[:, :5 * L].reshape(P, L, 5)
+    shapes = gemv_shapes(cfg)
+    gemv_idx = {"qkv": 0, "o": 2, "gate_up": 3, "down": 4}
+    gemv_ms = {k: float(per[:, :, i].mean()) for k, i in gemv_idx.items()}
+    gemv_total_ms = sum(gemv_ms.values())
+    gemv_total_bytes = sum(gemv_bytes(*shapes[k]) for k in gemv_idx)
+    achieved = gemv_total_bytes / (gemv_total_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peaks()
+    kernel_split = {"attention_ms": float(per[:, :, 1].mean()), "lm_head_ms": float(prof[:, -1].mean()),
+                    **{f"{k}_ms": v for k, v in gemv_ms.items()},
+                    **{f"{k}_gbs": gemv_bytes(*shapes[k]) / (gemv_ms[k] / 1000.0) / 1e9 for k in gemv_ms}}
+    traffic = profiled_traffic()
+
+    mean_pos = (pos0 + pos1 - 1) / 2.0
+    sb = step_bytes(cfg, mean_pos)
+    step_gbs = sb / (ms_max / K / 1000.0) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, n, threads, desc = cpu_decode_sample(cfg, w, args.cpu_seconds)
+            cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+        except Exception as ex:  # the GPU number stands without it
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode",
+                       "dim": cfg["dim"], "n_layers": cfg["n_layers"], "n_heads": cfg["n_heads"],
+                       "head_dim": cfg["head_dim"], "ffn_dim": cfg["ffn_dim"], "vocab": cfg["vocab"],
+                       "ctx": cfg["max_seq"], "prompt": PROMPT, "positions": [pos0, pos1],
+                       "weights": "4-bit codes, fp16 scale per 32, fp32 embedding/lm_head",
+                       "l2": "inputs larger than L2: 4.1 GB of weights streamed per step",
+                       "parallelism": "replicas" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "gemv_q4_kernel (all decode dequant-GEMVs, M=1)",
+                         "bytes_per_step": gemv_total_bytes * L},
+            "decode_step": {"algorithmic_bytes": sb, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
+                            **kernel_split},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12,
+                    "d2h_bytes_per_step": 4 * cfg["vocab"],
+                    "call": "aaedn_model_forward (transformer_forward) + host argmax"},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,180 @@
+/*
+ * aaedn_b200.h — C ABI of the B200 (sm_100a) token loop.
+ *
+ * Plain pointers and sizes only. Every entry point returns an int status
+ * (AAEDN_OK = 0, negative on failure) and never aborts; the message of the
+ * last failure on the calling thread is aaedn_last_error(). Pointers named
+ * d_* are device pointers (cudaMalloc / the model's arena); h_* are host
+ * pointers. `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ * stream). Kernels are asynchronous on that stream unless the entry point
+ * says it synchronises.
+ *
+ * Each declaration names the reference interface it replaces
+ * (file:line in the reference project). The C++ API that mirrors the
+ * reference headers (namespace aaedn, project-aaedn_b200/host/include) is a
+ * thin layer over these functions.
+ */
+#ifndef AAEDN_B200_H
+#define AAEDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AAEDN_OK 0
+#define AAEDN_EINVAL (-1)     /* bad argument (null, size, alignment, host pointer) */
+#define AAEDN_ECUDA (-2)      /* CUDA runtime error */
+#define AAEDN_ETIMEOUT (-3)   /* a bounded device wait ran out */
+#define AAEDN_EFORMAT (-4)    /* model/quant file rejected */
+#define AAEDN_ENOMEM (-5)     /* allocation or arena overflow */
+#define AAEDN_EUNSUPPORTED (-6)
+#define AAEDN_ESTATE (-7)     /* object not initialised / sequence full */
+
+/* scale_kind for the block-quant entry points */
+#define AAEDN_SCALE_F16 0     /* u16 holds IEEE fp16 bits (tools/convert_model.py:49) */
+#define AAEDN_SCALE_U16INT 1  /* u16 cast to float as an integer (src/dequant.cpp:19) */
+
+const char* aaedn_last_error(void);
+int aaedn_version(void);
+/* Number of kernels this library has launched in this process (all entry
+ * points, graph replays counted per kernel node). */
+uint64_t aaedn_kernel_launches(void);
+
+/* ---- device memory helpers (plain cudaMalloc / cudaMemcpy) -------------- */
+int aaedn_dev_alloc(void** d_ptr, size_t bytes);
+int aaedn_dev_free(void* d_ptr);
+int aaedn_memcpy_h2d(void* d_dst, const void* h_src, size_t bytes, void* stream);
+int aaedn_memcpy_d2h(void* h_dst, const void* d_src, size_t bytes, void* stream);
+int aaedn_stream_sync(void* stream);
+int aaedn_device_sync(void);
+
+/* ---- host-side quant tools (no GPU needed) ------------------------------- */
+/* tools/convert_model.py:36-55 quantize_block_4bit_unsigned, bit-exact:
+ * 32-element blocks in flat order, scale = fp16(max|x|/7), codes
+ * clip(rint(x/scale), 0, 15), low nibble = even element. data: (n+1)/2 B,
+ * scales: ceil(n/32) u16. Multi-threaded. */
+int aaedn_quantize_q4(const float* h_x, size_t n, uint8_t* h_data, uint16_t* h_scales);
+/* tools/convert_model.py:16-21 / src/quant.cpp:12-20 FNV-1a 32. */
+uint32_t aaedn_fnv1a32(const uint8_t* h_p, size_t n, uint32_t seed);
+/* Seeded synthetic tensors: N(0, std) fp32 from a counter-based generator
+ * keyed by (seed, tensor_id, index); identical on every host. */
+int aaedn_synth_normal(uint64_t seed, uint64_t tensor_id, float std_dev, float* h_out, size_t n);
+/* Uniform token ids in [0, vocab). */
+int aaedn_synth_tokens(uint64_t seed, uint64_t stream_id, uint32_t vocab, uint32_t* h_out, size_t n);
+/* RoPE tables [max_seq][hd/2]. formula 0: src/rope.cpp:26 (freq =
+ * 10000/2^(i/half), fp32 as the reference); formula 1: pos*theta^(-2i/hd)
+ * in fp64 rounded to fp32 (the model path). */
+int aaedn_rope_table(float* h_cos, float* h_sin, size_t max_seq, size_t head_dim, double theta, int formula);
+
+/* ---- kernels (device pointers) ------------------------------------------ */
+/* include/dequant.hpp:10 dequant_4bit (src/dequant.cpp:7-28): out[i] =
+ * code(i) * scale(i/32); all-zero output when data/scales are null or
+ * scales[0] == 0 (checked on the device). Bit-exact. */
+int aaedn_cu_dequant_4bit(const uint8_t* d_data, const uint16_t* d_scales, float* d_out, size_t n,
+                          int scale_kind, void* stream);
+
+/* include/fused_matmul.hpp:13 fused_matmul: out[m*ldc+n] = sum_k
+ * in[m*lda+k] * code(n,k) * scale(n,k/32). Weights are [N][K] rows of ldb
+ * codes (ldb/2 bytes, ldb/32 scales per row), K and ldb multiples of 32.
+ * M == 0 or N == 0 or K == 0 is a no-op (src/fused_matmul.cpp:76-77). */
+int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, const uint16_t* d_scales, float* d_out,
+                          size_t M, size_t N, size_t K, size_t lda, size_t ldb, size_t ldc, int scale_kind,
+                          void* stream);
+
+/* fp32 weights: out[m*ldc+n] = sum_k in[m*lda+k]*w[n*ldw+k] (the lm_head
+ * product of src/transformer.cpp:232-238). */
+int aaedn_cu_f32_matmul(const float* d_in, const float* d_w, float* d_out, size_t M, size_t N, size_t K,
+                        size_t lda, size_t ldw, size_t ldc, void* stream);
+
+/* include/rmsnorm.hpp:10 rmsnorm (src/rmsnorm.cpp:8-51). */
+int aaedn_cu_rmsnorm(const float* d_in, float* d_out, const float* d_w, size_t n, float eps, void* stream);
+
+/* include/rope.hpp:21 rope_apply (src/rope.cpp:36-63): rows 0..seq_len-1 of
+ * q and k ([seq_len][head_dim]) rotated by table rows 0..seq_len-1. */
+int aaedn_cu_rope_apply(float* d_q, float* d_k, size_t seq_len, size_t head_dim, const float* d_cos,
+                        const float* d_sin, void* stream);
+
+/* include/attention.hpp:13 attention (src/attention.cpp:10-84, head index
+ * added): k/v rows are tokens of n_heads*head_dim floats; h_segments holds
+ * num_segments (start_token, length) pairs on the HOST (at most 64, the
+ * reference keeps 32 per agent: src/kvcache.cpp:33). */
+int aaedn_cu_attention(const float* d_q, const float* d_k, const float* d_v, const uint32_t* h_segments,
+                       size_t num_segments, float* d_out, size_t n_heads, size_t head_dim, float scale,
+                       void* stream);
+
+/* ---- the token loop ------------------------------------------------------
+ * include/transformer.hpp:15-44 Transformer / transformer_init /
+ * transformer_forward. One model owns one device arena (a single
+ * cudaMalloc at creation: the reference's no-allocation-after-startup rule,
+ * docs/mpd.md:59), the weights, a paged fp32 KV cache and one stream. */
+typedef struct aaedn_model aaedn_model;
+
+typedef struct {
+    uint32_t dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq;
+    float rope_theta;
+    float eps;
+} aaedn_model_config;
+
+/* Host weights of one layer in logical order, [out][in] rows, quantized
+ * with aaedn_quantize_q4 (fp16 scales). */
+typedef struct {
+    const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const uint16_t *sq, *sk, *sv, *so, *sg, *su, *sd;
+    const float *attn_norm, *ffn_norm; /* [dim] */
+} aaedn_layer_host;
+
+int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** out);
+int aaedn_model_destroy(aaedn_model* m);
+int aaedn_model_config_get(const aaedn_model* m, aaedn_model_config* out);
+void* aaedn_model_stream(aaedn_model* m);
+/* Device bytes the arena holds. */
+size_t aaedn_model_arena_bytes(const aaedn_model* m);
+int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn_layer_host* w);
+/* embedding [vocab][dim], final_norm [dim], lm_head [vocab][dim], fp32 host. */
+int aaedn_model_set_globals(aaedn_model* m, const float* h_embedding, const float* h_final_norm,
+                            const float* h_lm_head);
+/* Fill every weight from the seeded generator (N(0,0.02) linear weights
+ * quantized with the block quantizer; fp32 embedding and lm_head; norm gains
+ * 1.0). Tensor ids: embedding 0, lm_head 1, layer l: 16 + 8l + {q,k,v,o,g,u,d}.
+ * Multi-threaded on the host, then uploaded. */
+int aaedn_model_synthesize(aaedn_model* m, uint64_t seed);
+/* Start a new sequence at position 0 (the KV cache content is discarded). */
+int aaedn_model_reset(aaedn_model* m);
+uint32_t aaedn_model_pos(aaedn_model* m);
+/* src/transformer.cpp:128-243 transformer_forward: process the n tokens at
+ * the current position (D7), return the last token's logits to h_logits
+ * [vocab] (may be NULL). Synchronises. */
+int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, size_t n, float* h_logits);
+/* Prompt, then greedy decode of n_new tokens entirely on the device (argmax
+ * ties to the lowest id). Synchronises and copies the ids to h_out. */
+int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, size_t n_prompt, size_t n_new,
+                         uint32_t* h_out);
+/* Device-resident greedy steps with no host synchronisation (one CUDA graph
+ * replay per step); the sequence must already hold at least one token. */
+int aaedn_model_decode_steps(aaedn_model* m, size_t n_steps);
+/* Move the sequence back to position pos (1 <= pos <= current): the cache
+ * below pos stays valid and decoding resumes from the greedy token of the
+ * last step (the reference REPL's /reset, src/main.cpp:83-86, keeps nothing;
+ * this keeps the prefix). */
+int aaedn_model_rewind(aaedn_model* m, uint32_t pos);
+/* Tracing: one decode step replayed as a CUDA graph with an event between
+ * every kernel; h_ms[i] receives the device time of kernel i in launch order
+ * (per layer: qkv, attention, o, gate/up, down; then lm_head). cap is the
+ * capacity of h_ms; returns the kernel count through *n_out. */
+int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t cap, uint32_t* n_out);
+/* Kernels launched by one decode step. */
+uint32_t aaedn_model_kernels_per_step(const aaedn_model* m);
+/* Copy the last step's logits ([vocab]) / the greedy tokens generated so far. */
+int aaedn_model_logits(aaedn_model* m, float* h_logits);
+int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n);
+/* Debug path (eager launches): one token, the residual stream after every
+ * layer to h_hidden [n_layers][dim] and the logits to h_logits. */
+int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* h_hidden, float* h_logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

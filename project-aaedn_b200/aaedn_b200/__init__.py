@@ -1,0 +1,354 @@
+"""ctypes binding of libaaedn_b200.so (the C ABI in include/aaedn_b200.h).
+
+The CUDA library is the only compute path: there is no CPU fallback. If the
+shared library is missing this module raises on import of any compute
+entry point; build it with ``python project-aaedn_b200/build.py``.
+
+Device buffers can be any CUDA allocation (torch tensors are convenient:
+pass ``t.data_ptr()``); host buffers are numpy arrays.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libaaedn_b200.so")
+
+OK = 0
+EINVAL, ECUDA, ETIMEOUT, EFORMAT, ENOMEM, EUNSUPPORTED, ESTATE = -1, -2, -3, -4, -5, -6, -7
+SCALE_F16, SCALE_U16INT = 0, 1
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_u32 = ctypes.c_uint32
+_u64 = ctypes.c_uint64
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+
+
+class AaednError(RuntimeError):
+    def __init__(self, rc, msg):
+        super().__init__(f"aaedn error {rc}: {msg}")
+        self.rc = rc
+
+
+class ModelConfig(ctypes.Structure):
+    _fields_ = [("dim", _u32), ("n_layers", _u32), ("n_heads", _u32), ("n_kv_heads", _u32), ("head_dim", _u32),
+                ("ffn_dim", _u32), ("vocab", _u32), ("max_seq", _u32), ("rope_theta", _f32), ("eps", _f32)]
+
+    def as_dict(self):
+        d = {k: getattr(self, k) for k, _ in self._fields_}
+        return d
+
+
+class LayerHost(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd",
+                                   "sq", "sk", "sv", "so", "sg", "su", "sd", "attn_norm", "ffn_norm")]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded shared library (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with python project-aaedn_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "aaedn_last_error": ([], ctypes.c_char_p),
+        "aaedn_version": ([], _int),
+        "aaedn_kernel_launches": ([], _u64),
+        "aaedn_dev_alloc": ([ctypes.POINTER(_vp), _sz], _int),
+        "aaedn_dev_free": ([_vp], _int),
+        "aaedn_memcpy_h2d": ([_vp, _vp, _sz, _vp], _int),
+        "aaedn_memcpy_d2h": ([_vp, _vp, _sz, _vp], _int),
+        "aaedn_stream_sync": ([_vp], _int),
+        "aaedn_device_sync": ([], _int),
+        "aaedn_quantize_q4": ([_vp, _sz, _vp, _vp], _int),
+        "aaedn_fnv1a32": ([_vp, _sz, _u32], _u32),
+        "aaedn_synth_normal": ([_u64, _u64, _f32, _vp, _sz], _int),
+        "aaedn_synth_tokens": ([_u64, _u64, _u32, _vp, _sz], _int),
+        "aaedn_rope_table": ([_vp, _vp, _sz, _sz, ctypes.c_double, _int], _int),
+        "aaedn_cu_dequant_4bit": ([_vp, _vp, _vp, _sz, _int, _vp], _int),
+        "aaedn_cu_fused_matmul": ([_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _int, _vp], _int),
+        "aaedn_cu_f32_matmul": ([_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp], _int),
+        "aaedn_cu_rmsnorm": ([_vp, _vp, _vp, _sz, _f32, _vp], _int),
+        "aaedn_cu_rope_apply": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _int),
+        "aaedn_cu_attention": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
+        "aaedn_model_create": ([ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], _int),
+        "aaedn_model_destroy": ([_vp], _int),
+        "aaedn_model_config_get": ([_vp, ctypes.POINTER(ModelConfig)], _int),
+        "aaedn_model_stream": ([_vp], _vp),
+        "aaedn_model_arena_bytes": ([_vp], _sz),
+        "aaedn_model_set_layer": ([_vp, _u32, ctypes.POINTER(LayerHost)], _int),
+        "aaedn_model_set_globals": ([_vp, _vp, _vp, _vp], _int),
+        "aaedn_model_synthesize": ([_vp, _u64], _int),
+        "aaedn_model_reset": ([_vp], _int),
+        "aaedn_model_pos": ([_vp], _u32),
+        "aaedn_model_forward": ([_vp, _vp, _sz, _vp], _int),
+        "aaedn_model_generate": ([_vp, _vp, _sz, _sz, _vp], _int),
+        "aaedn_model_decode_steps": ([_vp, _sz], _int),
+        "aaedn_model_kernels_per_step": ([_vp], _u32),
+        "aaedn_model_logits": ([_vp, _vp], _int),
+        "aaedn_model_tokens": ([_vp, _vp, _sz], _int),
+        "aaedn_model_forward_debug": ([_vp, _u32, _vp, _vp], _int),
+        "aaedn_model_rewind": ([_vp, _u32], _int),
+        "aaedn_model_profile_step": ([_vp, _vp, _u32, ctypes.POINTER(_u32)], _int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def exported_symbols():
+    """Names declared in include/aaedn_b200.h that the library must export."""
+    import re
+    hdr = os.path.join(os.path.dirname(os.path.dirname(HERE)), "include", "aaedn_b200.h")
+    txt = open(hdr).read()
+    return sorted(set(re.findall(r"\b(aaedn_[a-z0-9_]+)\s*\(", txt)))
+
+
+def last_error():
+    return lib().aaedn_last_error().decode(errors="replace")
+
+
+def check(rc):
+    if rc != OK:
+        raise AaednError(rc, last_error())
+    return rc
+
+
+def kernel_launches():
+    return int(lib().aaedn_kernel_launches())
+
+
+def _p(a):
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data_as(_vp)
+
+
+# ---------------------------------------------------------------- host tools
+def quantize_q4(x):
+    """tools/convert_model.py:36-55, bit-exact; returns (codes, fp16 scales)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    data = np.zeros((x.size + 1) // 2, np.uint8)
+    scales = np.zeros((x.size + 31) // 32, np.uint16)
+    check(lib().aaedn_quantize_q4(_p(x), x.size, _p(data), _p(scales)))
+    return data, scales
+
+
+def fnv1a32(b, seed=0x811C9DC5):
+    b = np.frombuffer(bytes(b), np.uint8)
+    return int(lib().aaedn_fnv1a32(_p(b), b.size, seed))
+
+
+def synth_normal(seed, tensor_id, n, std=0.02):
+    out = np.empty(n, np.float32)
+    check(lib().aaedn_synth_normal(seed, tensor_id, std, _p(out), n))
+    return out
+
+
+def synth_tokens(seed, stream_id, vocab, n):
+    out = np.empty(n, np.uint32)
+    check(lib().aaedn_synth_tokens(seed, stream_id, vocab, _p(out), n))
+    return out
+
+
+def rope_table(max_seq, head_dim, theta=10000.0, formula=1):
+    c = np.empty(max_seq * (head_dim // 2), np.float32)
+    s = np.empty_like(c)
+    check(lib().aaedn_rope_table(_p(c), _p(s), max_seq, head_dim, theta, formula))
+    return c, s
+
+
+# ------------------------------------------------------------------ kernels
+def dequant_4bit(d_data, d_scales, d_out, n, scale_kind=SCALE_U16INT, stream=None):
+    check(lib().aaedn_cu_dequant_4bit(_p(d_data), _p(d_scales), _p(d_out), n, scale_kind, stream))
+
+
+def fused_matmul(d_in, d_w, d_scales, d_out, M, N, K, lda=None, ldb=None, ldc=None, scale_kind=SCALE_F16,
+                 stream=None):
+    check(lib().aaedn_cu_fused_matmul(_p(d_in), _p(d_w), _p(d_scales), _p(d_out), M, N, K, lda or K, ldb or K,
+                                      ldc or N, scale_kind, stream))
+
+
+def f32_matmul(d_in, d_w, d_out, M, N, K, stream=None):
+    check(lib().aaedn_cu_f32_matmul(_p(d_in), _p(d_w), _p(d_out), M, N, K, K, K, N, stream))
+
+
+def rmsnorm(d_in, d_out, d_w, n, eps=1e-6, stream=None):
+    check(lib().aaedn_cu_rmsnorm(_p(d_in), _p(d_out), _p(d_w), n, eps, stream))
+
+
+def rope_apply(d_q, d_k, seq_len, head_dim, d_cos, d_sin, stream=None):
+    check(lib().aaedn_cu_rope_apply(_p(d_q), _p(d_k), seq_len, head_dim, _p(d_cos), _p(d_sin), stream))
+
+
+def attention(d_q, d_k, d_v, segments, d_out, n_heads, head_dim, scale, stream=None):
+    segs = np.ascontiguousarray(segments, np.uint32).reshape(-1)
+    check(lib().aaedn_cu_attention(_p(d_q), _p(d_k), _p(d_v), _p(segs), segs.size // 2, _p(d_out), n_heads,
+                                   head_dim, scale, stream))
+
+
+def device_sync():
+    check(lib().aaedn_device_sync())
+
+
+# -------------------------------------------------------------------- model
+TINY = dict(dim=288, n_layers=6, n_heads=6, n_kv_heads=6, head_dim=48, ffn_dim=768, vocab=32000, max_seq=256,
+            rope_theta=10000.0, eps=1e-6)
+LLAMA2_7B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, head_dim=128, ffn_dim=11008, vocab=32000,
+                 max_seq=4096, rope_theta=10000.0, eps=1e-6)
+LLAMA3_8B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336, vocab=128256,
+                 max_seq=4096, rope_theta=500000.0, eps=1e-6)
+
+LAYER_MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
+
+
+def layer_shapes(cfg):
+    D, hd, H, KV, F = cfg["dim"], cfg["head_dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["ffn_dim"]
+    return {"wq": (H * hd, D), "wk": (KV * hd, D), "wv": (KV * hd, D), "wo": (D, H * hd), "wg": (F, D),
+            "wu": (F, D), "wd": (D, F)}
+
+
+def synthetic_weights(cfg, seed):
+    """Host weights of the seeded synthetic model in logical layout, the same
+    tensors aaedn_model_synthesize uploads: N(0, 0.02) linear weights
+    quantized with the block quantizer, fp32 embedding/lm_head, gains 1.0.
+    Tensor ids: embedding 0, lm_head 1, layer l: 16 + 8l + index in
+    (q, k, v, o, g, u, d)."""
+    L, D, V = cfg["n_layers"], cfg["dim"], cfg["vocab"]
+    shapes = layer_shapes(cfg)
+    w = {k: [] for k in LAYER_MATS}
+    w["attn_norm"] = [np.ones(D, np.float32) for _ in range(L)]
+    w["ffn_norm"] = [np.ones(D, np.float32) for _ in range(L)]
+    for l in range(L):
+        for i, name in enumerate(LAYER_MATS):
+            r, c = shapes[name]
+            x = synth_normal(seed, 16 + 8 * l + i, r * c)
+            w[name].append(quantize_q4(x))
+    w["embedding"] = synth_normal(seed, 0, V * D).reshape(V, D)
+    w["lm_head"] = synth_normal(seed, 1, V * D).reshape(V, D)
+    w["final_norm"] = np.ones(D, np.float32)
+    return w
+
+
+class Model:
+    """One aaedn_model (device arena, weights, paged KV cache, stream)."""
+
+    def __init__(self, cfg):
+        self.cfg = dict(cfg)
+        c = ModelConfig(**{k: self.cfg[k] for k, _ in ModelConfig._fields_})
+        h = _vp()
+        check(lib().aaedn_model_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().aaedn_model_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def stream(self):
+        return lib().aaedn_model_stream(self.h)
+
+    @property
+    def arena_bytes(self):
+        return int(lib().aaedn_model_arena_bytes(self.h))
+
+    @property
+    def pos(self):
+        return int(lib().aaedn_model_pos(self.h))
+
+    @property
+    def kernels_per_step(self):
+        return int(lib().aaedn_model_kernels_per_step(self.h))
+
+    def set_weights(self, w):
+        keep = []
+        for l in range(self.cfg["n_layers"]):
+            lh = LayerHost()
+            for name in LAYER_MATS:
+                d, s = w[name][l]
+                d = np.ascontiguousarray(d)
+                s = np.ascontiguousarray(s)
+                keep += [d, s]
+                setattr(lh, name, _p(d))
+                setattr(lh, "s" + name[1], _p(s))
+            an = np.ascontiguousarray(w["attn_norm"][l], np.float32)
+            fn = np.ascontiguousarray(w["ffn_norm"][l], np.float32)
+            keep += [an, fn]
+            lh.attn_norm, lh.ffn_norm = _p(an), _p(fn)
+            check(lib().aaedn_model_set_layer(self.h, l, ctypes.byref(lh)))
+        emb = np.ascontiguousarray(w["embedding"], np.float32)
+        fnorm = np.ascontiguousarray(w["final_norm"], np.float32)
+        lm = np.ascontiguousarray(w["lm_head"], np.float32)
+        check(lib().aaedn_model_set_globals(self.h, _p(emb), _p(fnorm), _p(lm)))
+
+    def synthesize(self, seed):
+        check(lib().aaedn_model_synthesize(self.h, seed))
+
+    def reset(self):
+        check(lib().aaedn_model_reset(self.h))
+
+    def forward(self, tokens, want_logits=True):
+        t = np.ascontiguousarray(tokens, np.uint32).reshape(-1)
+        logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        check(lib().aaedn_model_forward(self.h, _p(t), t.size, _p(logits)))
+        return logits
+
+    def generate(self, prompt, n_new):
+        p = np.ascontiguousarray(prompt, np.uint32).reshape(-1)
+        out = np.empty(n_new, np.uint32)
+        check(lib().aaedn_model_generate(self.h, _p(p), p.size, n_new, _p(out)))
+        return out
+
+    def decode_steps(self, n):
+        check(lib().aaedn_model_decode_steps(self.h, n))
+
+    def logits(self):
+        out = np.empty(self.cfg["vocab"], np.float32)
+        check(lib().aaedn_model_logits(self.h, _p(out)))
+        return out
+
+    def tokens(self, n):
+        out = np.empty(n, np.uint32)
+        check(lib().aaedn_model_tokens(self.h, _p(out), n))
+        return out
+
+    def rewind(self, pos):
+        check(lib().aaedn_model_rewind(self.h, pos))
+
+    def profile_step(self):
+        """Device ms of every kernel of one decode step (launch order)."""
+        n = self.kernels_per_step
+        out = np.empty(n, np.float32)
+        got = _u32()
+        check(lib().aaedn_model_profile_step(self.h, _p(out), n, ctypes.byref(got)))
+        return out[:got.value]
+
+    def forward_debug(self, token):
+        hidden = np.empty((self.cfg["n_layers"], self.cfg["dim"]), np.float32)
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        check(lib().aaedn_model_forward_debug(self.h, int(token), _p(hidden), _p(logits)))
+        return hidden, logits

@@ -1,0 +1,126 @@
+// common.cuh — shared device/host helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "../../include/aaedn_b200.h"
+#include "../host/host_common.hpp"
+
+namespace aaedn_dev
+{
+
+using aaedn_host::set_error;
+
+// Kernels launched by this library (host-side count, graph replays add the
+// per-step node count).
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+#define AAEDN_CUDA_TRY(expr)                                                                                  \
+    do                                                                                                        \
+    {                                                                                                         \
+        cudaError_t _e = (expr);                                                                              \
+        if (_e != cudaSuccess)                                                                                \
+            return ::aaedn_host::set_error(AAEDN_ECUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                                           __FILE__, __LINE__);                                               \
+    } while (0)
+
+#define AAEDN_LAUNCH_CHECK(name)                                                                              \
+    do                                                                                                        \
+    {                                                                                                         \
+        cudaError_t _e = cudaGetLastError();                                                                  \
+        if (_e != cudaSuccess)                                                                                \
+            return ::aaedn_host::set_error(AAEDN_ECUDA, "launch of %s failed: %s", name, cudaGetErrorString(_e)); \
+        ::aaedn_dev::count_launch();                                                                          \
+    } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Scale decode: 0 = IEEE fp16 bits, 1 = integer cast (src/dequant.cpp:19).
+template <int SK>
+__device__ __forceinline__ float decode_scale(uint16_t s)
+{
+    if constexpr (SK == AAEDN_SCALE_F16)
+        return __half2float(__ushort_as_half(s));
+    else
+        return (float)s;
+}
+
+// Streaming 16-byte load of weights: read once, do not keep in L1.
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p)
+{
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p)
+{
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float4 ldg_stream_f4(const float* p)
+{
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// two bf16 (lo = first element) in one 32-bit register
+__device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 lo, __nv_bfloat16 hi)
+{
+    return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// D += A(16x16 bf16, row) * B(16x8 bf16, col), fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float& d0, float& d1, float& d2, float& d3, uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Nibble pairs of one 32-bit weight word (8 codes, code i in bits 4i..4i+3)
+// as bf16x2 values 16 + code: the code lands in mantissa bits 3..6 of each
+// half under the exponent of 16.0 (0x4180). E0 = codes (0,4), E1 = (1,5),
+// E2 = (2,6), E3 = (3,7).
+__device__ __forceinline__ uint32_t nib_e0(uint32_t w) { return ((w << 3) & 0x00780078u) | 0x41804180u; }
+__device__ __forceinline__ uint32_t nib_e1(uint32_t w) { return ((w >> 1) & 0x00780078u) | 0x41804180u; }
+__device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return ((w >> 5) & 0x00780078u) | 0x41804180u; }
+__device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return ((w >> 9) & 0x00780078u) | 0x41804180u; }
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+} // namespace aaedn_dev

@@ -1,0 +1,1013 @@
+// model.cu — the token loop on one B200: src/transformer.cpp:34-243
+// (transformer_init / transformer_forward) rebuilt as a device-resident
+// decode step.
+//
+// One step (one token at position pos) is 5 kernels per layer + 1:
+//   qkv   : RMSNorm prologue (layer 0: embedding gather) -> fused QKV
+//           dequant-GEMV -> RoPE on q,k -> k,v appended to the paged cache
+//   attn  : split-K decode attention over the cache, GQA-aware
+//   o     : dequant-GEMV + residual add into the hidden state
+//   gu    : RMSNorm prologue -> fused gate/up dequant-GEMV -> silu(g)*u
+//   down  : dequant-GEMV + residual add
+//   lm    : final RMSNorm -> fp32 lm_head GEMV -> greedy argmax -> state
+// The step reads its position and input token from device memory, so a
+// whole step is captured once as a CUDA graph and replayed.
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv_q4.cuh"
+
+using namespace aaedn_dev;
+
+namespace
+{
+
+struct LmParams
+{
+    const float* hidden;
+    const float* gain;
+    float eps;
+    int dim;
+    const float* w; // [vocab][dim] fp32
+    int vocab;
+    float* logits;
+    float* part_val;
+    int* part_idx;
+    DecodeState* state;
+    uint32_t* out_tokens;
+    int max_seq;
+    int rows_per_cta;
+};
+
+// Final RMSNorm (src/transformer.cpp:230), fp32 lm_head GEMV
+// (:232-238) and greedy argmax with ties to the lowest id; the last CTA
+// advances the decode state.
+__global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
+{
+    extern __shared__ __align__(16) float xs[];
+    float* misc = xs + p.dim;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float ss = 0.0f;
+    for (int i = tid; i < p.dim; i += blockDim.x)
+        ss = fmaf(p.hidden[i], p.hidden[i], ss);
+    ss = block_sum(ss, misc);
+    const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.dim), p.eps));
+    for (int i = tid; i < p.dim; i += blockDim.x)
+        xs[i] = __fmul_rn(__fmul_rn(p.hidden[i], rms), p.gain[i]);
+    __syncthreads();
+
+    const int n0 = blockIdx.x * p.rows_per_cta;
+    const int n1 = min(p.vocab, n0 + p.rows_per_cta);
+    const int d4 = p.dim >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int n = n0 + warp; n < n1; n += 8)
+    {
+        const float4* wr = reinterpret_cast<const float4*>(p.w + (size_t)n * p.dim);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int k = lane; k < d4; k += 32)
+        {
+            const float4 wv = ldg_stream_f4(reinterpret_cast<const float*>(wr + k));
+            const float4 xv = x4[k];
+            acc = fmaf(wv.x, xv.x, acc);
+            acc = fmaf(wv.y, xv.y, acc);
+            acc = fmaf(wv.z, xv.z, acc);
+            acc = fmaf(wv.w, xv.w, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0)
+            p.logits[n] = acc;
+        if (acc > bv)
+        {
+            bv = acc;
+            bi = n;
+        }
+    }
+    __shared__ float s_v[8];
+    __shared__ int s_i[8];
+    __shared__ unsigned s_last;
+    if (lane == 0)
+    {
+        s_v[warp] = bv;
+        s_i[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0)
+    {
+        float v = s_v[0];
+        int i = s_i[0];
+        for (int w = 1; w < 8; ++w)
+            if (s_v[w] > v || (s_v[w] == v && s_i[w] < i))
+            {
+                v = s_v[w];
+                i = s_i[w];
+            }
+        p.part_val[blockIdx.x] = v;
+        p.part_idx[blockIdx.x] = i;
+        __threadfence();
+        const unsigned prev = atomicAdd(&p.state->lm_counter, 1u);
+        s_last = prev == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_last)
+        return;
+    __threadfence();
+    float v = -INFINITY;
+    int i = INT_MAX;
+    for (int b = tid; b < (int)gridDim.x; b += blockDim.x)
+    {
+        const float pv = __ldcg(p.part_val + b);
+        const int pi = __ldcg(p.part_idx + b);
+        if (pv > v || (pv == v && pi < i))
+        {
+            v = pv;
+            i = pi;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i))
+        {
+            v = ov;
+            i = oi;
+        }
+    }
+    if (lane == 0)
+    {
+        s_v[warp] = v;
+        s_i[warp] = i;
+    }
+    __syncthreads();
+    if (tid == 0)
+    {
+        v = s_v[0];
+        i = s_i[0];
+        for (int w = 1; w < 8; ++w)
+            if (s_v[w] > v || (s_v[w] == v && s_i[w] < i))
+            {
+                v = s_v[w];
+                i = s_i[w];
+            }
+        const uint32_t token = (i == INT_MAX) ? 0u : (uint32_t)i;
+        DecodeState* st = p.state;
+        const uint32_t pos = st->pos;
+        if (pos + 1 >= st->n_prompt)
+        {
+            const uint32_t gi = pos + 1 - st->n_prompt;
+            if (gi < (uint32_t)p.max_seq)
+                p.out_tokens[gi] = token;
+        }
+        st->next_token = token;
+        st->pos = pos + 1;
+        st->lm_counter = 0u;
+    }
+}
+
+struct DevLayer
+{
+    uint8_t *wqkv, *wo, *wgu, *wd;
+    uint16_t *sqkv, *so, *sgu, *sd;
+    float *attn_norm, *ffn_norm;
+    float *k, *v; // [n_pages][n_kv][P][hd]
+};
+
+int pick_rows_per_cta(int groups)
+{
+    if (groups >= 4 * 2 * 148)
+        return 4;
+    if (groups >= 2 * 2 * 148)
+        return 2;
+    return 1;
+}
+
+template <int PRO, int EPI, int R>
+int launch_model_gemv(const GemvParams& p, cudaStream_t st)
+{
+    constexpr int S = GEMV_WARPS / R;
+    auto kern = gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, R, S>;
+    const int groups = (p.N + 15) / 16;
+    const int grid = (groups + R - 1) / R;
+    const size_t smem = gemv_smem_bytes(1, p.kt1 - p.kt0, R, S);
+    kern<<<grid, GEMV_WARPS * 32, smem, st>>>(p);
+    AAEDN_LAUNCH_CHECK("gemv_q4_kernel(model)");
+    return AAEDN_OK;
+}
+
+template <int PRO, int EPI>
+int model_gemv(const GemvParams& p, cudaStream_t st)
+{
+    const int R = pick_rows_per_cta((p.N + 15) / 16);
+    if (R == 4)
+        return launch_model_gemv<PRO, EPI, 4>(p, st);
+    if (R == 2)
+        return launch_model_gemv<PRO, EPI, 2>(p, st);
+    return launch_model_gemv<PRO, EPI, 1>(p, st);
+}
+
+// Opt every model kernel into large dynamic shared memory once, before any
+// stream capture.
+template <int PRO, int EPI>
+int set_gemv_attrs()
+{
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 1, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 2, 4>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 4, 2>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return AAEDN_OK;
+}
+
+int set_model_kernel_attrs()
+{
+    int rc = set_gemv_attrs<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_RMSNORM, EPI_QKV_ROPE>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_PLAIN, EPI_RESIDUAL>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_RMSNORM, EPI_SWIGLU>();
+    return rc;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+} // namespace
+
+struct aaedn_model
+{
+    aaedn_model_config cfg{};
+    cudaStream_t stream = nullptr;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0, used = 0;
+    std::vector<DevLayer> layers;
+    float *embedding = nullptr, *final_norm = nullptr, *lm_head = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    DecodeState* state = nullptr;
+    uint32_t *prompt = nullptr, *out_tokens = nullptr;
+    int* page_table = nullptr;
+    float *hidden = nullptr, *qbuf = nullptr, *attn_out = nullptr, *act = nullptr, *logits = nullptr;
+    float* attn_part = nullptr;
+    unsigned* attn_counters = nullptr;
+    float* lm_part_val = nullptr;
+    int* lm_part_idx = nullptr;
+    float* dbg_hidden = nullptr;
+    int page_size = 64, n_pages = 0;
+    int attn_S = 1, attn_max_tok = 1;
+    int lm_ctas = 1, lm_rows = 8;
+    cudaGraphExec_t graph_exec = nullptr;
+    uint32_t kernels_per_step = 0;
+    uint32_t h_pos = 0;
+    uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
+    bool weights_set = false;
+
+    template <typename T>
+    T* take(size_t bytes)
+    {
+        size_t off = align_up(used, 256);
+        used = off + bytes;
+        return reinterpret_cast<T*>(arena + off);
+    }
+};
+
+static size_t plan_arena(aaedn_model* m, bool carve)
+{
+    const aaedn_model_config& c = m->cfg;
+    const size_t D = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim, V = c.vocab;
+    const size_t qkv_rows = (H + 2 * KV) * hd;
+    m->used = 0;
+    if (carve)
+        m->layers.resize(c.n_layers);
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        DevLayer L{};
+        L.wqkv = m->take<uint8_t>(qkv_rows * D / 2);
+        L.sqkv = m->take<uint16_t>(qkv_rows * D / 32 * 2);
+        L.wo = m->take<uint8_t>(D * H * hd / 2);
+        L.so = m->take<uint16_t>(D * H * hd / 32 * 2);
+        L.wgu = m->take<uint8_t>(2 * F * D / 2);
+        L.sgu = m->take<uint16_t>(2 * F * D / 32 * 2);
+        L.wd = m->take<uint8_t>(D * F / 2);
+        L.sd = m->take<uint16_t>(D * F / 32 * 2);
+        L.attn_norm = m->take<float>(D * 4);
+        L.ffn_norm = m->take<float>(D * 4);
+        L.k = m->take<float>((size_t)m->n_pages * KV * m->page_size * hd * 4);
+        L.v = m->take<float>((size_t)m->n_pages * KV * m->page_size * hd * 4);
+        if (carve)
+            m->layers[l] = L;
+    }
+    m->embedding = m->take<float>(V * D * 4);
+    m->lm_head = m->take<float>(V * D * 4);
+    m->final_norm = m->take<float>(D * 4);
+    m->rope_cos = m->take<float>((size_t)c.max_seq * (hd / 2) * 4);
+    m->rope_sin = m->take<float>((size_t)c.max_seq * (hd / 2) * 4);
+    m->state = m->take<DecodeState>(sizeof(DecodeState));
+    m->prompt = m->take<uint32_t>((size_t)c.max_seq * 4);
+    m->out_tokens = m->take<uint32_t>((size_t)c.max_seq * 4);
+    m->page_table = m->take<int>((size_t)m->n_pages * 4);
+    m->hidden = m->take<float>(D * 4);
+    m->qbuf = m->take<float>(H * hd * 4);
+    m->attn_out = m->take<float>(H * hd * 4);
+    m->act = m->take<float>(F * 4);
+    m->logits = m->take<float>(V * 4);
+    m->attn_part = m->take<float>(H * (size_t)m->attn_S * (hd + 2) * 4);
+    m->attn_counters = m->take<unsigned>(KV * 4);
+    m->lm_part_val = m->take<float>((size_t)m->lm_ctas * 4);
+    m->lm_part_idx = m->take<int>((size_t)m->lm_ctas * 4);
+    m->dbg_hidden = m->take<float>((size_t)c.n_layers * D * 4);
+    return align_up(m->used, 256);
+}
+
+static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr)
+{
+    size_t evi = 0;
+    auto mark = [&]() -> int {
+        if (ev && evi < ev->size())
+            AAEDN_CUDA_TRY(cudaEventRecord((*ev)[evi++], st));
+        return AAEDN_OK;
+    };
+    int mrc = mark();
+    if (mrc)
+        return mrc;
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads, F = (int)c.ffn_dim;
+    int rc;
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        const DevLayer& L = m->layers[l];
+        // --- QKV (+RMSNorm prologue, +RoPE/KV-append epilogue)
+        GemvParams q{};
+        q.w = L.wqkv;
+        q.s = L.sqkv;
+        q.ldb = (size_t)D;
+        q.N = (H + 2 * KV) * hd;
+        q.K = D;
+        q.kt0 = 0;
+        q.kt1 = (D + 127) / 128;
+        q.x = m->hidden;
+        q.lda = (size_t)D;
+        q.gain = L.attn_norm;
+        q.eps = c.eps;
+        q.embedding = m->embedding;
+        q.prompt = m->prompt;
+        q.state = m->state;
+        q.hidden_out = m->hidden;
+        q.q_rows = H * hd;
+        q.kv_rows = KV * hd;
+        q.head_dim = hd;
+        q.n_kv = KV;
+        q.page_size = m->page_size;
+        q.max_pos = (int)c.max_seq;
+        q.qbuf = m->qbuf;
+        q.k_layer = L.k;
+        q.v_layer = L.v;
+        q.page_table = m->page_table;
+        q.rope_cos = m->rope_cos;
+        q.rope_sin = m->rope_sin;
+        rc = (l == 0) ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st) : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st);
+        if (rc)
+            return rc;
+        if ((rc = mark()))
+            return rc;
+        // --- attention
+        AttnParams a{};
+        a.q = m->qbuf;
+        a.k = L.k;
+        a.v = L.v;
+        a.out = m->attn_out;
+        a.part = m->attn_part;
+        a.counters = m->attn_counters;
+        a.n_heads = H;
+        a.n_kv = KV;
+        a.head_dim = hd;
+        a.S = m->attn_S;
+        a.scale = 1.0f / std::sqrt((float)hd); // src/transformer.cpp:198
+        a.state = m->state;
+        a.max_len = (int)c.max_seq;
+        a.max_tok = m->attn_max_tok;
+        a.page_table = m->page_table;
+        a.page_size = m->page_size;
+        const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
+        attn_split_kernel<1><<<dim3(KV, m->attn_S), ATTN_THREADS, asmem, st>>>(a);
+        AAEDN_LAUNCH_CHECK("attn_split_kernel(model)");
+        if ((rc = mark()))
+            return rc;
+        // --- O projection + residual
+        GemvParams o{};
+        o.w = L.wo;
+        o.s = L.so;
+        o.ldb = (size_t)H * hd;
+        o.N = D;
+        o.K = H * hd;
+        o.kt0 = 0;
+        o.kt1 = (H * hd + 127) / 128;
+        o.x = m->attn_out;
+        o.lda = (size_t)H * hd;
+        o.y = m->hidden;
+        o.ldc = (size_t)D;
+        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st);
+        if (rc)
+            return rc;
+        if ((rc = mark()))
+            return rc;
+        // --- gate/up (+RMSNorm prologue, SwiGLU epilogue)
+        GemvParams gu{};
+        gu.w = L.wgu;
+        gu.s = L.sgu;
+        gu.ldb = (size_t)D;
+        gu.N = 2 * F;
+        gu.K = D;
+        gu.kt0 = 0;
+        gu.kt1 = (D + 127) / 128;
+        gu.x = m->hidden;
+        gu.lda = (size_t)D;
+        gu.gain = L.ffn_norm;
+        gu.eps = c.eps;
+        gu.act = m->act;
+        rc = model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st);
+        if (rc)
+            return rc;
+        if ((rc = mark()))
+            return rc;
+        // --- down + residual
+        GemvParams dn{};
+        dn.w = L.wd;
+        dn.s = L.sd;
+        dn.ldb = (size_t)F;
+        dn.N = D;
+        dn.K = F;
+        dn.kt0 = 0;
+        dn.kt1 = (F + 127) / 128;
+        dn.x = m->act;
+        dn.lda = (size_t)F;
+        dn.y = m->hidden;
+        dn.ldc = (size_t)D;
+        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st);
+        if (rc)
+            return rc;
+        if ((rc = mark()))
+            return rc;
+        if (debug)
+            AAEDN_CUDA_TRY(cudaMemcpyAsync(m->dbg_hidden + (size_t)l * D, m->hidden, (size_t)D * 4,
+                                           cudaMemcpyDeviceToDevice, st));
+    }
+    LmParams lp{};
+    lp.hidden = m->hidden;
+    lp.gain = m->final_norm;
+    lp.eps = c.eps;
+    lp.dim = D;
+    lp.w = m->lm_head;
+    lp.vocab = (int)c.vocab;
+    lp.logits = m->logits;
+    lp.part_val = m->lm_part_val;
+    lp.part_idx = m->lm_part_idx;
+    lp.state = m->state;
+    lp.out_tokens = m->out_tokens;
+    lp.max_seq = (int)c.max_seq;
+    lp.rows_per_cta = m->lm_rows;
+    lm_head_argmax_kernel<<<m->lm_ctas, 256, (size_t)(D + 64) * 4, st>>>(lp);
+    AAEDN_LAUNCH_CHECK("lm_head_argmax_kernel");
+        if ((rc = mark()))
+            return rc;
+    return AAEDN_OK;
+}
+
+static int ensure_graph(aaedn_model* m)
+{
+    if (m->graph_exec)
+        return AAEDN_OK;
+    const uint64_t before = g_launches.load();
+    AAEDN_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, m->stream, false);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    const uint64_t after = g_launches.load();
+    g_launches.fetch_sub(after - before);
+    m->kernels_per_step = (uint32_t)(after - before);
+    if (rc)
+    {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "graph capture failed: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->graph_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess)
+    {
+        m->graph_exec = nullptr;
+        return set_error(AAEDN_ECUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+    }
+    return AAEDN_OK;
+}
+
+static int run_steps(aaedn_model* m, size_t n)
+{
+    int rc = ensure_graph(m);
+    if (rc)
+        return rc;
+    for (size_t i = 0; i < n; ++i)
+    {
+        AAEDN_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->stream));
+        count_launch(m->kernels_per_step);
+    }
+    return AAEDN_OK;
+}
+
+// pos / n_prompt words of the device state
+static int write_state(aaedn_model* m, uint32_t pos, uint32_t n_prompt)
+{
+    uint32_t* st = m->pinned + m->cfg.max_seq;
+    st[0] = pos;
+    st[1] = n_prompt;
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->state, st, 8, cudaMemcpyHostToDevice, m->stream));
+    return AAEDN_OK;
+}
+
+static int put_tokens(aaedn_model* m, const uint32_t* h_tokens, size_t n)
+{
+    // staging must not be rewritten while an earlier copy may still read it
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    std::memcpy(m->pinned, h_tokens, n * 4);
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->prompt + m->h_pos, m->pinned, n * 4, cudaMemcpyHostToDevice, m->stream));
+    return AAEDN_OK;
+}
+
+#define MODEL_OK(m)                                                                                           \
+    do                                                                                                        \
+    {                                                                                                         \
+        if (!(m))                                                                                             \
+            return set_error(AAEDN_EINVAL, "null model");                                                    \
+    } while (0)
+
+extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** out)
+{
+    if (!cfg || !out)
+        return set_error(AAEDN_EINVAL, "aaedn_model_create: null argument");
+    *out = nullptr;
+    const aaedn_model_config& c = *cfg;
+    if (c.dim == 0 || c.n_layers == 0 || c.n_heads == 0 || c.n_kv_heads == 0 || c.head_dim == 0 || c.ffn_dim == 0 ||
+        c.vocab == 0 || c.max_seq == 0)
+        return set_error(AAEDN_EINVAL, "aaedn_model_create: zero dimension");
+    if (c.dim % 32 || (c.n_heads * c.head_dim) % 32 || c.ffn_dim % 32 || c.head_dim % 16 || c.dim % 4 ||
+        c.n_heads % c.n_kv_heads || c.head_dim > (uint32_t)ATTN_MAX_HD || c.n_heads / c.n_kv_heads > 32)
+        return set_error(AAEDN_EINVAL,
+                         "aaedn_model_create: need dim, n_heads*head_dim, ffn_dim multiples of 32, head_dim a "
+                         "multiple of 16 (<= %d), n_kv_heads dividing n_heads",
+                         ATTN_MAX_HD);
+    if (c.dim > 65536 || c.ffn_dim > 32768 || c.max_seq > (1u << 20))
+        return set_error(AAEDN_EINVAL, "aaedn_model_create: dimension too large");
+    aaedn_model* m = new aaedn_model();
+    m->cfg = c;
+    m->page_size = 64;
+    m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
+    int S = (int)((2 * 148 + c.n_kv_heads - 1) / c.n_kv_heads);
+    S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
+    S = std::min(S, 64);
+    m->attn_S = S;
+    m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
+    int rows = (int)((c.vocab + 4 * 148 - 1) / (4 * 148));
+    rows = (rows + 7) / 8 * 8;
+    m->lm_rows = std::max(8, rows);
+    m->lm_ctas = (int)((c.vocab + m->lm_rows - 1) / m->lm_rows);
+    const size_t bytes = plan_arena(m, false);
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&m->arena), bytes);
+    if (e != cudaSuccess)
+    {
+        delete m;
+        return set_error(e == cudaErrorMemoryAllocation ? AAEDN_ENOMEM : AAEDN_ECUDA,
+                         "aaedn_model_create: device arena of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    m->arena_bytes = bytes;
+    plan_arena(m, true);
+    int rc = AAEDN_OK;
+    auto fail = [&](int code) {
+        aaedn_model_destroy(m);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_error(AAEDN_ECUDA, "stream creation failed"));
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), ((size_t)c.max_seq + 16) * 4) != cudaSuccess)
+        return fail(set_error(AAEDN_ENOMEM, "pinned staging allocation failed"));
+    if (cudaMemset(m->arena, 0, bytes) != cudaSuccess)
+        return fail(set_error(AAEDN_ECUDA, "arena clear failed"));
+    // RoPE tables (D3) and the identity page table of the single sequence
+    std::vector<float> cs((size_t)c.max_seq * (c.head_dim / 2)), sn(cs.size());
+    rc = aaedn_rope_table(cs.data(), sn.data(), c.max_seq, c.head_dim, (double)c.rope_theta, 1);
+    if (rc)
+        return fail(rc);
+    std::vector<int> pt(m->n_pages);
+    for (int i = 0; i < m->n_pages; ++i)
+        pt[i] = i;
+    std::vector<float> ones(c.dim, 1.0f);
+    if (cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->final_norm, ones.data(), c.dim * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(set_error(AAEDN_ECUDA, "table upload failed"));
+    for (auto& L : m->layers)
+        if (cudaMemcpy(L.attn_norm, ones.data(), c.dim * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(L.ffn_norm, ones.data(), c.dim * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(set_error(AAEDN_ECUDA, "norm upload failed"));
+    const size_t lm_smem = (size_t)(c.dim + 64) * 4;
+    if (lm_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lm_smem) !=
+            cudaSuccess)
+        return fail(set_error(AAEDN_ECUDA, "lm_head smem attribute failed"));
+    if (cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        cudaSuccess)
+        return fail(set_error(AAEDN_ECUDA, "attention smem attribute failed"));
+    rc = set_model_kernel_attrs();
+    if (rc)
+        return fail(rc);
+    *out = m;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_destroy(aaedn_model* m)
+{
+    if (!m)
+        return AAEDN_OK;
+    if (m->stream)
+        cudaStreamSynchronize(m->stream);
+    if (m->graph_exec)
+        cudaGraphExecDestroy(m->graph_exec);
+    if (m->arena)
+        cudaFree(m->arena);
+    if (m->pinned)
+        cudaFreeHost(m->pinned);
+    if (m->stream)
+        cudaStreamDestroy(m->stream);
+    delete m;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_config_get(const aaedn_model* m, aaedn_model_config* out)
+{
+    MODEL_OK(m);
+    if (!out)
+        return set_error(AAEDN_EINVAL, "null output");
+    *out = m->cfg;
+    return AAEDN_OK;
+}
+
+extern "C" void* aaedn_model_stream(aaedn_model* m) { return m ? (void*)m->stream : nullptr; }
+extern "C" size_t aaedn_model_arena_bytes(const aaedn_model* m) { return m ? m->arena_bytes : 0; }
+extern "C" uint32_t aaedn_model_pos(aaedn_model* m) { return m ? m->h_pos : 0; }
+extern "C" uint32_t aaedn_model_kernels_per_step(const aaedn_model* m)
+{
+    return m ? 5u * m->cfg.n_layers + 1u : 0u;
+}
+
+// Device row r of a rope-paired head block holds logical row
+// 8j + r (r < 8) or half + 8j + r - 8 (r >= 8), j = r_in_head / 16.
+static inline size_t rope_pair_row(size_t r_in_head, size_t hd)
+{
+    const size_t j = r_in_head / 16, r = r_in_head % 16;
+    return r < 8 ? 8 * j + r : hd / 2 + 8 * j + (r - 8);
+}
+
+static void copy_row(std::vector<uint8_t>& dd, std::vector<uint16_t>& ds, size_t drow, const uint8_t* sd,
+                     const uint16_t* ss, size_t srow, size_t K)
+{
+    std::memcpy(dd.data() + drow * K / 2, sd + srow * K / 2, K / 2);
+    std::memcpy(ds.data() + drow * K / 32, ss + srow * K / 32, K / 32 * 2);
+}
+
+extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn_layer_host* w)
+{
+    MODEL_OK(m);
+    if (!w || layer >= m->cfg.n_layers)
+        return set_error(AAEDN_EINVAL, "aaedn_model_set_layer: bad layer or null weights");
+    if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->sq || !w->sk || !w->sv || !w->so ||
+        !w->sg || !w->su || !w->sd)
+        return set_error(AAEDN_EINVAL, "aaedn_model_set_layer: null tensor");
+    const aaedn_model_config& c = m->cfg;
+    const size_t D = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim;
+    const DevLayer& L = m->layers[layer];
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    {
+        const size_t rows = (H + 2 * KV) * hd;
+        std::vector<uint8_t> dd(rows * D / 2);
+        std::vector<uint16_t> ds(rows * D / 32);
+        for (size_t dr = 0; dr < rows; ++dr)
+        {
+            if (dr < H * hd)
+                copy_row(dd, ds, dr, w->wq, w->sq, (dr / hd) * hd + rope_pair_row(dr % hd, hd), D);
+            else if (dr < (H + KV) * hd)
+            {
+                const size_t rel = dr - H * hd;
+                copy_row(dd, ds, dr, w->wk, w->sk, (rel / hd) * hd + rope_pair_row(rel % hd, hd), D);
+            }
+            else
+                copy_row(dd, ds, dr, w->wv, w->sv, dr - (H + KV) * hd, D);
+        }
+        AAEDN_CUDA_TRY(cudaMemcpy(L.wqkv, dd.data(), dd.size(), cudaMemcpyHostToDevice));
+        AAEDN_CUDA_TRY(cudaMemcpy(L.sqkv, ds.data(), ds.size() * 2, cudaMemcpyHostToDevice));
+    }
+    AAEDN_CUDA_TRY(cudaMemcpy(L.wo, w->wo, D * H * hd / 2, cudaMemcpyHostToDevice));
+    AAEDN_CUDA_TRY(cudaMemcpy(L.so, w->so, D * H * hd / 32 * 2, cudaMemcpyHostToDevice));
+    {
+        const size_t rows = 2 * F;
+        std::vector<uint8_t> dd(rows * D / 2);
+        std::vector<uint16_t> ds(rows * D / 32);
+        for (size_t dr = 0; dr < rows; ++dr)
+        {
+            const size_t j = dr / 16, r = dr % 16;
+            if (r < 8)
+                copy_row(dd, ds, dr, w->wg, w->sg, 8 * j + r, D);
+            else
+                copy_row(dd, ds, dr, w->wu, w->su, 8 * j + r - 8, D);
+        }
+        AAEDN_CUDA_TRY(cudaMemcpy(L.wgu, dd.data(), dd.size(), cudaMemcpyHostToDevice));
+        AAEDN_CUDA_TRY(cudaMemcpy(L.sgu, ds.data(), ds.size() * 2, cudaMemcpyHostToDevice));
+    }
+    AAEDN_CUDA_TRY(cudaMemcpy(L.wd, w->wd, D * F / 2, cudaMemcpyHostToDevice));
+    AAEDN_CUDA_TRY(cudaMemcpy(L.sd, w->sd, D * F / 32 * 2, cudaMemcpyHostToDevice));
+    if (w->attn_norm)
+        AAEDN_CUDA_TRY(cudaMemcpy(L.attn_norm, w->attn_norm, D * 4, cudaMemcpyHostToDevice));
+    if (w->ffn_norm)
+        AAEDN_CUDA_TRY(cudaMemcpy(L.ffn_norm, w->ffn_norm, D * 4, cudaMemcpyHostToDevice));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_set_globals(aaedn_model* m, const float* h_embedding, const float* h_final_norm,
+                                       const float* h_lm_head)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    if (h_embedding)
+        AAEDN_CUDA_TRY(cudaMemcpy(m->embedding, h_embedding, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice));
+    if (h_final_norm)
+        AAEDN_CUDA_TRY(cudaMemcpy(m->final_norm, h_final_norm, (size_t)c.dim * 4, cudaMemcpyHostToDevice));
+    if (h_lm_head)
+        AAEDN_CUDA_TRY(cudaMemcpy(m->lm_head, h_lm_head, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_synthesize(aaedn_model* m, uint64_t seed)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    const size_t D = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim, V = c.vocab;
+    struct Mat
+    {
+        size_t rows, cols;
+        std::vector<uint8_t> d;
+        std::vector<uint16_t> s;
+    };
+    Mat mats[7] = {{H * hd, D, {}, {}}, {KV * hd, D, {}, {}}, {KV * hd, D, {}, {}}, {D, H * hd, {}, {}},
+                   {F, D, {}, {}},      {F, D, {}, {}},       {D, F, {}, {}}};
+    std::vector<float> buf;
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        for (int i = 0; i < 7; ++i)
+        {
+            const size_t n = mats[i].rows * mats[i].cols;
+            buf.resize(n);
+            aaedn_host::synth_normal(seed, 16 + 8ull * l + (uint64_t)i, 0.02f, buf.data(), n);
+            mats[i].d.assign((n + 1) / 2, 0);
+            mats[i].s.assign((n + 31) / 32, 0);
+            aaedn_host::quantize_q4(buf.data(), n, mats[i].d.data(), mats[i].s.data());
+        }
+        aaedn_layer_host w{};
+        w.wq = mats[0].d.data();
+        w.sq = mats[0].s.data();
+        w.wk = mats[1].d.data();
+        w.sk = mats[1].s.data();
+        w.wv = mats[2].d.data();
+        w.sv = mats[2].s.data();
+        w.wo = mats[3].d.data();
+        w.so = mats[3].s.data();
+        w.wg = mats[4].d.data();
+        w.sg = mats[4].s.data();
+        w.wu = mats[5].d.data();
+        w.su = mats[5].s.data();
+        w.wd = mats[6].d.data();
+        w.sd = mats[6].s.data();
+        int rc = aaedn_model_set_layer(m, l, &w);
+        if (rc)
+            return rc;
+    }
+    buf.assign(V * D, 0.0f);
+    aaedn_host::synth_normal(seed, 0, 0.02f, buf.data(), V * D);
+    int rc = aaedn_model_set_globals(m, buf.data(), nullptr, nullptr);
+    if (rc)
+        return rc;
+    aaedn_host::synth_normal(seed, 1, 0.02f, buf.data(), V * D);
+    return aaedn_model_set_globals(m, nullptr, nullptr, buf.data());
+}
+
+extern "C" int aaedn_model_reset(aaedn_model* m)
+{
+    MODEL_OK(m);
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    AAEDN_CUDA_TRY(cudaMemsetAsync(m->state, 0, sizeof(DecodeState), m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->h_pos = 0;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, size_t n, float* h_logits)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    if (n == 0 || !h_tokens) // src/transformer.cpp:130-135: zero logits
+    {
+        if (h_logits)
+            std::memset(h_logits, 0, (size_t)c.vocab * 4);
+        return AAEDN_OK;
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (h_tokens[i] >= c.vocab) // src/transformer.cpp:137-142
+        {
+            if (h_logits)
+                std::memset(h_logits, 0, (size_t)c.vocab * 4);
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_tokens[i], c.vocab);
+        }
+    if ((size_t)m->h_pos + n > c.max_seq)
+        return set_error(AAEDN_ESTATE, "sequence full: pos %u + %zu > max_seq %u", m->h_pos, n, c.max_seq);
+    int rc = put_tokens(m, h_tokens, n);
+    if (!rc)
+        rc = write_state(m, m->h_pos, m->h_pos + (uint32_t)n);
+    if (!rc)
+        rc = run_steps(m, n);
+    if (rc)
+        return rc;
+    m->h_pos += (uint32_t)n;
+    if (h_logits)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, size_t n_prompt, size_t n_new,
+                                    uint32_t* h_out)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    if (!h_prompt || n_prompt == 0 || (n_new && !h_out))
+        return set_error(AAEDN_EINVAL, "aaedn_model_generate: empty prompt or null output");
+    for (size_t i = 0; i < n_prompt; ++i)
+        if (h_prompt[i] >= c.vocab)
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_prompt[i], c.vocab);
+    const size_t steps = n_prompt + (n_new ? n_new - 1 : 0);
+    if ((size_t)m->h_pos + steps > c.max_seq)
+        return set_error(AAEDN_ESTATE, "sequence full: pos %u + %zu steps > max_seq %u", m->h_pos, steps, c.max_seq);
+    int rc = put_tokens(m, h_prompt, n_prompt);
+    if (!rc)
+        rc = write_state(m, m->h_pos, m->h_pos + (uint32_t)n_prompt);
+    if (!rc)
+        rc = run_steps(m, steps);
+    if (rc)
+        return rc;
+    m->h_pos += (uint32_t)steps;
+    if (n_new)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_out, m->out_tokens, n_new * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_decode_steps(aaedn_model* m, size_t n_steps)
+{
+    MODEL_OK(m);
+    if (m->h_pos == 0)
+        return set_error(AAEDN_ESTATE, "aaedn_model_decode_steps: no token in the sequence yet");
+    if ((size_t)m->h_pos + n_steps > m->cfg.max_seq)
+        return set_error(AAEDN_ESTATE, "sequence full: pos %u + %zu > max_seq %u", m->h_pos, n_steps, m->cfg.max_seq);
+    int rc = run_steps(m, n_steps);
+    if (rc)
+        return rc;
+    m->h_pos += (uint32_t)n_steps;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_logits(aaedn_model* m, float* h_logits)
+{
+    MODEL_OK(m);
+    if (!h_logits)
+        return set_error(AAEDN_EINVAL, "null output");
+    AAEDN_CUDA_TRY(
+        cudaMemcpyAsync(h_logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n)
+{
+    MODEL_OK(m);
+    if (n > m->cfg.max_seq || (n && !h_out))
+        return set_error(AAEDN_EINVAL, "aaedn_model_tokens: bad count");
+    if (n)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_out, m->out_tokens, n * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* h_hidden, float* h_logits)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    if (token >= c.vocab)
+        return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", token, c.vocab);
+    if (m->h_pos + 1 > c.max_seq)
+        return set_error(AAEDN_ESTATE, "sequence full");
+    int rc = put_tokens(m, &token, 1);
+    if (!rc)
+        rc = write_state(m, m->h_pos, m->h_pos + 1);
+    if (!rc)
+        rc = enqueue_step(m, m->stream, true);
+    if (rc)
+        return rc;
+    m->h_pos += 1;
+    if (h_hidden)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_hidden, m->dbg_hidden, (size_t)c.n_layers * c.dim * 4,
+                                       cudaMemcpyDeviceToHost, m->stream));
+    if (h_logits)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_rewind(aaedn_model* m, uint32_t pos)
+{
+    MODEL_OK(m);
+    if (pos == 0 || pos > m->h_pos)
+        return set_error(AAEDN_EINVAL, "aaedn_model_rewind: pos %u outside [1, %u]", pos, m->h_pos);
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    // inputs from here on are the greedy tokens: n_prompt <= pos
+    int rc = write_state(m, pos, pos);
+    if (rc)
+        return rc;
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->h_pos = pos;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t cap, uint32_t* n_out)
+{
+    MODEL_OK(m);
+    const uint32_t nk = aaedn_model_kernels_per_step(m);
+    if (n_out)
+        *n_out = nk;
+    if (!h_ms || cap < nk)
+        return set_error(AAEDN_EINVAL, "aaedn_model_profile_step: need room for %u timings", nk);
+    if (m->h_pos == 0 || m->h_pos + 1 > m->cfg.max_seq)
+        return set_error(AAEDN_ESTATE, "aaedn_model_profile_step: sequence empty or full");
+    std::vector<cudaEvent_t> ev(nk + 1, nullptr);
+    for (auto& e : ev)
+        AAEDN_CUDA_TRY(cudaEventCreate(&e));
+    auto cleanup = [&]() {
+        for (auto& e : ev)
+            if (e)
+                cudaEventDestroy(e);
+    };
+    // one replay of a graph holding the step and its event records, so the
+    // kernels run back to back as in the decode graph
+    const uint64_t before = g_launches.load();
+    cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess)
+    {
+        cleanup();
+        return set_error(AAEDN_ECUDA, "profile capture: %s", cudaGetErrorString(e));
+    }
+    int rc = enqueue_step(m, m->stream, false, &ev);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(m->stream, &g);
+    g_launches.fetch_sub(g_launches.load() - before);
+    cudaGraphExec_t ex = nullptr;
+    if (!rc && e == cudaSuccess)
+        e = cudaGraphInstantiate(&ex, g, 0);
+    if (g)
+        cudaGraphDestroy(g);
+    if (!rc && e == cudaSuccess)
+        e = cudaGraphLaunch(ex, m->stream);
+    if (!rc && e == cudaSuccess)
+        e = cudaStreamSynchronize(m->stream);
+    if (ex)
+        cudaGraphExecDestroy(ex);
+    if (!rc && e == cudaSuccess)
+    {
+        count_launch(nk);
+        for (uint32_t i = 0; i < nk && e == cudaSuccess; ++i)
+            e = cudaEventElapsedTime(&h_ms[i], ev[i], ev[i + 1]);
+    }
+    cleanup();
+    if (rc)
+        return rc;
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "profile step: %s", cudaGetErrorString(e));
+    m->h_pos += 1;
+    return AAEDN_OK;
+}

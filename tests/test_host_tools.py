@@ -1,0 +1,77 @@
+"""CPU checks of the product's host side: the C ABI library loads and
+exports every symbol of include/aaedn_b200.h, and the host quant tools
+(block quantizer, FNV-1a, RoPE tables) are bit-exact against the reference
+quantizer's golden vectors and the oracle. No kernel is launched."""
+import ctypes
+import subprocess
+
+import numpy as np
+import pytest
+
+import aaedn_b200 as ab
+
+
+def test_library_exports_every_declared_symbol():
+    L = ab.lib()
+    names = ab.exported_symbols()
+    assert len(names) > 30
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", ab.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.strip()}
+    assert set(names) <= exported
+
+
+def test_version_and_error_state():
+    assert ab.lib().aaedn_version() >= 1
+    # host-only call with a bad argument sets the thread's last error
+    rc = ab.lib().aaedn_synth_tokens(1, 0, 0, None, 4)
+    assert rc == ab.EINVAL
+    assert "synth_tokens" in ab.last_error()
+
+
+def test_quantizer_matches_reference_golden(quant_golden):
+    g = quant_golden
+    for name in g["names"]:
+        data, scales = ab.quantize_q4(g[f"{name}__x"])
+        np.testing.assert_array_equal(data, g[f"{name}__data"], err_msg=name)
+        np.testing.assert_array_equal(scales, g[f"{name}__scales"], err_msg=name)
+
+
+def test_quantizer_matches_oracle_on_large_input(oracle):
+    x = ab.synth_normal(7, 3, 1 << 20)
+    d1, s1 = ab.quantize_q4(x)
+    d2, s2 = oracle.quantize(x)
+    np.testing.assert_array_equal(d1, d2)
+    np.testing.assert_array_equal(s1, s2)
+    # unsigned quantizer: negative weights become code 0, codes <= 7 in practice
+    codes = np.stack([d1 & 15, d1 >> 4], 1).reshape(-1)
+    assert codes.max() <= 8 and (codes == 0).mean() > 0.5
+
+
+def test_fnv1a(quant_golden):
+    assert ab.fnv1a32(quant_golden["fnv_payload"].tobytes()) == int(quant_golden["fnv_value"][0])
+
+
+def test_rope_tables_match_oracle(oracle):
+    for hd, ms in ((48, 256), (128, 512)):
+        c, s = ab.rope_table(ms, hd, formula=0)
+        c2, s2 = oracle.rope_tables_ref(ms, hd)
+        np.testing.assert_array_equal(c, c2)
+        np.testing.assert_array_equal(s, s2)
+        for theta in (10000.0, 500000.0):
+            c, s = ab.rope_table(ms, hd, theta, formula=1)
+            c2, s2 = oracle.rope_tables(ms, hd, theta)
+            np.testing.assert_array_equal(c, c2)
+            np.testing.assert_array_equal(s, s2)
+
+
+def test_synthetic_generator_is_deterministic_and_normal():
+    a = ab.synth_normal(1234, 16, 1 << 18)
+    b = ab.synth_normal(1234, 16, 1 << 18)
+    c = ab.synth_normal(1234, 17, 1 << 18)
+    np.testing.assert_array_equal(a, b)
+    assert not np.array_equal(a, c)
+    assert abs(a.mean()) < 2e-4 and abs(a.std() - 0.02) < 2e-4
+    t = ab.synth_tokens(1234, 0, 32000, 10000)
+    assert t.max() < 32000 and len(np.unique(t)) > 8000
