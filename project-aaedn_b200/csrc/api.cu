@@ -123,41 +123,23 @@ __global__ void zero_kernel(float* out, size_t n)
 // fused_matmul launcher: M rows in chunks of <= 8, K in chunks that fit in
 // shared memory (first chunk stores, later chunks accumulate).
 // ---------------------------------------------------------------------------
-template <int NM, int SK, int R, int S>
-static int launch_gemv_plain(const GemvParams& base, int first_chunk, size_t smem, cudaStream_t st)
+template <int NM, int SK>
+static int gemv_dispatch(const GemvParams& p, int first_chunk, cudaStream_t st)
 {
-    auto kern = first_chunk ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK, R, S>
-                            : gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK, R, S>;
+    auto kern = first_chunk ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK>
+                            : gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK>;
     static bool attr_done[2] = {false, false};
     if (!attr_done[first_chunk])
     {
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr_done[first_chunk] = true;
     }
-    const int groups = (base.N + 15) / 16;
-    const int grid = (groups + R - 1) / R;
-    kern<<<grid, GEMV_WARPS * 32, smem, st>>>(base);
+    const int groups = (p.N + 15) / 16;
+    const int grid = groups < sm_count() ? groups : sm_count();
+    const size_t smem = gemv_smem_bytes(NM, p.kt1 - p.kt0);
+    kern<<<grid, GEMV_WARPS * 32, smem, st>>>(p);
     AAEDN_LAUNCH_CHECK("gemv_q4_kernel");
     return AAEDN_OK;
-}
-
-template <int NM, int SK>
-static int gemv_dispatch(const GemvParams& p, int first_chunk, cudaStream_t st)
-{
-    const int groups = (p.N + 15) / 16;
-    const int ntile = p.kt1 - p.kt0;
-    // pick the widest row grouping that still gives >= 2 CTAs per SM
-    int R = 1;
-    if (groups >= 4 * 2 * 148)
-        R = 4;
-    else if (groups >= 2 * 2 * 148)
-        R = 2;
-    const size_t smem = gemv_smem_bytes(NM, ntile, R, GEMV_WARPS / R);
-    if (R == 4)
-        return launch_gemv_plain<NM, SK, 4, 2>(p, first_chunk, smem, st);
-    if (R == 2)
-        return launch_gemv_plain<NM, SK, 2, 4>(p, first_chunk, smem, st);
-    return launch_gemv_plain<NM, SK, 1, 8>(p, first_chunk, smem, st);
 }
 
 template <int SK>
@@ -305,8 +287,9 @@ extern "C" int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, cons
     for (size_t m0 = 0; m0 < M; m0 += 8)
     {
         const int nm = (int)((M - m0) < 8 ? (M - m0) : 8);
-        // tiles per chunk so that the activation fragments fit in ~160 KB
-        const int max_tiles = (int)((160 * 1024 - 64 * 4 - nm * 8 * 16 * 4) / (nm * 528));
+        // tiles per chunk so that ring + activation fragments fit in 200 KB
+        const size_t fixed = gemv_smem_bytes(nm, 0);
+        const int max_tiles = (int)((200 * 1024 - fixed) / ((size_t)nm * 528));
         for (int kt0 = 0; kt0 < ntile_total; kt0 += max_tiles)
         {
             GemvParams p{};
@@ -321,6 +304,8 @@ extern "C" int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, cons
             p.lda = lda;
             p.y = d_out + m0 * ldc;
             p.ldc = ldc;
+            p.scale_pairs = ((ldb >> 5) & 1) == 0 && (reinterpret_cast<uintptr_t>(d_scales) & 3) == 0;
+            p.full_shape = (N % 16) == 0 && (K % 128) == 0;
             int rc = scale_kind == AAEDN_SCALE_F16 ? gemv_dispatch_m<AAEDN_SCALE_F16>(nm, p, kt0 == 0, st)
                                                    : gemv_dispatch_m<AAEDN_SCALE_U16INT>(nm, p, kt0 == 0, st);
             if (rc)
@@ -394,9 +379,12 @@ extern "C" int aaedn_cu_attention(const float* d_q, const float* d_k, const floa
         AAEDN_LAUNCH_CHECK("zero_kernel");
         return AAEDN_OK;
     }
-    if (num_segments > (size_t)ATTN_MAX_SEG || head_dim > (size_t)ATTN_MAX_HD || total > (size_t)INT32_MAX)
-        return set_error(AAEDN_EINVAL, "aaedn_cu_attention: at most %d segments and head_dim <= %d", ATTN_MAX_SEG,
-                         ATTN_MAX_HD);
+    if (num_segments > (size_t)ATTN_MAX_SEG || head_dim > (size_t)ATTN_MAX_HD || (head_dim & 3) ||
+        total > (size_t)INT32_MAX)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_attention: at most %d segments and head_dim a multiple of 4 <= %d",
+                         ATTN_MAX_SEG, ATTN_MAX_HD);
+    if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_k) | reinterpret_cast<uintptr_t>(d_v)) & 15)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_attention: q/k/v must be 16-byte aligned");
     CHECK_DEV(d_q);
     CHECK_DEV(d_k);
     CHECK_DEV(d_v);
@@ -444,12 +432,14 @@ extern "C" int aaedn_cu_attention(const float* d_q, const float* d_k, const floa
     static bool attr = false;
     if (!attr)
     {
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            200 * 1024));
+        int arc = attn_set_attrs_g<0, 1>();
+        if (arc)
+            return arc;
         attr = true;
     }
-    attn_split_kernel<0><<<dim3((unsigned)n_heads, (unsigned)S), ATTN_THREADS, smem, st>>>(p);
-    AAEDN_LAUNCH_CHECK("attn_split_kernel");
+    int lrc = attn_launch<0>(p, dim3((unsigned)n_heads, (unsigned)S), smem, st);
     AAEDN_CUDA_TRY(cudaFreeAsync(part, st));
+    if (lrc)
+        return lrc;
     return AAEDN_OK;
 }

@@ -7,6 +7,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <utility>
 
 #include "../../include/aaedn_b200.h"
 #include "../host/host_common.hpp"
@@ -40,6 +41,23 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
     } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// SMs of the current device (cached per device).
+inline int sm_count()
+{
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64)
+        dev = 0;
+    if (!cache[dev])
+    {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
 
 // ---------------------------------------------------------------------------
 // device helpers
@@ -122,5 +140,94 @@ __device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return ((w >> 5) & 0x00
 __device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return ((w >> 9) & 0x00780078u) | 0x41804180u; }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+// ---- asynchronous global -> shared copies (per-thread, L2 only) ----------
+__device__ __forceinline__ uint32_t smem_addr(const void* p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// 16 bytes; src_bytes == 0 writes zeros without reading global memory.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+// 16 bytes of a stream that continues at the following addresses: L2 fetches
+// the surrounding 256 bytes from DRAM in one request.
+__device__ __forceinline__ void cp_async_16_pf256(void* dst, const void* src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+
+// 4 bytes (cache at all levels form: .ca is the only one allowed below 16 B)
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr)
+{
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr)
+{
+    uint32_t r;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(addr));
+    return r;
+}
+
+__device__ __forceinline__ float ldsf(uint32_t addr)
+{
+    float r;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
+    return r;
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// Lets the next kernel in the stream start launching (its blocks then run
+// their independent prologue: weight prefetch) ...
+__device__ __forceinline__ void pdl_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// ... and blocks until the previous kernel has completed and its writes are
+// visible. A no-op when the kernel was not launched as a dependent.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Kernel launch, optionally as a programmatic dependent of the previous
+// kernel in the stream (it may start while that one drains; it must call
+// pdl_wait() before touching that kernel's outputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 bool pdl, Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 } // namespace aaedn_dev

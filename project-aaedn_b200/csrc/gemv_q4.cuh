@@ -88,14 +88,23 @@ struct GemvParams
     const float* rope_sin;
     // SwiGLU epilogue
     float* act;
+    // scales can be staged as aligned u32 pairs (even scales per row, 4-byte
+    // aligned array)
+    bool scale_pairs;
+    // N % 16 == 0 and K % 128 == 0: no padding rows or blocks anywhere
+    bool full_shape;
 };
 
 constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_STAGES = 6; // per-thread cp.async ring depth (tiles)
 
-// Dynamic shared memory of one CTA.
-inline size_t gemv_smem_bytes(int nm, int ntile, int R, int S)
+// Dynamic shared memory of one CTA: the cp.async ring (6 stages x 256
+// threads x 40 B), the activation fragments, block biases, two reduction
+// buffers.
+inline size_t gemv_smem_bytes(int nm, int ntile)
 {
-    return (size_t)nm * ntile * 512 + (size_t)nm * ntile * 16 + (size_t)nm * S * R * 16 * 4 + 64 * 4;
+    return (size_t)GEMV_STAGES * GEMV_WARPS * 32 * 40 + (size_t)(nm * ntile + 1) * 512 + (size_t)nm * ntile * 16 +
+           (size_t)2 * nm * GEMV_WARPS * 16 * 4 + 64 * 4;
 }
 
 __device__ __forceinline__ uint32_t u4get(const uint4& v, int q)
@@ -152,10 +161,14 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
         for (int m = 0; m < NM; ++m)
         {
             float ss = 0.0f;
-            for (int i = tid; i < p.K; i += nth)
+            const float4* s4 = reinterpret_cast<const float4*>(src[m]);
+            for (int i = tid; i < (p.K >> 2); i += nth)
             {
-                float v = src[m][i];
-                ss = fmaf(v, v, ss);
+                const float4 v = s4[i];
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
             }
             ss = block_sum(ss, misc);
             // src/rmsnorm.cpp:34
@@ -185,13 +198,26 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
             for (int mm = 1; mm < NM; ++mm)
                 if (mm == m)
                     r = rms[mm];
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
+            if ((reinterpret_cast<uintptr_t>(xp + k0) & 15) == 0)
             {
-                float xv = xp[k0 + c];
-                if constexpr (PRO != PRO_PLAIN)
-                    xv = __fmul_rn(__fmul_rn(xv, r), p.gain[k0 + c]); // src/rmsnorm.cpp:42-43
-                v[c] = xv;
+                const float4 a = *reinterpret_cast<const float4*>(xp + k0);
+                const float4 b = *reinterpret_cast<const float4*>(xp + k0 + 4);
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+            }
+            else
+            {
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    v[c] = xp[k0 + c];
+            }
+            if constexpr (PRO != PRO_PLAIN)
+            {
+                const float4 ga = *reinterpret_cast<const float4*>(p.gain + k0);
+                const float4 gb = *reinterpret_cast<const float4*>(p.gain + k0 + 4);
+                const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    v[c] = __fmul_rn(__fmul_rn(v[c], r), gv[c]); // src/rmsnorm.cpp:42-43
             }
         }
         else
@@ -224,130 +250,25 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
     }
 }
 
-template <int NM, int PRO, int EPI, int SK, int R, int S>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_q4_kernel(const GemvParams p)
+// Epilogue of one 16-row group on one warp: sums the 8 K-split partial
+// sums of each row in fixed order, then stores / accumulates / adds the
+// residual, or pairs rows (8j + r, 8j + r + 8) for SwiGLU and for RoPE +
+// the KV-cache append.
+template <int NM, int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* rb, int group, int lane)
 {
-    static_assert(R * S == GEMV_WARPS, "R*S warps per CTA");
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int ntile = p.kt1 - p.kt0;
-    uint4* frag = reinterpret_cast<uint4*>(smem);
-    float* tb = reinterpret_cast<float*>(smem + (size_t)NM * ntile * 512);
-    float* red = tb + (size_t)NM * ntile * 4;
-    float* misc = red + NM * S * R * 16;
-
-    gemv_build_frags<NM, PRO>(p, frag, tb, misc, ntile);
-    __syncthreads();
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int r = warp / S, s = warp - r * S;
-    const int group = blockIdx.x * R + r;
-    const int row0 = group * 16 + g, row1 = row0 + 8;
-    const bool ok0 = row0 < p.N, ok1 = row1 < p.N;
-    const int nblk = p.K >> 5;
-    const uint8_t* w0p = p.w + (size_t)(ok0 ? row0 : 0) * (p.ldb >> 1);
-    const uint8_t* w1p = p.w + (size_t)(ok1 ? row1 : 0) * (p.ldb >> 1);
-    const uint16_t* s0p = p.s + (size_t)(ok0 ? row0 : 0) * (p.ldb >> 5);
-    const uint16_t* s1p = p.s + (size_t)(ok1 ? row1 : 0) * (p.ldb >> 5);
-    const int tA = (ntile * s) / S, tB = (ntile * (s + 1)) / S;
-    const bool bact = (g >> 1) == t;
-    const int la = 2 * t + (g & 1);
-
-    float acc0[NM], acc1[NM];
-#pragma unroll
-    for (int m = 0; m < NM; ++m)
-        acc0[m] = acc1[m] = 0.0f;
-
-    if (group * 16 < p.N)
-    {
-        constexpr int PF = 4;
-        uint4 W0[PF], W1[PF];
-        float SC0[PF], SC1[PF];
-#pragma unroll
-        for (int i = 0; i < PF; ++i)
-        {
-            const int tt = tA + i;
-            const int blk = (p.kt0 + tt) * 4 + t;
-            const bool v = tt < tB && blk < nblk;
-            W0[i] = (v && ok0) ? ldg_stream_v4(w0p + (size_t)blk * 16) : make_uint4(0, 0, 0, 0);
-            W1[i] = (v && ok1) ? ldg_stream_v4(w1p + (size_t)blk * 16) : make_uint4(0, 0, 0, 0);
-            SC0[i] = (v && ok0) ? decode_scale<SK>(ldg_u16(s0p + blk)) : 0.0f;
-            SC1[i] = (v && ok1) ? decode_scale<SK>(ldg_u16(s1p + blk)) : 0.0f;
-        }
-        for (int tt0 = tA; tt0 < tB; tt0 += PF)
-        {
-#pragma unroll
-            for (int i = 0; i < PF; ++i)
-            {
-                const int tt = tt0 + i;
-                if (tt < tB)
-                {
-                    float d0[NM], d1[NM], d2[NM], d3[NM];
-#pragma unroll
-                    for (int m = 0; m < NM; ++m)
-                        d0[m] = d1[m] = d2[m] = d3[m] = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                    {
-                        const uint32_t wa = u4get(W0[i], q), wb = u4get(W1[i], q);
-                        const uint32_t a0 = nib_e0(wa), a1 = nib_e0(wb), a2 = nib_e1(wa), a3 = nib_e1(wb);
-                        const uint32_t c0 = nib_e2(wa), c1 = nib_e2(wb), c2 = nib_e3(wa), c3 = nib_e3(wb);
-#pragma unroll
-                        for (int m = 0; m < NM; ++m)
-                        {
-                            uint4 b = make_uint4(0, 0, 0, 0);
-                            if (bact)
-                                b = frag[(((size_t)m * ntile + tt) * 4 + q) * 8 + la];
-                            mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], a0, a1, a2, a3, b.x, b.y);
-                            mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], c0, c1, c2, c3, b.z, b.w);
-                        }
-                    }
-#pragma unroll
-                    for (int m = 0; m < NM; ++m)
-                    {
-                        const float tbv = tb[((size_t)m * ntile + tt) * 4 + t];
-                        acc0[m] = fmaf(SC0[i], (d0[m] + d1[m]) - tbv, acc0[m]);
-                        acc1[m] = fmaf(SC1[i], (d2[m] + d3[m]) - tbv, acc1[m]);
-                    }
-                    // refill this slot with the tile PF ahead
-                    const int tn = tt + PF;
-                    const int blk = (p.kt0 + tn) * 4 + t;
-                    const bool v = tn < tB && blk < nblk;
-                    W0[i] = (v && ok0) ? ldg_stream_v4(w0p + (size_t)blk * 16) : make_uint4(0, 0, 0, 0);
-                    W1[i] = (v && ok1) ? ldg_stream_v4(w1p + (size_t)blk * 16) : make_uint4(0, 0, 0, 0);
-                    SC0[i] = (v && ok0) ? decode_scale<SK>(ldg_u16(s0p + blk)) : 0.0f;
-                    SC1[i] = (v && ok1) ? decode_scale<SK>(ldg_u16(s1p + blk)) : 0.0f;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < NM; ++m)
-    {
-        acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 1);
-        acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 2);
-        acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 1);
-        acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 2);
-        if (t == 0)
-        {
-            red[(m * S + s) * (R * 16) + r * 16 + g] = acc0[m];
-            red[(m * S + s) * (R * 16) + r * 16 + g + 8] = acc1[m];
-        }
-    }
-    __syncthreads();
-
-    // ---------------- epilogues ----------------
+    constexpr int S = GEMV_WARPS;
     if constexpr (EPI == EPI_STORE || EPI == EPI_ACCUM || EPI == EPI_RESIDUAL)
     {
-        for (int idx = tid; idx < NM * R * 16; idx += blockDim.x)
+        for (int idx = lane; idx < NM * 16; idx += 32)
         {
-            const int m = idx / (R * 16), rr = idx - m * R * 16;
-            const int row = blockIdx.x * R * 16 + rr;
+            const int m = idx >> 4, rr = idx & 15;
+            const int row = group * 16 + rr;
             if (row >= p.N)
                 continue;
             float v = 0.0f;
             for (int ss = 0; ss < S; ++ss)
-                v += red[(m * S + ss) * (R * 16) + rr];
+                v += rb[(m * S + ss) * 16 + rr];
             float* yp = p.y + (size_t)m * p.ldc + row;
             if constexpr (EPI == EPI_STORE)
                 *yp = v;
@@ -357,65 +278,350 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_q4_kernel(const GemvPara
     }
     else
     {
-        for (int idx = tid; idx < R * 8; idx += blockDim.x)
+        const int jj = lane;
+        const int rbase = group * 16;
+        if (jj >= 8 || rbase >= p.N)
+            return;
+        float v0 = 0.0f, v1 = 0.0f;
+        for (int ss = 0; ss < S; ++ss)
         {
-            const int rr = idx >> 3, jj = idx & 7;
-            const int grp = blockIdx.x * R + rr;
-            const int rbase = grp * 16;
-            if (rbase >= p.N)
-                continue;
-            float v0 = 0.0f, v1 = 0.0f;
-            for (int ss = 0; ss < S; ++ss)
+            v0 += rb[ss * 16 + jj];
+            v1 += rb[ss * 16 + jj + 8];
+        }
+        if constexpr (EPI == EPI_SWIGLU)
+        {
+            // rows 8j..8j+7 of the gate and of up share one group (D6)
+            p.act[group * 8 + jj] = __fmul_rn(silu_f(v0), v1);
+        }
+        else
+        {
+            const int hd = p.head_dim, half = hd >> 1;
+            const uint32_t pos = p.state->pos;
+            if (pos >= (uint32_t)p.max_pos)
             {
-                v0 += red[ss * (R * 16) + rr * 16 + jj];
-                v1 += red[ss * (R * 16) + rr * 16 + jj + 8];
+                if (jj == 0)
+                    p.state->err = 1u;
+                return;
             }
-            if constexpr (EPI == EPI_SWIGLU)
+            const int page = p.page_table[pos / p.page_size];
+            const int slot = pos % p.page_size;
+            if (rbase < p.q_rows + p.kv_rows)
             {
-                // rows 8j..8j+7 of the gate and of up share one group (D6)
-                p.act[grp * 8 + jj] = __fmul_rn(silu_f(v0), v1);
+                const bool isq = rbase < p.q_rows;
+                const int rel = isq ? rbase : rbase - p.q_rows;
+                const int h = rel / hd, i = ((rel % hd) >> 4) * 8 + jj;
+                const float c = p.rope_cos[(size_t)pos * half + i];
+                const float sn = p.rope_sin[(size_t)pos * half + i];
+                // rotate-half (src/rope.cpp:53-54) at the absolute position (D3)
+                const float o0 = __fsub_rn(__fmul_rn(c, v0), __fmul_rn(sn, v1));
+                const float o1 = __fadd_rn(__fmul_rn(sn, v0), __fmul_rn(c, v1));
+                float* dst;
+                if (isq)
+                    dst = p.qbuf + (size_t)h * hd;
+                else
+                    dst = p.k_layer + (((size_t)page * p.n_kv + h) * p.page_size + slot) * hd;
+                dst[i] = o0;
+                dst[i + half] = o1;
             }
             else
             {
-                const int hd = p.head_dim, half = hd >> 1;
-                const uint32_t pos = p.state->pos;
-                if (pos >= (uint32_t)p.max_pos)
-                {
-                    if (jj == 0)
-                        p.state->err = 1u;
-                    continue;
-                }
-                const int page = p.page_table[pos / p.page_size];
-                const int slot = pos % p.page_size;
-                if (rbase < p.q_rows + p.kv_rows)
-                {
-                    const bool isq = rbase < p.q_rows;
-                    const int rel = isq ? rbase : rbase - p.q_rows;
-                    const int h = rel / hd, i = ((rel % hd) >> 4) * 8 + jj;
-                    const float c = p.rope_cos[(size_t)pos * half + i];
-                    const float sn = p.rope_sin[(size_t)pos * half + i];
-                    // rotate-half (src/rope.cpp:53-54) at the absolute position (D3)
-                    const float o0 = __fsub_rn(__fmul_rn(c, v0), __fmul_rn(sn, v1));
-                    const float o1 = __fadd_rn(__fmul_rn(sn, v0), __fmul_rn(c, v1));
-                    float* dst;
-                    if (isq)
-                        dst = p.qbuf + (size_t)h * hd;
-                    else
-                        dst = p.k_layer + (((size_t)page * p.n_kv + h) * p.page_size + slot) * hd;
-                    dst[i] = o0;
-                    dst[i + half] = o1;
-                }
-                else
-                {
-                    const int rel = rbase - p.q_rows - p.kv_rows;
-                    const int h = rel / hd, d = rel % hd + jj;
-                    float* dst = p.v_layer + (((size_t)page * p.n_kv + h) * p.page_size + slot) * hd;
-                    dst[d] = v0;
-                    dst[d + 8] = v1;
-                }
+                const int rel = rbase - p.q_rows - p.kv_rows;
+                const int h = rel / hd, d = rel % hd + jj;
+                float* dst = p.v_layer + (((size_t)page * p.n_kv + h) * p.page_size + slot) * hd;
+                dst[d] = v0;
+                dst[d + 8] = v1;
             }
         }
     }
+}
+
+// The main loop for full shapes (N a multiple of 16, K a multiple of 128,
+// scales staged in pairs): every copy and every fragment read is
+// unconditional and all shared-memory addresses are 32-bit.
+template <int NM, int EPI, int SK, typename Issue>
+__device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, uint32_t* sts, uint4* frag, float* tb,
+                                               float* red, int my_groups, int tA, int tB, int ntile, Issue& issue)
+{
+    constexpr int D = GEMV_STAGES;
+    constexpr int NT = GEMV_WARPS * 32;
+    constexpr int S = GEMV_WARPS;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const bool bact = (g >> 1) == t;
+    const int la = 2 * t + (g & 1);
+    // scale pair half: blk & 1 == t & 1 for every tile of this thread
+    const uint32_t hsel = (t & 1) ? 0x3232u : 0x1010u;
+    const uint32_t w_base = smem_addr(stw) + (uint32_t)tid * 32;
+    const uint32_t s_base = smem_addr(sts) + (uint32_t)tid * 8;
+    // inactive lanes read their (zero) B operand from the fragment area of a
+    // tile past the end, which the prologue zero-fills
+    const uint32_t f_base = smem_addr(frag) + (uint32_t)la * 16;
+    const uint32_t f_zero = smem_addr(frag) + (uint32_t)NM * ntile * 512;
+    const uint32_t tb_base = smem_addr(tb) + (uint32_t)t * 4;
+    uint32_t c_off_w = 0, c_off_s = 0;
+    for (int gl = 0; gl < my_groups; ++gl)
+    {
+        const int group = blockIdx.x + gl * gridDim.x;
+        float acc0[NM], acc1[NM];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+            acc0[m] = acc1[m] = 0.0f;
+        uint32_t fa = bact ? f_base + (uint32_t)tA * 512 : f_zero;
+        const uint32_t fstep = bact ? 512u : 0u;
+        const uint32_t mstride = bact ? (uint32_t)ntile * 512 : 0u;
+        uint32_t ta = tb_base + (uint32_t)tA * 16;
+        for (int tt = tA; tt < tB; ++tt, fa += fstep, ta += 16)
+        {
+            cp_async_wait<D - 2>();
+            const uint4 wa4 = lds128(w_base + c_off_w);
+            const uint4 wb4 = lds128(w_base + c_off_w + 16);
+            const uint32_t pa = lds32(s_base + c_off_s), pb = lds32(s_base + c_off_s + 4);
+            const float sc0 = decode_scale<SK>((uint16_t)__byte_perm(pa, 0, hsel));
+            const float sc1 = decode_scale<SK>((uint16_t)__byte_perm(pb, 0, hsel));
+            c_off_w = (c_off_w == (D - 1) * NT * 32) ? 0u : c_off_w + NT * 32;
+            c_off_s = (c_off_s == (D - 1) * NT * 8) ? 0u : c_off_s + NT * 8;
+            issue();
+
+            float d0[NM], d1[NM], d2[NM], d3[NM];
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+                d0[m] = d1[m] = d2[m] = d3[m] = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+            {
+                const uint32_t wa = u4get(wa4, q), wb = u4get(wb4, q);
+                const uint32_t a0 = nib_e0(wa), a1 = nib_e0(wb), a2 = nib_e1(wa), a3 = nib_e1(wb);
+                const uint32_t c0 = nib_e2(wa), c1 = nib_e2(wb), c2 = nib_e3(wa), c3 = nib_e3(wb);
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+                {
+                    const uint4 b = lds128(fa + (uint32_t)m * mstride + (uint32_t)(q * 128));
+                    mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], a0, a1, a2, a3, b.x, b.y);
+                    mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], c0, c1, c2, c3, b.z, b.w);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+            {
+                const float tbv = ldsf(ta + (uint32_t)(m * ntile * 16));
+                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) - tbv, acc0[m]);
+                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) - tbv, acc1[m]);
+            }
+        }
+        float* rb = red + (size_t)(gl & 1) * NM * S * 16;
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+        {
+            acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 1);
+            acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 2);
+            acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 1);
+            acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 2);
+            if (t == 0)
+            {
+                rb[(m * S + warp) * 16 + g] = acc0[m];
+                rb[(m * S + warp) * 16 + g + 8] = acc1[m];
+            }
+        }
+        __syncthreads();
+        if (warp == (gl & (GEMV_WARPS - 1)))
+            gemv_epilogue<NM, EPI>(p, rb, group, lane);
+    }
+}
+
+// One CTA of 8 warps per SM (persistent): the CTA takes row groups
+// blockIdx.x, blockIdx.x + gridDim.x, ... and its 8 warps split K of each
+// group. Every thread streams its 16-byte code words (rows g and g+8) and
+// scale pairs through a private cp.async ring that runs straight through group
+// boundaries. A CTA needs well under half of an SM, so the next kernel of a
+// decode step (launched as a programmatic dependent) becomes resident at once
+// and fills its own ring while this one computes.
+template <int NM, int PRO, int EPI, int SK>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvParams p)
+{
+    constexpr int D = GEMV_STAGES;
+    constexpr int NT = GEMV_WARPS * 32;
+    constexpr int S = GEMV_WARPS; // K splits of a group
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int ntile = p.kt1 - p.kt0;
+    // [D][NT][2] code words of rows g and g+8, [D][NT][2] scale pairs, then
+    // the activation fragments, block biases, two reduction buffers.
+    uint4* stw = reinterpret_cast<uint4*>(smem);
+    uint32_t* sts = reinterpret_cast<uint32_t*>(smem + (size_t)D * NT * 32);
+    uint4* frag = reinterpret_cast<uint4*>(smem + (size_t)D * NT * 40);
+    // one zero tile after the fragments: the B operand of inactive lanes
+    float* tb = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) + (size_t)(NM * ntile + 1) * 512);
+    float* red = tb + (size_t)NM * ntile * 4; // [2][NM][S][16]
+    float* misc = red + 2 * NM * S * 16;
+
+    // the next kernel in the stream may start its own weight prefetch now
+    pdl_launch_dependents();
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int s = warp;
+    const int nblk = p.K >> 5;
+    const int n_groups = (p.N + 15) >> 4;
+    const int my_groups = blockIdx.x < n_groups ? (n_groups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int tA = (ntile * s) / S, tB = (ntile * (s + 1)) / S;
+    const bool bact = (g >> 1) == t;
+    const int la = 2 * t + (g & 1);
+    const bool pairs = p.scale_pairs;
+    const size_t wrow = p.ldb >> 1, srow = p.ldb >> 5;
+    const size_t gstride_w = (size_t)16 * gridDim.x * wrow, gstride_s = (size_t)16 * gridDim.x * srow;
+    const int blk0 = p.kt0 * 4 + t; // block of tile 0 of this thread
+    const int shift = (blk0 & 1) * 16; // which half of a scale pair (constant per thread)
+
+    // ---- issue cursor: walks (group, tile) pairs in order, no divisions
+    int i_tt = tA, i_left = (tB > tA) ? my_groups : 0, i_slot = 0;
+    int i_row0 = blockIdx.x * 16 + g;
+    const uint8_t* i_w0 = p.w + (size_t)i_row0 * wrow + (size_t)blk0 * 16;
+    const uint8_t* i_w1 = i_w0 + 8 * wrow;
+    const uint16_t* i_s0 = p.s + (size_t)i_row0 * srow + (blk0 & ~1);
+    const uint16_t* i_s1 = i_s0 + 8 * srow;
+    const uint32_t ring_w = smem_addr(stw) + (uint32_t)tid * 32;
+    const uint32_t ring_s = smem_addr(sts) + (uint32_t)tid * 8;
+    const bool full = p.full_shape;
+    auto issue = [&]() {
+        if (i_left > 0)
+        {
+            const bool vb = full || blk0 + 4 * i_tt < nblk;
+            const bool v0 = full || (vb && i_row0 < p.N), v1 = full || (vb && i_row0 + 8 < p.N);
+            const size_t off = (size_t)i_tt * 64;
+            const uint32_t dw = ring_w + (uint32_t)i_slot * (NT * 32);
+            asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16, %2;" ::"r"(dw),
+                         "l"(v0 ? i_w0 + off : p.w), "r"(v0 ? 16u : 0u)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16, %2;" ::"r"(dw + 16),
+                         "l"(v1 ? i_w1 + off : p.w), "r"(v1 ? 16u : 0u)
+                         : "memory");
+            if (pairs)
+            {
+                const uint32_t ds = ring_s + (uint32_t)i_slot * (NT * 8);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(ds),
+                             "l"(v0 ? i_s0 + 4 * i_tt : p.s), "r"(v0 ? 4u : 0u)
+                             : "memory");
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(ds + 4),
+                             "l"(v1 ? i_s1 + 4 * i_tt : p.s), "r"(v1 ? 4u : 0u)
+                             : "memory");
+            }
+            if (++i_tt == tB)
+            {
+                i_tt = tA;
+                --i_left;
+                i_row0 += 16 * gridDim.x;
+                i_w0 += gstride_w;
+                i_w1 += gstride_w;
+                i_s0 += gstride_s;
+                i_s1 += gstride_s;
+            }
+        }
+        i_slot = (i_slot + 1 == D) ? 0 : i_slot + 1;
+        cp_async_commit();
+    };
+
+    // The weights do not depend on the activations: the first D-1 items are
+    // requested before waiting for the previous kernel and before the
+    // activation prologue, so their HBM latency overlaps both.
+#pragma unroll
+    for (int i = 0; i < D - 1; ++i)
+        issue();
+
+    pdl_wait();
+    gemv_build_frags<NM, PRO>(p, frag, tb, misc, ntile);
+    if (tid < 32)
+        frag[(size_t)NM * ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+
+    if (p.full_shape && pairs)
+    {
+        gemv_lean_loop<NM, EPI, SK>(p, stw, sts, frag, tb, red, my_groups, tA, tB, ntile, issue);
+        cp_async_wait<0>();
+        return;
+    }
+
+    int c_slot = 0;
+    int row0 = blockIdx.x * 16 + g;
+    for (int gl = 0; gl < my_groups; ++gl, row0 += 16 * gridDim.x)
+    {
+        const int group = blockIdx.x + gl * gridDim.x;
+        const bool ok0 = row0 < p.N, ok1 = row0 + 8 < p.N;
+        float acc0[NM], acc1[NM];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+            acc0[m] = acc1[m] = 0.0f;
+        const uint4* fb = frag + (size_t)tA * 32 + la;
+        const float* tbp = tb + (size_t)tA * 4 + t;
+        for (int tt = tA; tt < tB; ++tt, fb += 32, tbp += 4)
+        {
+            cp_async_wait<D - 2>(); // this thread's copies of this item have landed
+            const uint4* wsl = stw + (size_t)c_slot * NT * 2 + (size_t)tid * 2;
+            const uint4 wa4 = wsl[0], wb4 = wsl[1];
+            float sc0, sc1;
+            if (pairs)
+            {
+                const uint32_t* ssl = sts + (size_t)c_slot * NT * 2 + (size_t)tid * 2;
+                sc0 = decode_scale<SK>((uint16_t)(ssl[0] >> shift));
+                sc1 = decode_scale<SK>((uint16_t)(ssl[1] >> shift));
+            }
+            else
+            {
+                const int blk = blk0 + 4 * tt;
+                const bool v = blk < nblk;
+                sc0 = (v && ok0) ? decode_scale<SK>(ldg_u16(p.s + (size_t)row0 * srow + blk)) : 0.0f;
+                sc1 = (v && ok1) ? decode_scale<SK>(ldg_u16(p.s + (size_t)(row0 + 8) * srow + blk)) : 0.0f;
+            }
+            c_slot = (c_slot + 1 == D) ? 0 : c_slot + 1;
+            // refill the slot consumed in the previous iteration
+            issue();
+
+            float d0[NM], d1[NM], d2[NM], d3[NM];
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+                d0[m] = d1[m] = d2[m] = d3[m] = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+            {
+                const uint32_t wa = u4get(wa4, q), wb = u4get(wb4, q);
+                const uint32_t a0 = nib_e0(wa), a1 = nib_e0(wb), a2 = nib_e1(wa), a3 = nib_e1(wb);
+                const uint32_t c0 = nib_e2(wa), c1 = nib_e2(wb), c2 = nib_e3(wa), c3 = nib_e3(wb);
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+                {
+                    uint4 b = make_uint4(0, 0, 0, 0);
+                    if (bact)
+                        b = fb[(size_t)m * ntile * 32 + q * 8];
+                    mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], a0, a1, a2, a3, b.x, b.y);
+                    mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], c0, c1, c2, c3, b.z, b.w);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+            {
+                const float tbv = tbp[(size_t)m * ntile * 4];
+                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) - tbv, acc0[m]);
+                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) - tbv, acc1[m]);
+            }
+        }
+        float* rb = red + (size_t)(gl & 1) * NM * S * 16;
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+        {
+            acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 1);
+            acc0[m] += __shfl_xor_sync(0xffffffffu, acc0[m], 2);
+            acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 1);
+            acc1[m] += __shfl_xor_sync(0xffffffffu, acc1[m], 2);
+            if (t == 0)
+            {
+                rb[(m * S + s) * 16 + g] = acc0[m];
+                rb[(m * S + s) * 16 + g + 8] = acc1[m];
+            }
+        }
+        __syncthreads(); // the reduction buffer of the other parity is free again
+        // epilogue of this group on the warp gl % 8 (the others stream on)
+        if (warp == (gl & (GEMV_WARPS - 1)))
+            gemv_epilogue<NM, EPI>(p, rb, group, lane);
+    }
+    cp_async_wait<0>(); // nothing of this thread stays in flight past here
 }
 
 } // namespace aaedn_dev

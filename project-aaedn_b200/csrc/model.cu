@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -50,6 +51,8 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
 {
     extern __shared__ __align__(16) float xs[];
     float* misc = xs + p.dim;
+    pdl_launch_dependents();
+    pdl_wait(); // the hidden state comes from the previous kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float ss = 0.0f;
     for (int i = tid; i < p.dim; i += blockDim.x)
@@ -70,7 +73,7 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
     {
         const float4* wr = reinterpret_cast<const float4*>(p.w + (size_t)n * p.dim);
         float acc = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
         for (int k = lane; k < d4; k += 32)
         {
             const float4 wv = ldg_stream_f4(reinterpret_cast<const float*>(wr + k));
@@ -180,37 +183,24 @@ struct DevLayer
     float *k, *v; // [n_pages][n_kv][P][hd]
 };
 
-int pick_rows_per_cta(int groups)
-{
-    if (groups >= 4 * 2 * 148)
-        return 4;
-    if (groups >= 2 * 2 * 148)
-        return 2;
-    return 1;
-}
-
-template <int PRO, int EPI, int R>
-int launch_model_gemv(const GemvParams& p, cudaStream_t st)
-{
-    constexpr int S = GEMV_WARPS / R;
-    auto kern = gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, R, S>;
-    const int groups = (p.N + 15) / 16;
-    const int grid = (groups + R - 1) / R;
-    const size_t smem = gemv_smem_bytes(1, p.kt1 - p.kt0, R, S);
-    kern<<<grid, GEMV_WARPS * 32, smem, st>>>(p);
-    AAEDN_LAUNCH_CHECK("gemv_q4_kernel(model)");
-    return AAEDN_OK;
-}
-
 template <int PRO, int EPI>
-int model_gemv(const GemvParams& p, cudaStream_t st)
+int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl)
 {
-    const int R = pick_rows_per_cta((p.N + 15) / 16);
-    if (R == 4)
-        return launch_model_gemv<PRO, EPI, 4>(p, st);
-    if (R == 2)
-        return launch_model_gemv<PRO, EPI, 2>(p, st);
-    return launch_model_gemv<PRO, EPI, 1>(p, st);
+    auto kern = gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16>;
+    static int per_sm = -1;
+    if (per_sm < 0)
+    {
+        const char* e = std::getenv("AAEDN_GEMV_CTAS_PER_SM");
+        per_sm = e ? std::max(1, std::atoi(e)) : 1;
+    }
+    const int groups = (p.N + 15) / 16;
+    const int grid = groups < per_sm * sm_count() ? groups : per_sm * sm_count();
+    const size_t smem = gemv_smem_bytes(1, p.kt1 - p.kt0);
+    cudaError_t e = launch_kernel(kern, dim3(grid), dim3(GEMV_WARPS * 32), smem, st, pdl, p);
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of gemv_q4_kernel(model) failed: %s", cudaGetErrorString(e));
+    count_launch();
+    return AAEDN_OK;
 }
 
 // Opt every model kernel into large dynamic shared memory once, before any
@@ -218,11 +208,7 @@ int model_gemv(const GemvParams& p, cudaStream_t st)
 template <int PRO, int EPI>
 int set_gemv_attrs()
 {
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 1, 8>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 2, 4>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, 4, 2>,
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return AAEDN_OK;
 }
@@ -269,6 +255,7 @@ struct aaedn_model
     uint32_t h_pos = 0;
     uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
     bool weights_set = false;
+    bool pdl = true; // programmatic dependent launch inside the decode graph
 
     template <typename T>
     T* take(size_t bytes)
@@ -329,10 +316,14 @@ static size_t plan_arena(aaedn_model* m, bool carve)
 
 static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr)
 {
+    // programmatic dependent launches between consecutive kernels (not when
+    // events or copies sit between them)
+    const bool pdl = m->pdl && !ev && !debug;
     size_t evi = 0;
     auto mark = [&]() -> int {
+        // external event nodes: timestamps are taken inside the graph
         if (ev && evi < ev->size())
-            AAEDN_CUDA_TRY(cudaEventRecord((*ev)[evi++], st));
+            AAEDN_CUDA_TRY(cudaEventRecordWithFlags((*ev)[evi++], st, cudaEventRecordExternal));
         return AAEDN_OK;
     };
     int mrc = mark();
@@ -373,7 +364,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         q.page_table = m->page_table;
         q.rope_cos = m->rope_cos;
         q.rope_sin = m->rope_sin;
-        rc = (l == 0) ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st) : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st);
+        q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
+        q.scale_pairs = ((D >> 5) & 1) == 0;
+        rc = (l == 0) ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl) : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -397,8 +390,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         a.page_table = m->page_table;
         a.page_size = m->page_size;
         const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
-        attn_split_kernel<1><<<dim3(KV, m->attn_S), ATTN_THREADS, asmem, st>>>(a);
-        AAEDN_LAUNCH_CHECK("attn_split_kernel(model)");
+        rc = attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl);
+        if (rc)
+            return rc;
         if ((rc = mark()))
             return rc;
         // --- O projection + residual
@@ -414,7 +408,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         o.lda = (size_t)H * hd;
         o.y = m->hidden;
         o.ldc = (size_t)D;
-        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st);
+        o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
+        o.scale_pairs = (((H * hd) >> 5) & 1) == 0;
+        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -433,7 +429,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         gu.gain = L.ffn_norm;
         gu.eps = c.eps;
         gu.act = m->act;
-        rc = model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st);
+        gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
+        gu.scale_pairs = ((D >> 5) & 1) == 0;
+        rc = model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -451,7 +449,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         dn.lda = (size_t)F;
         dn.y = m->hidden;
         dn.ldc = (size_t)D;
-        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st);
+        dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
+        dn.scale_pairs = ((F >> 5) & 1) == 0;
+        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -474,8 +474,13 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     lp.out_tokens = m->out_tokens;
     lp.max_seq = (int)c.max_seq;
     lp.rows_per_cta = m->lm_rows;
-    lm_head_argmax_kernel<<<m->lm_ctas, 256, (size_t)(D + 64) * 4, st>>>(lp);
-    AAEDN_LAUNCH_CHECK("lm_head_argmax_kernel");
+    {
+        cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(256), (size_t)(D + 64) * 4, st, pdl,
+                                      lp);
+        if (e != cudaSuccess)
+            return set_error(AAEDN_ECUDA, "launch of lm_head_argmax_kernel failed: %s", cudaGetErrorString(e));
+        count_launch();
+    }
         if ((rc = mark()))
             return rc;
     return AAEDN_OK;
@@ -560,23 +565,31 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
         c.vocab == 0 || c.max_seq == 0)
         return set_error(AAEDN_EINVAL, "aaedn_model_create: zero dimension");
     if (c.dim % 32 || (c.n_heads * c.head_dim) % 32 || c.ffn_dim % 32 || c.head_dim % 16 || c.dim % 4 ||
-        c.n_heads % c.n_kv_heads || c.head_dim > (uint32_t)ATTN_MAX_HD || c.n_heads / c.n_kv_heads > 32)
+        c.n_heads % c.n_kv_heads || c.head_dim > (uint32_t)ATTN_MAX_HD ||
+        (c.n_heads / c.n_kv_heads != 1 && c.n_heads / c.n_kv_heads != 2 && c.n_heads / c.n_kv_heads != 4 &&
+         c.n_heads / c.n_kv_heads != 8))
         return set_error(AAEDN_EINVAL,
                          "aaedn_model_create: need dim, n_heads*head_dim, ffn_dim multiples of 32, head_dim a "
-                         "multiple of 16 (<= %d), n_kv_heads dividing n_heads",
+                         "multiple of 16 (<= %d), n_heads / n_kv_heads in {1, 2, 4, 8}",
                          ATTN_MAX_HD);
     if (c.dim > 65536 || c.ffn_dim > 32768 || c.max_seq > (1u << 20))
         return set_error(AAEDN_EINVAL, "aaedn_model_create: dimension too large");
     aaedn_model* m = new aaedn_model();
     m->cfg = c;
+    {
+        const char* e = std::getenv("AAEDN_PDL");
+        m->pdl = !(e && e[0] == '0');
+    }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
-    int S = (int)((2 * 148 + c.n_kv_heads - 1) / c.n_kv_heads);
+    // about one attention CTA per SM (the CTA walks its token range in
+    // 64-token chunks, so any split count covers any context length)
+    int S = std::max(1, sm_count() / (int)c.n_kv_heads);
     S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
     S = std::min(S, 64);
     m->attn_S = S;
     m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
-    int rows = (int)((c.vocab + 4 * 148 - 1) / (4 * 148));
+    int rows = (int)((c.vocab + 2 * sm_count() - 1) / (2 * sm_count()));
     rows = (rows + 7) / 8 * 8;
     m->lm_rows = std::max(8, rows);
     m->lm_ctas = (int)((c.vocab + m->lm_rows - 1) / m->lm_rows);
@@ -624,9 +637,9 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
         cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lm_smem) !=
             cudaSuccess)
         return fail(set_error(AAEDN_ECUDA, "lm_head smem attribute failed"));
-    if (cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-        cudaSuccess)
-        return fail(set_error(AAEDN_ECUDA, "attention smem attribute failed"));
+    rc = attn_set_attrs<1>();
+    if (rc)
+        return fail(rc);
     rc = set_model_kernel_attrs();
     if (rc)
         return fail(rc);

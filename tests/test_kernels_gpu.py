@@ -80,8 +80,8 @@ def test_fused_matmul_strides_and_integer_scales(oracle):
     import pyoracle
     oracle.lib.or_q4_matmul(pyoracle.ptr(np.ascontiguousarray(xm)), pyoracle.ptr(data), pyoracle.ptr(scales),
                             pyoracle.ptr(want), M, N, K, lda, ldb, N, 1)
-    w = np.stack([oracle.dequant(data[r * ldb // 2:(r + 1) * ldb // 2], scales[r * ldb // 32:(r + 1) * ldb // 32],
-                                 ldb)[:K] for r in range(N)])
+    codes = np.stack([data & 15, data >> 4], 1).reshape(N, ldb).astype(np.float32)
+    w = (codes * np.repeat(scales.reshape(N, ldb // 32).astype(np.float32), 32, axis=1))[:, :K]
     bound = 2e-5 * (np.abs(xm[:, :K]) @ np.abs(w).T) + 1e-6
     assert np.all(np.abs(got - want) <= bound)
 
