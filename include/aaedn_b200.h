@@ -165,6 +165,12 @@ int aaedn_model_rewind(aaedn_model* m, uint32_t pos);
  * (per layer: qkv, attention, o, gate/up, down; then lm_head). cap is the
  * capacity of h_ms; returns the kernel count through *n_out. */
 int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t cap, uint32_t* n_out);
+/* Tracing: device time of sub-graphs of one decode step replayed `reps`
+ * times back to back with the decode graph's launch setup; h_ms (>= 8
+ * entries) receives ms per step of: all kernels, the dequant-GEMVs, qkv,
+ * attention, o, gate/up, down, lm_head. Leaves the KV cache and hidden state
+ * undefined (rewind or reset afterwards). */
+int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32_t cap);
 /* Kernels launched by one decode step. */
 uint32_t aaedn_model_kernels_per_step(const aaedn_model* m);
 /* Copy the last step's logits ([vocab]) / the greedy tokens generated so far. */

@@ -97,6 +97,7 @@ def lib():
         "aaedn_model_tokens": ([_vp, _vp, _sz], _int),
         "aaedn_model_forward_debug": ([_vp, _u32, _vp, _vp], _int),
         "aaedn_model_rewind": ([_vp, _u32], _int),
+        "aaedn_model_profile_parts": ([_vp, _u32, _vp, _u32], _int),
         "aaedn_model_profile_step": ([_vp, _vp, _u32, ctypes.POINTER(_u32)], _int),
     }
     for name, (args, res) in sig.items():
@@ -346,6 +347,14 @@ class Model:
         got = _u32()
         check(lib().aaedn_model_profile_step(self.h, _p(out), n, ctypes.byref(got)))
         return out[:got.value]
+
+    PART_NAMES = ("step", "gemv", "qkv", "attention", "o", "gate_up", "down", "lm_head")
+
+    def profile_parts(self, reps=10):
+        """ms per step of sub-graphs of the decode step (tracing)."""
+        out = np.empty(8, np.float32)
+        check(lib().aaedn_model_profile_parts(self.h, reps, _p(out), 8))
+        return dict(zip(self.PART_NAMES, out.tolist()))
 
     def forward_debug(self, token):
         hidden = np.empty((self.cfg["n_layers"], self.cfg["dim"]), np.float32)

@@ -126,13 +126,16 @@ __global__ void zero_kernel(float* out, size_t n)
 template <int NM, int SK>
 static int gemv_dispatch(const GemvParams& p, int first_chunk, cudaStream_t st)
 {
-    auto kern = first_chunk ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK>
-                            : gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK>;
-    static bool attr_done[2] = {false, false};
-    if (!attr_done[first_chunk])
+    const int full = (p.full_shape && p.scale_pairs) ? 1 : 0;
+    auto kern = first_chunk ? (full ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK, true>
+                                    : gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK, false>)
+                            : (full ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK, true>
+                                    : gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK, false>);
+    static bool attr_done[2][2] = {{false, false}, {false, false}};
+    if (!attr_done[first_chunk][full])
     {
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_done[first_chunk] = true;
+        attr_done[first_chunk][full] = true;
     }
     const int groups = (p.N + 15) / 16;
     const int grid = groups < sm_count() ? groups : sm_count();

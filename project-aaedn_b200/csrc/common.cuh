@@ -134,10 +134,17 @@ __device__ __forceinline__ void mma_bf16_16816(float& d0, float& d1, float& d2, 
 // as bf16x2 values 16 + code: the code lands in mantissa bits 3..6 of each
 // half under the exponent of 16.0 (0x4180). E0 = codes (0,4), E1 = (1,5),
 // E2 = (2,6), E3 = (3,7).
-__device__ __forceinline__ uint32_t nib_e0(uint32_t w) { return ((w << 3) & 0x00780078u) | 0x41804180u; }
-__device__ __forceinline__ uint32_t nib_e1(uint32_t w) { return ((w >> 1) & 0x00780078u) | 0x41804180u; }
-__device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return ((w >> 5) & 0x00780078u) | 0x41804180u; }
-__device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return ((w >> 9) & 0x00780078u) | 0x41804180u; }
+// (x & 0x00780078) | 0x41804180 as one LOP3 (truth table 0xEA = (a & b) | c)
+__device__ __forceinline__ uint32_t lop3_bias(uint32_t x)
+{
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(x), "n"(0x00780078), "n"(0x41804180));
+    return d;
+}
+__device__ __forceinline__ uint32_t nib_e0(uint32_t w) { return lop3_bias(w << 3); }
+__device__ __forceinline__ uint32_t nib_e1(uint32_t w) { return lop3_bias(w >> 1); }
+__device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return lop3_bias(w >> 5); }
+__device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return lop3_bias(w >> 9); }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
@@ -197,6 +204,73 @@ __device__ __forceinline__ float ldsf(uint32_t addr)
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"(addr));
     return r;
+}
+
+// ---- mbarriers and bulk (TMA) copies --------------------------------------
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(addr), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// arrive (count 1) and announce tx bytes that bulk copies will complete
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t addr, uint32_t tx)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(addr), "r"(tx) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t addr)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(addr), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete, for at most
+// limit_ns; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t addr, uint32_t parity, uint64_t limit_ns)
+{
+    if (mbar_try_wait(addr, parity))
+        return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(addr, parity))
+        if (globaltimer_ns() - t0 > limit_ns)
+            return false;
+    return true;
+}
+
+// global -> shared bulk copy completing on an mbarrier (size multiple of 16,
+// both addresses 16-byte aligned)
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+
+// named barrier over `count` threads (warps 0..count/32-1)
+__device__ __forceinline__ void named_bar_sync(int id, int count)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- programmatic dependent launch ----------------------------------------

@@ -112,6 +112,24 @@ __device__ __forceinline__ uint32_t u4get(const uint4& v, int q)
     return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
 }
 
+// Sum over the first NTH threads (warps 0..NTH/32-1, named barrier 1);
+// every one of them receives the result. scratch >= NTH/32 floats.
+template <int NTH>
+__device__ __forceinline__ float group_sum(float v, float* scratch)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    named_bar_sync(1, NTH);
+    if (lane == 0)
+        scratch[warp] = v;
+    named_bar_sync(1, NTH);
+    float t = 0.0f;
+    for (int i = 0; i < NTH / 32; ++i) // fixed order: deterministic
+        t += scratch[i];
+    named_bar_sync(1, NTH);
+    return t;
+}
+
 // Block-wide sum; every thread receives the result. scratch >= 33 floats.
 __device__ __forceinline__ float block_sum(float v, float* scratch)
 {
@@ -132,11 +150,11 @@ __device__ __forceinline__ float block_sum(float v, float* scratch)
 // (block tp of the tile, part p), the 4 bf16x2 registers of mmas 2q and
 // 2q+1: (x[8q+0],x[8q+4]), (x[8q+1],x[8q+5]), (x[8q+2],x[8q+6]),
 // (x[8q+3],x[8q+7]) of that block. tb[(m*ntile+tt)*4+tp] = 16 * sum(hi+lo).
-template <int NM, int PRO>
+template <int NM, int PRO, int NTH = GEMV_WARPS * 32>
 __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* frag, float* tb, float* misc,
                                                  int ntile)
 {
-    const int tid = threadIdx.x, nth = blockDim.x;
+    const int tid = threadIdx.x, nth = NTH;
     const int nblk = p.K >> 5;
     const float* src[NM];
     float rms[NM];
@@ -170,7 +188,7 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
                 ss = fmaf(v.z, v.z, ss);
                 ss = fmaf(v.w, v.w, ss);
             }
-            ss = block_sum(ss, misc);
+            ss = group_sum<NTH>(ss, misc);
             // src/rmsnorm.cpp:34
             rms[m] = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.eps));
         }
@@ -250,14 +268,13 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
     }
 }
 
-// Epilogue of one 16-row group on one warp: sums the 8 K-split partial
+// Epilogue of one 16-row group on one warp: sums the S K-split partial
 // sums of each row in fixed order, then stores / accumulates / adds the
 // residual, or pairs rows (8j + r, 8j + r + 8) for SwiGLU and for RoPE +
 // the KV-cache append.
-template <int NM, int EPI>
+template <int NM, int EPI, int S = GEMV_WARPS>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* rb, int group, int lane)
 {
-    constexpr int S = GEMV_WARPS;
     if constexpr (EPI == EPI_STORE || EPI == EPI_ACCUM || EPI == EPI_RESIDUAL)
     {
         for (int idx = lane; idx < NM * 16; idx += 32)
@@ -435,7 +452,7 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
 // boundaries. A CTA needs well under half of an SM, so the next kernel of a
 // decode step (launched as a programmatic dependent) becomes resident at once
 // and fills its own ring while this one computes.
-template <int NM, int PRO, int EPI, int SK>
+template <int NM, int PRO, int EPI, int SK, bool FULL = false>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvParams p)
 {
     constexpr int D = GEMV_STAGES;
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
     const uint16_t* i_s1 = i_s0 + 8 * srow;
     const uint32_t ring_w = smem_addr(stw) + (uint32_t)tid * 32;
     const uint32_t ring_s = smem_addr(sts) + (uint32_t)tid * 8;
-    const bool full = p.full_shape;
+    constexpr bool full = FULL;
     auto issue = [&]() {
         if (i_left > 0)
         {
@@ -532,7 +549,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
         frag[(size_t)NM * ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
-    if (p.full_shape && pairs)
+    if (FULL)
     {
         gemv_lean_loop<NM, EPI, SK>(p, stw, sts, frag, tb, red, my_groups, tA, tB, ntile, issue);
         cp_async_wait<0>();

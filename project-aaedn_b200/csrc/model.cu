@@ -21,6 +21,45 @@
 
 #include "attention.cuh"
 #include "gemv_q4.cuh"
+#include "gemv_tiled.cuh"
+#include "gemv_tma.cuh"
+
+namespace aaedn_dev
+{
+void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t K, uint8_t* out)
+{
+    const size_t ntile = K / 128, nchunk = (ntile + GT_CHUNK_TILES - 1) / GT_CHUNK_TILES;
+    const size_t group_bytes = ntile * GT_TILE_BYTES;
+    aaedn_host::parallel_for(N / 16, 1, [&](size_t g0, size_t g1) {
+        for (size_t gi = g0; gi < g1; ++gi)
+        {
+            uint8_t* o = out + gi * group_bytes;
+            for (size_t c = 0; c < nchunk; ++c)
+            {
+                const size_t tiles = std::min<size_t>(GT_CHUNK_TILES, ntile - c * GT_CHUNK_TILES);
+                for (size_t i = 0; i < tiles; ++i) // codes in A-fragment order
+                    for (int h = 0; h < 2; ++h)
+                        for (int l = 0; l < 32; ++l)
+                        {
+                            const size_t row = gi * 16 + (l >> 2) + 8 * h;
+                            const size_t blk = (c * GT_CHUNK_TILES + i) * 4 + (l & 3);
+                            std::memcpy(o, codes + row * (K / 2) + blk * 16, 16);
+                            o += 16;
+                        }
+                for (size_t i = 0; i < tiles; ++i) // then the scales, same order
+                    for (int h = 0; h < 2; ++h)
+                        for (int l = 0; l < 32; ++l)
+                        {
+                            const size_t row = gi * 16 + (l >> 2) + 8 * h;
+                            const size_t blk = (c * GT_CHUNK_TILES + i) * 4 + (l & 3);
+                            std::memcpy(o, scales + row * (K / 32) + blk, 2);
+                            o += 2;
+                        }
+            }
+        }
+    });
+}
+} // namespace aaedn_dev
 
 using namespace aaedn_dev;
 
@@ -177,21 +216,69 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
 
 struct DevLayer
 {
+    // codes and scales of a matrix are one region: row-major codes followed
+    // by the scales, or (when the shape tiles) the tile-major repacking
     uint8_t *wqkv, *wo, *wgu, *wd;
     uint16_t *sqkv, *so, *sgu, *sd;
+    bool tqkv, to, tgu, td;
     float *attn_norm, *ffn_norm;
     float *k, *v; // [n_pages][n_kv][P][hd]
 };
 
-template <int PRO, int EPI>
-int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl)
+// Shapes the TMA-fed kernel covers: whole 16-row groups, K and the row
+// pitch in whole 256-code chunks, 16-byte aligned codes and scales.
+inline bool tma_ok(const GemvParams& p)
 {
-    auto kern = gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16>;
+    return (p.N % 16) == 0 && (p.K % 256) == 0 && (p.ldb % 256) == 0 && (p.kt0 % 2) == 0 &&
+           ((p.kt1 - p.kt0) % 2) == 0 && (reinterpret_cast<uintptr_t>(p.w) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(p.s) & 15) == 0;
+}
+
+bool use_tma()
+{
+    static int v = -1;
+    if (v < 0)
+    {
+        const char* e = std::getenv("AAEDN_GEMV_TMA");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
+inline bool tiles_ok(size_t N, size_t K) { return N % 16 == 0 && K % 128 == 0; }
+
+template <int PRO, int EPI>
+int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = false)
+{
+    if (tiled)
+    {
+        const int groups = p.N / 16;
+        const int grid = groups < sm_count() ? groups : sm_count();
+        cudaError_t e = launch_kernel(gemv_tiled_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
+                                      gemv_tiled_smem_bytes(p.K / 128), st, pdl, p);
+        if (e != cudaSuccess)
+            return set_error(AAEDN_ECUDA, "launch of gemv_tiled_kernel failed: %s", cudaGetErrorString(e));
+        count_launch();
+        return AAEDN_OK;
+    }
+    if (use_tma() && tma_ok(p))
+    {
+        const int groups = p.N / 16;
+        const int grid = groups < sm_count() ? groups : sm_count();
+        cudaError_t e = launch_kernel(gemv_tma_kernel<PRO, EPI>, dim3(grid), dim3(GEMV_TMA_THREADS),
+                                      gemv_tma_smem_bytes(p.kt1 - p.kt0), st, pdl, p);
+        if (e != cudaSuccess)
+            return set_error(AAEDN_ECUDA, "launch of gemv_tma_kernel failed: %s", cudaGetErrorString(e));
+        count_launch();
+        return AAEDN_OK;
+    }
+    auto kern = (p.full_shape && p.scale_pairs) ? gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>
+                                                : gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>;
     static int per_sm = -1;
     if (per_sm < 0)
     {
         const char* e = std::getenv("AAEDN_GEMV_CTAS_PER_SM");
-        per_sm = e ? std::max(1, std::atoi(e)) : 1;
+        per_sm = e ? std::max(1, std::atoi(e)) : 2;
     }
     const int groups = (p.N + 15) / 16;
     const int grid = groups < per_sm * sm_count() ? groups : per_sm * sm_count();
@@ -208,8 +295,14 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl)
 template <int PRO, int EPI>
 int set_gemv_attrs()
 {
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16>,
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tma_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024));
     return AAEDN_OK;
 }
 
@@ -255,7 +348,8 @@ struct aaedn_model
     uint32_t h_pos = 0;
     uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
     bool weights_set = false;
-    bool pdl = true; // programmatic dependent launch inside the decode graph
+    bool pdl = true;   // programmatic dependent launch inside the decode graph
+    bool tiled = true; // tile-major repacking of the matrices whose shape allows it
 
     template <typename T>
     T* take(size_t bytes)
@@ -277,14 +371,15 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     for (uint32_t l = 0; l < c.n_layers; ++l)
     {
         DevLayer L{};
-        L.wqkv = m->take<uint8_t>(qkv_rows * D / 2);
-        L.sqkv = m->take<uint16_t>(qkv_rows * D / 32 * 2);
-        L.wo = m->take<uint8_t>(D * H * hd / 2);
-        L.so = m->take<uint16_t>(D * H * hd / 32 * 2);
-        L.wgu = m->take<uint8_t>(2 * F * D / 2);
-        L.sgu = m->take<uint16_t>(2 * F * D / 32 * 2);
-        L.wd = m->take<uint8_t>(D * F / 2);
-        L.sd = m->take<uint16_t>(D * F / 32 * 2);
+        auto mat = [&](uint8_t*& w, uint16_t*& sc, bool& tiled, size_t N, size_t K) {
+            w = m->take<uint8_t>(N * K / 2 + N * K / 32 * 2);
+            sc = reinterpret_cast<uint16_t*>(w + N * K / 2);
+            tiled = m->tiled && tiles_ok(N, K);
+        };
+        mat(L.wqkv, L.sqkv, L.tqkv, qkv_rows, D);
+        mat(L.wo, L.so, L.to, D, H * hd);
+        mat(L.wgu, L.sgu, L.tgu, 2 * F, D);
+        mat(L.wd, L.sd, L.td, D, F);
         L.attn_norm = m->take<float>(D * 4);
         L.ffn_norm = m->take<float>(D * 4);
         L.k = m->take<float>((size_t)m->n_pages * KV * m->page_size * hd * 4);
@@ -314,7 +409,20 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     return align_up(m->used, 256);
 }
 
-static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr)
+// Kernel classes of a decode step (mask bits for the tracing sub-graphs).
+enum
+{
+    K_QKV = 1,
+    K_ATTN = 2,
+    K_O = 4,
+    K_GU = 8,
+    K_DOWN = 16,
+    K_LM = 32,
+    K_ALL = 63,
+};
+
+static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr,
+                        int mask = K_ALL)
 {
     // programmatic dependent launches between consecutive kernels (not when
     // events or copies sit between them)
@@ -366,7 +474,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         q.rope_sin = m->rope_sin;
         q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
         q.scale_pairs = ((D >> 5) & 1) == 0;
-        rc = (l == 0) ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl) : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl);
+        rc = !(mask & K_QKV) ? AAEDN_OK
+             : (l == 0)      ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
+                             : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -390,7 +500,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         a.page_table = m->page_table;
         a.page_size = m->page_size;
         const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
-        rc = attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl);
+        rc = (mask & K_ATTN) ? attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -410,7 +520,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         o.ldc = (size_t)D;
         o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
         o.scale_pairs = (((H * hd) >> 5) & 1) == 0;
-        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl);
+        rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -431,7 +541,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         gu.act = m->act;
         gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
         gu.scale_pairs = ((D >> 5) & 1) == 0;
-        rc = model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl);
+        rc = (mask & K_GU) ? model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -451,7 +561,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         dn.ldc = (size_t)D;
         dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
         dn.scale_pairs = ((F >> 5) & 1) == 0;
-        rc = model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl);
+        rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -474,6 +584,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     lp.out_tokens = m->out_tokens;
     lp.max_seq = (int)c.max_seq;
     lp.rows_per_cta = m->lm_rows;
+    if (mask & K_LM)
     {
         cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(256), (size_t)(D + 64) * 4, st, pdl,
                                       lp);
@@ -579,10 +690,12 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
     {
         const char* e = std::getenv("AAEDN_PDL");
         m->pdl = !(e && e[0] == '0');
+        const char* t = std::getenv("AAEDN_TILED");
+        m->tiled = !(t && t[0] == '0');
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
-    // about one attention CTA per SM (the CTA walks its token range in
+    // about one attention CTA per SM (a CTA walks its token range in
     // 64-token chunks, so any split count covers any context length)
     int S = std::max(1, sm_count() / (int)c.n_kv_heads);
     S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
@@ -690,6 +803,23 @@ static inline size_t rope_pair_row(size_t r_in_head, size_t hd)
     return r < 8 ? 8 * j + r : hd / 2 + 8 * j + (r - 8);
 }
 
+// Uploads one matrix (row-major host codes/scales, rows already in device
+// order) into its region: tile-major when the layer says so.
+static int upload_matrix(uint8_t* dw, uint16_t* ds, bool tiled, const uint8_t* codes, const uint16_t* scales,
+                         size_t N, size_t K)
+{
+    if (tiled)
+    {
+        std::vector<uint8_t> blob(tiled_bytes(N, K));
+        repack_tiled(codes, scales, N, K, blob.data());
+        AAEDN_CUDA_TRY(cudaMemcpy(dw, blob.data(), blob.size(), cudaMemcpyHostToDevice));
+        return AAEDN_OK;
+    }
+    AAEDN_CUDA_TRY(cudaMemcpy(dw, codes, N * K / 2, cudaMemcpyHostToDevice));
+    AAEDN_CUDA_TRY(cudaMemcpy(ds, scales, N * K / 32 * 2, cudaMemcpyHostToDevice));
+    return AAEDN_OK;
+}
+
 static void copy_row(std::vector<uint8_t>& dd, std::vector<uint16_t>& ds, size_t drow, const uint8_t* sd,
                      const uint16_t* ss, size_t srow, size_t K)
 {
@@ -725,11 +855,15 @@ extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn
             else
                 copy_row(dd, ds, dr, w->wv, w->sv, dr - (H + KV) * hd, D);
         }
-        AAEDN_CUDA_TRY(cudaMemcpy(L.wqkv, dd.data(), dd.size(), cudaMemcpyHostToDevice));
-        AAEDN_CUDA_TRY(cudaMemcpy(L.sqkv, ds.data(), ds.size() * 2, cudaMemcpyHostToDevice));
+        int rc = upload_matrix(L.wqkv, L.sqkv, L.tqkv, dd.data(), ds.data(), rows, D);
+        if (rc)
+            return rc;
     }
-    AAEDN_CUDA_TRY(cudaMemcpy(L.wo, w->wo, D * H * hd / 2, cudaMemcpyHostToDevice));
-    AAEDN_CUDA_TRY(cudaMemcpy(L.so, w->so, D * H * hd / 32 * 2, cudaMemcpyHostToDevice));
+    {
+        int rc = upload_matrix(L.wo, L.so, L.to, w->wo, w->so, D, H * hd);
+        if (rc)
+            return rc;
+    }
     {
         const size_t rows = 2 * F;
         std::vector<uint8_t> dd(rows * D / 2);
@@ -742,11 +876,15 @@ extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn
             else
                 copy_row(dd, ds, dr, w->wu, w->su, 8 * j + r - 8, D);
         }
-        AAEDN_CUDA_TRY(cudaMemcpy(L.wgu, dd.data(), dd.size(), cudaMemcpyHostToDevice));
-        AAEDN_CUDA_TRY(cudaMemcpy(L.sgu, ds.data(), ds.size() * 2, cudaMemcpyHostToDevice));
+        int rc = upload_matrix(L.wgu, L.sgu, L.tgu, dd.data(), ds.data(), rows, D);
+        if (rc)
+            return rc;
     }
-    AAEDN_CUDA_TRY(cudaMemcpy(L.wd, w->wd, D * F / 2, cudaMemcpyHostToDevice));
-    AAEDN_CUDA_TRY(cudaMemcpy(L.sd, w->sd, D * F / 32 * 2, cudaMemcpyHostToDevice));
+    {
+        int rc = upload_matrix(L.wd, L.sd, L.td, w->wd, w->sd, D, F);
+        if (rc)
+            return rc;
+    }
     if (w->attn_norm)
         AAEDN_CUDA_TRY(cudaMemcpy(L.attn_norm, w->attn_norm, D * 4, cudaMemcpyHostToDevice));
     if (w->ffn_norm)
@@ -1023,4 +1161,69 @@ extern "C" int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t ca
         return set_error(AAEDN_ECUDA, "profile step: %s", cudaGetErrorString(e));
     m->h_pos += 1;
     return AAEDN_OK;
+}
+
+// Tracing: device time of sub-graphs of one decode step, each replayed
+// `reps` times back to back (same launch setup as the decode graph).
+// h_ms[i] = ms per step of: 0 all kernels, 1 the four dequant-GEMVs of every
+// layer, 2 qkv, 3 attention, 4 o, 5 gate/up, 6 down, 7 lm_head. The KV cache
+// and hidden state are left in an undefined state: rewind or reset after.
+extern "C" int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32_t cap)
+{
+    MODEL_OK(m);
+    static const int masks[8] = {K_ALL, K_QKV | K_O | K_GU | K_DOWN, K_QKV, K_ATTN, K_O, K_GU, K_DOWN, K_LM};
+    if (!h_ms || cap < 8 || reps == 0)
+        return set_error(AAEDN_EINVAL, "aaedn_model_profile_parts: need 8 outputs and reps > 0");
+    if (m->h_pos == 0 || (size_t)m->h_pos + reps + 2 > m->cfg.max_seq)
+        return set_error(AAEDN_ESTATE, "aaedn_model_profile_parts: sequence empty or too full for %u replays", reps);
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    AAEDN_CUDA_TRY(cudaEventCreate(&e0));
+    AAEDN_CUDA_TRY(cudaEventCreate(&e1));
+    int rc = AAEDN_OK;
+    for (int i = 0; i < 8 && rc == AAEDN_OK; ++i)
+    {
+        // the step must not advance the position: keep pos fixed by restoring it
+        const uint64_t before = g_launches.load();
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ex = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess)
+        {
+            rc = enqueue_step(m, m->stream, false, nullptr, masks[i]);
+            e = cudaStreamEndCapture(m->stream, &g);
+        }
+        g_launches.fetch_sub(g_launches.load() - before);
+        if (!rc && e == cudaSuccess)
+            e = cudaGraphInstantiate(&ex, g, 0);
+        if (g)
+            cudaGraphDestroy(g);
+        if (!rc && e == cudaSuccess)
+            e = cudaGraphLaunch(ex, m->stream); // warm
+        if (!rc && e == cudaSuccess)
+            e = cudaEventRecord(e0, m->stream);
+        for (uint32_t r = 0; r < reps && !rc && e == cudaSuccess; ++r)
+            e = cudaGraphLaunch(ex, m->stream);
+        if (!rc && e == cudaSuccess)
+            e = cudaEventRecord(e1, m->stream);
+        if (!rc && e == cudaSuccess)
+            e = cudaEventSynchronize(e1);
+        float ms = 0.0f;
+        if (!rc && e == cudaSuccess)
+            e = cudaEventElapsedTime(&ms, e0, e1);
+        if (ex)
+            cudaGraphExecDestroy(ex);
+        if (!rc && e != cudaSuccess)
+            rc = set_error(AAEDN_ECUDA, "profile parts: %s", cudaGetErrorString(e));
+        h_ms[i] = ms / reps;
+        // lm_head advanced the device position once per replay: put it back
+        if (!rc && (masks[i] & K_LM))
+            rc = write_state(m, m->h_pos, m->h_pos);
+        if (!rc)
+            rc = (cudaStreamSynchronize(m->stream) == cudaSuccess) ? AAEDN_OK
+                                                                    : set_error(AAEDN_ECUDA, "profile sync");
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return rc;
 }
