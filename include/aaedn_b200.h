@@ -105,6 +105,24 @@ int aaedn_cu_attention(const float* d_q, const float* d_k, const float* d_v, con
                        size_t num_segments, float* d_out, size_t n_heads, size_t head_dim, float scale,
                        void* stream);
 
+/* No counterpart in the reference. The same attention as
+ * aaedn_cu_attention for callers that cannot let a library allocate device
+ * memory (for example an application that hands all device memory to one
+ * fixed pool at startup and forbids allocation afterwards, the rule the
+ * reference states in docs/sdd.md:78 and README.md:18). It calls no
+ * cudaMalloc or cudaFree: its scratch (the per-split partial results and the
+ * split counters) is a fixed AAEDN_ATTN_NOALLOC_SCRATCH_BYTES array that
+ * every GPU loading this library holds until the process exits. Shapes whose
+ * scratch would not fit (n_heads > 1024, or n_heads*(head_dim+2)*4 bytes
+ * above the partial area) are rejected with AAEDN_EINVAL. The first call on
+ * each device looks up the array's device address: make that first call
+ * before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (another stream, another thread) race; serialise them. */
+#define AAEDN_ATTN_NOALLOC_SCRATCH_BYTES (1u << 20)
+int aaedn_cu_attention_noalloc(const float* d_q, const float* d_k, const float* d_v, const uint32_t* h_segments,
+                               size_t num_segments, float* d_out, size_t n_heads, size_t head_dim, float scale,
+                               void* stream);
+
 /* ---- the token loop ------------------------------------------------------
  * include/transformer.hpp:15-44 Transformer / transformer_init /
  * transformer_forward. One model owns one device arena (a single

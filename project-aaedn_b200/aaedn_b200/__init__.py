@@ -79,6 +79,7 @@ def lib():
         "aaedn_cu_rmsnorm": ([_vp, _vp, _vp, _sz, _f32, _vp], _int),
         "aaedn_cu_rope_apply": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _int),
         "aaedn_cu_attention": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
+        "aaedn_cu_attention_noalloc": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
         "aaedn_model_create": ([ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], _int),
         "aaedn_model_destroy": ([_vp], _int),
         "aaedn_model_config_get": ([_vp, ctypes.POINTER(ModelConfig)], _int),
@@ -201,6 +202,18 @@ def attention(d_q, d_k, d_v, segments, d_out, n_heads, head_dim, scale, stream=N
     segs = np.ascontiguousarray(segments, np.uint32).reshape(-1)
     check(lib().aaedn_cu_attention(_p(d_q), _p(d_k), _p(d_v), _p(segs), segs.size // 2, _p(d_out), n_heads,
                                    head_dim, scale, stream))
+
+
+def attention_noalloc(d_q, d_k, d_v, segments, d_out, n_heads, head_dim, scale, stream=None):
+    """attention() for callers that cannot allocate device memory: the
+    library uses its fixed 1 MiB scratch array instead of allocating, so
+    calls that overlap on the GPU race and must be serialised."""
+    segs = np.ascontiguousarray(segments, np.uint32).reshape(-1)
+    check(lib().aaedn_cu_attention_noalloc(_p(d_q), _p(d_k), _p(d_v), _p(segs), segs.size // 2, _p(d_out), n_heads,
+                                           head_dim, scale, stream))
+
+
+ATTN_NOALLOC_SCRATCH_BYTES = 1 << 20
 
 
 def device_sync():

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "attention.cuh"
 #include "gemv_q4.cuh"
@@ -445,4 +446,129 @@ extern "C" int aaedn_cu_attention(const float* d_q, const float* d_k, const floa
     if (lrc)
         return lrc;
     return AAEDN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Attention for callers that cannot allocate: the scratch is a fixed array in
+// device global memory, resolved to a device address once per device.
+// ---------------------------------------------------------------------------
+namespace
+{
+constexpr size_t NOALLOC_COUNTER_BYTES = 4096; // split counters of up to 1024 heads
+static __device__ __align__(256) uint8_t g_attn_noalloc_scratch[AAEDN_ATTN_NOALLOC_SCRATCH_BYTES];
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_base[64] = {}; // device address of the array, per device
+
+int noalloc_scratch(uint8_t** out)
+{
+    int dev = 0;
+    AAEDN_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64)
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_cu_attention_noalloc: device ordinal %d >= 64", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev])
+    {
+        // host code only sees a stand-in for the array: ask the runtime for
+        // its address on the current device
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(AAEDN_ECUDA, "aaedn_cu_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                             cudaGetErrorString(e));
+        g_noalloc_base[dev] = static_cast<uint8_t*>(p);
+    }
+    *out = g_noalloc_base[dev];
+    return AAEDN_OK;
+}
+} // namespace
+
+extern "C" int aaedn_cu_attention_noalloc(const float* d_q, const float* d_k, const float* d_v,
+                                          const uint32_t* h_segments, size_t num_segments, float* d_out,
+                                          size_t n_heads, size_t head_dim, float scale, void* stream)
+{
+    if (n_heads == 0 || head_dim == 0)
+        return AAEDN_OK;
+    CHECK_DEV(d_out);
+    cudaStream_t st = as_stream(stream);
+    size_t total = 0;
+    if (h_segments)
+        for (size_t i = 0; i < num_segments; ++i)
+            total += h_segments[2 * i + 1];
+    if (!d_q || !d_k || !d_v || !h_segments || total == 0) // src/attention.cpp:13-18
+    {
+        const size_t n = n_heads * head_dim;
+        zero_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(d_out, n);
+        AAEDN_LAUNCH_CHECK("zero_kernel");
+        return AAEDN_OK;
+    }
+    if (num_segments > (size_t)ATTN_MAX_SEG || head_dim > (size_t)ATTN_MAX_HD || (head_dim & 3) ||
+        total > (size_t)INT32_MAX)
+        return set_error(AAEDN_EINVAL,
+                         "aaedn_cu_attention_noalloc: at most %d segments and head_dim a multiple of 4 <= %d",
+                         ATTN_MAX_SEG, ATTN_MAX_HD);
+    const size_t part_cap = AAEDN_ATTN_NOALLOC_SCRATCH_BYTES - NOALLOC_COUNTER_BYTES;
+    const size_t per_split = n_heads * (head_dim + 2) * sizeof(float);
+    if (n_heads * sizeof(unsigned) > NOALLOC_COUNTER_BYTES || per_split > part_cap)
+        return set_error(AAEDN_EINVAL,
+                         "aaedn_cu_attention_noalloc: %zu heads x head_dim %zu need more than the %u-byte "
+                         "scratch (at most 1024 heads and n_heads*(head_dim+2)*4 <= %zu bytes)",
+                         n_heads, head_dim, AAEDN_ATTN_NOALLOC_SCRATCH_BYTES, part_cap);
+    if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_k) | reinterpret_cast<uintptr_t>(d_v)) & 15)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_attention_noalloc: q/k/v must be 16-byte aligned");
+    CHECK_DEV(d_q);
+    CHECK_DEV(d_k);
+    CHECK_DEV(d_v);
+    uint8_t* base = nullptr;
+    int rc = noalloc_scratch(&base);
+    if (rc)
+        return rc;
+    AttnParams p{};
+    p.q = d_q;
+    p.k = d_k;
+    p.v = d_v;
+    p.out = d_out;
+    p.n_heads = (int)n_heads;
+    p.n_kv = (int)n_heads;
+    p.head_dim = (int)head_dim;
+    p.scale = scale;
+    p.len_static = (int)total;
+    p.max_len = (int)total;
+    // the split count of aaedn_cu_attention, capped by the scratch
+    int S = (int)((2 * 148 + n_heads - 1) / n_heads);
+    if (S > (int)((total + 7) / 8))
+        S = (int)((total + 7) / 8);
+    if (S > (int)(part_cap / per_split))
+        S = (int)(part_cap / per_split);
+    if (S < 1)
+        S = 1;
+    if (S > 256)
+        S = 256;
+    p.S = S;
+    p.max_tok = (int)((total + S - 1) / S);
+    const size_t smem = attn_smem_bytes(1, (int)head_dim, p.max_tok);
+    if (smem > 200 * 1024)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_attention_noalloc: too many tokens per split");
+    p.nseg = (int)num_segments;
+    uint32_t off = 0;
+    for (size_t i = 0; i < num_segments; ++i)
+    {
+        p.seg_start[i] = h_segments[2 * i];
+        p.seg_off[i] = off;
+        off += h_segments[2 * i + 1];
+    }
+    p.seg_off[num_segments] = off;
+    p.counters = reinterpret_cast<unsigned*>(base);
+    p.part = reinterpret_cast<float*>(base + NOALLOC_COUNTER_BYTES);
+    // the array keeps whatever the last call left: the split counters must
+    // start at zero (the partials are written before they are read)
+    AAEDN_CUDA_TRY(cudaMemsetAsync(p.counters, 0, n_heads * sizeof(unsigned), st));
+    static bool attr = false;
+    if (!attr)
+    {
+        int arc = attn_set_attrs_g<0, 1>();
+        if (arc)
+            return arc;
+        attr = true;
+    }
+    return attn_launch<0>(p, dim3((unsigned)n_heads, (unsigned)S), smem, st);
 }
