@@ -54,12 +54,21 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller cases of the same model for profiler captures (not bench lines)
+    ap.add_argument("--layers", type=int, default=None, help="profiling case: fewer layers than the 7B model")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="profiling case: prompt length")
+    ap.add_argument("--ctx", type=int, default=None, help="profiling case: context length")
     return ap.parse_args()
 
 
-def model_cfg():
+def model_cfg(args=None):
     import aaedn_b200 as ab
-    return dict(ab.LLAMA2_7B)
+    cfg = dict(ab.LLAMA2_7B)
+    if args is not None and args.layers:
+        cfg["n_layers"] = args.layers
+    if args is not None and args.ctx:
+        cfg["max_seq"] = args.ctx
+    return cfg
 
 
 def gemv_shapes(cfg):
@@ -94,7 +103,7 @@ def measured_peaks():
 
 def profiled_traffic():
     """dram bytes per GEMV launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "gemv_tiled_decode_7b.md")
+    p = os.path.join(ROOT, "profiles", "gemv_tiled_i8_decode_7b.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -236,17 +245,17 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    cfg = model_cfg()
+    cfg = model_cfg(args)
     K, W = args.steps, max(3, args.warmup)
     E, P = args.e2e_steps, args.profile_steps
-    if PROMPT + W + K + E + P + 2 > cfg["max_seq"]:
+    if args.prompt + W + K + E + P + 2 > cfg["max_seq"]:
         raise SystemExit(f"steps+warmup too large for ctx {cfg['max_seq']}")
 
     w = host_weights(cfg)
     model = ab.Model(cfg)
     model.set_weights(w)
     stream = torch.cuda.ExternalStream(model.stream)
-    prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], PROMPT)
+    prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], args.prompt)
 
     # prefill (one graph replay per prompt token), then W warm-up decode steps
     model.forward(prompt, want_logits=False)
@@ -332,16 +341,18 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": "llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode",
+            "config": {"workload": ("llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode"
+                                    if (cfg["n_layers"], args.prompt) == (32, 128) else
+                                    f"profiling case: {cfg['n_layers']} layers, {args.prompt}-token prompt"),
                        "dim": cfg["dim"], "n_layers": cfg["n_layers"], "n_heads": cfg["n_heads"],
                        "head_dim": cfg["head_dim"], "ffn_dim": cfg["ffn_dim"], "vocab": cfg["vocab"],
-                       "ctx": cfg["max_seq"], "prompt": PROMPT, "positions": [pos0, pos1],
+                       "ctx": cfg["max_seq"], "prompt": args.prompt, "positions": [pos0, pos1],
                        "weights": "4-bit codes, fp16 scale per 32, fp32 embedding/lm_head",
                        "l2": "inputs larger than L2: 4.1 GB of weights streamed per step",
                        "parallelism": "replicas" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "gemv_tiled_kernel (the 4 dequant-GEMVs of every layer, M=1)",
+                         "kernel": "gemv_tiled_i8_kernel (the 4 dequant-GEMVs of every layer, M=1)",
                          "launches_per_step": 4 * L, "bytes_per_launch_avg": gemv_total_bytes / 4,
                          "bytes_per_step": gemv_total_bytes * L,
                          "timing": "sub-graph of the step's GEMVs replayed back to back, CUDA events"},

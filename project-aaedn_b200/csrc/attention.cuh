@@ -5,18 +5,17 @@
 //
 // Grid (n_kv_heads, S): CTA (h, s) owns tokens [L*s/S, L*(s+1)/S) of kv head
 // h and all G = n_heads/n_kv query heads that share it, so each K/V row is
-// read from HBM once per step. Inside a CTA the scores are exact (max, then
-// exp(s - max), then the V sum: the three passes of src/attention.cpp:46-82);
-// the S partial results (max, sum, unnormalised output) are merged by the
-// last CTA of each kv head in fixed split order, so the result is
+// read from HBM once per step. Warp w of a CTA takes tokens w, w + 8, ... of
+// that range, a batch at a time: each lane loads its 16-byte slices of the
+// batch's K and V rows straight into registers (every load of the batch in
+// flight at once), the q.k dots are finished with warp shuffles, and the
+// softmax is carried online per warp (running max, sum and unnormalised V
+// sum, rescaled when the max grows). The 8 warps, then the S splits (by the
+// last CTA of each kv head), are merged in fixed order, so the result is
 // deterministic. All arithmetic is fp32 with expf.
 //
-// Memory-level parallelism (the K/V stream is HBM-bound): a CTA stages its
-// rows 64 tokens at a time in shared memory with asynchronous 16-byte copies
-// (every row of K and V of the chunk in flight at once). Rows written in
-// earlier decode steps are requested before waiting for the previous kernel,
-// so their latency overlaps it; across chunks the softmax is carried online
-// (running max and sum, rescaled per chunk).
+// In the model the K/V rows of earlier positions do not depend on the
+// previous kernel: a CTA asks L2 for its first rows before waiting for it.
 #pragma once
 
 #include "gemv_q4.cuh"
@@ -29,6 +28,7 @@ constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_MAX_SEG = 64;
 constexpr int ATTN_MAX_HD = 256;
 constexpr int ATTN_MAX_G = 8; // query heads per kv head (template values 1, 2, 4, 8)
+constexpr int ATTN_PREFETCH_TOKENS = 64; // rows per CTA requested from L2 ahead
 
 struct AttnParams
 {
@@ -43,7 +43,7 @@ struct AttnParams
     const DecodeState* state; // MODE 1: L = pos + 1
     int len_static;           // MODE 0: L
     int max_len;              // bound on L (cache capacity)
-    int max_tok;              // smem bound on tokens per split
+    int max_tok;              // unused (kept for the launch interface)
     const int* page_table;
     int page_size;
     int nseg;
@@ -51,23 +51,11 @@ struct AttnParams
     uint32_t seg_off[ATTN_MAX_SEG + 1]; // prefix sums of the lengths
 };
 
-// Score rows are padded to a multiple of 4 floats so the float4 regions
-// after them stay 16-byte aligned.
-__host__ __device__ inline int attn_score_stride(int max_tok) { return (max_tok + 3) & ~3; }
-
-constexpr int ATTN_CHUNK = 64; // tokens staged in shared memory at a time
-
-// Rows of K and V in shared memory are padded by 16 bytes so that threads
-// reading different rows at the same offset hit different banks.
-__host__ __device__ inline int attn_row_stride(int hd) { return hd + 4; }
-
+// Shared memory: per-warp running max and sum [8][G] each, per-warp V sums
+// [8][G][hd].
 inline size_t attn_smem_bytes(int G, int hd, int /*max_tok*/)
 {
-    // K and V chunks [CH][hd+4], q [G][hd], scores [G][CH], per-slice V sums
-    // [8][G][hd], per-head running max/sum/rescale [3][G]
-    return ((size_t)2 * ATTN_CHUNK * attn_row_stride(hd) + (size_t)G * hd + (size_t)G * ATTN_CHUNK +
-            (size_t)8 * G * hd + 3 * ATTN_MAX_G + 8) *
-           4;
+    return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd) * 4;
 }
 
 template <int MODE>
@@ -90,13 +78,20 @@ __device__ __forceinline__ size_t attn_row(const AttnParams& p, int t, int kvh)
 }
 
 // G: query heads per kv head; HDM: bound on head_dim (128 or 256).
+// Registers: 64 per thread for MHA at head_dim <= 128 (4 CTAs per SM; a CTA
+// also fits beside a GEMV CTA), more for the q and V-sum slices of several
+// query heads.
+constexpr int attn_min_blocks(int G, int HDM) { return (G == 1 && HDM == 128) ? 4 : (G * HDM >= 2048 ? 1 : 2); }
+
 template <int MODE, int G, int HDM>
-__global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const AttnParams p)
+__global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_split_kernel(const AttnParams p)
 {
     extern __shared__ __align__(16) float asmem[];
+    constexpr int NCH = HDM / 128;                         // float4 slices per lane
+    constexpr int TB = (G == 1 && HDM == 128) ? 4 : 2;     // tokens per warp batch
     pdl_launch_dependents();
     const int kvh = blockIdx.x, split = blockIdx.y, S = p.S;
-    const int hd = p.head_dim, hd4 = hd >> 2, rs = attn_row_stride(hd);
+    const int hd = p.head_dim, hd4 = hd >> 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The position only changes at the end of a decode step (lm_head), so it
     // can be read before waiting for the previous kernel.
@@ -105,181 +100,175 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const AttnPara
         L = p.max_len;
     const int t0 = (int)(((long long)L * split) / S);
     const int t1 = (int)(((long long)L * (split + 1)) / S);
-    // The row of the current position is written by the previous kernel;
-    // every other row was written in earlier steps.
-    const int cur = (MODE == 1) ? L - 1 : -1;
-
-    float* ks = asmem;                           // [CH][rs]
-    float* vs = ks + ATTN_CHUNK * rs;            // [CH][rs]
-    float* qs = vs + ATTN_CHUNK * rs;            // [G][hd]
-    float* sc = qs + G * hd;                     // [G][CH]
-    float* vred = sc + G * ATTN_CHUNK;           // [8][G][hd]
-    float* run = vred + 8 * G * hd;              // [3][G]: running max, sum, rescale
-
-    auto stage = [&](int c0, int c1) { // async copies of rows [c0, c1) except cur
-        const int n = c1 - c0;
-        for (int i = tid; i < n * hd4; i += ATTN_THREADS)
-        {
-            const int j = i / hd4, c = i - j * hd4, tk = c0 + j;
-            if (tk == cur)
-                continue;
-            const size_t ro = attn_row<MODE>(p, tk, kvh);
-            cp_async_16(ks + j * rs + 4 * c, p.k + ro + 4 * c, 16u);
-            cp_async_16(vs + j * rs + 4 * c, p.v + ro + 4 * c, 16u);
-        }
-        cp_async_commit();
-    };
-
-    const int c_end0 = t0 + ATTN_CHUNK < t1 ? t0 + ATTN_CHUNK : t1;
-    if (t1 > t0)
-        stage(t0, c_end0);
-    pdl_wait();
-    for (int i = tid; i < G * hd; i += ATTN_THREADS)
-        qs[i] = p.q[(size_t)kvh * G * hd + i];
-    if (tid < G)
+    if constexpr (MODE == 1)
     {
-        run[tid] = -INFINITY;
-        run[G + tid] = 0.0f;
+        // rows of earlier positions: into L2 while the previous kernel runs
+        // (a prefetch never returns stale data)
+        const int pf1 = min(t1, min(L - 1, t0 + ATTN_PREFETCH_TOKENS));
+        const int lines = (hd * 4 + 127) >> 7;
+        for (int i = tid; i < (pf1 - t0) * lines * 2; i += ATTN_THREADS)
+        {
+            const int r = i / (lines * 2), rem = i - r * lines * 2, kv = rem / lines, ln = rem - kv * lines;
+            const size_t ro = attn_row<MODE>(p, t0 + r, kvh);
+            const float* src = (kv ? p.v : p.k) + ro + ln * 32;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+        }
     }
+    float* wm = asmem;                   // [8][G] running max per warp
+    float* wl = wm + ATTN_WARPS * G;     // [8][G] running sum per warp
+    float* wacc = wl + ATTN_WARPS * G;   // [8][G][hd]
+    pdl_wait();
 
-    // per-thread V accumulators: chunk c4 = tid % 32 of the row (float4),
-    // token slice z = tid / 32
-    constexpr int NC = HDM / 128;
-    float4 acc[G][NC];
+    // lane slices of q (scaled once: s = (q*scale).k would round differently,
+    // so the scale is applied to the dot as src/attention.cpp:42 does)
+    float4 qv[G][NCH];
 #pragma unroll
     for (int gi = 0; gi < G; ++gi)
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
+        for (int c = 0; c < NCH; ++c)
+        {
+            const int ch = lane + 32 * c;
+            qv[gi][c] = ch < hd4 ? reinterpret_cast<const float4*>(p.q + ((size_t)kvh * G + gi) * hd)[ch]
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    float m[G], l[G];
+    float4 acc[G][NCH];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+    {
+        m[gi] = -INFINITY;
+        l[gi] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
             acc[gi][c] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-    for (int c0 = t0; c0 < t1; c0 += ATTN_CHUNK)
-    {
-        const int c1 = c0 + ATTN_CHUNK < t1 ? c0 + ATTN_CHUNK : t1;
-        const int n = c1 - c0;
-        if (c0 != t0)
-            stage(c0, c1);
-        if (cur >= c0 && cur < c1) // the fresh row, after the previous kernel
-            for (int c = tid; c < hd4; c += ATTN_THREADS)
-            {
-                const size_t ro = attn_row<MODE>(p, cur, kvh);
-                reinterpret_cast<float4*>(ks + (cur - c0) * rs)[c] = reinterpret_cast<const float4*>(p.k + ro)[c];
-                reinterpret_cast<float4*>(vs + (cur - c0) * rs)[c] = reinterpret_cast<const float4*>(p.v + ro)[c];
-            }
-        cp_async_wait<0>();
-        __syncthreads();
-
-        // scores: one thread per (token, query head)
-        for (int idx = tid; idx < n * G; idx += ATTN_THREADS)
-        {
-            const int j = idx / G, gi = idx - j * G;
-            const float4* kr = reinterpret_cast<const float4*>(ks + j * rs);
-            const float4* qr = reinterpret_cast<const float4*>(qs + gi * hd);
-            float dot = 0.0f;
-            for (int c = 0; c < hd4; ++c)
-            {
-                const float4 a = qr[c], b = kr[c];
-                dot = fmaf(a.x, b.x, dot);
-                dot = fmaf(a.y, b.y, dot);
-                dot = fmaf(a.z, b.z, dot);
-                dot = fmaf(a.w, b.w, dot);
-            }
-            sc[gi * ATTN_CHUNK + j] = dot * p.scale; // src/attention.cpp:42
-        }
-        __syncthreads();
-
-        // running max / exp / sum per query head (src/attention.cpp:46-59)
-        for (int gi = warp; gi < G; gi += ATTN_WARPS)
-        {
-            float mx = -INFINITY;
-            for (int j = lane; j < n; j += 32)
-                mx = fmaxf(mx, sc[gi * ATTN_CHUNK + j]);
-            mx = warp_max(mx);
-            const float m_old = run[gi];
-            const float m_new = fmaxf(m_old, mx);
-            float sum = 0.0f;
-            for (int j = lane; j < n; j += 32)
-            {
-                const float e = expf(sc[gi * ATTN_CHUNK + j] - m_new);
-                sc[gi * ATTN_CHUNK + j] = e;
-                sum += e;
-            }
-            sum = warp_sum(sum);
-            if (lane == 0)
-            {
-                const float resc = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-                run[gi] = m_new;
-                run[G + gi] = run[G + gi] * resc + sum;
-                run[2 * G + gi] = resc;
-            }
-        }
-        __syncthreads();
-
-        // V: thread (slice z, chunk c4) sums tokens z, z+8, ... of the chunk
-        {
-            const int z = tid >> 5, c4 = tid & 31;
-#pragma unroll
-            for (int gi = 0; gi < G; ++gi)
-            {
-                const float rsc = run[2 * G + gi];
-#pragma unroll
-                for (int c = 0; c < NC; ++c)
-                {
-                    acc[gi][c].x *= rsc;
-                    acc[gi][c].y *= rsc;
-                    acc[gi][c].z *= rsc;
-                    acc[gi][c].w *= rsc;
-                }
-            }
-            for (int j = z; j < n; j += 8)
-            {
-#pragma unroll
-                for (int c = 0; c < NC; ++c)
-                {
-                    const int ch = c4 + 32 * c;
-                    if (ch < hd4)
-                    {
-                        const float4 vv = reinterpret_cast<const float4*>(vs + j * rs)[ch];
-#pragma unroll
-                        for (int gi = 0; gi < G; ++gi)
-                        {
-                            const float e = sc[gi * ATTN_CHUNK + j];
-                            acc[gi][c].x = fmaf(e, vv.x, acc[gi][c].x);
-                            acc[gi][c].y = fmaf(e, vv.y, acc[gi][c].y);
-                            acc[gi][c].z = fmaf(e, vv.z, acc[gi][c].z);
-                            acc[gi][c].w = fmaf(e, vv.w, acc[gi][c].w);
-                        }
-                    }
-                }
-            }
-        }
-        __syncthreads(); // the chunk buffers are rewritten next
     }
+
+    for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
     {
-        const int z = tid >> 5, c4 = tid & 31;
+        // batch: tokens tb0 + 8j, j < TB
+        float4 kr[TB][NCH], vr[TB][NCH];
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+        {
+            const int t = tb0 + ATTN_WARPS * j;
+            const bool live = t < t1;
+            const size_t ro = live ? attn_row<MODE>(p, t, kvh) : 0;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+            {
+                const int ch = lane + 32 * c;
+                if (live && ch < hd4)
+                {
+                    kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                    vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                }
+                else
+                {
+                    kr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
 #pragma unroll
         for (int gi = 0; gi < G; ++gi)
+        {
+            float sj[TB];
 #pragma unroll
-            for (int c = 0; c < NC; ++c)
+            for (int j = 0; j < TB; ++j)
             {
-                const int ch = c4 + 32 * c;
-                if (ch < hd4)
-                    reinterpret_cast<float4*>(vred + ((size_t)z * G + gi) * hd)[ch] = acc[gi][c];
+                float d = 0.0f;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    d = fmaf(qv[gi][c].x, kr[j][c].x, d);
+                    d = fmaf(qv[gi][c].y, kr[j][c].y, d);
+                    d = fmaf(qv[gi][c].z, kr[j][c].z, d);
+                    d = fmaf(qv[gi][c].w, kr[j][c].w, d);
+                }
+                sj[j] = d;
             }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int j = 0; j < TB; ++j)
+                    sj[j] += __shfl_xor_sync(0xffffffffu, sj[j], o);
+            float bm = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+            {
+                sj[j] = (tb0 + ATTN_WARPS * j < t1) ? sj[j] * p.scale : -INFINITY; // src/attention.cpp:42
+                bm = fmaxf(bm, sj[j]);
+            }
+            const float mn = fmaxf(m[gi], bm);
+            if (mn == -INFINITY)
+                continue; // nothing live yet
+            const float rs = (m[gi] == -INFINITY) ? 0.0f : expf(m[gi] - mn);
+            m[gi] = mn;
+            l[gi] *= rs;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+            {
+                acc[gi][c].x *= rs;
+                acc[gi][c].y *= rs;
+                acc[gi][c].z *= rs;
+                acc[gi][c].w *= rs;
+            }
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+            {
+                const float e = expf(sj[j] - mn); // 0 for dead slots
+                l[gi] += e;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    acc[gi][c].x = fmaf(e, vr[j][c].x, acc[gi][c].x);
+                    acc[gi][c].y = fmaf(e, vr[j][c].y, acc[gi][c].y);
+                    acc[gi][c].z = fmaf(e, vr[j][c].z, acc[gi][c].z);
+                    acc[gi][c].w = fmaf(e, vr[j][c].w, acc[gi][c].w);
+                }
+            }
+        }
+    }
+
+    // merge the 8 warps (fixed order) into this split's partial result
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+    {
+        if (lane == 0)
+        {
+            wm[warp * G + gi] = m[gi];
+            wl[warp * G + gi] = l[gi];
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+        {
+            const int ch = lane + 32 * c;
+            if (ch < hd4)
+                reinterpret_cast<float4*>(wacc + ((size_t)warp * G + gi) * hd)[ch] = acc[gi][c];
+        }
     }
     __syncthreads();
     for (int i = tid; i < G * hd; i += ATTN_THREADS)
     {
         const int gi = i / hd, d = i - gi * hd;
-        float o = 0.0f;
-        for (int z = 0; z < 8; ++z) // fixed order
-            o += vred[((size_t)z * G + gi) * hd + d];
+        float M = -INFINITY;
+        for (int w = 0; w < ATTN_WARPS; ++w)
+            M = fmaxf(M, wm[w * G + gi]);
+        float o = 0.0f, den = 0.0f;
+        for (int w = 0; w < ATTN_WARPS; ++w)
+        {
+            const float mw = wm[w * G + gi];
+            const float f = (mw == -INFINITY) ? 0.0f : expf(mw - M);
+            o = fmaf(wacc[((size_t)w * G + gi) * hd + d], f, o);
+            den = fmaf(wl[w * G + gi], f, den);
+        }
         const int h = kvh * G + gi;
         float* pp = p.part + ((size_t)h * S + split) * (hd + 2);
         pp[d] = o;
         if (d == 0)
         {
-            pp[hd] = (t1 > t0) ? run[gi] : -INFINITY;
-            pp[hd + 1] = run[G + gi];
+            pp[hd] = M;
+            pp[hd + 1] = den;
         }
     }
 

@@ -146,6 +146,17 @@ __device__ __forceinline__ uint32_t nib_e1(uint32_t w) { return lop3_bias(w >> 1
 __device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return lop3_bias(w >> 5); }
 __device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return lop3_bias(w >> 9); }
 
+// D += A (16x32 u8, row) * B (32x8 s8, col) with s32 accumulators: the dot
+// product engine of the integer GEMV (exact: no rounding anywhere).
+__device__ __forceinline__ void mma_u8s8_16832(int& d0, int& d1, int& d2, int& d3, uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+r"(d0), "+r"(d1), "+r"(d2), "+r"(d3)
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 // ---- asynchronous global -> shared copies (per-thread, L2 only) ----------

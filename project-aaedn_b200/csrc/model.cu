@@ -81,48 +81,149 @@ struct LmParams
     uint32_t* out_tokens;
     int max_seq;
     int rows_per_cta;
+    int stages;    // rows in the shared-memory ring, a multiple of consumers
+    int consumers; // consumer warps that take rows (<= LM_CONSUMERS)
 };
+
+constexpr int LM_CONSUMERS = 8;
+constexpr int LM_THREADS = (LM_CONSUMERS + 1) * 32;
+constexpr int LM_MAX_STAGES = 16;
+
+// Shared memory of the lm_head kernel: the row ring, x, the barriers.
+inline size_t lm_smem_bytes(int dim, int stages)
+{
+    return (size_t)stages * dim * 4 + (size_t)dim * 4 + (size_t)stages * 16 + 64 * 4;
+}
 
 // Final RMSNorm (src/transformer.cpp:230), fp32 lm_head GEMV
 // (:232-238) and greedy argmax with ties to the lowest id; the last CTA
 // advances the decode state.
-__global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
+//
+// CTA b owns rows [b * rows_per_cta, ...): one contiguous run of the
+// [vocab][dim] matrix. A producer warp streams it row by row with bulk copies
+// into shared memory, starting before the programmatic-dependent wait (the
+// weights do not depend on the previous kernel). Consumer warp w (w < C =
+// p.consumers) takes rows w, w + C, ...; its k-th row lands in its own stage
+// w + C * (k % SW) (SW = stages / C), so every stage is waited on by one warp,
+// one use after the other (a parity wait two phases ahead would pass at once).
+__global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmParams p)
 {
-    extern __shared__ __align__(16) float xs[];
-    float* misc = xs + p.dim;
+    constexpr int NC = LM_CONSUMERS;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int NS = p.stages, C = p.consumers, SW = NS / C;
+    const uint32_t row_bytes = (uint32_t)p.dim * 4u;
+    uint8_t* ring = smem;
+    float* xs = reinterpret_cast<float*>(smem + (size_t)NS * row_bytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(xs + p.dim); // full[NS], empty[NS]
+    float* misc = reinterpret_cast<float*>(bars + 2 * NS);
+    __shared__ float s_v[NC];
+    __shared__ int s_i[NC];
+    __shared__ unsigned s_last;
+    __shared__ int s_abort_mem;
+    volatile int& s_abort = s_abort_mem;
+
     pdl_launch_dependents();
-    pdl_wait(); // the hidden state comes from the previous kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float ss = 0.0f;
-    for (int i = tid; i < p.dim; i += blockDim.x)
-        ss = fmaf(p.hidden[i], p.hidden[i], ss);
-    ss = block_sum(ss, misc);
-    const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.dim), p.eps));
-    for (int i = tid; i < p.dim; i += blockDim.x)
-        xs[i] = __fmul_rn(__fmul_rn(p.hidden[i], rms), p.gain[i]);
+    const int n0 = blockIdx.x * p.rows_per_cta;
+    const int nrows = max(0, min(p.vocab, n0 + p.rows_per_cta) - n0);
+    const uint32_t ring_a = smem_addr(ring);
+    const uint32_t full_a = smem_addr(bars), empty_a = full_a + NS * 8;
+    if (tid == 0)
+    {
+        for (int i = 0; i < NS; ++i)
+        {
+            mbar_init(full_a + 8 * i, 1);
+            mbar_init(empty_a + 8 * i, 1);
+        }
+        mbar_init_fence();
+        s_abort = 0;
+    }
     __syncthreads();
 
-    const int n0 = blockIdx.x * p.rows_per_cta;
-    const int n1 = min(p.vocab, n0 + p.rows_per_cta);
+    if (warp == NC)
+    {
+        // ---------------- producer warp ----------------
+        bool ok = true;
+        int j = 0;
+        for (; j < nrows; ++j)
+        {
+            const int w = j % C, k = j / C;
+            const uint32_t stage = (uint32_t)(w + C * (k % SW)), use = (uint32_t)(k / SW);
+            if (use > 0 && !mbar_wait_bounded(empty_a + 8 * stage, (use - 1) & 1, GEMV_WAIT_LIMIT_NS))
+            {
+                ok = false;
+                break;
+            }
+            if (lane == 0)
+            {
+                mbar_arrive_expect_tx(full_a + 8 * stage, row_bytes);
+                bulk_g2s(ring_a + stage * row_bytes, p.w + (size_t)(n0 + j) * p.dim, row_bytes, full_a + 8 * stage);
+            }
+            __syncwarp();
+        }
+        if (!ok)
+        {
+            s_abort = 1;
+            if (lane == 0)
+                p.state->err = 2u;
+        }
+        // every issued copy has landed before the CTA may exit: the last
+        // use of each stage that was issued
+        for (int st = 0; st < NS; ++st)
+        {
+            const int w = st % C, slot = st / C;
+            const int nk = j > w ? (j - w + C - 1) / C : 0; // rows issued to warp w
+            if (nk > slot)
+            {
+                const int kl = slot + ((nk - 1 - slot) / SW) * SW; // last k with k % SW == slot
+                mbar_wait_bounded(full_a + 8 * st, (uint32_t)(kl / SW) & 1, GEMV_WAIT_LIMIT_NS);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    pdl_wait(); // the hidden state comes from the previous kernel
+    float ss = 0.0f;
+    for (int i = tid; i < p.dim; i += NC * 32)
+        ss = fmaf(p.hidden[i], p.hidden[i], ss);
+    ss = group_sum<NC * 32>(ss, misc);
+    const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.dim), p.eps));
+    for (int i = tid; i < p.dim; i += NC * 32)
+        xs[i] = __fmul_rn(__fmul_rn(p.hidden[i], rms), p.gain[i]);
+    named_bar_sync(1, NC * 32);
+
     const int d4 = p.dim >> 2;
-    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    const uint32_t xs_a = smem_addr(xs);
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int n = n0 + warp; n < n1; n += 8)
+    for (int j = warp, k = 0; warp < C && j < nrows; j += C, ++k)
     {
-        const float4* wr = reinterpret_cast<const float4*>(p.w + (size_t)n * p.dim);
+        const uint32_t stage = (uint32_t)(warp + C * (k % SW));
+        if (!mbar_wait_bounded(full_a + 8 * stage, (uint32_t)(k / SW) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
+        {
+            s_abort = 1;
+            if (lane == 0)
+                p.state->err = 2u;
+            break;
+        }
+        const uint32_t wr = ring_a + stage * row_bytes;
         float acc = 0.0f;
 #pragma unroll 8
         for (int k = lane; k < d4; k += 32)
         {
-            const float4 wv = ldg_stream_f4(reinterpret_cast<const float*>(wr + k));
-            const float4 xv = x4[k];
-            acc = fmaf(wv.x, xv.x, acc);
-            acc = fmaf(wv.y, xv.y, acc);
-            acc = fmaf(wv.z, xv.z, acc);
-            acc = fmaf(wv.w, xv.w, acc);
+            const uint4 wv = lds128(wr + (uint32_t)k * 16);
+            const uint4 xv = lds128(xs_a + (uint32_t)k * 16);
+            acc = fmaf(__uint_as_float(wv.x), __uint_as_float(xv.x), acc);
+            acc = fmaf(__uint_as_float(wv.y), __uint_as_float(xv.y), acc);
+            acc = fmaf(__uint_as_float(wv.z), __uint_as_float(xv.z), acc);
+            acc = fmaf(__uint_as_float(wv.w), __uint_as_float(xv.w), acc);
         }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(empty_a + 8 * stage);
         acc = warp_sum(acc);
+        const int n = n0 + j;
         if (lane == 0)
             p.logits[n] = acc;
         if (acc > bv)
@@ -131,20 +232,17 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
             bi = n;
         }
     }
-    __shared__ float s_v[8];
-    __shared__ int s_i[8];
-    __shared__ unsigned s_last;
     if (lane == 0)
     {
         s_v[warp] = bv;
         s_i[warp] = bi;
     }
-    __syncthreads();
+    named_bar_sync(1, NC * 32);
     if (tid == 0)
     {
         float v = s_v[0];
         int i = s_i[0];
-        for (int w = 1; w < 8; ++w)
+        for (int w = 1; w < NC; ++w)
             if (s_v[w] > v || (s_v[w] == v && s_i[w] < i))
             {
                 v = s_v[w];
@@ -156,13 +254,13 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
         const unsigned prev = atomicAdd(&p.state->lm_counter, 1u);
         s_last = prev == gridDim.x - 1 ? 1u : 0u;
     }
-    __syncthreads();
+    named_bar_sync(1, NC * 32);
     if (!s_last)
         return;
     __threadfence();
     float v = -INFINITY;
     int i = INT_MAX;
-    for (int b = tid; b < (int)gridDim.x; b += blockDim.x)
+    for (int b = tid; b < (int)gridDim.x; b += NC * 32)
     {
         const float pv = __ldcg(p.part_val + b);
         const int pi = __ldcg(p.part_idx + b);
@@ -188,12 +286,12 @@ __global__ void __launch_bounds__(256) lm_head_argmax_kernel(const LmParams p)
         s_v[warp] = v;
         s_i[warp] = i;
     }
-    __syncthreads();
+    named_bar_sync(1, NC * 32);
     if (tid == 0)
     {
         v = s_v[0];
         i = s_i[0];
-        for (int w = 1; w < 8; ++w)
+        for (int w = 1; w < NC; ++w)
             if (s_v[w] > v || (s_v[w] == v && s_i[w] < i))
             {
                 v = s_v[w];
@@ -245,17 +343,31 @@ bool use_tma()
     return v == 1;
 }
 
-inline bool tiles_ok(size_t N, size_t K) { return N % 16 == 0 && K % 128 == 0; }
+constexpr size_t TILED_SMEM_MAX = 226 * 1024; // under the 227 KB opt-in maximum of one CTA (static smem too)
+
+inline bool tiles_ok(size_t N, size_t K)
+{
+    return N % 16 == 0 && K % 128 == 0 && K > 0 && gemv_tiled_smem_bytes((int)(K / 128)) <= TILED_SMEM_MAX &&
+           gemv_tiled_i8_smem_bytes((int)(K / 128)) <= TILED_SMEM_MAX;
+}
 
 template <int PRO, int EPI>
 int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = false)
 {
     if (tiled)
     {
+        static int i8 = -1;
+        if (i8 < 0)
+        {
+            const char* ev = std::getenv("AAEDN_I8");
+            i8 = ev ? std::atoi(ev) != 0 : 1;
+        }
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
-        cudaError_t e = launch_kernel(gemv_tiled_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
-                                      gemv_tiled_smem_bytes(p.K / 128), st, pdl, p);
+        cudaError_t e = i8 ? launch_kernel(gemv_tiled_i8_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
+                                           gemv_tiled_i8_smem_bytes(p.K / 128), st, pdl, p)
+                           : launch_kernel(gemv_tiled_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
+                                           gemv_tiled_smem_bytes(p.K / 128), st, pdl, p);
         if (e != cudaSuccess)
             return set_error(AAEDN_ECUDA, "launch of gemv_tiled_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
@@ -302,7 +414,9 @@ int set_gemv_attrs()
     AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tma_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         200 * 1024));
     AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024));
+                                        (int)TILED_SMEM_MAX));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_i8_kernel<PRO, EPI>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TILED_SMEM_MAX));
     return AAEDN_OK;
 }
 
@@ -342,7 +456,7 @@ struct aaedn_model
     float* dbg_hidden = nullptr;
     int page_size = 64, n_pages = 0;
     int attn_S = 1, attn_max_tok = 1;
-    int lm_ctas = 1, lm_rows = 8;
+    int lm_ctas = 1, lm_rows = 8, lm_stages = 8, lm_consumers = 8;
     cudaGraphExec_t graph_exec = nullptr;
     uint32_t kernels_per_step = 0;
     uint32_t h_pos = 0;
@@ -584,10 +698,12 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     lp.out_tokens = m->out_tokens;
     lp.max_seq = (int)c.max_seq;
     lp.rows_per_cta = m->lm_rows;
+    lp.stages = m->lm_stages;
+    lp.consumers = m->lm_consumers;
     if (mask & K_LM)
     {
-        cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(256), (size_t)(D + 64) * 4, st, pdl,
-                                      lp);
+        cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(LM_THREADS),
+                                      lm_smem_bytes(D, m->lm_stages), st, pdl, lp);
         if (e != cudaSuccess)
             return set_error(AAEDN_ECUDA, "launch of lm_head_argmax_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
@@ -683,8 +799,9 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
                          "aaedn_model_create: need dim, n_heads*head_dim, ffn_dim multiples of 32, head_dim a "
                          "multiple of 16 (<= %d), n_heads / n_kv_heads in {1, 2, 4, 8}",
                          ATTN_MAX_HD);
-    if (c.dim > 65536 || c.ffn_dim > 32768 || c.max_seq > (1u << 20))
-        return set_error(AAEDN_EINVAL, "aaedn_model_create: dimension too large");
+    // dim <= 16384: the lm_head ring holds x and at least two rows
+    if (c.dim > 16384 || c.ffn_dim > 32768 || c.max_seq > (1u << 20))
+        return set_error(AAEDN_EINVAL, "aaedn_model_create: dimension too large (dim <= 16384, ffn_dim <= 32768)");
     aaedn_model* m = new aaedn_model();
     m->cfg = c;
     {
@@ -695,17 +812,23 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
-    // about one attention CTA per SM (a CTA walks its token range in
-    // 64-token chunks, so any split count covers any context length)
-    int S = std::max(1, sm_count() / (int)c.n_kv_heads);
+    // about two attention CTAs per SM (a CTA walks its token range in
+    // batches, so any split count covers any context length)
+    int S = std::max(1, (2 * sm_count() + (int)c.n_kv_heads - 1) / (int)c.n_kv_heads);
     S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
     S = std::min(S, 64);
     m->attn_S = S;
     m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
-    int rows = (int)((c.vocab + 2 * sm_count() - 1) / (2 * sm_count()));
-    rows = (rows + 7) / 8 * 8;
-    m->lm_rows = std::max(8, rows);
+    // lm_head: one CTA per SM, each streaming one contiguous run of rows
+    m->lm_rows = std::max(1, (int)((c.vocab + sm_count() - 1) / sm_count()));
     m->lm_ctas = (int)((c.vocab + m->lm_rows - 1) / m->lm_rows);
+    {
+        // rows that fit beside x; every consumer warp owns stages/consumers
+        const int fit = (int)std::min<size_t>(LM_MAX_STAGES,
+                                              (200 * 1024 - (size_t)c.dim * 4 - 1024) / ((size_t)c.dim * 4));
+        m->lm_consumers = fit >= LM_CONSUMERS ? LM_CONSUMERS : (fit >= 4 ? 4 : (fit >= 2 ? 2 : 1));
+        m->lm_stages = fit / m->lm_consumers * m->lm_consumers;
+    }
     const size_t bytes = plan_arena(m, false);
     cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&m->arena), bytes);
     if (e != cudaSuccess)
@@ -745,10 +868,9 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
         if (cudaMemcpy(L.attn_norm, ones.data(), c.dim * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemcpy(L.ffn_norm, ones.data(), c.dim * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return fail(set_error(AAEDN_ECUDA, "norm upload failed"));
-    const size_t lm_smem = (size_t)(c.dim + 64) * 4;
-    if (lm_smem > 48 * 1024 &&
-        cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lm_smem) !=
-            cudaSuccess)
+    // one process-wide value that covers every model (lm_smem_bytes <= 200 KB)
+    if (cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+        cudaSuccess)
         return fail(set_error(AAEDN_ECUDA, "lm_head smem attribute failed"));
     rc = attn_set_attrs<1>();
     if (rc)
