@@ -48,6 +48,7 @@ int aaedn_dev_alloc(void** d_ptr, size_t bytes);
 int aaedn_dev_free(void* d_ptr);
 int aaedn_memcpy_h2d(void* d_dst, const void* h_src, size_t bytes, void* stream);
 int aaedn_memcpy_d2h(void* h_dst, const void* d_src, size_t bytes, void* stream);
+int aaedn_memcpy_d2d(void* d_dst, const void* d_src, size_t bytes, void* stream);
 int aaedn_stream_sync(void* stream);
 int aaedn_device_sync(void);
 
@@ -68,6 +69,27 @@ int aaedn_synth_tokens(uint64_t seed, uint64_t stream_id, uint32_t vocab, uint32
  * 10000/2^(i/half), fp32 as the reference); formula 1: pos*theta^(-2i/hd)
  * in fp64 rounded to fp32 (the model path). */
 int aaedn_rope_table(float* h_cos, float* h_sin, size_t max_seq, size_t head_dim, double theta, int formula);
+
+/* ---- .abn model files (tools/convert_model.py:138, src/quant.cpp:31-119) -- */
+/* The 64-byte little-endian header "<8sIQI6IB15s": magic "AAEDNMDL",
+ * version, payload_size, payload_checksum (FNV-1a 32 of the payload),
+ * n_layers, n_heads, head_dim, vocab_size, hidden_dim, ffn_dim, quant_type. */
+typedef struct {
+    uint32_t version;
+    uint64_t payload_size;
+    uint32_t payload_checksum;
+    uint32_t n_layers, n_heads, head_dim, vocab_size, hidden_dim, ffn_dim;
+    uint8_t quant_type;
+} aaedn_abn_header;
+/* Reads and checks the header as quant_load does (src/quant.cpp:50-72):
+ * magic, version 2 and payload_size == hidden^2/2 + hidden^2/16.
+ * AAEDN_EFORMAT when the file is short or rejected. */
+int aaedn_abn_read_header(const char* path, aaedn_abn_header* h_out);
+/* Reads the payload after a header accepted by aaedn_abn_read_header into
+ * h_data (hidden^2/2 bytes) and h_scales (hidden^2/32 u16) and checks the
+ * FNV-1a checksum (src/quant.cpp:87-111). AAEDN_EFORMAT on a short file or a
+ * checksum mismatch. */
+int aaedn_abn_read_payload(const char* path, const aaedn_abn_header* h_hdr, uint8_t* h_data, uint16_t* h_scales);
 
 /* ---- kernels (device pointers) ------------------------------------------ */
 /* include/dequant.hpp:10 dequant_4bit (src/dequant.cpp:7-28): out[i] =
@@ -104,6 +126,20 @@ int aaedn_cu_rope_apply(float* d_q, float* d_k, size_t seq_len, size_t head_dim,
 int aaedn_cu_attention(const float* d_q, const float* d_k, const float* d_v, const uint32_t* h_segments,
                        size_t num_segments, float* d_out, size_t n_heads, size_t head_dim, float scale,
                        void* stream);
+
+/* include/ffn.hpp:12 ffn_swiglu (src/ffn.cpp:18-77): out[b] = W_down *
+ * act(W_gate * in[b], W_up * in[b]) for batch rows of hidden floats; weights
+ * [out][in] row-major 4-bit codes (gate/up: ffn x hidden, down: hidden x
+ * ffn). AAEDN_FFN_MODEL: fp16 scale per (row, 32 inputs), act = silu(g)*u
+ * (the model path). AAEDN_FFN_REFERENCE: what src/ffn.cpp:41-72 computes
+ * (scale of output row j = scales[j/32] as an integer, act = g*silu(g)*u).
+ * Null weights or scales give zero output (src/ffn.cpp:22-27). */
+#define AAEDN_FFN_MODEL 0
+#define AAEDN_FFN_REFERENCE 1
+int aaedn_cu_ffn_swiglu(const float* d_in, float* d_out, size_t batch, size_t hidden, size_t ffn,
+                        const uint8_t* d_gate, const uint8_t* d_up, const uint8_t* d_down,
+                        const uint16_t* d_gate_scales, const uint16_t* d_up_scales, const uint16_t* d_down_scales,
+                        int semantics, void* stream);
 
 /* No counterpart in the reference. The same attention as
  * aaedn_cu_attention for callers that cannot let a library allocate device
@@ -189,6 +225,13 @@ int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t cap, uint32_t
  * attention, o, gate/up, down, lm_head. Leaves the KV cache and hidden state
  * undefined (rewind or reset afterwards). */
 int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32_t cap);
+/* Tracing of the persistent step kernel (when the model runs it): one step
+ * with cycle counters; h_cta [n_ctas][8]: consumer waits for weights,
+ * grid-barrier waits, producer waits for free stages, total, attention,
+ * activation builds, lm_head (SM cycles); h_phase [5 * n_layers + 1][2]: CTA
+ * 0's clock when it reached / left each grid barrier. The position is left
+ * where it was. */
+int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase, size_t cap_phase);
 /* Kernels launched by one decode step. */
 uint32_t aaedn_model_kernels_per_step(const aaedn_model* m);
 /* Copy the last step's logits ([vocab]) / the greedy tokens generated so far. */

@@ -42,6 +42,12 @@ class ModelConfig(ctypes.Structure):
         return d
 
 
+class AbnHeader(ctypes.Structure):
+    _fields_ = [("version", _u32), ("payload_size", _u64), ("payload_checksum", _u32), ("n_layers", _u32),
+                ("n_heads", _u32), ("head_dim", _u32), ("vocab_size", _u32), ("hidden_dim", _u32),
+                ("ffn_dim", _u32), ("quant_type", ctypes.c_uint8)]
+
+
 class LayerHost(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd",
                                    "sq", "sk", "sv", "so", "sg", "su", "sd", "attn_norm", "ffn_norm")]
@@ -80,6 +86,10 @@ def lib():
         "aaedn_cu_rope_apply": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _int),
         "aaedn_cu_attention": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
         "aaedn_cu_attention_noalloc": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
+        "aaedn_cu_ffn_swiglu": ([_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp], _int),
+        "aaedn_memcpy_d2d": ([_vp, _vp, _sz, _vp], _int),
+        "aaedn_abn_read_header": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader)], _int),
+        "aaedn_abn_read_payload": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader), _vp, _vp], _int),
         "aaedn_model_create": ([ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], _int),
         "aaedn_model_destroy": ([_vp], _int),
         "aaedn_model_config_get": ([_vp, ctypes.POINTER(ModelConfig)], _int),
@@ -100,6 +110,7 @@ def lib():
         "aaedn_model_rewind": ([_vp, _u32], _int),
         "aaedn_model_profile_parts": ([_vp, _u32, _vp, _u32], _int),
         "aaedn_model_profile_step": ([_vp, _vp, _u32, ctypes.POINTER(_u32)], _int),
+        "aaedn_model_trace_step": ([_vp, _vp, _sz, _vp, _sz], _int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -202,6 +213,29 @@ def attention(d_q, d_k, d_v, segments, d_out, n_heads, head_dim, scale, stream=N
     segs = np.ascontiguousarray(segments, np.uint32).reshape(-1)
     check(lib().aaedn_cu_attention(_p(d_q), _p(d_k), _p(d_v), _p(segs), segs.size // 2, _p(d_out), n_heads,
                                    head_dim, scale, stream))
+
+
+FFN_MODEL, FFN_REFERENCE = 0, 1
+
+
+def ffn_swiglu(d_in, d_out, batch, hidden, ffn, d_gate, d_up, d_down, d_gs, d_us, d_ds, semantics=FFN_MODEL,
+               stream=None):
+    """include/ffn.hpp ffn_swiglu on device buffers (FFN_MODEL: fp16 block
+    scales, silu(g)*u; FFN_REFERENCE: what src/ffn.cpp computes)."""
+    check(lib().aaedn_cu_ffn_swiglu(_p(d_in), _p(d_out), batch, hidden, ffn, _p(d_gate), _p(d_up), _p(d_down),
+                                    _p(d_gs), _p(d_us), _p(d_ds), semantics, stream))
+
+
+def abn_read(path):
+    """Header and payload of an .abn v2 file (quant_load's checks); raises
+    AaednError(EFORMAT) when the file is rejected."""
+    h = AbnHeader()
+    check(lib().aaedn_abn_read_header(str(path).encode(), ctypes.byref(h)))
+    n = h.hidden_dim
+    data = np.empty(n * n // 2, np.uint8)
+    scales = np.empty(n * n // 32, np.uint16)
+    check(lib().aaedn_abn_read_payload(str(path).encode(), ctypes.byref(h), _p(data), _p(scales)))
+    return h, data, scales
 
 
 def attention_noalloc(d_q, d_k, d_v, segments, d_out, n_heads, head_dim, scale, stream=None):
@@ -368,6 +402,17 @@ class Model:
         out = np.empty(8, np.float32)
         check(lib().aaedn_model_profile_parts(self.h, reps, _p(out), 8))
         return dict(zip(self.PART_NAMES, out.tolist()))
+
+    def trace_step(self, n_ctas=None):
+        """Cycle counters of one step of the persistent kernel: per-CTA
+        [wait weights, wait barriers, producer wait, total, attention, build,
+        lm_head] and CTA 0's barrier arrival / exit clocks."""
+        import os
+        n_ctas = n_ctas or 256
+        cta = np.zeros(n_ctas * 8, np.uint64)
+        ph = np.zeros((self.cfg["n_layers"] * 5 + 1) * 2, np.int64)
+        check(lib().aaedn_model_trace_step(self.h, _p(cta), cta.size, _p(ph), ph.size))
+        return cta.reshape(-1, 8), ph.reshape(-1, 2)
 
     def forward_debug(self, token):
         hidden = np.empty((self.cfg["n_layers"], self.cfg["dim"]), np.float32)

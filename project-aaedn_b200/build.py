@@ -23,15 +23,15 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 INCS = ["-I" + os.path.join(ROOT, "include"), "-I" + HOST, "-I" + os.path.join(HOST, "include")]
 
-CU_SRCS = ["api.cu", "model.cu"]
-CPP_SRCS = ["errors.cpp", "quant_tools.cpp", "aaedn_api.cpp"]
+CU_SRCS = ["api.cu", "model.cu", "ffn.cu"]
+CPP_SRCS = ["errors.cpp", "quant_tools.cpp", "abn_file.cpp", "aaedn_api.cpp"]
 
 
 def _deps(src):
     if src.endswith(".cu"):
         return [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [os.path.join(ROOT, "include", "aaedn_b200.h"),
                                                                       os.path.join(HOST, "host_common.hpp")]
-    inc = os.path.join(HOST, "include")
+    inc = os.path.join(HOST, "include", "aaedn")
     hdrs = [os.path.join(inc, f) for f in os.listdir(inc)] if os.path.isdir(inc) else []
     return [os.path.join(ROOT, "include", "aaedn_b200.h"), os.path.join(HOST, "host_common.hpp")] + hdrs
 

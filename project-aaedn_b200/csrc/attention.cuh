@@ -36,7 +36,8 @@ struct AttnParams
     const float* k; // MODE 0: [token][n_heads][hd]; MODE 1: [page][n_kv][P][hd]
     const float* v;
     float* out;         // [n_heads][hd]
-    float* part;        // [n_heads][S][hd + 2]
+    float* part;        // [n_heads][S][pstride]: hd sums, max, sum
+    int pstride;        // floats per partial result (0: hd + 2)
     unsigned* counters; // [n_kv], zero between launches
     int n_heads, n_kv, head_dim, S;
     float scale;
@@ -46,6 +47,7 @@ struct AttnParams
     int max_tok;              // unused (kept for the launch interface)
     const int* page_table;
     int page_size;
+    int no_combine; // leave the S partial results for the consumer to merge
     int nseg;
     uint32_t seg_start[ATTN_MAX_SEG];
     uint32_t seg_off[ATTN_MAX_SEG + 1]; // prefix sums of the lengths
@@ -53,7 +55,7 @@ struct AttnParams
 
 // Shared memory: per-warp running max and sum [8][G] each, per-warp V sums
 // [8][G][hd].
-inline size_t attn_smem_bytes(int G, int hd, int /*max_tok*/)
+__host__ __device__ inline size_t attn_smem_bytes(int G, int hd, int /*max_tok*/)
 {
     return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd) * 4;
 }
@@ -83,70 +85,45 @@ __device__ __forceinline__ size_t attn_row(const AttnParams& p, int t, int kvh)
 // query heads.
 constexpr int attn_min_blocks(int G, int HDM) { return (G == 1 && HDM == 128) ? 4 : (G * HDM >= 2048 ? 1 : 2); }
 
-template <int MODE, int G, int HDM>
-__global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_split_kernel(const AttnParams p)
+// Token range [t0, t1) of split `split` of S over L tokens.
+__device__ __forceinline__ void attn_range(int L, int split, int S, int& t0, int& t1)
 {
-    extern __shared__ __align__(16) float asmem[];
+    t0 = (int)(((long long)L * split) / S);
+    t1 = (int)(((long long)L * (split + 1)) / S);
+}
+
+template <int MODE>
+__device__ __forceinline__ int attn_len(const AttnParams& p)
+{
+    int L = (MODE == 1) ? (int)p.state->pos + 1 : p.len_static;
+    return L > p.max_len ? p.max_len : L;
+}
+
+// One work item, (kv head, split), on a group of ATTN_THREADS threads (tid =
+// 0..255 within the group) that synchronise on named barrier bar_id: the
+// split's partial result, and the merge of all S splits by the group that
+// finishes a kv head last. asmem: attn_smem_bytes; s_last: one word of
+// shared memory.
+template <int MODE, int G, int HDM>
+__device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int split, int tid, float* asmem,
+                                          unsigned* s_last, int bar_id)
+{
     constexpr int NCH = HDM / 128;                         // float4 slices per lane
     constexpr int TB = (G == 1 && HDM == 128) ? 4 : 2;     // tokens per warp batch
-    pdl_launch_dependents();
-    const int kvh = blockIdx.x, split = blockIdx.y, S = p.S;
+    const int S = p.S;
     const int hd = p.head_dim, hd4 = hd >> 2;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // The position only changes at the end of a decode step (lm_head), so it
-    // can be read before waiting for the previous kernel.
-    int L = (MODE == 1) ? (int)p.state->pos + 1 : p.len_static;
-    if (L > p.max_len)
-        L = p.max_len;
-    const int t0 = (int)(((long long)L * split) / S);
-    const int t1 = (int)(((long long)L * (split + 1)) / S);
-    if constexpr (MODE == 1)
-    {
-        // rows of earlier positions: into L2 while the previous kernel runs
-        // (a prefetch never returns stale data)
-        const int pf1 = min(t1, min(L - 1, t0 + ATTN_PREFETCH_TOKENS));
-        const int lines = (hd * 4 + 127) >> 7;
-        for (int i = tid; i < (pf1 - t0) * lines * 2; i += ATTN_THREADS)
-        {
-            const int r = i / (lines * 2), rem = i - r * lines * 2, kv = rem / lines, ln = rem - kv * lines;
-            const size_t ro = attn_row<MODE>(p, t0 + r, kvh);
-            const float* src = (kv ? p.v : p.k) + ro + ln * 32;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
-        }
-    }
+    const int lane = tid & 31, warp = tid >> 5;
+    const int L = attn_len<MODE>(p);
+    const int ps = p.pstride ? p.pstride : hd + 2;
+    int t0, t1;
+    attn_range(L, split, S, t0, t1);
     float* wm = asmem;                   // [8][G] running max per warp
     float* wl = wm + ATTN_WARPS * G;     // [8][G] running sum per warp
     float* wacc = wl + ATTN_WARPS * G;   // [8][G][hd]
-    pdl_wait();
 
-    // lane slices of q (scaled once: s = (q*scale).k would round differently,
-    // so the scale is applied to the dot as src/attention.cpp:42 does)
-    float4 qv[G][NCH];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-        for (int c = 0; c < NCH; ++c)
-        {
-            const int ch = lane + 32 * c;
-            qv[gi][c] = ch < hd4 ? reinterpret_cast<const float4*>(p.q + ((size_t)kvh * G + gi) * hd)[ch]
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    float m[G], l[G];
-    float4 acc[G][NCH];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi)
-    {
-        m[gi] = -INFINITY;
-        l[gi] = 0.0f;
-#pragma unroll
-        for (int c = 0; c < NCH; ++c)
-            acc[gi][c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-
-    for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
-    {
-        // batch: tokens tb0 + 8j, j < TB
-        float4 kr[TB][NCH], vr[TB][NCH];
+    // batch loader: tokens tb0 + 8j, j < TB, K and V slices of this lane
+    float4 kr[TB][NCH], vr[TB][NCH];
+    auto load_batch = [&](int tb0) {
 #pragma unroll
         for (int j = 0; j < TB; ++j)
         {
@@ -169,6 +146,40 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
                 }
             }
         }
+    };
+    // the first batch's rows are requested before q: their latencies overlap
+    if (t0 + warp < t1)
+        load_batch(t0 + warp);
+    // lane slices of q (scaled once: s = (q*scale).k would round differently,
+    // so the scale is applied to the dot as src/attention.cpp:42 does)
+    float4 qv[G][NCH];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+        {
+            const int ch = lane + 32 * c;
+            // L2 load: q is rewritten every layer (by other CTAs in the
+            // persistent step kernel)
+            qv[gi][c] = ch < hd4 ? __ldcg(reinterpret_cast<const float4*>(p.q + ((size_t)kvh * G + gi) * hd) + ch)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    float m[G], l[G];
+    float4 acc[G][NCH];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+    {
+        m[gi] = -INFINITY;
+        l[gi] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+            acc[gi][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+
+    for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
+    {
+        if (tb0 != t0 + warp)
+            load_batch(tb0);
 #pragma unroll
         for (int gi = 0; gi < G; ++gi)
         {
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
                 reinterpret_cast<float4*>(wacc + ((size_t)warp * G + gi) * hd)[ch] = acc[gi][c];
         }
     }
-    __syncthreads();
+    named_bar_sync(bar_id, ATTN_THREADS);
     for (int i = tid; i < G * hd; i += ATTN_THREADS)
     {
         const int gi = i / hd, d = i - gi * hd;
@@ -263,7 +274,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
             den = fmaf(wl[w * G + gi], f, den);
         }
         const int h = kvh * G + gi;
-        float* pp = p.part + ((size_t)h * S + split) * (hd + 2);
+        float* pp = p.part + ((size_t)h * S + split) * ps;
         pp[d] = o;
         if (d == 0)
         {
@@ -272,39 +283,71 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
         }
     }
 
+    if (p.no_combine)
+        return;
     // last CTA of this kv head merges the S splits in order
     __threadfence();
-    __syncthreads();
-    __shared__ unsigned s_last;
+    named_bar_sync(bar_id, ATTN_THREADS);
     if (tid == 0)
     {
         const unsigned prev = atomicAdd(&p.counters[kvh], 1u);
-        s_last = (prev == (unsigned)S - 1) ? 1u : 0u;
+        *s_last = (prev == (unsigned)S - 1) ? 1u : 0u;
     }
-    __syncthreads();
-    if (!s_last)
+    named_bar_sync(bar_id, ATTN_THREADS);
+    if (!*s_last)
         return;
     __threadfence();
     for (int i = tid; i < G * hd; i += ATTN_THREADS)
     {
         const int gi = i / hd, d = i - gi * hd;
         const int h = kvh * G + gi;
-        const float* pb = p.part + (size_t)h * S * (hd + 2);
+        const float* pb = p.part + (size_t)h * S * ps;
         float M = -INFINITY;
         for (int s2 = 0; s2 < S; ++s2)
-            M = fmaxf(M, __ldcg(pb + (size_t)s2 * (hd + 2) + hd));
+            M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
         float num = 0.0f, den = 0.0f;
         for (int s2 = 0; s2 < S; ++s2)
         {
-            const float ms = __ldcg(pb + (size_t)s2 * (hd + 2) + hd);
+            const float ms = __ldcg(pb + (size_t)s2 * ps + hd);
             const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            num = fmaf(__ldcg(pb + (size_t)s2 * (hd + 2) + d), w, num);
-            den = fmaf(__ldcg(pb + (size_t)s2 * (hd + 2) + hd + 1), w, den);
+            num = fmaf(__ldcg(pb + (size_t)s2 * ps + d), w, num);
+            den = fmaf(__ldcg(pb + (size_t)s2 * ps + hd + 1), w, den);
         }
         p.out[(size_t)h * hd + d] = den > 0.0f ? num / den : 0.0f;
     }
     if (tid == 0)
         p.counters[kvh] = 0u;
+}
+
+
+template <int MODE, int G, int HDM>
+__global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_split_kernel(const AttnParams p)
+{
+    extern __shared__ __align__(16) float asmem[];
+    __shared__ unsigned s_last;
+    pdl_launch_dependents();
+    const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
+    if constexpr (MODE == 1)
+    {
+        // The position only changes at the end of a decode step (lm_head), so
+        // it can be read before waiting for the previous kernel; rows of
+        // earlier positions go into L2 while that kernel runs (a prefetch
+        // never returns stale data).
+        const int L = attn_len<MODE>(p), hd = p.head_dim;
+        int t0, t1;
+        attn_range(L, split, p.S, t0, t1);
+        const int pf1 = min(t1, min(L - 1, t0 + ATTN_PREFETCH_TOKENS));
+        const int lines = (hd * 4 + 127) >> 7;
+        for (int i = tid; i < (pf1 - t0) * lines * 2; i += ATTN_THREADS)
+        {
+            const int r = i / (lines * 2), rem = i - r * lines * 2, kv = rem / lines, ln = rem - kv * lines;
+            const size_t ro = attn_row<MODE>(p, t0 + r, kvh);
+            const float* src = (kv ? p.v : p.k) + ro + ln * 32;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+        }
+    }
+    pdl_wait();
+    attn_item<MODE, G, HDM>(p, kvh, split, tid, asmem, &s_last, 0);
 }
 
 } // namespace aaedn_dev

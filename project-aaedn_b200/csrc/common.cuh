@@ -278,10 +278,44 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                  : "memory");
 }
 
+// L2 policy for data read once per step (the weight stream): evicted first,
+// so it does not push the small hot data (activations, norms, recent KV
+// rows) out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// bulk_g2s with an L2 cache policy
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar,
+                                              uint64_t policy)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+                 "[%3], %4;" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(mbar), "l"(policy)
+                 : "memory");
+}
+
 // named barrier over `count` threads (warps 0..count/32-1)
 __device__ __forceinline__ void named_bar_sync(int id, int count)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// named barrier that also ORs a predicate over the `count` threads: every
+// thread gets the same answer (failure decisions taken together, so no thread
+// leaves a loop whose barrier the others still wait at)
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred)
+{
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r)
+                 : "r"((uint32_t)pred), "r"(id), "r"(count)
+                 : "memory");
+    return r != 0;
 }
 
 // ---- programmatic dependent launch ----------------------------------------

@@ -33,6 +33,9 @@ enum
     PRO_PLAIN = 0,
     PRO_RMSNORM = 1,
     PRO_EMBED_RMSNORM = 2,
+    // x = the attention output, merged here from the per-split partial
+    // results (max, sum, unnormalised sum of V rows) of every head
+    PRO_ATTN_COMBINE = 3,
 };
 
 enum
@@ -88,6 +91,11 @@ struct GemvParams
     const float* rope_sin;
     // SwiGLU epilogue
     float* act;
+    // PRO_ATTN_COMBINE: partials [n_heads][attn_S][attn_pstride] (head_dim
+    // sums, max, sum; attn_pstride a multiple of 4)
+    const float* attn_part;
+    int attn_S, attn_pstride;
+    int l2_hint; // stream the weights with the L2 evict-first policy
     // scales can be staged as aligned u32 pairs (even scales per row, 4-byte
     // aligned array)
     bool scale_pairs;
@@ -272,8 +280,22 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
 // sums of each row in fixed order, then stores / accumulates / adds the
 // residual, or pairs rows (8j + r, 8j + r + 8) for SwiGLU and for RoPE +
 // the KV-cache append.
+// Epilogue inputs staged in shared memory before a CTA's first group (so
+// the warp that runs an epilogue does not wait on global loads while the
+// other warps need it to release ring stages): the residual rows of the
+// CTA's groups (resid[gl * 16 + r], gl = the CTA's group number), or the RoPE
+// row of the position (cos[half], sin[half]) and the cache page.
+struct EpiCache
+{
+    const float* resid;
+    const float* cos;
+    const float* sin;
+    int page;
+};
+
 template <int NM, int EPI, int S = GEMV_WARPS>
-__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* rb, int group, int lane)
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* rb, int group, int lane,
+                                              float post = 1.0f, const EpiCache* ec = nullptr, int gl = 0)
 {
     if constexpr (EPI == EPI_STORE || EPI == EPI_ACCUM || EPI == EPI_RESIDUAL)
     {
@@ -286,11 +308,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
             float v = 0.0f;
             for (int ss = 0; ss < S; ++ss)
                 v += rb[(m * S + ss) * 16 + rr];
+            v *= post; // the RMSNorm factor of the warp-built operand (1: exact no-op)
             float* yp = p.y + (size_t)m * p.ldc + row;
             if constexpr (EPI == EPI_STORE)
                 *yp = v;
-            else
-                *yp = v + *yp; // residual / K-chunk accumulation (src/transformer.cpp:214)
+            else // residual / K-chunk accumulation (src/transformer.cpp:214)
+                *yp = v + (ec ? ec->resid[gl * 16 + rr] : __ldcg(yp));
         }
     }
     else
@@ -305,6 +328,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
             v0 += rb[ss * 16 + jj];
             v1 += rb[ss * 16 + jj + 8];
         }
+        v0 *= post;
+        v1 *= post;
         if constexpr (EPI == EPI_SWIGLU)
         {
             // rows 8j..8j+7 of the gate and of up share one group (D6)
@@ -320,15 +345,15 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
                     p.state->err = 1u;
                 return;
             }
-            const int page = p.page_table[pos / p.page_size];
+            const int page = ec ? ec->page : p.page_table[pos / p.page_size];
             const int slot = pos % p.page_size;
             if (rbase < p.q_rows + p.kv_rows)
             {
                 const bool isq = rbase < p.q_rows;
                 const int rel = isq ? rbase : rbase - p.q_rows;
                 const int h = rel / hd, i = ((rel % hd) >> 4) * 8 + jj;
-                const float c = p.rope_cos[(size_t)pos * half + i];
-                const float sn = p.rope_sin[(size_t)pos * half + i];
+                const float c = ec ? ec->cos[i] : p.rope_cos[(size_t)pos * half + i];
+                const float sn = ec ? ec->sin[i] : p.rope_sin[(size_t)pos * half + i];
                 // rotate-half (src/rope.cpp:53-54) at the absolute position (D3)
                 const float o0 = __fsub_rn(__fmul_rn(c, v0), __fmul_rn(sn, v1));
                 const float o1 = __fadd_rn(__fmul_rn(sn, v0), __fmul_rn(c, v1));

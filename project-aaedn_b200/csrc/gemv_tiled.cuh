@@ -31,6 +31,13 @@ constexpr int GT_STAGES = 4;
 constexpr int GT_CHUNK_TILES = 32; // two tiles per consumer warp
 constexpr int GT_TILE_BYTES = 1024 + 128; // codes + scales of one tile (16 rows x 128 codes)
 constexpr int GT_STAGE_BYTES = GT_CHUNK_TILES * GT_TILE_BYTES; // 36 KB
+// Group reductions in flight (integer engine): RB buffers of [16 warps][16
+// rows] partial sums, each with an arrival counter; the warp that completes a
+// group runs its epilogue, the others go on (no CTA-wide barrier per group).
+constexpr int GT_RB = 8;
+constexpr int GT_RED_BYTES = GT_RB * GT_CONSUMERS * 16 * 4 + GT_RB * 4 + 96;
+// Shared memory for the staged epilogue inputs (EpiCache): 2048 floats.
+constexpr int GT_ECACHE_FLOATS = 2048;
 
 // Bytes of a repacked matrix (same as the row-major codes + scales).
 inline size_t tiled_bytes(size_t N, size_t K) { return N * K / 2 + N * K / 32 * 2; }
@@ -266,194 +273,274 @@ __device__ __forceinline__ void digits4(float v, int (&d)[4])
 // and digit parity j: words (digit j even-code elements, digit j odd, digit
 // 2+j even, digit 2+j odd)) and the zero tile after them; misc[0] receives
 // the output factor max|x| / (127 * 128). NTH threads (named barrier 1).
+//
+// One pass over x: item it = tid + NTH * k is 8 consecutive elements (one
+// code word of one block); a thread parks its items' raw values in the very
+// 32 bytes of frag their digits will occupy, so between the reduction (sum
+// of squares, max) and the digits the activation stays on chip, it crosses
+// L2 once and the CTA synchronises twice.
 template <int PRO, int NTH>
 __device__ __forceinline__ void gemv_build_i8(const GemvParams& p, uint4* frag, float* misc, int ntile)
 {
-    const int tid = threadIdx.x;
+    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* src = p.x;
     if constexpr (PRO == PRO_EMBED_RMSNORM)
     {
         const uint32_t pos = p.state->pos;
         const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
         src = p.embedding + (size_t)tok * p.K;
-        if (blockIdx.x == 0)
-            for (int i = tid; i < p.K; i += NTH)
-                p.hidden_out[i] = src[i];
     }
-    // pass 1: sum of squares (RMSNorm) and the largest |v * gain|
+    const int items = ntile * 16;
     float ss = 0.0f, mx = 0.0f;
     bool finite = true;
-    {
-        const float4* s4 = reinterpret_cast<const float4*>(src);
-        const float4* g4 = reinterpret_cast<const float4*>(p.gain);
-        for (int i = tid; i < (p.K >> 2); i += NTH)
-        {
-            const float4 v = s4[i];
-            float4 a = v;
-            if constexpr (PRO != PRO_PLAIN)
-            {
-                ss = fmaf(v.x, v.x, ss);
-                ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss);
-                ss = fmaf(v.w, v.w, ss);
-                const float4 g = g4[i];
-                a = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-            }
-            const float m4 = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
-            finite = finite && (m4 <= 3.0e38f) && (a.x == a.x) && (a.y == a.y) && (a.z == a.z) && (a.w == a.w);
-            mx = fmaxf(mx, m4);
-        }
-    }
-    float rms = 1.0f;
-    if constexpr (PRO != PRO_PLAIN)
-    {
-        ss = group_sum<NTH>(ss, misc);
-        rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.eps)); // src/rmsnorm.cpp:34
-    }
-    // block-wide max; a non-finite activation makes every output NaN
-    mx = finite ? mx : __int_as_float(0x7f800000);
-    mx = warp_max(mx);
-    named_bar_sync(1, NTH);
-    if ((tid & 31) == 0)
-        misc[8 + (tid >> 5)] = mx;
-    named_bar_sync(1, NTH);
-    mx = 0.0f;
-    for (int i = 0; i < NTH / 32; ++i)
-        mx = fmaxf(mx, misc[8 + i]);
-    mx *= rms;
-    const bool bad = !(mx <= 3.0e38f);
-    const float inv = (mx > 0.0f && !bad) ? 127.0f / mx : 0.0f;
-    // pass 2: the digits, 8 elements (one code word of one block) per item
-    const int items = ntile * 16;
     for (int it = tid; it < items; it += NTH)
     {
         const int tile = it >> 4, tb = (it >> 2) & 3, s = it & 3;
         const int k0 = tile * 128 + tb * 32 + s * 8;
-        const float4 a = *reinterpret_cast<const float4*>(src + k0);
-        const float4 b = *reinterpret_cast<const float4*>(src + k0 + 4);
-        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        if constexpr (PRO != PRO_PLAIN)
+        float4 a, b;
+        if constexpr (PRO == PRO_ATTN_COMBINE)
         {
-            const float4 ga = *reinterpret_cast<const float4*>(p.gain + k0);
-            const float4 gb = *reinterpret_cast<const float4*>(p.gain + k0 + 4);
+            // elements k0..k0+7 of head h: the merge of its S split results,
+            // in split order, as the attention kernel's own merge does; all
+            // loads of up to SU splits are issued at once
+            constexpr int SU = 16;
+            const int hd = p.head_dim, h = k0 / hd, d0 = k0 - h * hd, S = p.attn_S, ps = p.attn_pstride;
+            const float* pb = p.attn_part + (size_t)h * S * ps;
+            float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, den = 0.0f;
+            if (S <= SU)
+            {
+                float ms[SU], ls[SU];
+#pragma unroll
+                for (int s2 = 0; s2 < SU; ++s2)
+                {
+                    const float2 ml = s2 < S ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)s2 * ps + hd))
+                                             : make_float2(-INFINITY, 0.0f);
+                    ms[s2] = ml.x;
+                    ls[s2] = ml.y;
+                }
+                float M = -INFINITY;
+#pragma unroll
+                for (int s2 = 0; s2 < SU; ++s2)
+                    M = fmaxf(M, ms[s2]);
+#pragma unroll
+                for (int s2 = 0; s2 < SU; ++s2)
+                    if (s2 < S)
+                    {
+                        const float* pv = pb + (size_t)s2 * ps + d0;
+                        const float4 va = __ldcg(reinterpret_cast<const float4*>(pv));
+                        const float4 vb = __ldcg(reinterpret_cast<const float4*>(pv + 4));
+                        const float w = (ms[s2] == -INFINITY) ? 0.0f : expf(ms[s2] - M);
+                        num[0] = fmaf(va.x, w, num[0]);
+                        num[1] = fmaf(va.y, w, num[1]);
+                        num[2] = fmaf(va.z, w, num[2]);
+                        num[3] = fmaf(va.w, w, num[3]);
+                        num[4] = fmaf(vb.x, w, num[4]);
+                        num[5] = fmaf(vb.y, w, num[5]);
+                        num[6] = fmaf(vb.z, w, num[6]);
+                        num[7] = fmaf(vb.w, w, num[7]);
+                        den = fmaf(ls[s2], w, den);
+                    }
+            }
+            else
+            {
+                float M = -INFINITY;
+                for (int s2 = 0; s2 < S; ++s2)
+                    M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
+                for (int s2 = 0; s2 < S; ++s2)
+                {
+                    const float* pv = pb + (size_t)s2 * ps;
+                    const float ms = __ldcg(pv + hd);
+                    const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        num[c] = fmaf(__ldcg(pv + d0 + c), w, num[c]);
+                    den = fmaf(__ldcg(pv + hd + 1), w, den);
+                }
+            }
+            float o[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                o[c] = den > 0.0f ? num[c] / den : 0.0f;
+            a = make_float4(o[0], o[1], o[2], o[3]);
+            b = make_float4(o[4], o[5], o[6], o[7]);
+        }
+        else
+        {
+            // L2 loads: in the persistent step kernel x was written by other
+            // CTAs after this SM may have cached an older copy in L1
+            a = __ldcg(reinterpret_cast<const float4*>(src + k0));
+            b = __ldcg(reinterpret_cast<const float4*>(src + k0 + 4));
+        }
+        if constexpr (PRO == PRO_EMBED_RMSNORM)
+            if (blockIdx.x == 0)
+            {
+                *reinterpret_cast<float4*>(p.hidden_out + k0) = a;
+                *reinterpret_cast<float4*>(p.hidden_out + k0 + 4) = b;
+            }
+        float4* park = reinterpret_cast<float4*>(frag + ((size_t)tile * 4 + s) * 8 + 2 * tb);
+        park[0] = a;
+        park[1] = b;
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+        if constexpr (NORM)
+        {
+            const float4 ga = __ldg(reinterpret_cast<const float4*>(p.gain + k0));
+            const float4 gb = __ldg(reinterpret_cast<const float4*>(p.gain + k0 + 4));
+            gv[0] = ga.x, gv[1] = ga.y, gv[2] = ga.z, gv[3] = ga.w;
+            gv[4] = gb.x, gv[5] = gb.y, gv[6] = gb.z, gv[7] = gb.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+        {
+            if constexpr (NORM)
+                ss = fmaf(v[c], v[c], ss);
+            const float a8 = fabsf(v[c] * gv[c]);
+            finite = finite && (a8 <= 3.0e38f);
+            mx = fmaxf(mx, a8);
+        }
+    }
+    // one reduction round for both: warp, then the NTH/32 warp results in
+    // fixed order (deterministic)
+    ss = warp_sum(ss);
+    mx = warp_max(finite ? mx : __int_as_float(0x7f800000));
+    if (lane == 0)
+    {
+        misc[8 + warp] = ss;
+        misc[8 + NTH / 32 + warp] = mx;
+    }
+    named_bar_sync(1, NTH);
+    float tss = 0.0f, tmx = 0.0f;
+    for (int i = 0; i < NTH / 32; ++i)
+    {
+        tss += misc[8 + i];
+        tmx = fmaxf(tmx, misc[8 + NTH / 32 + i]);
+    }
+    float rms = 1.0f;
+    if constexpr (NORM)
+        rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tss, (float)p.K), p.eps)); // src/rmsnorm.cpp:34
+    tmx *= rms;
+    const bool bad = !(tmx <= 3.0e38f);
+    const float inv = (tmx > 0.0f && !bad) ? 127.0f / tmx : 0.0f;
+    for (int it = tid; it < items; it += NTH)
+    {
+        const int tile = it >> 4, tb = (it >> 2) & 3, s = it & 3;
+        const int k0 = tile * 128 + tb * 32 + s * 8;
+        uint4* dst = frag + ((size_t)tile * 4 + s) * 8 + 2 * tb;
+        const float4 a = reinterpret_cast<const float4*>(dst)[0];
+        const float4 b = reinterpret_cast<const float4*>(dst)[1];
+        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        if constexpr (NORM)
+        {
+            const float4 ga = __ldg(reinterpret_cast<const float4*>(p.gain + k0));
+            const float4 gb = __ldg(reinterpret_cast<const float4*>(p.gain + k0 + 4));
             const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 v[c] = __fmul_rn(__fmul_rn(v[c], rms), gv[c]); // src/rmsnorm.cpp:42-43
         }
-        int d[8][4];
+        // words of lane 2*tb (digits 0 and 2) and lane 2*tb+1 (digits 1 and
+        // 3): [even, odd] element bytes, packed as they are made
+        uint32_t w0[4] = {0u, 0u, 0u, 0u}, w1[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
         for (int c = 0; c < 8; ++c)
         {
             // even elements as y, odd ones as y/16 (their codes enter as 16*c)
             const float y = __fmul_rn(v[c], inv) * ((c & 1) ? 0.0625f : 1.0f);
-            digits4(y, d[c]);
+            int d[4];
+            digits4(y, d);
+            const int sh = 8 * (c >> 1), e = c & 1;
+            w0[e] |= (uint32_t)(d[0] & 0xFF) << sh;
+            w0[2 + e] |= (uint32_t)(d[2] & 0xFF) << sh;
+            w1[e] |= (uint32_t)(d[1] & 0xFF) << sh;
+            w1[2 + e] |= (uint32_t)(d[3] & 0xFF) << sh;
         }
-        uint4* dst = frag + ((size_t)tile * 4 + s) * 8 + 2 * tb;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-            dst[j] = make_uint4(pack_s8x4(d[0][j], d[2][j], d[4][j], d[6][j]),
-                                pack_s8x4(d[1][j], d[3][j], d[5][j], d[7][j]),
-                                pack_s8x4(d[0][2 + j], d[2][2 + j], d[4][2 + j], d[6][2 + j]),
-                                pack_s8x4(d[1][2 + j], d[3][2 + j], d[5][2 + j], d[7][2 + j]));
+        dst[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+        dst[1] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
     }
     if (tid < 32)
         frag[(size_t)ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
     if (tid == 0)
-        misc[0] = bad ? __int_as_float(0x7fc00000) : mx / (127.0f * 128.0f);
+        misc[0] = bad ? __int_as_float(0x7fc00000) : tmx / (127.0f * 128.0f);
     named_bar_sync(1, NTH);
 }
 
 inline size_t gemv_tiled_i8_smem_bytes(int ntile)
 {
-    return (size_t)GT_STAGES * GT_STAGE_BYTES + (size_t)GT_STAGES * 16 + (size_t)(ntile + 1) * 512 +
-           (size_t)2 * GT_CONSUMERS * 16 * 4 + 64 * 4;
+    return (size_t)GT_STAGES * GT_STAGE_BYTES + (size_t)GT_STAGES * 16 + (size_t)ntile * (512 + 16) + GT_RED_BYTES +
+           64 * 4 + GT_ECACHE_FLOATS * 4;
 }
 
-// Same CTA shape, ring and layout as gemv_tiled_kernel; the consumers use the
-// integer engine above.
-template <int PRO, int EPI>
-__global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
+// The shared-memory ring of a tiled GEMV CTA: stage i at ring + i * 36 KB,
+// full[i] / empty[i] mbarriers. Chunks are numbered in the order the producer
+// issues them (q); chunk q sits in stage q % GT_STAGES, use q / GT_STAGES.
+struct TiledRing
+{
+    uint32_t ring, full, empty; // shared-memory addresses
+};
+
+// Producer warp: issues, for every row group this CTA owns (cta, cta + ncta,
+// ...), its chunks of the tile-major matrix w ([N/16][K/128 tiles]). Returns
+// false if a wait for a free stage ran out (the caller drains and stops).
+__device__ __forceinline__ bool tiled_produce(const uint8_t* w, int N, int K, const TiledRing& r, uint32_t& q,
+                                              int cta, int ncta, int lane, unsigned long long* wait_cycles = nullptr,
+                                              bool hint = false)
+{
+    constexpr int NS = GT_STAGES, CT = GT_CHUNK_TILES;
+    const int ntile = K >> 7, nchunk = (ntile + CT - 1) / CT, n_groups = N >> 4;
+    const size_t group_bytes = (size_t)ntile * GT_TILE_BYTES;
+    for (int group = cta; group < n_groups; group += ncta)
+    {
+        const uint8_t* gsrc = w + (size_t)group * group_bytes;
+        for (int c = 0; c < nchunk; ++c, ++q)
+        {
+            const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
+            const uint32_t stage = q % NS, use = q / NS;
+            const long long c0 = wait_cycles ? clock64() : 0;
+            if (use > 0 && !mbar_wait_bounded(r.empty + 8 * stage, (use - 1) & 1, GEMV_WAIT_LIMIT_NS))
+                return false;
+            if (wait_cycles)
+                *wait_cycles += (unsigned long long)(clock64() - c0);
+            if (lane == 0)
+            {
+                const uint32_t bytes = (uint32_t)tiles * GT_TILE_BYTES;
+                mbar_arrive_expect_tx(r.full + 8 * stage, bytes);
+                if (hint)
+                    bulk_g2s_hint(r.ring + stage * GT_STAGE_BYTES, gsrc + (size_t)c * CT * GT_TILE_BYTES, bytes,
+                                  r.full + 8 * stage, l2_evict_first_policy());
+                else
+                    bulk_g2s(r.ring + stage * GT_STAGE_BYTES, gsrc + (size_t)c * CT * GT_TILE_BYTES, bytes,
+                             r.full + 8 * stage);
+            }
+            __syncwarp();
+        }
+    }
+    return true;
+}
+
+// Producer warp before exit: every issued chunk (q of them) has landed.
+__device__ __forceinline__ void tiled_drain(const TiledRing& r, uint32_t q)
+{
+    constexpr int NS = GT_STAGES;
+    for (uint32_t k = (q > NS ? q - NS : 0); k < q; ++k)
+        mbar_wait_bounded(r.full + 8 * (k % NS), (k / NS) & 1, GEMV_WAIT_LIMIT_NS);
+}
+
+// Consumer warps (16): the row groups of one tiled GEMV in the producer's
+// order, with the activation already built into frag (gemv_build_i8) and its
+// output factor in out_scale; the epilogue EPI of each group runs on one
+// warp. Returns false on a timed-out wait or an abort (s_abort).
+template <int EPI>
+__device__ __forceinline__ bool tiled_i8_consume(const GemvParams& p, const TiledRing& r, uint32_t& q,
+                                                 const uint4* frag, float* red, float out_scale, int cta, int ncta,
+                                                 volatile int& s_abort, unsigned long long* wait_cycles = nullptr)
 {
     constexpr int NS = GT_STAGES;
     constexpr int NC = GT_CONSUMERS;
     constexpr int NCT = NC * 32;
     constexpr int CT = GT_CHUNK_TILES;
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int ntile = p.K >> 7;
-    const int nchunk = (ntile + CT - 1) / CT;
-    uint8_t* ring = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GT_STAGE_BYTES); // full[NS], empty[NS]
-    uint4* frag = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + (size_t)NS * 16);
-    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) + (size_t)(ntile + 1) * 512);
-    float* misc = red + 2 * NC * 16; // [0] output factor, [8..8+NC) max scratch
-    __shared__ int s_abort_mem;
-    volatile int& s_abort = s_abort_mem;
-
-    pdl_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_groups = p.N >> 4;
-    const int my_groups = blockIdx.x < n_groups ? (n_groups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const uint32_t ring_a = smem_addr(ring);
-    const uint32_t full_a = smem_addr(bars), empty_a = full_a + NS * 8;
-    const size_t group_bytes = (size_t)ntile * GT_TILE_BYTES;
-
-    if (tid == 0)
-    {
-        for (int i = 0; i < NS; ++i)
-        {
-            mbar_init(full_a + 8 * i, 1);
-            mbar_init(empty_a + 8 * i, NC);
-        }
-        mbar_init_fence();
-        s_abort = 0;
-    }
-    __syncthreads();
-
-    if (warp == NC)
-    {
-        // ---------------- producer warp: one bulk copy per chunk ----------------
-        uint32_t q = 0;
-        bool ok = true;
-        for (int gl = 0; gl < my_groups && ok; ++gl)
-        {
-            const uint8_t* gsrc = p.w + (size_t)(blockIdx.x + gl * gridDim.x) * group_bytes;
-            for (int c = 0; c < nchunk; ++c, ++q)
-            {
-                const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-                const uint32_t stage = q % NS, use = q / NS;
-                if (use > 0 && !mbar_wait_bounded(empty_a + 8 * stage, (use - 1) & 1, GEMV_WAIT_LIMIT_NS))
-                {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0)
-                {
-                    const uint32_t bytes = (uint32_t)tiles * GT_TILE_BYTES;
-                    mbar_arrive_expect_tx(full_a + 8 * stage, bytes);
-                    bulk_g2s(ring_a + stage * GT_STAGE_BYTES, gsrc + (size_t)c * CT * GT_TILE_BYTES, bytes,
-                             full_a + 8 * stage);
-                }
-                __syncwarp();
-            }
-        }
-        if (!ok)
-        {
-            s_abort = 1;
-            if (lane == 0 && p.state)
-                p.state->err = 2u;
-        }
-        // drain: every issued chunk has landed before the CTA may exit
-        for (uint32_t k = (q > NS ? q - NS : 0); k < q; ++k)
-            mbar_wait_bounded(full_a + 8 * (k % NS), (k / NS) & 1, GEMV_WAIT_LIMIT_NS);
-        return;
-    }
-
-    // ---------------- consumer warps ----------------
-    pdl_wait();
-    gemv_build_i8<PRO, NCT>(p, frag, misc, ntile);
-    const float out_scale = misc[0];
-
+    const int ntile = p.K >> 7, nchunk = (ntile + CT - 1) / CT, n_groups = p.N >> 4;
     const int g = lane >> 2, t = lane & 3;
     const bool bact = (g >> 1) == t;
     // active lanes read their own 16 B of every (tile, word) row of the
@@ -462,24 +549,26 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
     const uint32_t f_step = bact ? 512u : 0u;
     const uint32_t f_sstep = bact ? 128u : 0u;
     bool ok = true;
-    uint32_t q = 0;
-    for (int gl = 0; gl < my_groups; ++gl)
+    int gl = 0;
+    for (int group = cta; group < n_groups; group += ncta, ++gl)
     {
-        const int group = blockIdx.x + gl * gridDim.x;
         float acc0 = 0.0f, acc1 = 0.0f;
         for (int c = 0; c < nchunk && ok; ++c, ++q)
         {
             const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
             const uint32_t stage = q % NS;
-            if (!mbar_wait_bounded(full_a + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
+            const long long c0 = wait_cycles ? clock64() : 0;
+            if (!mbar_wait_bounded(r.full + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
             {
                 ok = false;
                 s_abort = 1;
                 break;
             }
+            if (wait_cycles)
+                *wait_cycles += (unsigned long long)(clock64() - c0);
             if (warp < tiles)
             {
-                const uint32_t st = ring_a + stage * GT_STAGE_BYTES;
+                const uint32_t st = r.ring + stage * GT_STAGE_BYTES;
                 const bool two = warp + NC < tiles;
                 const int ia = warp, ib = two ? warp + NC : warp;
                 uint4 w0[2], w1[2];
@@ -528,9 +617,17 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
             }
             __syncwarp();
             if (lane == 0)
-                mbar_arrive(empty_a + 8 * stage);
+                mbar_arrive(r.empty + 8 * stage);
         }
-        float* rb = red + (size_t)(gl & 1) * NC * 16;
+        if (!ok)
+            break;
+        // this warp's share of the group into buffer gl % RB; the warp that
+        // brings the count to NC runs the epilogue (buffer gl % RB is free
+        // again by the time any warp reaches group gl + RB: warps are at most
+        // GT_STAGES chunks apart)
+        const int b = gl & (GT_RB - 1);
+        float* rb = red + (size_t)b * NC * 16;
+        unsigned* cnt = reinterpret_cast<unsigned*>(red + (size_t)GT_RB * NC * 16);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
@@ -540,16 +637,483 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
             rb[warp * 16 + g] = acc0 * out_scale;
             rb[warp * 16 + g + 8] = acc1 * out_scale;
         }
-        named_bar_sync(1, NCT);
-        if (!ok || s_abort)
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0)
         {
+            __threadfence_block();
+            last = atomicAdd(cnt + b, 1u) == (unsigned)NC - 1 ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last)
+        {
+            __threadfence_block();
+            gemv_epilogue<1, EPI, NC>(p, rb, group, lane);
+            __syncwarp();
+            if (lane == 0)
+                cnt[b] = 0u;
+        }
+    }
+    // the threads decide together (a thread that returned alone would strand
+    // the others at the next barrier)
+    return !named_bar_or(1, NCT, !ok);
+}
+
+// ---------------------------------------------------------------------------
+// Warp-built operand (the persistent step kernel's GEMVs).
+//
+// Consumer warp w only ever reads tiles w and w + 16 of every chunk, so it
+// builds exactly those tiles' B operands itself: no CTA-wide barrier between
+// the activation and the first weight chunk. The activation is scaled per
+// 32-element block (y = x * 127 / max|x| over the block, unit = max / (127 *
+// 128) kept in bscale), so the digits need no reduction over the whole
+// vector; the RMSNorm factor is a scalar applied after the dot product
+// (W (r * (x o g)) = r * W (x o g)), from the per-warp sums of squares in
+// wss, summed in fixed order by the warp that runs each group's epilogue.
+// ---------------------------------------------------------------------------
+
+// Builds this warp's tiles: frag slots, bscale[tile * 4 + block] and (NORM)
+// wss[warp]. zero16: a 16-byte zero in shared memory (B of inactive lanes).
+template <int PRO>
+__device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, float* bscale, float* wss,
+                                              unsigned long long* pass_a_cycles = nullptr)
+{
+    const long long c_start = pass_a_cycles ? clock64() : 0;
+    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
+    constexpr int NC = GT_CONSUMERS, CT = GT_CHUNK_TILES;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the CTA's warps start on different tiles (CTA c shifts by c): 148 CTAs
+    // do not all ask L2 for the same lines of x at the same moment
+    const int wv = (warp + (int)blockIdx.x) & (NC - 1);
+    const int ntile = p.K >> 7, nchunk = (ntile + CT - 1) / CT;
+    const float* src = p.x;
+    if constexpr (PRO == PRO_EMBED_RMSNORM)
+    {
+        const uint32_t pos = p.state->pos;
+        const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
+        src = p.embedding + (size_t)tok * p.K;
+    }
+    const int item = lane & 15, tb = item >> 2, s = item & 3;
+    float ss = 0.0f;
+    // pass A: every chunk's loads issued back to back (one L2 round trip for
+    // the whole operand); the raw x*g values are parked in their frag slots
+#pragma unroll 4
+    for (int c = 0; c < nchunk; ++c)
+    {
+        const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
+        const int ti = wv + NC * (lane >> 4); // lanes 0-15: tile wv, 16-31: tile wv + 16
+        const bool live = ti < tiles;
+        const int tile = c * CT + ti;
+        const int k0 = tile * 128 + tb * 32 + s * 8;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (live)
+        {
+            float4 a, b;
+            if constexpr (PRO == PRO_ATTN_COMBINE)
+            {
+                // elements k0..k0+7 of head h: the merge of its S split
+                // results, in split order, as the attention kernel's own merge
+                constexpr int SU = 16;
+                const int hd = p.head_dim, h = k0 / hd, d0 = k0 - h * hd, S = p.attn_S, ps = p.attn_pstride;
+                const float* pb = p.attn_part + (size_t)h * S * ps;
+                float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, den = 0.0f;
+                if (S <= SU)
+                {
+                    float ms[SU], ls[SU];
+#pragma unroll
+                    for (int s2 = 0; s2 < SU; ++s2)
+                    {
+                        const float2 ml = s2 < S ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)s2 * ps + hd))
+                                                 : make_float2(-INFINITY, 0.0f);
+                        ms[s2] = ml.x;
+                        ls[s2] = ml.y;
+                    }
+                    float M = -INFINITY;
+#pragma unroll
+                    for (int s2 = 0; s2 < SU; ++s2)
+                        M = fmaxf(M, ms[s2]);
+#pragma unroll
+                    for (int s2 = 0; s2 < SU; ++s2)
+                        if (s2 < S)
+                        {
+                            const float* pv = pb + (size_t)s2 * ps + d0;
+                            const float4 va = __ldcg(reinterpret_cast<const float4*>(pv));
+                            const float4 vb = __ldcg(reinterpret_cast<const float4*>(pv + 4));
+                            const float w = (ms[s2] == -INFINITY) ? 0.0f : expf(ms[s2] - M);
+                            num[0] = fmaf(va.x, w, num[0]);
+                            num[1] = fmaf(va.y, w, num[1]);
+                            num[2] = fmaf(va.z, w, num[2]);
+                            num[3] = fmaf(va.w, w, num[3]);
+                            num[4] = fmaf(vb.x, w, num[4]);
+                            num[5] = fmaf(vb.y, w, num[5]);
+                            num[6] = fmaf(vb.z, w, num[6]);
+                            num[7] = fmaf(vb.w, w, num[7]);
+                            den = fmaf(ls[s2], w, den);
+                        }
+                }
+                else
+                {
+                    float M = -INFINITY;
+                    for (int s2 = 0; s2 < S; ++s2)
+                        M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
+                    for (int s2 = 0; s2 < S; ++s2)
+                    {
+                        const float* pv = pb + (size_t)s2 * ps;
+                        const float ms = __ldcg(pv + hd);
+                        const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc)
+                            num[cc] = fmaf(__ldcg(pv + d0 + cc), w, num[cc]);
+                        den = fmaf(__ldcg(pv + hd + 1), w, den);
+                    }
+                }
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc)
+                    v[cc] = den > 0.0f ? num[cc] / den : 0.0f;
+            }
+            else
+            {
+                // L2 loads: in the persistent step kernel x was written by
+                // other CTAs after this SM may have cached an older copy in L1
+                a = __ldcg(reinterpret_cast<const float4*>(src + k0));
+                b = __ldcg(reinterpret_cast<const float4*>(src + k0 + 4));
+                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+                if constexpr (PRO == PRO_EMBED_RMSNORM)
+                    if (blockIdx.x == 0)
+                    {
+                        *reinterpret_cast<float4*>(p.hidden_out + k0) = a;
+                        *reinterpret_cast<float4*>(p.hidden_out + k0 + 4) = b;
+                    }
+            }
+            if constexpr (NORM)
+            {
+                const float4 ga = __ldg(reinterpret_cast<const float4*>(p.gain + k0));
+                const float4 gb = __ldg(reinterpret_cast<const float4*>(p.gain + k0 + 4));
+                const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc)
+                {
+                    ss = fmaf(v[cc], v[cc], ss);
+                    v[cc] = __fmul_rn(v[cc], gv[cc]); // src/rmsnorm.cpp:42-43 without the 1/rms
+                }
+            }
+        }
+        if (live)
+        {
+            float4* park = reinterpret_cast<float4*>(frag + ((size_t)tile * 4 + s) * 8 + 2 * tb);
+            park[0] = make_float4(v[0], v[1], v[2], v[3]);
+            park[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+    }
+    __syncwarp();
+    if (pass_a_cycles)
+        *pass_a_cycles += (unsigned long long)(clock64() - c_start);
+    // pass B: block maxima and digits, in place
+    for (int c = 0; c < nchunk; ++c)
+    {
+        const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
+        const int ti = wv + NC * (lane >> 4);
+        const bool live = ti < tiles;
+        const int tile = c * CT + ti;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (live)
+        {
+            const float4* park = reinterpret_cast<const float4*>(frag + ((size_t)tile * 4 + s) * 8 + 2 * tb);
+            const float4 a = park[0], b = park[1];
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        }
+        // block max over the 4 lanes of the block (items s = 0..3); a
+        // non-finite value makes the block's unit NaN (so its outputs are)
+        float mx = 0.0f;
+        bool fin = true;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)
+        {
+            const float a8 = fabsf(v[cc]);
+            fin = fin && (a8 <= 3.0e38f);
+            mx = fmaxf(mx, a8);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const unsigned bad = __ballot_sync(0xffffffffu, !fin);
+        const bool bbad = ((bad >> (lane & ~3)) & 0xFu) != 0;
+        const float inv = (mx > 0.0f && !bbad) ? 127.0f / mx : 0.0f;
+        if (live)
+        {
+            // balanced base-128 digits of Y = round(y * 2^21) (odd elements:
+            // of y/16, so Y = round(y * 2^17)), exact integer arithmetic:
+            // Y = d0 2^21 + d1 2^14 + d2 2^7 + d3, d0 in [-127, 127], the
+            // others in [-64, 64]
+            int dg[8][4];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+            {
+                const float y = __fmul_rn(v[cc], inv);
+                const int Y = __float2int_rn(y * ((cc & 1) ? 131072.0f : 2097152.0f));
+                const int d0 = (Y + (1 << 20)) >> 21;
+                const int r0 = Y - (d0 << 21);
+                const int d1 = (r0 + (1 << 13)) >> 14;
+                const int r1 = r0 - (d1 << 14);
+                const int d2 = (r1 + 64) >> 7;
+                dg[cc][0] = d0;
+                dg[cc][1] = d1;
+                dg[cc][2] = d2;
+                dg[cc][3] = r1 - (d2 << 7);
+            }
+            // one word = the bytes of one digit of elements e, e+2, e+4, e+6
+            auto pack = [&](int e, int k) {
+                const uint32_t lo = __byte_perm((uint32_t)dg[e][k], (uint32_t)dg[e + 2][k], 0x0040);
+                const uint32_t hi = __byte_perm((uint32_t)dg[e + 4][k], (uint32_t)dg[e + 6][k], 0x0040);
+                return __byte_perm(lo, hi, 0x5410);
+            };
+            const uint32_t w0[4] = {pack(0, 0), pack(1, 0), pack(0, 2), pack(1, 2)};
+            const uint32_t w1[4] = {pack(0, 1), pack(1, 1), pack(0, 3), pack(1, 3)};
+            uint4* dst = frag + ((size_t)tile * 4 + s) * 8 + 2 * tb;
+            dst[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+            dst[1] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+            if (s == 0)
+                bscale[tile * 4 + tb] = bbad ? __int_as_float(0x7fc00000) : mx / (127.0f * 128.0f);
+        }
+    }
+    if constexpr (NORM)
+    {
+        ss = warp_sum(ss);
+        if (lane == 0)
+            wss[warp] = ss;
+    }
+    __syncwarp();
+}
+
+// Consumer warps of one GEMV with warp-built operands (warp_build_i8 first,
+// in the same warp). zero16: shared address of 16 zero bytes.
+template <int PRO, int EPI>
+__device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const TiledRing& r, uint32_t& q,
+                                                 const uint4* frag, const float* bscale, const float* wss,
+                                                 uint32_t zero16, float* red, float* ecache, int cta, int ncta,
+                                                 volatile int& s_abort, unsigned long long* wait_cycles = nullptr)
+{
+    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
+    constexpr int NS = GT_STAGES;
+    constexpr int NC = GT_CONSUMERS;
+    constexpr int NCT = NC * 32;
+    constexpr int CT = GT_CHUNK_TILES;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wv = (warp + (int)blockIdx.x) & (NC - 1); // the tiles warp_build_i8 gave this warp
+    const int ntile = p.K >> 7, nchunk = (ntile + CT - 1) / CT, n_groups = p.N >> 4;
+    const int g = lane >> 2, t = lane & 3;
+    const bool bact = (g >> 1) == t;
+    const uint32_t f_base = bact ? smem_addr(frag) + (uint32_t)g * 16 : zero16;
+    const uint32_t f_step = bact ? 512u : 0u;
+    const uint32_t f_sstep = bact ? 128u : 0u;
+    const uint32_t bs_base = smem_addr(bscale) + (uint32_t)t * 4;
+    // epilogue inputs into shared memory (read by whichever warp completes a
+    // group; every warp has stored its share before its first arrival)
+    EpiCache ec{};
+    const EpiCache* ecp = nullptr;
+    if constexpr (EPI == EPI_RESIDUAL)
+    {
+        const int my_groups = cta < n_groups ? (n_groups - 1 - cta) / ncta + 1 : 0;
+        if (my_groups * 16 <= GT_ECACHE_FLOATS)
+        {
+            for (int i = tid; i < my_groups * 16; i += NCT)
+                ecache[i] = __ldcg(p.y + (size_t)(cta + (i >> 4) * ncta) * 16 + (i & 15));
+            ec.resid = ecache;
+            ecp = &ec;
+        }
+    }
+    else if constexpr (EPI == EPI_QKV_ROPE)
+    {
+        const int half = p.head_dim >> 1;
+        const uint32_t pos = p.state->pos;
+        if (half <= GT_ECACHE_FLOATS / 2 - 1 && pos < (uint32_t)p.max_pos)
+        {
+            for (int i = tid; i < half; i += NCT)
+            {
+                ecache[i] = __ldg(p.rope_cos + (size_t)pos * half + i);
+                ecache[GT_ECACHE_FLOATS / 2 + i] = __ldg(p.rope_sin + (size_t)pos * half + i);
+            }
+            ec.cos = ecache;
+            ec.sin = ecache + GT_ECACHE_FLOATS / 2;
+            ec.page = __ldg(p.page_table + pos / p.page_size);
+            ecp = &ec;
+        }
+    }
+    bool ok = true;
+    int gl = 0;
+    for (int group = cta; group < n_groups; group += ncta, ++gl)
+    {
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int c = 0; c < nchunk && ok; ++c, ++q)
+        {
+            const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
+            const uint32_t stage = q % NS;
+            const long long c0 = wait_cycles ? clock64() : 0;
+            if (!mbar_wait_bounded(r.full + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
+            {
+                ok = false;
+                s_abort = 1;
+                break;
+            }
+            if (wait_cycles)
+                *wait_cycles += (unsigned long long)(clock64() - c0);
+            if (wv < tiles)
+            {
+                const uint32_t st = r.ring + stage * GT_STAGE_BYTES;
+                const bool two = wv + NC < tiles;
+                const int ia = wv, ib = two ? wv + NC : wv;
+                uint4 w0[2], w1[2];
+                uint16_t sh0[2], sh1[2];
+                uint32_t fa[2];
+                float bsc[2];
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+                {
+                    const int i = k ? ib : ia, tt = c * CT + i;
+                    w0[k] = lds128(st + i * 1024 + lane * 16);
+                    w1[k] = lds128(st + i * 1024 + 512 + lane * 16);
+                    const uint32_t sa = st + tiles * 1024 + i * 128 + lane * 2; // u16 scales
+                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh0[k]) : "r"(sa));
+                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh1[k]) : "r"(sa + 64));
+                    fa[k] = f_base + (uint32_t)tt * f_step;
+                    bsc[k] = ldsf(bs_base + (uint32_t)tt * 16);
+                }
+                int dp[2][4] = {}, dq[2][4] = {};
+#pragma unroll
+                for (int s = 0; s < 4; ++s)
+                {
+#pragma unroll
+                    for (int k = 0; k < 2; ++k)
+                    {
+                        const uint32_t wa = u4get(w0[k], s), wb = u4get(w1[k], s);
+                        const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = wb & 0x0F0F0F0Fu;
+                        const uint32_t a2 = wa & 0xF0F0F0F0u, a3 = wb & 0xF0F0F0F0u;
+                        const uint4 b = lds128(fa[k] + (uint32_t)s * f_sstep);
+                        mma_u8s8_16832(dp[k][0], dp[k][1], dp[k][2], dp[k][3], a0, a1, a2, a3, b.x, b.y);
+                        mma_u8s8_16832(dq[k][0], dq[k][1], dq[k][2], dq[k][3], a0, a1, a2, a3, b.z, b.w);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+                {
+                    if (k == 1 && !two)
+                        break;
+                    const float r0 = fmaf((float)(dq[k][0] * 128 + dq[k][1]), 1.0f / 16384.0f,
+                                          (float)(dp[k][0] * 128 + dp[k][1]));
+                    const float r1 = fmaf((float)(dq[k][2] * 128 + dq[k][3]), 1.0f / 16384.0f,
+                                          (float)(dp[k][2] * 128 + dp[k][3]));
+                    acc0 = fmaf(decode_scale<AAEDN_SCALE_F16>(sh0[k]) * bsc[k], r0, acc0);
+                    acc1 = fmaf(decode_scale<AAEDN_SCALE_F16>(sh1[k]) * bsc[k], r1, acc1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(r.empty + 8 * stage);
+        }
+        if (!ok)
+            break;
+        const int b = gl & (GT_RB - 1);
+        float* rb = red + (size_t)b * NC * 16;
+        unsigned* cnt = reinterpret_cast<unsigned*>(red + (size_t)GT_RB * NC * 16);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        if (t == 0)
+        {
+            rb[warp * 16 + g] = acc0;
+            rb[warp * 16 + g + 8] = acc1;
+        }
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0)
+        {
+            __threadfence_block();
+            last = atomicAdd(cnt + b, 1u) == (unsigned)NC - 1 ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last)
+        {
+            __threadfence_block();
+            float post = 1.0f;
+            if constexpr (NORM)
+            {
+                float tss = 0.0f;
+                for (int i = 0; i < NC; ++i) // fixed order
+                    tss += wss[i];
+                post = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tss, (float)p.K), p.eps)); // src/rmsnorm.cpp:34
+            }
+            gemv_epilogue<1, EPI, NC>(p, rb, group, lane, post, ecp, gl);
+            __syncwarp();
+            if (lane == 0)
+                cnt[b] = 0u;
+        }
+    }
+    return !named_bar_or(1, NCT, !ok);
+}
+
+// Same CTA shape, ring and layout as gemv_tiled_kernel; the consumers use the
+// integer engine above.
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
+{
+    constexpr int NS = GT_STAGES;
+    constexpr int NC = GT_CONSUMERS;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int ntile = p.K >> 7;
+    uint8_t* ring = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GT_STAGE_BYTES); // full[NS], empty[NS]
+    uint4* frag = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + (size_t)NS * 16);
+    float* bscale = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) + (size_t)ntile * 512);
+    float* red = bscale + (size_t)ntile * 4;
+    float* misc = red + GT_RED_BYTES / 4; // [32, 48) per-warp sums of squares, [48, 52) zero
+    float* ecache = misc + 64;
+    __shared__ int s_abort_mem;
+    volatile int& s_abort = s_abort_mem;
+
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    TiledRing r;
+    r.ring = smem_addr(ring);
+    r.full = smem_addr(bars);
+    r.empty = r.full + NS * 8;
+
+    if (tid == 0)
+    {
+        for (int i = 0; i < NS; ++i)
+        {
+            mbar_init(r.full + 8 * i, 1);
+            mbar_init(r.empty + 8 * i, NC);
+        }
+        mbar_init_fence();
+        s_abort = 0;
+    }
+    if (tid < GT_RB)
+        reinterpret_cast<unsigned*>(red + (size_t)GT_RB * NC * 16)[tid] = 0u;
+    if (tid < 4)
+        misc[48 + tid] = 0.0f;
+    __syncthreads();
+
+    if (warp == NC)
+    {
+        // producer warp: the weights do not depend on the previous kernel
+        uint32_t q = 0;
+        if (!tiled_produce(p.w, p.N, p.K, r, q, blockIdx.x, gridDim.x, lane, nullptr, p.l2_hint != 0))
+        {
+            s_abort = 1;
             if (lane == 0 && p.state)
                 p.state->err = 2u;
-            break;
         }
-        if (warp == (gl & (NC - 1)))
-            gemv_epilogue<1, EPI, NC>(p, rb, group, lane);
+        tiled_drain(r, q);
+        return;
     }
+
+    pdl_wait();
+    warp_build_i8<PRO>(p, frag, bscale, misc + 32);
+    uint32_t q = 0;
+    if (!tiled_wb_consume<PRO, EPI>(p, r, q, frag, bscale, misc + 32, smem_addr(misc + 48), red, ecache,
+                                    blockIdx.x, gridDim.x, s_abort))
+        if (lane == 0 && p.state)
+            p.state->err = 2u;
 }
 
 } // namespace aaedn_dev

@@ -22,6 +22,7 @@
 #include "attention.cuh"
 #include "gemv_q4.cuh"
 #include "gemv_tiled.cuh"
+#include "mega.cuh"
 #include "gemv_tma.cuh"
 
 namespace aaedn_dev
@@ -83,6 +84,7 @@ struct LmParams
     int rows_per_cta;
     int stages;    // rows in the shared-memory ring, a multiple of consumers
     int consumers; // consumer warps that take rows (<= LM_CONSUMERS)
+    int l2_hint;   // stream the rows with the L2 evict-first policy
 };
 
 constexpr int LM_CONSUMERS = 8;
@@ -157,7 +159,11 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
             if (lane == 0)
             {
                 mbar_arrive_expect_tx(full_a + 8 * stage, row_bytes);
-                bulk_g2s(ring_a + stage * row_bytes, p.w + (size_t)(n0 + j) * p.dim, row_bytes, full_a + 8 * stage);
+                if (p.l2_hint)
+                    bulk_g2s_hint(ring_a + stage * row_bytes, p.w + (size_t)(n0 + j) * p.dim, row_bytes,
+                                  full_a + 8 * stage, l2_evict_first_policy());
+                else
+                    bulk_g2s(ring_a + stage * row_bytes, p.w + (size_t)(n0 + j) * p.dim, row_bytes, full_a + 8 * stage);
             }
             __syncwarp();
         }
@@ -464,6 +470,14 @@ struct aaedn_model
     bool weights_set = false;
     bool pdl = true;   // programmatic dependent launch inside the decode graph
     bool tiled = true; // tile-major repacking of the matrices whose shape allows it
+    bool l2_hint = true; // weight streams with the L2 evict-first policy
+    // the whole step as one persistent kernel (decode_step_kernel)
+    bool mega = false;
+    int mega_S = 1, mega_ctas = 0, mega_R = 1;
+    size_t mega_smem = 0;
+    GemvParams* d_gemv = nullptr; // [n_layers][4]
+    AttnParams* d_attn = nullptr; // [n_layers]
+    unsigned* mega_bar = nullptr; // [5 * n_layers]
 
     template <typename T>
     T* take(size_t bytes)
@@ -515,10 +529,14 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->attn_out = m->take<float>(H * hd * 4);
     m->act = m->take<float>(F * 4);
     m->logits = m->take<float>(V * 4);
-    m->attn_part = m->take<float>(H * (size_t)m->attn_S * (hd + 2) * 4);
+    m->attn_part = m->take<float>(H * (size_t)std::max(m->attn_S, m->mega_S) * (hd + 4) * 4);
     m->attn_counters = m->take<unsigned>(KV * 4);
-    m->lm_part_val = m->take<float>((size_t)m->lm_ctas * 4);
-    m->lm_part_idx = m->take<int>((size_t)m->lm_ctas * 4);
+    const size_t lm_parts = (size_t)std::max(m->lm_ctas, sm_count());
+    m->lm_part_val = m->take<float>(lm_parts * 4);
+    m->lm_part_idx = m->take<int>(lm_parts * 4);
+    m->d_gemv = m->take<GemvParams>((size_t)c.n_layers * 4 * sizeof(GemvParams));
+    m->d_attn = m->take<AttnParams>((size_t)c.n_layers * sizeof(AttnParams));
+    m->mega_bar = m->take<unsigned>((size_t)c.n_layers * 5 * 4);
     m->dbg_hidden = m->take<float>((size_t)c.n_layers * D * 4);
     return align_up(m->used, 256);
 }
@@ -535,9 +553,304 @@ enum
     K_ALL = 63,
 };
 
+// Parameters of the kernels of layer l (shared by the per-kernel decode
+// graph and the persistent step kernel).
+static GemvParams qkv_params(const aaedn_model* m, uint32_t l)
+{
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads;
+    const DevLayer& L = m->layers[l];
+    GemvParams q{};
+    q.w = L.wqkv;
+    q.s = L.sqkv;
+    q.ldb = (size_t)D;
+    q.N = (H + 2 * KV) * hd;
+    q.K = D;
+    q.kt0 = 0;
+    q.kt1 = (D + 127) / 128;
+    q.x = m->hidden;
+    q.lda = (size_t)D;
+    q.gain = L.attn_norm;
+    q.eps = c.eps;
+    q.embedding = m->embedding;
+    q.prompt = m->prompt;
+    q.state = m->state;
+    q.hidden_out = m->hidden;
+    q.q_rows = H * hd;
+    q.kv_rows = KV * hd;
+    q.head_dim = hd;
+    q.n_kv = KV;
+    q.page_size = m->page_size;
+    q.max_pos = (int)c.max_seq;
+    q.qbuf = m->qbuf;
+    q.k_layer = L.k;
+    q.v_layer = L.v;
+    q.page_table = m->page_table;
+    q.rope_cos = m->rope_cos;
+    q.rope_sin = m->rope_sin;
+    q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
+    q.scale_pairs = ((D >> 5) & 1) == 0;
+    q.l2_hint = m->l2_hint;
+    return q;
+}
+
+static AttnParams attn_params(const aaedn_model* m, uint32_t l, int S)
+{
+    const aaedn_model_config& c = m->cfg;
+    const int hd = (int)c.head_dim;
+    const DevLayer& L = m->layers[l];
+    AttnParams a{};
+    a.q = m->qbuf;
+    a.k = L.k;
+    a.v = L.v;
+    a.out = m->attn_out;
+    a.part = m->attn_part;
+    a.counters = m->attn_counters;
+    a.n_heads = (int)c.n_heads;
+    a.n_kv = (int)c.n_kv_heads;
+    a.head_dim = hd;
+    a.S = S;
+    a.scale = 1.0f / std::sqrt((float)hd); // src/transformer.cpp:198
+    a.state = m->state;
+    a.max_len = (int)c.max_seq;
+    a.max_tok = m->attn_max_tok;
+    a.page_table = m->page_table;
+    a.page_size = m->page_size;
+    a.pstride = hd + 4; // 16-byte rows: the o-proj build reads them as float4
+    return a;
+}
+
+static GemvParams o_params(const aaedn_model* m, uint32_t l)
+{
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads;
+    const DevLayer& L = m->layers[l];
+    GemvParams o{};
+    o.w = L.wo;
+    o.s = L.so;
+    o.ldb = (size_t)H * hd;
+    o.N = D;
+    o.K = H * hd;
+    o.kt0 = 0;
+    o.kt1 = (H * hd + 127) / 128;
+    o.x = m->attn_out;
+    o.lda = (size_t)H * hd;
+    o.y = m->hidden;
+    o.ldc = (size_t)D;
+    o.state = m->state;
+    o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
+    o.scale_pairs = (((H * hd) >> 5) & 1) == 0;
+    o.l2_hint = m->l2_hint;
+    return o;
+}
+
+static GemvParams gu_params(const aaedn_model* m, uint32_t l)
+{
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, F = (int)c.ffn_dim;
+    const DevLayer& L = m->layers[l];
+    GemvParams gu{};
+    gu.w = L.wgu;
+    gu.s = L.sgu;
+    gu.ldb = (size_t)D;
+    gu.N = 2 * F;
+    gu.K = D;
+    gu.kt0 = 0;
+    gu.kt1 = (D + 127) / 128;
+    gu.x = m->hidden;
+    gu.lda = (size_t)D;
+    gu.gain = L.ffn_norm;
+    gu.eps = c.eps;
+    gu.act = m->act;
+    gu.state = m->state;
+    gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
+    gu.scale_pairs = ((D >> 5) & 1) == 0;
+    gu.l2_hint = m->l2_hint;
+    return gu;
+}
+
+static GemvParams down_params(const aaedn_model* m, uint32_t l)
+{
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, F = (int)c.ffn_dim;
+    const DevLayer& L = m->layers[l];
+    GemvParams dn{};
+    dn.w = L.wd;
+    dn.s = L.sd;
+    dn.ldb = (size_t)F;
+    dn.N = D;
+    dn.K = F;
+    dn.kt0 = 0;
+    dn.kt1 = (F + 127) / 128;
+    dn.x = m->act;
+    dn.lda = (size_t)F;
+    dn.y = m->hidden;
+    dn.ldc = (size_t)D;
+    dn.state = m->state;
+    dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
+    dn.scale_pairs = ((F >> 5) & 1) == 0;
+    dn.l2_hint = m->l2_hint;
+    return dn;
+}
+
+static LmParams lm_params(const aaedn_model* m)
+{
+    const aaedn_model_config& c = m->cfg;
+    LmParams lp{};
+    lp.hidden = m->hidden;
+    lp.gain = m->final_norm;
+    lp.eps = c.eps;
+    lp.dim = (int)c.dim;
+    lp.w = m->lm_head;
+    lp.vocab = (int)c.vocab;
+    lp.logits = m->logits;
+    lp.part_val = m->lm_part_val;
+    lp.part_idx = m->lm_part_idx;
+    lp.state = m->state;
+    lp.out_tokens = m->out_tokens;
+    lp.max_seq = (int)c.max_seq;
+    lp.rows_per_cta = m->lm_rows;
+    lp.stages = m->lm_stages;
+    lp.consumers = m->lm_consumers;
+    lp.l2_hint = m->l2_hint;
+    return lp;
+}
+
+// decode_step_kernel instantiation for G query heads per kv head and head_dim
+template <int HDM>
+static void* mega_kernel_for(int G)
+{
+    switch (G)
+    {
+    case 1: return reinterpret_cast<void*>(decode_step_kernel<1, HDM>);
+    case 2: return reinterpret_cast<void*>(decode_step_kernel<2, HDM>);
+    case 4: return reinterpret_cast<void*>(decode_step_kernel<4, HDM>);
+    case 8: return reinterpret_cast<void*>(decode_step_kernel<8, HDM>);
+    default: return nullptr;
+    }
+}
+
+static void* mega_kernel(const aaedn_model* m)
+{
+    const int G = (int)(m->cfg.n_heads / m->cfg.n_kv_heads);
+    return m->cfg.head_dim > 128 ? mega_kernel_for<256>(G) : mega_kernel_for<128>(G);
+}
+
+static MegaParams mega_params(const aaedn_model* m)
+{
+    const aaedn_model_config& c = m->cfg;
+    MegaParams P{};
+    P.gemv = m->d_gemv;
+    P.attn = m->d_attn;
+    P.state = m->state;
+    P.bar = m->mega_bar;
+    P.n_layers = (int)c.n_layers;
+    P.attn_items = (int)c.n_kv_heads * m->mega_S;
+    P.lm.hidden = m->hidden;
+    P.lm.gain = m->final_norm;
+    P.lm.w = m->lm_head;
+    P.lm.logits = m->logits;
+    P.lm.part_val = m->lm_part_val;
+    P.lm.part_idx = m->lm_part_idx;
+    P.lm.out_tokens = m->out_tokens;
+    P.lm.eps = c.eps;
+    P.lm.dim = (int)c.dim;
+    P.lm.vocab = (int)c.vocab;
+    P.lm.max_seq = (int)c.max_seq;
+    P.lm.rows_per_cta = ((int)c.vocab + m->mega_ctas - 1) / m->mega_ctas;
+    P.lm.rows_per_chunk = m->mega_R;
+    return P;
+}
+
+// Decides whether this model runs as the persistent step kernel and uploads
+// its per-layer parameter arrays. Called once the arena is carved.
+static int setup_mega(aaedn_model* m)
+{
+    m->mega = false;
+    const char* e = std::getenv("AAEDN_MEGA");
+    if (!(e && e[0] == '1'))
+        return AAEDN_OK;
+    const aaedn_model_config& c = m->cfg;
+    for (const DevLayer& L : m->layers)
+        if (!(L.tqkv && L.to && L.tgu && L.td))
+            return AAEDN_OK; // every matrix must be tile-major
+    const int G = (int)(c.n_heads / c.n_kv_heads);
+    void* kern = mega_kernel(m);
+    if (!kern || c.head_dim > 256)
+        return AAEDN_OK;
+    // lm_head rows per ring stage: a power of two, every warp slice whole
+    int R = 16;
+    while (R > 1 && (size_t)R * c.dim * 4 > (size_t)GT_STAGE_BYTES)
+        R >>= 1;
+    if ((size_t)c.dim * 4 > (size_t)GT_STAGE_BYTES || ((c.dim / 4) % (GT_CONSUMERS / R)) != 0 || c.dim % 4)
+        return AAEDN_OK;
+    const int max_ntile = (int)(std::max({c.dim, c.n_heads * c.head_dim, c.ffn_dim}) / 128);
+    const size_t work = mega_work_bytes(max_ntile, attn_smem_bytes(G, (int)c.head_dim, 0), (int)c.dim);
+    const size_t smem = mega_smem_bytes(work);
+    if (smem > TILED_SMEM_MAX)
+        return AAEDN_OK;
+    int dev = 0, coop = 0, nb = 0;
+    AAEDN_CUDA_TRY(cudaGetDevice(&dev));
+    AAEDN_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+    if (!coop)
+        return AAEDN_OK;
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TILED_SMEM_MAX));
+    AAEDN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, GT_THREADS, smem));
+    if (nb < 1)
+        return AAEDN_OK;
+    m->mega_ctas = sm_count();
+    m->mega_R = R;
+    m->mega_smem = smem;
+    std::vector<GemvParams> gp((size_t)c.n_layers * 4);
+    std::vector<AttnParams> ap(c.n_layers);
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        gp[4 * l + 0] = qkv_params(m, l);
+        gp[4 * l + 1] = o_params(m, l);
+        gp[4 * l + 1].attn_part = m->attn_part; // the o build merges the attention splits
+        gp[4 * l + 1].attn_S = m->mega_S;
+        gp[4 * l + 1].attn_pstride = (int)c.head_dim + 4;
+        gp[4 * l + 1].head_dim = (int)c.head_dim;
+        gp[4 * l + 2] = gu_params(m, l);
+        gp[4 * l + 3] = down_params(m, l);
+        ap[l] = attn_params(m, l, m->mega_S);
+        ap[l].no_combine = 1;
+    }
+    AAEDN_CUDA_TRY(cudaMemcpy(m->d_gemv, gp.data(), gp.size() * sizeof(GemvParams), cudaMemcpyHostToDevice));
+    AAEDN_CUDA_TRY(cudaMemcpy(m->d_attn, ap.data(), ap.size() * sizeof(AttnParams), cudaMemcpyHostToDevice));
+    m->mega = true;
+    return AAEDN_OK;
+}
+
+static int enqueue_mega(aaedn_model* m, cudaStream_t st, unsigned long long* trace_cta = nullptr,
+                        long long* trace_phase = nullptr)
+{
+    MegaParams P = mega_params(m);
+    P.trace_cta = trace_cta;
+    P.trace_phase = trace_phase;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)m->mega_ctas);
+    cfg.blockDim = dim3(GT_THREADS);
+    cfg.dynamicSmemBytes = m->mega_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const void* args[1] = {&P};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel(m), const_cast<void**>(args));
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of decode_step_kernel failed: %s", cudaGetErrorString(e));
+    count_launch();
+    return AAEDN_OK;
+}
+
 static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr,
                         int mask = K_ALL)
 {
+    if (m->mega && !debug && !ev && mask == K_ALL)
+        return enqueue_mega(m, st);
     // programmatic dependent launches between consecutive kernels (not when
     // events or copies sit between them)
     const bool pdl = m->pdl && !ev && !debug;
@@ -552,42 +865,13 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     if (mrc)
         return mrc;
     const aaedn_model_config& c = m->cfg;
-    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads, F = (int)c.ffn_dim;
+    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads;
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l)
     {
         const DevLayer& L = m->layers[l];
         // --- QKV (+RMSNorm prologue, +RoPE/KV-append epilogue)
-        GemvParams q{};
-        q.w = L.wqkv;
-        q.s = L.sqkv;
-        q.ldb = (size_t)D;
-        q.N = (H + 2 * KV) * hd;
-        q.K = D;
-        q.kt0 = 0;
-        q.kt1 = (D + 127) / 128;
-        q.x = m->hidden;
-        q.lda = (size_t)D;
-        q.gain = L.attn_norm;
-        q.eps = c.eps;
-        q.embedding = m->embedding;
-        q.prompt = m->prompt;
-        q.state = m->state;
-        q.hidden_out = m->hidden;
-        q.q_rows = H * hd;
-        q.kv_rows = KV * hd;
-        q.head_dim = hd;
-        q.n_kv = KV;
-        q.page_size = m->page_size;
-        q.max_pos = (int)c.max_seq;
-        q.qbuf = m->qbuf;
-        q.k_layer = L.k;
-        q.v_layer = L.v;
-        q.page_table = m->page_table;
-        q.rope_cos = m->rope_cos;
-        q.rope_sin = m->rope_sin;
-        q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
-        q.scale_pairs = ((D >> 5) & 1) == 0;
+        const GemvParams q = qkv_params(m, l);
         rc = !(mask & K_QKV) ? AAEDN_OK
              : (l == 0)      ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
                              : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv);
@@ -596,23 +880,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if ((rc = mark()))
             return rc;
         // --- attention
-        AttnParams a{};
-        a.q = m->qbuf;
-        a.k = L.k;
-        a.v = L.v;
-        a.out = m->attn_out;
-        a.part = m->attn_part;
-        a.counters = m->attn_counters;
-        a.n_heads = H;
-        a.n_kv = KV;
-        a.head_dim = hd;
-        a.S = m->attn_S;
-        a.scale = 1.0f / std::sqrt((float)hd); // src/transformer.cpp:198
-        a.state = m->state;
-        a.max_len = (int)c.max_seq;
-        a.max_tok = m->attn_max_tok;
-        a.page_table = m->page_table;
-        a.page_size = m->page_size;
+        const AttnParams a = attn_params(m, l, m->attn_S);
         const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
         rc = (mask & K_ATTN) ? attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl) : AAEDN_OK;
         if (rc)
@@ -620,61 +888,21 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if ((rc = mark()))
             return rc;
         // --- O projection + residual
-        GemvParams o{};
-        o.w = L.wo;
-        o.s = L.so;
-        o.ldb = (size_t)H * hd;
-        o.N = D;
-        o.K = H * hd;
-        o.kt0 = 0;
-        o.kt1 = (H * hd + 127) / 128;
-        o.x = m->attn_out;
-        o.lda = (size_t)H * hd;
-        o.y = m->hidden;
-        o.ldc = (size_t)D;
-        o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
-        o.scale_pairs = (((H * hd) >> 5) & 1) == 0;
+        const GemvParams o = o_params(m, l);
         rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- gate/up (+RMSNorm prologue, SwiGLU epilogue)
-        GemvParams gu{};
-        gu.w = L.wgu;
-        gu.s = L.sgu;
-        gu.ldb = (size_t)D;
-        gu.N = 2 * F;
-        gu.K = D;
-        gu.kt0 = 0;
-        gu.kt1 = (D + 127) / 128;
-        gu.x = m->hidden;
-        gu.lda = (size_t)D;
-        gu.gain = L.ffn_norm;
-        gu.eps = c.eps;
-        gu.act = m->act;
-        gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
-        gu.scale_pairs = ((D >> 5) & 1) == 0;
+        const GemvParams gu = gu_params(m, l);
         rc = (mask & K_GU) ? model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- down + residual
-        GemvParams dn{};
-        dn.w = L.wd;
-        dn.s = L.sd;
-        dn.ldb = (size_t)F;
-        dn.N = D;
-        dn.K = F;
-        dn.kt0 = 0;
-        dn.kt1 = (F + 127) / 128;
-        dn.x = m->act;
-        dn.lda = (size_t)F;
-        dn.y = m->hidden;
-        dn.ldc = (size_t)D;
-        dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
-        dn.scale_pairs = ((F >> 5) & 1) == 0;
+        const GemvParams dn = down_params(m, l);
         rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
         if (rc)
             return rc;
@@ -684,22 +912,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             AAEDN_CUDA_TRY(cudaMemcpyAsync(m->dbg_hidden + (size_t)l * D, m->hidden, (size_t)D * 4,
                                            cudaMemcpyDeviceToDevice, st));
     }
-    LmParams lp{};
-    lp.hidden = m->hidden;
-    lp.gain = m->final_norm;
-    lp.eps = c.eps;
-    lp.dim = D;
-    lp.w = m->lm_head;
-    lp.vocab = (int)c.vocab;
-    lp.logits = m->logits;
-    lp.part_val = m->lm_part_val;
-    lp.part_idx = m->lm_part_idx;
-    lp.state = m->state;
-    lp.out_tokens = m->out_tokens;
-    lp.max_seq = (int)c.max_seq;
-    lp.rows_per_cta = m->lm_rows;
-    lp.stages = m->lm_stages;
-    lp.consumers = m->lm_consumers;
+    const LmParams lp = lm_params(m);
     if (mask & K_LM)
     {
         cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(LM_THREADS),
@@ -708,8 +921,8 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return set_error(AAEDN_ECUDA, "launch of lm_head_argmax_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
     }
-        if ((rc = mark()))
-            return rc;
+    if ((rc = mark()))
+        return rc;
     return AAEDN_OK;
 }
 
@@ -809,6 +1022,8 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
         m->pdl = !(e && e[0] == '0');
         const char* t = std::getenv("AAEDN_TILED");
         m->tiled = !(t && t[0] == '0');
+        const char* h = std::getenv("AAEDN_L2HINT");
+        m->l2_hint = !(h && h[0] == '0');
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
@@ -819,6 +1034,10 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
     S = std::min(S, 64);
     m->attn_S = S;
     m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
+    // the persistent step kernel runs two attention items per CTA at once:
+    // at most 2 * SMs items
+    m->mega_S = std::max(1, std::min<int>(64, 2 * sm_count() / (int)c.n_kv_heads));
+    m->mega_S = std::max(1, std::min<int>(m->mega_S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
     // lm_head: one CTA per SM, each streaming one contiguous run of rows
     m->lm_rows = std::max(1, (int)((c.vocab + sm_count() - 1) / sm_count()));
     m->lm_ctas = (int)((c.vocab + m->lm_rows - 1) / m->lm_rows);
@@ -876,6 +1095,9 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
     if (rc)
         return fail(rc);
     rc = set_model_kernel_attrs();
+    if (rc)
+        return fail(rc);
+    rc = setup_mega(m);
     if (rc)
         return fail(rc);
     *out = m;
@@ -1347,5 +1569,47 @@ extern "C" int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h
     }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    return rc;
+}
+
+extern "C" int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase,
+                                      size_t cap_phase)
+{
+    MODEL_OK(m);
+    if (!m->mega)
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_step: the model does not run the persistent kernel");
+    const aaedn_model_config& c = m->cfg;
+    const size_t ncta = (size_t)m->mega_ctas * MEGA_TRACE_CTA, nph = ((size_t)c.n_layers * 5 + 1) * 2;
+    if (!h_cta || !h_phase || cap_cta < ncta || cap_phase < nph)
+        return set_error(AAEDN_EINVAL, "aaedn_model_trace_step: need %zu + %zu outputs", ncta, nph);
+    if (m->h_pos == 0 || (size_t)m->h_pos + 2 > c.max_seq)
+        return set_error(AAEDN_ESTATE, "aaedn_model_trace_step: sequence empty or full");
+    unsigned long long* d_cta = nullptr;
+    long long* d_ph = nullptr;
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    AAEDN_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_cta), ncta * 8));
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&d_ph), nph * 8);
+    if (e == cudaSuccess)
+        e = cudaMemsetAsync(d_cta, 0, ncta * 8, m->stream);
+    if (e == cudaSuccess)
+        e = cudaMemsetAsync(d_ph, 0, nph * 8, m->stream);
+    int rc = e == cudaSuccess ? enqueue_mega(m, m->stream, d_cta, d_ph)
+                              : set_error(AAEDN_ECUDA, "trace buffers: %s", cudaGetErrorString(e));
+    if (!rc)
+    {
+        e = cudaMemcpyAsync(h_cta, d_cta, ncta * 8, cudaMemcpyDeviceToHost, m->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(h_phase, d_ph, nph * 8, cudaMemcpyDeviceToHost, m->stream);
+        if (e == cudaSuccess)
+            e = cudaStreamSynchronize(m->stream);
+        if (e != cudaSuccess)
+            rc = set_error(AAEDN_ECUDA, "trace step: %s", cudaGetErrorString(e));
+    }
+    cudaFree(d_cta);
+    cudaFree(d_ph);
+    if (!rc)
+        rc = write_state(m, m->h_pos, m->h_pos); // the traced step does not count
+    if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess)
+        rc = set_error(AAEDN_ECUDA, "trace step sync");
     return rc;
 }

@@ -75,3 +75,42 @@ def test_synthetic_generator_is_deterministic_and_normal():
     assert abs(a.mean()) < 2e-4 and abs(a.std() - 0.02) < 2e-4
     t = ab.synth_tokens(1234, 0, 32000, 10000)
     assert t.max() < 32000 and len(np.unique(t)) > 8000
+
+
+def _abn(hidden=64, version=2, magic=b"AAEDNMDL", corrupt=False, truncate=0, size_delta=0):
+    import struct
+    rng = np.random.default_rng(hidden)
+    codes = rng.integers(0, 256, hidden * hidden // 2, dtype=np.uint8)
+    scales = rng.integers(0, 65536, hidden * hidden // 32, dtype=np.uint16)
+    payload = codes.tobytes() + scales.tobytes()
+    head = struct.pack("<8sIQI6IB15s", magic, version, len(payload) + size_delta, ab.fnv1a32(payload), 2, 4, 16,
+                       1000, hidden, 4 * hidden, 0, b"\x00" * 15)
+    blob = bytearray(head + payload)
+    if corrupt:
+        blob[64 + 5] ^= 1
+    if truncate:
+        blob = blob[:-truncate]
+    return bytes(blob), codes, scales
+
+
+@pytest.mark.parametrize("case", ["valid", "magic", "version", "size", "checksum", "short", "header"])
+def test_abn_reader_matches_oracle(oracle, tmp_path, case):
+    """quant_load's checks (src/quant.cpp:50-111) in the host reader, and the
+    oracle's restatement of them, give the same verdict."""
+    kw = {"valid": {}, "magic": {"magic": b"AAEDNXXX"}, "version": {"version": 3}, "size": {"size_delta": 2},
+          "checksum": {"corrupt": True}, "short": {"truncate": 3}, "header": {"truncate": 10 ** 6}}[case]
+    blob, codes, scales = _abn(**kw) if case != "header" else (_abn()[0][:40], None, None)
+    path = tmp_path / f"{case}.abn"
+    path.write_bytes(blob)
+    accepted = oracle.abn_v2_accepts(blob)
+    try:
+        h, data, sc = ab.abn_read(path)
+        ok = True
+    except ab.AaednError as e:
+        assert e.rc == ab.EFORMAT
+        ok = False
+    assert ok == accepted == (case == "valid")
+    if ok:
+        assert h.version == 2 and h.hidden_dim == 64 and h.vocab_size == 1000
+        np.testing.assert_array_equal(data, codes)
+        np.testing.assert_array_equal(sc, scales)

@@ -150,3 +150,46 @@ def test_attention_empty_segments_give_zeros():
     q = dev(np.ones(128, np.float32))
     ab.attention(q, q, q, np.zeros((1, 2), np.uint32), out, 1, 128, 0.1)
     assert np.all(host(out) == 0)
+
+
+def test_ffn_swiglu_reference_semantics_vs_reference(ref_golden):
+    """src/ffn.cpp compiled from the reference sources produced ffn_out."""
+    g = ref_golden
+    B, Hd, F = (int(v) for v in g["ffn_dims"])
+    out = empty_f32(B * Hd)
+    ab.ffn_swiglu(dev(g["ffn_x"]), out, B, Hd, F, *(dev(g[f"ffn_{k}"]) for k in ("g", "u", "d", "gs", "us", "ds")),
+                  semantics=ab.FFN_REFERENCE)
+    np.testing.assert_allclose(host(out), g["ffn_out"], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("B,Hd,F", [(1, 4096, 11008), (3, 256, 768)])
+def test_ffn_swiglu_model_semantics(B, Hd, F):
+    """silu(g) * u with fp16 block scales (the model path's FFN), against an
+    fp64 evaluation; bound as for the GEMV."""
+    rng = np.random.default_rng(F)
+    wg, wu, wd = (ab.quantize_q4(rng.normal(0, 0.02, n).astype(np.float32)) for n in (F * Hd, F * Hd, Hd * F))
+    x = rng.normal(0, 1, B * Hd).astype(np.float32)
+    out = empty_f32(B * Hd)
+    ab.ffn_swiglu(dev(x), out, B, Hd, F, dev(wg[0]), dev(wu[0]), dev(wd[0]), dev(wg[1]), dev(wu[1]), dev(wd[1]),
+                  semantics=ab.FFN_MODEL)
+
+    def deq(q, n, k):
+        d, s = q
+        c = np.stack([d & 15, d >> 4], 1).reshape(-1).astype(np.float64)
+        return (c * np.repeat(s.view(np.float16).astype(np.float64), 32)).reshape(n, k)
+
+    G, U, D = deq(wg, F, Hd), deq(wu, F, Hd), deq(wd, Hd, F)
+    X = x.reshape(B, Hd).astype(np.float64)
+    g, u = X @ G.T, X @ U.T
+    act = g / (1 + np.exp(-g)) * u
+    want = act @ D.T
+    mag = np.abs(act) @ np.abs(D.T)
+    err = np.abs(host(out).reshape(B, Hd) - want)
+    assert np.all(err <= 1e-4 * mag + 1e-5), float((err / (mag + 1e-9)).max())
+
+
+def test_ffn_swiglu_null_weights_give_zeros():
+    out = empty_f32(2 * 64)
+    x = dev(np.ones(2 * 64, np.float32))
+    ab.ffn_swiglu(x, out, 2, 64, 96, None, None, None, None, None, None)
+    assert np.all(host(out) == 0)
