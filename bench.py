@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="tp", choices=["tp", "replicas"],
+                    help="N > 1 GPUs: one sequence tensor-parallel over the N GPUs (strong scaling), or N "
+                         "independent replicas (weak scaling)")
     # smaller cases of the same model for profiler captures (not bench lines)
     ap.add_argument("--layers", type=int, default=None, help="profiling case: fewer layers than the 7B model")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="profiling case: prompt length")
@@ -251,9 +254,12 @@ def run_ours(args):
     if args.prompt + W + K + E + P + 2 > cfg["max_seq"]:
         raise SystemExit(f"steps+warmup too large for ctx {cfg['max_seq']}")
 
+    tp = world > 1 and args.mode == "tp"
     w = host_weights(cfg)
-    model = ab.Model(cfg)
+    model = ab.Model(cfg, tp=(rank, world) if tp else None)
     model.set_weights(w)
+    if tp:
+        model.connect_tp()
     stream = torch.cuda.ExternalStream(model.stream)
     prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], args.prompt)
 
@@ -282,7 +288,8 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * K / (ms_max / 1000.0)
+    streams = 1 if tp else world  # tensor parallel: the N GPUs decode one sequence
+    value = streams * K / (ms_max / 1000.0)
     pos1 = model.pos
 
     # ---- end to end through the reference-facing call (host token in, host
@@ -294,7 +301,9 @@ def run_ours(args):
     e0.record(stream)
     tok = np.empty(1, np.uint32)
     for _ in range(E):
-        tok[0] = int(np.argmax(logits))
+        # tensor parallel: each rank holds a vocabulary slice of the logits;
+        # the ranks' argmax exchange already chose the token on the device
+        tok[0] = model.next_token() if tp else int(np.argmax(logits))
         logits = model.forward(tok)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -303,7 +312,7 @@ def run_ours(args):
     te = torch.tensor([e2e_ms], device="cuda")
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * E / (float(te.item()) / 1000.0)
+    e2e_value = streams * E / (float(te.item()) / 1000.0)
 
     # ---- per-kernel-class device times: sub-graphs of the decode step (only
     # the dequant-GEMVs, only attention, ...) replayed P times back to back,
@@ -314,18 +323,20 @@ def run_ours(args):
     shapes = gemv_shapes(cfg)
     gemv_total_ms = parts["gemv"]
     gemv_total_bytes = sum(gemv_bytes(*shapes[k]) for k in ("qkv", "o", "gate_up", "down"))
-    achieved = gemv_total_bytes * L / (gemv_total_ms / 1000.0) / 1e9
+    # tensor parallel: each GPU streams its 1/N share of every matrix
+    share = 1.0 / world if tp else 1.0
+    achieved = gemv_total_bytes * share * L / (gemv_total_ms / 1000.0) / 1e9
     peak, peak_kind = measured_peaks()
     kernel_split = {"step_ms": parts["step"], "gemv_ms": parts["gemv"], "attention_ms": parts["attention"],
                     "lm_head_ms": parts["lm_head"],
                     **{f"{k}_ms": parts[k] for k in ("qkv", "o", "gate_up", "down")},
-                    **{f"{k}_gbs": gemv_bytes(*shapes[k]) * L / (parts[k] / 1000.0) / 1e9
+                    **{f"{k}_gbs": gemv_bytes(*shapes[k]) * share * L / (parts[k] / 1000.0) / 1e9
                        for k in ("qkv", "o", "gate_up", "down")},
-                    "lm_head_gbs": cfg["vocab"] * cfg["dim"] * 4 / (parts["lm_head"] / 1000.0) / 1e9}
+                    "lm_head_gbs": cfg["vocab"] * cfg["dim"] * 4 * share / (parts["lm_head"] / 1000.0) / 1e9}
     traffic = profiled_traffic()
 
     mean_pos = (pos0 + pos1 - 1) / 2.0
-    sb = step_bytes(cfg, mean_pos)
+    sb = step_bytes(cfg, mean_pos) * share  # per GPU
     step_gbs = sb / (ms_max / K / 1000.0) / 1e9
 
     cpu = None
@@ -339,7 +350,8 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
             "config": {"workload": ("llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode"
                                     if (cfg["n_layers"], args.prompt) == (32, 128) else
@@ -349,23 +361,27 @@ def run_ours(args):
                        "ctx": cfg["max_seq"], "prompt": args.prompt, "positions": [pos0, pos1],
                        "weights": "4-bit codes, fp16 scale per 32, fp32 embedding/lm_head",
                        "l2": "inputs larger than L2: 4.1 GB of weights streamed per step",
-                       "parallelism": "replicas" if world > 1 else "single GPU"},
+                       "parallelism": (f"tp{world} (heads, ffn rows, lm_head rows; partials added over NVLink "
+                                       "peer memory)" if tp else f"replicas x{world}" if world > 1 else "single GPU")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "gemv_tiled_i8_kernel (the 4 dequant-GEMVs of every layer, M=1)",
-                         "launches_per_step": 4 * L, "bytes_per_launch_avg": gemv_total_bytes / 4,
-                         "bytes_per_step": gemv_total_bytes * L,
+                         "launches_per_step": 4 * L, "bytes_per_launch_avg": gemv_total_bytes * share / 4,
+                         "bytes_per_step": gemv_total_bytes * share * L,
                          "timing": "sub-graph of the step's GEMVs replayed back to back, CUDA events"},
             "decode_step": {"algorithmic_bytes": sb, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
                             **kernel_split},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12,
-                    "d2h_bytes_per_step": 4 * cfg["vocab"],
-                    "call": "aaedn_model_forward (transformer_forward) + host argmax"},
+                    "d2h_bytes_per_step": (4 * ab.tp_plan(cfg, rank, world)["vocab"] + 4) if tp else 4 * cfg["vocab"],
+                    "call": ("aaedn_model_forward (transformer_forward, this rank's logits slice) + the "
+                             "device's next token" if tp else
+                             "aaedn_model_forward (transformer_forward) + host argmax")},
             "gpu_launches": int(launches),
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    barrier()  # tensor parallel: no rank frees memory a peer may still read
     model.close()
     if world > 1:
         dist.destroy_process_group()

@@ -181,6 +181,39 @@ typedef struct {
 } aaedn_layer_host;
 
 int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** out);
+
+/* ---- tensor parallelism over the GPUs of one node -------------------------
+ * No counterpart in the reference (its token loop is single-process CPU);
+ * this is the multi-GPU decomposition of src/transformer.cpp:128-243. Rank r
+ * of tp_size (1, 2, 4, 8; one process per GPU, that GPU current) holds heads
+ * [r*H/T, (r+1)*H/T) and their KV cache, gate/up rows [r*F/T, ...), the
+ * matching input columns of o and down, and lm_head rows [r*ceil(V/T), ...).
+ * set_layer / set_globals / synthesize take the WHOLE tensors on every rank;
+ * config_get returns the whole model's dims. After o and down the ranks'
+ * partial sums are added through each other's memory (CUDA IPC over NVLink):
+ * every rank exports its handle with aaedn_model_tp_handle, gathers all
+ * tp_size handles in rank order (any host channel) and passes them to
+ * aaedn_model_tp_connect before its first step. All ranks then run the same
+ * calls with the same tokens (lockstep); forward's h_logits receives this
+ * rank's vocabulary slice. Waits between ranks are bounded (2 s; a timeout
+ * reports AAEDN_ETIMEOUT-class failure through the step's error). Destroy on
+ * every rank only after all ranks are done stepping. */
+#define AAEDN_TP_HANDLE_BYTES 64
+/* The share of rank tp_rank (host only, no GPU): heads [q_head0, +n_heads),
+ * kv heads [kv_head0, +n_kv_heads), ffn rows [ffn_row0, +ffn_dim), lm_head
+ * rows / token ids [vocab0, +vocab); o and down take input columns
+ * [q_head0*head_dim, +n_heads*head_dim) and [ffn_row0, +ffn_dim), padded to
+ * o_k / down_k columns on the device. AAEDN_EINVAL if the shape does not
+ * divide (n_kv_heads % T, ffn_dim % (32 T)). */
+typedef struct {
+    uint32_t n_heads, n_kv_heads, ffn_dim, vocab;
+    uint32_t q_head0, kv_head0, ffn_row0, vocab0;
+    uint32_t o_k, down_k;
+} aaedn_tp_plan;
+int aaedn_tp_plan_get(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size, aaedn_tp_plan* out);
+int aaedn_model_create_tp(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size, aaedn_model** out);
+int aaedn_model_tp_handle(aaedn_model* m, uint8_t* h_handle);
+int aaedn_model_tp_connect(aaedn_model* m, const uint8_t* h_handles);
 int aaedn_model_destroy(aaedn_model* m);
 int aaedn_model_config_get(const aaedn_model* m, aaedn_model_config* out);
 void* aaedn_model_stream(aaedn_model* m);
@@ -232,6 +265,14 @@ int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32
  * 0's clock when it reached / left each grid barrier. The position is left
  * where it was. */
 int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase, size_t cap_phase);
+/* Synchronises and reports the sticky device-side error of the decode state
+ * (AAEDN_ESTATE: a position past the cache; AAEDN_ETIMEOUT: a bounded device
+ * wait ran out). forward and generate check it themselves; decode_steps does
+ * not synchronise, so call this after it. */
+int aaedn_model_status(aaedn_model* m);
+/* The greedy token of the last step (the next input), from the device
+ * state (synchronises). */
+int aaedn_model_next_token(aaedn_model* m, uint32_t* h_token);
 /* Kernels launched by one decode step. */
 uint32_t aaedn_model_kernels_per_step(const aaedn_model* m);
 /* Copy the last step's logits ([vocab]) / the greedy tokens generated so far. */

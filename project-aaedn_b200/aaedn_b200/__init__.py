@@ -48,6 +48,19 @@ class AbnHeader(ctypes.Structure):
                 ("ffn_dim", _u32), ("quant_type", ctypes.c_uint8)]
 
 
+class TpPlan(ctypes.Structure):
+    _fields_ = [(n, _u32) for n in ("n_heads", "n_kv_heads", "ffn_dim", "vocab", "q_head0", "kv_head0",
+                                    "ffn_row0", "vocab0", "o_k", "down_k")]
+
+
+def tp_plan(cfg, rank, size):
+    """The share of tensor-parallel rank `rank` of `size` (host only)."""
+    c = ModelConfig(**{k: cfg[k] for k, _ in ModelConfig._fields_})
+    p = TpPlan()
+    check(lib().aaedn_tp_plan_get(ctypes.byref(c), rank, size, ctypes.byref(p)))
+    return {k: getattr(p, k) for k, _ in TpPlan._fields_}
+
+
 class LayerHost(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd",
                                    "sq", "sk", "sv", "so", "sg", "su", "sd", "attn_norm", "ffn_norm")]
@@ -91,6 +104,12 @@ def lib():
         "aaedn_abn_read_header": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader)], _int),
         "aaedn_abn_read_payload": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader), _vp, _vp], _int),
         "aaedn_model_create": ([ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], _int),
+        "aaedn_model_create_tp": ([ctypes.POINTER(ModelConfig), _u32, _u32, ctypes.POINTER(_vp)], _int),
+        "aaedn_model_tp_handle": ([_vp, _vp], _int),
+        "aaedn_model_tp_connect": ([_vp, _vp], _int),
+        "aaedn_model_status": ([_vp], _int),
+        "aaedn_model_next_token": ([_vp, ctypes.POINTER(_u32)], _int),
+        "aaedn_tp_plan_get": ([ctypes.POINTER(ModelConfig), _u32, _u32, ctypes.POINTER(TpPlan)], _int),
         "aaedn_model_destroy": ([_vp], _int),
         "aaedn_model_config_get": ([_vp, ctypes.POINTER(ModelConfig)], _int),
         "aaedn_model_stream": ([_vp], _vp),
@@ -293,15 +312,57 @@ def synthetic_weights(cfg, seed):
     return w
 
 
-class Model:
-    """One aaedn_model (device arena, weights, paged KV cache, stream)."""
+TP_HANDLE_BYTES = 64
 
-    def __init__(self, cfg):
+
+class Model:
+    """One aaedn_model (device arena, weights, paged KV cache, stream).
+
+    tp=(rank, size) makes this process the tensor-parallel rank `rank` of
+    `size` (one process per GPU, that GPU current). Every rank then calls
+    tp_connect with the handles of all ranks (see connect_tp) before its
+    first step, and all ranks run the same calls with the same tokens."""
+
+    def __init__(self, cfg, tp=None):
         self.cfg = dict(cfg)
         c = ModelConfig(**{k: self.cfg[k] for k, _ in ModelConfig._fields_})
         h = _vp()
-        check(lib().aaedn_model_create(ctypes.byref(c), ctypes.byref(h)))
+        if tp is None or tp[1] == 1:
+            check(lib().aaedn_model_create(ctypes.byref(c), ctypes.byref(h)))
+            self.tp = (0, 1)
+        else:
+            check(lib().aaedn_model_create_tp(ctypes.byref(c), int(tp[0]), int(tp[1]), ctypes.byref(h)))
+            self.tp = (int(tp[0]), int(tp[1]))
         self.h = h
+
+    def tp_handle(self):
+        """This rank's peer handle (bytes) for the other ranks."""
+        out = np.zeros(TP_HANDLE_BYTES, np.uint8)
+        check(lib().aaedn_model_tp_handle(self.h, _p(out)))
+        return out.tobytes()
+
+    def tp_connect(self, handles):
+        """handles: the tp_handle() bytes of every rank, in rank order."""
+        buf = np.frombuffer(b"".join(handles), np.uint8).copy()
+        check(lib().aaedn_model_tp_connect(self.h, _p(buf)))
+
+    def connect_tp(self, group=None):
+        """Exchanges handles over torch.distributed and connects."""
+        import torch.distributed as dist
+        hs = [None] * self.tp[1]
+        dist.all_gather_object(hs, self.tp_handle(), group=group)
+        self.tp_connect(hs)
+
+    def next_token(self):
+        """The greedy token of the last step (synchronises)."""
+        t = _u32()
+        check(lib().aaedn_model_next_token(self.h, ctypes.byref(t)))
+        return int(t.value)
+
+    def status(self):
+        """Raises if a bounded device wait ran out or a position passed the
+        cache (synchronises)."""
+        check(lib().aaedn_model_status(self.h))
 
     def close(self):
         if getattr(self, "h", None):

@@ -23,6 +23,7 @@
 #include "gemv_q4.cuh"
 #include "gemv_tiled.cuh"
 #include "mega.cuh"
+#include "tp.cuh"
 #include "gemv_tma.cuh"
 
 namespace aaedn_dev
@@ -85,6 +86,8 @@ struct LmParams
     int stages;    // rows in the shared-memory ring, a multiple of consumers
     int consumers; // consumer warps that take rows (<= LM_CONSUMERS)
     int l2_hint;   // stream the rows with the L2 evict-first policy
+    int row0;      // token id of row 0 (tensor parallel: this rank's first row)
+    int defer;     // leave the per-CTA results (the ranks' argmax exchange finishes)
 };
 
 constexpr int LM_CONSUMERS = 8;
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
         if (acc > bv)
         {
             bv = acc;
-            bi = n;
+            bi = n + p.row0;
         }
     }
     if (lane == 0)
@@ -256,9 +259,13 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
             }
         p.part_val[blockIdx.x] = v;
         p.part_idx[blockIdx.x] = i;
-        __threadfence();
-        const unsigned prev = atomicAdd(&p.state->lm_counter, 1u);
-        s_last = prev == gridDim.x - 1 ? 1u : 0u;
+        s_last = 0u;
+        if (!p.defer)
+        {
+            __threadfence();
+            const unsigned prev = atomicAdd(&p.state->lm_counter, 1u);
+            s_last = prev == gridDim.x - 1 ? 1u : 0u;
+        }
     }
     named_bar_sync(1, NC * 32);
     if (!s_last)
@@ -435,6 +442,8 @@ int set_model_kernel_attrs()
         rc = set_gemv_attrs<PRO_PLAIN, EPI_RESIDUAL>();
     if (!rc)
         rc = set_gemv_attrs<PRO_RMSNORM, EPI_SWIGLU>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_PLAIN, EPI_STORE>();
     return rc;
 }
 
@@ -471,6 +480,18 @@ struct aaedn_model
     bool pdl = true;   // programmatic dependent launch inside the decode graph
     bool tiled = true; // tile-major repacking of the matrices whose shape allows it
     bool l2_hint = true; // weight streams with the L2 evict-first policy
+    // tensor parallelism: cfg holds this rank's dims (heads, ffn rows and
+    // lm_head rows of the rank), full the model's
+    aaedn_model_config full{};
+    int tp_rank = 0, tp_size = 1;
+    uint32_t v0 = 0;           // first lm_head row (token id) of this rank
+    uint32_t kpo = 0, kpd = 0; // K of o and down (padded to whole tiles when sharded)
+    uint8_t* tp_region = nullptr; // peer-visible: partials [2][dim], flags, argmax slots
+    size_t tp_region_bytes = 0;
+    void* tp_peer[TP_MAX] = {};
+    TpComm tp{};
+    bool tp_ready = false;
+    unsigned* tp_epoch = nullptr;
     // the whole step as one persistent kernel (decode_step_kernel)
     bool mega = false;
     int mega_S = 1, mega_ctas = 0, mega_R = 1;
@@ -505,9 +526,9 @@ static size_t plan_arena(aaedn_model* m, bool carve)
             tiled = m->tiled && tiles_ok(N, K);
         };
         mat(L.wqkv, L.sqkv, L.tqkv, qkv_rows, D);
-        mat(L.wo, L.so, L.to, D, H * hd);
+        mat(L.wo, L.so, L.to, D, m->kpo);
         mat(L.wgu, L.sgu, L.tgu, 2 * F, D);
-        mat(L.wd, L.sd, L.td, D, F);
+        mat(L.wd, L.sd, L.td, D, m->kpd);
         L.attn_norm = m->take<float>(D * 4);
         L.ffn_norm = m->take<float>(D * 4);
         L.k = m->take<float>((size_t)m->n_pages * KV * m->page_size * hd * 4);
@@ -515,7 +536,7 @@ static size_t plan_arena(aaedn_model* m, bool carve)
         if (carve)
             m->layers[l] = L;
     }
-    m->embedding = m->take<float>(V * D * 4);
+    m->embedding = m->take<float>((size_t)m->full.vocab * D * 4); // every rank: the whole table
     m->lm_head = m->take<float>(V * D * 4);
     m->final_norm = m->take<float>(D * 4);
     m->rope_cos = m->take<float>((size_t)c.max_seq * (hd / 2) * 4);
@@ -526,8 +547,8 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->page_table = m->take<int>((size_t)m->n_pages * 4);
     m->hidden = m->take<float>(D * 4);
     m->qbuf = m->take<float>(H * hd * 4);
-    m->attn_out = m->take<float>(H * hd * 4);
-    m->act = m->take<float>(F * 4);
+    m->attn_out = m->take<float>(std::max<size_t>(H * hd, m->kpo) * 4); // padding stays zero
+    m->act = m->take<float>(std::max<size_t>(F, m->kpd) * 4);
     m->logits = m->take<float>(V * 4);
     m->attn_part = m->take<float>(H * (size_t)std::max(m->attn_S, m->mega_S) * (hd + 4) * 4);
     m->attn_counters = m->take<unsigned>(KV * 4);
@@ -537,6 +558,7 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->d_gemv = m->take<GemvParams>((size_t)c.n_layers * 4 * sizeof(GemvParams));
     m->d_attn = m->take<AttnParams>((size_t)c.n_layers * sizeof(AttnParams));
     m->mega_bar = m->take<unsigned>((size_t)c.n_layers * 5 * 4);
+    m->tp_epoch = m->take<unsigned>(64);
     m->dbg_hidden = m->take<float>((size_t)c.n_layers * D * 4);
     return align_up(m->used, 256);
 }
@@ -628,18 +650,18 @@ static GemvParams o_params(const aaedn_model* m, uint32_t l)
     GemvParams o{};
     o.w = L.wo;
     o.s = L.so;
-    o.ldb = (size_t)H * hd;
+    o.ldb = (size_t)m->kpo;
     o.N = D;
-    o.K = H * hd;
+    o.K = (int)m->kpo;
     o.kt0 = 0;
-    o.kt1 = (H * hd + 127) / 128;
+    o.kt1 = ((int)m->kpo + 127) / 128;
     o.x = m->attn_out;
-    o.lda = (size_t)H * hd;
-    o.y = m->hidden;
+    o.lda = (size_t)m->kpo;
+    o.y = m->tp_size > 1 ? m->tp.part[m->tp_rank][0] : m->hidden; // sharded: this rank's partial
     o.ldc = (size_t)D;
     o.state = m->state;
     o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
-    o.scale_pairs = (((H * hd) >> 5) & 1) == 0;
+    o.scale_pairs = ((m->kpo >> 5) & 1) == 0;
     o.l2_hint = m->l2_hint;
     return o;
 }
@@ -677,18 +699,18 @@ static GemvParams down_params(const aaedn_model* m, uint32_t l)
     GemvParams dn{};
     dn.w = L.wd;
     dn.s = L.sd;
-    dn.ldb = (size_t)F;
+    dn.ldb = (size_t)m->kpd;
     dn.N = D;
-    dn.K = F;
+    dn.K = (int)m->kpd;
     dn.kt0 = 0;
-    dn.kt1 = (F + 127) / 128;
+    dn.kt1 = ((int)m->kpd + 127) / 128;
     dn.x = m->act;
-    dn.lda = (size_t)F;
-    dn.y = m->hidden;
+    dn.lda = (size_t)m->kpd;
+    dn.y = m->tp_size > 1 ? m->tp.part[m->tp_rank][1] : m->hidden;
     dn.ldc = (size_t)D;
     dn.state = m->state;
     dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
-    dn.scale_pairs = ((F >> 5) & 1) == 0;
+    dn.scale_pairs = ((m->kpd >> 5) & 1) == 0;
     dn.l2_hint = m->l2_hint;
     return dn;
 }
@@ -713,6 +735,8 @@ static LmParams lm_params(const aaedn_model* m)
     lp.stages = m->lm_stages;
     lp.consumers = m->lm_consumers;
     lp.l2_hint = m->l2_hint;
+    lp.row0 = (int)m->v0;
+    lp.defer = m->tp_size > 1 ? 1 : 0;
     return lp;
 }
 
@@ -768,7 +792,7 @@ static int setup_mega(aaedn_model* m)
 {
     m->mega = false;
     const char* e = std::getenv("AAEDN_MEGA");
-    if (!(e && e[0] == '1'))
+    if (!(e && e[0] == '1') || m->tp_size > 1)
         return AAEDN_OK;
     const aaedn_model_config& c = m->cfg;
     for (const DevLayer& L : m->layers)
@@ -846,9 +870,30 @@ static int enqueue_mega(aaedn_model* m, cudaStream_t st, unsigned long long* tra
     return AAEDN_OK;
 }
 
+// hidden += the sum of the ranks' partials in buffer buf (o: 0, down: 1)
+static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase)
+{
+    if (!m->tp_ready)
+        return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
+    TpReduceParams rp{};
+    rp.c = m->tp;
+    rp.hidden = m->hidden;
+    rp.dim = (int)m->cfg.dim;
+    rp.buf = buf;
+    rp.phase = phase;
+    rp.epoch = m->tp_epoch;
+    rp.state = m->state;
+    const int blocks = std::max(1, std::min(32, (int)(m->cfg.dim + 255) / 256));
+    tp_reduce_kernel<<<blocks, 256, 0, st>>>(rp);
+    AAEDN_LAUNCH_CHECK("tp_reduce_kernel");
+    return AAEDN_OK;
+}
+
 static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr,
                         int mask = K_ALL)
 {
+    if (m->tp_size > 1 && !m->tp_ready)
+        return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
     if (m->mega && !debug && !ev && mask == K_ALL)
         return enqueue_mega(m, st);
     // programmatic dependent launches between consecutive kernels (not when
@@ -887,9 +932,17 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         if ((rc = mark()))
             return rc;
-        // --- O projection + residual
+        // --- O projection + residual (sharded: this rank's partial, then the
+        // reduction over the ranks adds the sum to the residual)
         const GemvParams o = o_params(m, l);
-        rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
+        if (m->tp_size > 1)
+        {
+            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_STORE>(o, st, pdl, L.to) : AAEDN_OK;
+            if (!rc && (mask & K_O))
+                rc = tp_reduce(m, st, 0, 2 * (int)l);
+        }
+        else
+            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -903,7 +956,14 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         // --- down + residual
         const GemvParams dn = down_params(m, l);
-        rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
+        if (m->tp_size > 1)
+        {
+            rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_STORE>(dn, st, pdl, L.td) : AAEDN_OK;
+            if (!rc && (mask & K_DOWN))
+                rc = tp_reduce(m, st, 1, 2 * (int)l + 1);
+        }
+        else
+            rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -920,6 +980,27 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if (e != cudaSuccess)
             return set_error(AAEDN_ECUDA, "launch of lm_head_argmax_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
+        if (m->tp_size > 1)
+        {
+            TpArgmaxParams ap{};
+            ap.c = m->tp;
+            ap.part_val = m->lm_part_val;
+            ap.part_idx = m->lm_part_idx;
+            ap.n_parts = m->lm_ctas;
+            ap.phase = 2 * (int)c.n_layers;
+            ap.epoch = m->tp_epoch;
+            ap.state = m->state;
+            ap.out_tokens = m->out_tokens;
+            ap.max_seq = (int)c.max_seq;
+            tp_argmax_kernel<<<1, 256, 0, st>>>(ap);
+            AAEDN_LAUNCH_CHECK("tp_argmax_kernel");
+        }
+    }
+    if (m->tp_size > 1)
+    {
+        // one step's worth of epochs, whatever part of the step was enqueued
+        tp_epoch_kernel<<<1, 32, 0, st>>>(m->tp_epoch, 2u * c.n_layers + 1u);
+        AAEDN_LAUNCH_CHECK("tp_epoch_kernel");
     }
     if ((rc = mark()))
         return rc;
@@ -979,6 +1060,24 @@ static int write_state(aaedn_model* m, uint32_t pos, uint32_t n_prompt)
     return AAEDN_OK;
 }
 
+// Synchronises and reports the device-side error flag of the decode state:
+// 1 = a position past the cache, 2 = a weight-stream wait ran out, 3 = a
+// grid barrier of the persistent kernel ran out, 4 = a wait for another
+// tensor-parallel rank ran out. The flag stays set until aaedn_model_reset.
+static int device_status(aaedn_model* m)
+{
+    uint32_t* w = m->pinned + m->cfg.max_seq + 4;
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(w, &m->state->err, 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    switch (*w)
+    {
+    case 0: return AAEDN_OK;
+    case 1: return set_error(AAEDN_ESTATE, "decode step past the cache capacity (max_seq %u)", m->cfg.max_seq);
+    case 4: return set_error(AAEDN_ETIMEOUT, "a wait for another tensor-parallel rank ran out");
+    default: return set_error(AAEDN_ETIMEOUT, "a bounded device wait ran out (code %u)", *w);
+    }
+}
+
 static int put_tokens(aaedn_model* m, const uint32_t* h_tokens, size_t n)
 {
     // staging must not be rewritten while an earlier copy may still read it
@@ -995,28 +1094,81 @@ static int put_tokens(aaedn_model* m, const uint32_t* h_tokens, size_t n)
             return set_error(AAEDN_EINVAL, "null model");                                                    \
     } while (0)
 
-extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** out)
+extern "C" int aaedn_tp_plan_get(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size,
+                                 aaedn_tp_plan* out)
+{
+    if (!cfg || !out)
+        return set_error(AAEDN_EINVAL, "aaedn_tp_plan_get: null argument");
+    const aaedn_model_config& fc = *cfg;
+    if (tp_size != 1 && tp_size != 2 && tp_size != 4 && tp_size != 8)
+        return set_error(AAEDN_EINVAL, "tensor parallel size must be 1, 2, 4 or 8");
+    if (tp_rank >= tp_size || fc.n_kv_heads == 0 || fc.n_kv_heads % tp_size || fc.n_heads % tp_size ||
+        fc.ffn_dim % (32 * tp_size) || fc.vocab < tp_size)
+        return set_error(AAEDN_EINVAL,
+                         "rank %u of %u: n_heads, n_kv_heads and ffn_dim / 32 must divide by the tensor-parallel size",
+                         tp_rank, tp_size);
+    aaedn_tp_plan p{};
+    p.n_heads = fc.n_heads / tp_size;
+    p.n_kv_heads = fc.n_kv_heads / tp_size;
+    p.ffn_dim = fc.ffn_dim / tp_size;
+    const uint32_t vper = (fc.vocab + tp_size - 1) / tp_size;
+    p.vocab0 = tp_rank * vper;
+    p.vocab = p.vocab0 < fc.vocab ? std::min(vper, fc.vocab - p.vocab0) : 0u;
+    p.q_head0 = tp_rank * p.n_heads;
+    p.kv_head0 = tp_rank * p.n_kv_heads;
+    p.ffn_row0 = tp_rank * p.ffn_dim;
+    const uint32_t ko = p.n_heads * fc.head_dim, kd = p.ffn_dim;
+    // sharded K of o and down: padded to whole 128-column tiles (zero
+    // weights, zero activations) so the tile-major GEMV serves them
+    p.o_k = tp_size > 1 ? (ko + 127) / 128 * 128 : ko;
+    p.down_k = tp_size > 1 ? (kd + 127) / 128 * 128 : kd;
+    if (p.vocab == 0 || (p.n_heads * fc.head_dim) % 32)
+        return set_error(AAEDN_EINVAL, "rank %u of %u: no share left", tp_rank, tp_size);
+    *out = p;
+    return AAEDN_OK;
+}
+
+static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size, aaedn_model** out)
 {
     if (!cfg || !out)
         return set_error(AAEDN_EINVAL, "aaedn_model_create: null argument");
     *out = nullptr;
-    const aaedn_model_config& c = *cfg;
-    if (c.dim == 0 || c.n_layers == 0 || c.n_heads == 0 || c.n_kv_heads == 0 || c.head_dim == 0 || c.ffn_dim == 0 ||
-        c.vocab == 0 || c.max_seq == 0)
+    const aaedn_model_config& fc = *cfg;
+    if (fc.dim == 0 || fc.n_layers == 0 || fc.n_heads == 0 || fc.n_kv_heads == 0 || fc.head_dim == 0 || fc.ffn_dim == 0 ||
+        fc.vocab == 0 || fc.max_seq == 0)
         return set_error(AAEDN_EINVAL, "aaedn_model_create: zero dimension");
-    if (c.dim % 32 || (c.n_heads * c.head_dim) % 32 || c.ffn_dim % 32 || c.head_dim % 16 || c.dim % 4 ||
-        c.n_heads % c.n_kv_heads || c.head_dim > (uint32_t)ATTN_MAX_HD ||
-        (c.n_heads / c.n_kv_heads != 1 && c.n_heads / c.n_kv_heads != 2 && c.n_heads / c.n_kv_heads != 4 &&
-         c.n_heads / c.n_kv_heads != 8))
+    if (fc.dim % 32 || (fc.n_heads * fc.head_dim) % 32 || fc.ffn_dim % 32 || fc.head_dim % 16 || fc.dim % 4 ||
+        fc.n_heads % fc.n_kv_heads || fc.head_dim > (uint32_t)ATTN_MAX_HD ||
+        (fc.n_heads / fc.n_kv_heads != 1 && fc.n_heads / fc.n_kv_heads != 2 && fc.n_heads / fc.n_kv_heads != 4 &&
+         fc.n_heads / fc.n_kv_heads != 8))
         return set_error(AAEDN_EINVAL,
                          "aaedn_model_create: need dim, n_heads*head_dim, ffn_dim multiples of 32, head_dim a "
                          "multiple of 16 (<= %d), n_heads / n_kv_heads in {1, 2, 4, 8}",
                          ATTN_MAX_HD);
     // dim <= 16384: the lm_head ring holds x and at least two rows
-    if (c.dim > 16384 || c.ffn_dim > 32768 || c.max_seq > (1u << 20))
+    if (fc.dim > 16384 || fc.ffn_dim > 32768 || fc.max_seq > (1u << 20))
         return set_error(AAEDN_EINVAL, "aaedn_model_create: dimension too large (dim <= 16384, ffn_dim <= 32768)");
+    aaedn_tp_plan plan{};
+    {
+        const int prc = aaedn_tp_plan_get(&fc, tp_rank, tp_size, &plan);
+        if (prc)
+            return prc;
+    }
+    // this rank's dims: heads, kv heads, ffn rows, lm_head rows
+    aaedn_model_config lc = fc;
+    lc.n_heads = plan.n_heads;
+    lc.n_kv_heads = plan.n_kv_heads;
+    lc.ffn_dim = plan.ffn_dim;
+    lc.vocab = plan.vocab;
     aaedn_model* m = new aaedn_model();
-    m->cfg = c;
+    m->cfg = lc;
+    m->full = fc;
+    m->tp_rank = (int)tp_rank;
+    m->tp_size = (int)tp_size;
+    m->v0 = plan.vocab0;
+    m->kpo = plan.o_k;
+    m->kpd = plan.down_k;
+    const aaedn_model_config& c = m->cfg;
     {
         const char* e = std::getenv("AAEDN_PDL");
         m->pdl = !(e && e[0] == '0');
@@ -1104,6 +1256,82 @@ extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** o
     return AAEDN_OK;
 }
 
+extern "C" int aaedn_model_create(const aaedn_model_config* cfg, aaedn_model** out)
+{
+    return create_impl(cfg, 0, 1, out);
+}
+
+extern "C" int aaedn_model_create_tp(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size,
+                                     aaedn_model** out)
+{
+    int rc = create_impl(cfg, tp_rank, tp_size, out);
+    if (rc || tp_size == 1)
+        return rc;
+    aaedn_model* m = *out;
+    // the peer-visible region: partials [2][dim], flags [TP_MAX][4], argmax
+    // slots [TP_MAX] (one cudaMalloc: an IPC handle covers it)
+    const size_t part = (size_t)m->cfg.dim * 4;
+    m->tp_region_bytes = 2 * part + TP_MAX * 16 + TP_MAX * 8 + 256;
+    if (cudaMalloc(reinterpret_cast<void**>(&m->tp_region), m->tp_region_bytes) != cudaSuccess ||
+        cudaMemset(m->tp_region, 0, m->tp_region_bytes) != cudaSuccess)
+    {
+        aaedn_model_destroy(m);
+        *out = nullptr;
+        return set_error(AAEDN_ENOMEM, "aaedn_model_create_tp: peer region");
+    }
+    m->tp.rank = (int)tp_rank;
+    m->tp.size = (int)tp_size;
+    return AAEDN_OK;
+}
+
+// addresses inside a rank's region
+static void tp_layout(uint8_t* base, size_t dim, float*& p0, float*& p1, unsigned*& flags, float2*& best)
+{
+    p0 = reinterpret_cast<float*>(base);
+    p1 = p0 + dim;
+    flags = reinterpret_cast<unsigned*>(base + 2 * dim * 4);
+    best = reinterpret_cast<float2*>(base + 2 * dim * 4 + TP_MAX * 16);
+}
+
+extern "C" int aaedn_model_tp_handle(aaedn_model* m, uint8_t* h_handle)
+{
+    MODEL_OK(m);
+    if (m->tp_size < 2 || !h_handle)
+        return set_error(AAEDN_EINVAL, "aaedn_model_tp_handle: not a tensor-parallel model or null output");
+    cudaIpcMemHandle_t h;
+    AAEDN_CUDA_TRY(cudaIpcGetMemHandle(&h, m->tp_region));
+    static_assert(sizeof(h) == AAEDN_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(h_handle, &h, sizeof h);
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_tp_connect(aaedn_model* m, const uint8_t* h_handles)
+{
+    MODEL_OK(m);
+    if (m->tp_size < 2 || !h_handles)
+        return set_error(AAEDN_EINVAL, "aaedn_model_tp_connect: not a tensor-parallel model or null handles");
+    if (m->tp_ready)
+        return AAEDN_OK;
+    const size_t dim = m->cfg.dim;
+    for (int r = 0; r < m->tp_size; ++r)
+    {
+        uint8_t* base = m->tp_region;
+        if (r != m->tp_rank)
+        {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, h_handles + (size_t)r * AAEDN_TP_HANDLE_BYTES, sizeof h);
+            void* p = nullptr;
+            AAEDN_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+            m->tp_peer[r] = p;
+            base = static_cast<uint8_t*>(p);
+        }
+        tp_layout(base, dim, m->tp.part[r][0], m->tp.part[r][1], m->tp.flags[r], m->tp.best[r]);
+    }
+    m->tp.my_flags = m->tp.flags[m->tp_rank];
+    m->tp_ready = true;
+    return AAEDN_OK;
+}
+
 extern "C" int aaedn_model_destroy(aaedn_model* m)
 {
     if (!m)
@@ -1112,6 +1340,11 @@ extern "C" int aaedn_model_destroy(aaedn_model* m)
         cudaStreamSynchronize(m->stream);
     if (m->graph_exec)
         cudaGraphExecDestroy(m->graph_exec);
+    for (int r = 0; r < TP_MAX; ++r)
+        if (m->tp_peer[r])
+            cudaIpcCloseMemHandle(m->tp_peer[r]);
+    if (m->tp_region)
+        cudaFree(m->tp_region);
     if (m->arena)
         cudaFree(m->arena);
     if (m->pinned)
@@ -1127,7 +1360,7 @@ extern "C" int aaedn_model_config_get(const aaedn_model* m, aaedn_model_config* 
     MODEL_OK(m);
     if (!out)
         return set_error(AAEDN_EINVAL, "null output");
-    *out = m->cfg;
+    *out = m->full; // the model's dims (cfg holds this rank's share)
     return AAEDN_OK;
 }
 
@@ -1164,13 +1397,20 @@ static int upload_matrix(uint8_t* dw, uint16_t* ds, bool tiled, const uint8_t* c
     return AAEDN_OK;
 }
 
-static void copy_row(std::vector<uint8_t>& dd, std::vector<uint16_t>& ds, size_t drow, const uint8_t* sd,
-                     const uint16_t* ss, size_t srow, size_t K)
+// Copies columns [col0, col0 + ncols) of source row srow (Ks columns) into
+// device-order row drow of a Kd-column matrix (the rest of the row stays
+// zero: padding). Columns come in whole 32-blocks.
+static void copy_row(std::vector<uint8_t>& dd, std::vector<uint16_t>& ds, size_t drow, size_t Kd, const uint8_t* sd,
+                     const uint16_t* ss, size_t srow, size_t Ks, size_t col0, size_t ncols)
 {
-    std::memcpy(dd.data() + drow * K / 2, sd + srow * K / 2, K / 2);
-    std::memcpy(ds.data() + drow * K / 32, ss + srow * K / 32, K / 32 * 2);
+    std::memcpy(dd.data() + drow * Kd / 2, sd + srow * Ks / 2 + col0 / 2, ncols / 2);
+    std::memcpy(ds.data() + drow * Kd / 32, ss + srow * Ks / 32 + col0 / 32, ncols / 32 * 2);
 }
 
+// Weights arrive whole (the model's dims); a tensor-parallel rank keeps its
+// share: q rows of its heads, k/v rows of its kv heads, gate/up rows
+// [r F/T, (r+1) F/T), and the matching input columns of o and down (padded
+// to kpo / kpd with zero columns).
 extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn_layer_host* w)
 {
     MODEL_OK(m);
@@ -1179,8 +1419,11 @@ extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn
     if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->sq || !w->sk || !w->sv || !w->so ||
         !w->sg || !w->su || !w->sd)
         return set_error(AAEDN_EINVAL, "aaedn_model_set_layer: null tensor");
-    const aaedn_model_config& c = m->cfg;
+    const aaedn_model_config& c = m->cfg; // this rank's share
     const size_t D = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim;
+    const size_t Hf = m->full.n_heads, Ff = m->full.ffn_dim;
+    const size_t r = (size_t)m->tp_rank;
+    const size_t q0 = r * H * hd, k0 = r * KV * hd, f0 = r * F; // first source row / column of the share
     const DevLayer& L = m->layers[layer];
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     {
@@ -1190,21 +1433,25 @@ extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn
         for (size_t dr = 0; dr < rows; ++dr)
         {
             if (dr < H * hd)
-                copy_row(dd, ds, dr, w->wq, w->sq, (dr / hd) * hd + rope_pair_row(dr % hd, hd), D);
+                copy_row(dd, ds, dr, D, w->wq, w->sq, q0 + (dr / hd) * hd + rope_pair_row(dr % hd, hd), D, 0, D);
             else if (dr < (H + KV) * hd)
             {
                 const size_t rel = dr - H * hd;
-                copy_row(dd, ds, dr, w->wk, w->sk, (rel / hd) * hd + rope_pair_row(rel % hd, hd), D);
+                copy_row(dd, ds, dr, D, w->wk, w->sk, k0 + (rel / hd) * hd + rope_pair_row(rel % hd, hd), D, 0, D);
             }
             else
-                copy_row(dd, ds, dr, w->wv, w->sv, dr - (H + KV) * hd, D);
+                copy_row(dd, ds, dr, D, w->wv, w->sv, k0 + dr - (H + KV) * hd, D, 0, D);
         }
         int rc = upload_matrix(L.wqkv, L.sqkv, L.tqkv, dd.data(), ds.data(), rows, D);
         if (rc)
             return rc;
     }
     {
-        int rc = upload_matrix(L.wo, L.so, L.to, w->wo, w->so, D, H * hd);
+        std::vector<uint8_t> dd(D * m->kpo / 2, 0);
+        std::vector<uint16_t> ds(D * m->kpo / 32, 0);
+        for (size_t n = 0; n < D; ++n)
+            copy_row(dd, ds, n, m->kpo, w->wo, w->so, n, Hf * hd, q0, H * hd);
+        int rc = upload_matrix(L.wo, L.so, L.to, dd.data(), ds.data(), D, m->kpo);
         if (rc)
             return rc;
     }
@@ -1214,18 +1461,22 @@ extern "C" int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn
         std::vector<uint16_t> ds(rows * D / 32);
         for (size_t dr = 0; dr < rows; ++dr)
         {
-            const size_t j = dr / 16, r = dr % 16;
-            if (r < 8)
-                copy_row(dd, ds, dr, w->wg, w->sg, 8 * j + r, D);
+            const size_t j = dr / 16, rr = dr % 16;
+            if (rr < 8)
+                copy_row(dd, ds, dr, D, w->wg, w->sg, f0 + 8 * j + rr, D, 0, D);
             else
-                copy_row(dd, ds, dr, w->wu, w->su, 8 * j + r - 8, D);
+                copy_row(dd, ds, dr, D, w->wu, w->su, f0 + 8 * j + rr - 8, D, 0, D);
         }
         int rc = upload_matrix(L.wgu, L.sgu, L.tgu, dd.data(), ds.data(), rows, D);
         if (rc)
             return rc;
     }
     {
-        int rc = upload_matrix(L.wd, L.sd, L.td, w->wd, w->sd, D, F);
+        std::vector<uint8_t> dd(D * m->kpd / 2, 0);
+        std::vector<uint16_t> ds(D * m->kpd / 32, 0);
+        for (size_t n = 0; n < D; ++n)
+            copy_row(dd, ds, n, m->kpd, w->wd, w->sd, n, Ff, f0, F);
+        int rc = upload_matrix(L.wd, L.sd, L.td, dd.data(), ds.data(), D, m->kpd);
         if (rc)
             return rc;
     }
@@ -1243,18 +1494,20 @@ extern "C" int aaedn_model_set_globals(aaedn_model* m, const float* h_embedding,
     const aaedn_model_config& c = m->cfg;
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     if (h_embedding)
-        AAEDN_CUDA_TRY(cudaMemcpy(m->embedding, h_embedding, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice));
+        AAEDN_CUDA_TRY(
+            cudaMemcpy(m->embedding, h_embedding, (size_t)m->full.vocab * c.dim * 4, cudaMemcpyHostToDevice));
     if (h_final_norm)
         AAEDN_CUDA_TRY(cudaMemcpy(m->final_norm, h_final_norm, (size_t)c.dim * 4, cudaMemcpyHostToDevice));
-    if (h_lm_head)
-        AAEDN_CUDA_TRY(cudaMemcpy(m->lm_head, h_lm_head, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice));
+    if (h_lm_head) // the whole matrix in; this rank keeps rows [v0, v0 + its share)
+        AAEDN_CUDA_TRY(cudaMemcpy(m->lm_head, h_lm_head + (size_t)m->v0 * c.dim, (size_t)c.vocab * c.dim * 4,
+                                  cudaMemcpyHostToDevice));
     return AAEDN_OK;
 }
 
 extern "C" int aaedn_model_synthesize(aaedn_model* m, uint64_t seed)
 {
     MODEL_OK(m);
-    const aaedn_model_config& c = m->cfg;
+    const aaedn_model_config& c = m->full; // whole tensors: set_layer keeps this rank's share
     const size_t D = c.dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads, F = c.ffn_dim, V = c.vocab;
     struct Mat
     {
@@ -1318,18 +1571,19 @@ extern "C" int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, siz
 {
     MODEL_OK(m);
     const aaedn_model_config& c = m->cfg;
+    const uint32_t V = m->full.vocab;
     if (n == 0 || !h_tokens) // src/transformer.cpp:130-135: zero logits
     {
         if (h_logits)
-            std::memset(h_logits, 0, (size_t)c.vocab * 4);
+            std::memset(h_logits, 0, (size_t)V * 4);
         return AAEDN_OK;
     }
     for (size_t i = 0; i < n; ++i)
-        if (h_tokens[i] >= c.vocab) // src/transformer.cpp:137-142
+        if (h_tokens[i] >= V) // src/transformer.cpp:137-142
         {
             if (h_logits)
-                std::memset(h_logits, 0, (size_t)c.vocab * 4);
-            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_tokens[i], c.vocab);
+                std::memset(h_logits, 0, (size_t)V * 4);
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_tokens[i], V);
         }
     if ((size_t)m->h_pos + n > c.max_seq)
         return set_error(AAEDN_ESTATE, "sequence full: pos %u + %zu > max_seq %u", m->h_pos, n, c.max_seq);
@@ -1341,10 +1595,10 @@ extern "C" int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, siz
     if (rc)
         return rc;
     m->h_pos += (uint32_t)n;
-    if (h_logits)
-        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
-    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-    return AAEDN_OK;
+    if (h_logits) // a tensor-parallel rank fills its own vocabulary slice
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits + m->v0, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost,
+                                       m->stream));
+    return device_status(m);
 }
 
 extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, size_t n_prompt, size_t n_new,
@@ -1355,8 +1609,8 @@ extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, si
     if (!h_prompt || n_prompt == 0 || (n_new && !h_out))
         return set_error(AAEDN_EINVAL, "aaedn_model_generate: empty prompt or null output");
     for (size_t i = 0; i < n_prompt; ++i)
-        if (h_prompt[i] >= c.vocab)
-            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_prompt[i], c.vocab);
+        if (h_prompt[i] >= m->full.vocab)
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_prompt[i], m->full.vocab);
     const size_t steps = n_prompt + (n_new ? n_new - 1 : 0);
     if ((size_t)m->h_pos + steps > c.max_seq)
         return set_error(AAEDN_ESTATE, "sequence full: pos %u + %zu steps > max_seq %u", m->h_pos, steps, c.max_seq);
@@ -1370,8 +1624,7 @@ extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, si
     m->h_pos += (uint32_t)steps;
     if (n_new)
         AAEDN_CUDA_TRY(cudaMemcpyAsync(h_out, m->out_tokens, n_new * 4, cudaMemcpyDeviceToHost, m->stream));
-    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-    return AAEDN_OK;
+    return device_status(m);
 }
 
 extern "C" int aaedn_model_decode_steps(aaedn_model* m, size_t n_steps)
@@ -1393,8 +1646,8 @@ extern "C" int aaedn_model_logits(aaedn_model* m, float* h_logits)
     MODEL_OK(m);
     if (!h_logits)
         return set_error(AAEDN_EINVAL, "null output");
-    AAEDN_CUDA_TRY(
-        cudaMemcpyAsync(h_logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits + m->v0, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                   m->stream));
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     return AAEDN_OK;
 }
@@ -1414,8 +1667,8 @@ extern "C" int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* 
 {
     MODEL_OK(m);
     const aaedn_model_config& c = m->cfg;
-    if (token >= c.vocab)
-        return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", token, c.vocab);
+    if (token >= m->full.vocab)
+        return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", token, m->full.vocab);
     if (m->h_pos + 1 > c.max_seq)
         return set_error(AAEDN_ESTATE, "sequence full");
     int rc = put_tokens(m, &token, 1);
@@ -1430,7 +1683,8 @@ extern "C" int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* 
         AAEDN_CUDA_TRY(cudaMemcpyAsync(h_hidden, m->dbg_hidden, (size_t)c.n_layers * c.dim * 4,
                                        cudaMemcpyDeviceToHost, m->stream));
     if (h_logits)
-        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+        AAEDN_CUDA_TRY(
+            cudaMemcpyAsync(h_logits + m->v0, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     return AAEDN_OK;
 }
@@ -1612,4 +1866,22 @@ extern "C" int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t ca
     if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess)
         rc = set_error(AAEDN_ECUDA, "trace step sync");
     return rc;
+}
+
+extern "C" int aaedn_model_status(aaedn_model* m)
+{
+    MODEL_OK(m);
+    return device_status(m);
+}
+
+extern "C" int aaedn_model_next_token(aaedn_model* m, uint32_t* h_token)
+{
+    MODEL_OK(m);
+    if (!h_token)
+        return set_error(AAEDN_EINVAL, "null output");
+    uint32_t* w = m->pinned + m->cfg.max_seq + 5;
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(w, &m->state->next_token, 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    *h_token = *w;
+    return AAEDN_OK;
 }
