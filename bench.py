@@ -318,8 +318,22 @@ def run_ours(args):
     # the dequant-GEMVs, only attention, ...) replayed P times back to back,
     # so the figures carry the same launch overlap as the decode graph and no
     # event overhead between kernels
-    parts = model.profile_parts(reps=P)
     L = cfg["n_layers"]
+    if tp:
+        # a part of a tensor-parallel step alone would wait for partials its
+        # peers never send: the split is taken from whole steps (per-kernel
+        # events, no launch overlap)
+        pk = np.stack([model.profile_step() for _ in range(max(1, P))]).mean(0)
+        # entries: per layer qkv, attention, o, gate/up, down (the last down
+        # with the final reduction); then lm_head with the argmax exchange
+        n5 = 5 * L
+        parts = {"step": float(pk.sum()), "lm_head": float(pk[n5])}
+        lay = pk[:n5].reshape(L, 5)
+        for i, k in enumerate(("qkv", "attention", "o", "gate_up", "down")):
+            parts[k] = float(lay[:, i].sum())
+        parts["gemv"] = parts["qkv"] + parts["o"] + parts["gate_up"] + parts["down"]
+    else:
+        parts = model.profile_parts(reps=P)
     shapes = gemv_shapes(cfg)
     gemv_total_ms = parts["gemv"]
     gemv_total_bytes = sum(gemv_bytes(*shapes[k]) for k in ("qkv", "o", "gate_up", "down"))
@@ -368,7 +382,8 @@ def run_ours(args):
                          "kernel": "gemv_tiled_i8_kernel (the 4 dequant-GEMVs of every layer, M=1)",
                          "launches_per_step": 4 * L, "bytes_per_launch_avg": gemv_total_bytes * share / 4,
                          "bytes_per_step": gemv_total_bytes * share * L,
-                         "timing": "sub-graph of the step's GEMVs replayed back to back, CUDA events"},
+                         "timing": ("per-kernel CUDA events inside whole steps" if tp else
+                                    "sub-graph of the step's GEMVs replayed back to back, CUDA events")},
             "decode_step": {"algorithmic_bytes": sb, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
                             **kernel_split},
             "cpu_baseline": cpu,

@@ -36,7 +36,13 @@ enum
     // x = the attention output, merged here from the per-split partial
     // results (max, sum, unnormalised sum of V rows) of every head
     PRO_ATTN_COMBINE = 3,
+    // tensor parallel: x = p.x + the sum over ranks of their partials
+    // (read from the peers once their flags show them complete), then the
+    // RMSNorm; CTA 0 stores the summed x to hidden_out
+    PRO_TP_RMSNORM = 4,
 };
+
+
 
 enum
 {
@@ -45,6 +51,10 @@ enum
     EPI_RESIDUAL = 2,
     EPI_QKV_ROPE = 3,
     EPI_SWIGLU = 4,
+    // tensor parallel: the rows of this rank's partial sum go to its slot of
+    // its own receive buffer; the kernel's last CTA pushes the slot to every
+    // other rank through peer memory
+    EPI_TP_PUSH = 5,
 };
 
 // Decode state that lives on the device so a whole step can be replayed as
@@ -59,6 +69,57 @@ struct DecodeState
     uint32_t err;        // sticky device-side error flag
     uint32_t pad[3];
 };
+
+constexpr int TP_MAX = 8;
+
+// The peer-visible regions of the tensor-parallel ranks (CUDA IPC): each
+// holds partials [2][dim] floats, flag words (one per writer rank, 16 bytes
+// apart) and argmax slots.
+struct TpComm
+{
+    // receive buffers of every rank (own included): recv[p] + (src * 2 +
+    // buf) * dim holds source rank src's partial `buf` (0: o, 1: down)
+    float* recv[TP_MAX];
+    unsigned* flags[TP_MAX]; // flag words of every rank: flags[p][4 * w] = epoch written by w
+    float2* best[TP_MAX];    // argmax slots of every rank: best[p][w] = (value, index) of w
+    unsigned* my_flags;      // == flags[rank]
+    int rank, size, dim;
+};
+
+constexpr uint64_t TP_WAIT_LIMIT_NS = 2000000000ull; // 2 s
+
+
+
+__device__ __forceinline__ bool tp_wait_flags(const TpComm& c, unsigned E, DecodeState* st)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (int w = 0; w < c.size; ++w)
+    {
+        volatile unsigned* f = c.my_flags + 4 * w;
+        while (*f < E)
+        {
+            if (globaltimer_ns() - t0 > TP_WAIT_LIMIT_NS)
+            {
+                st->err = 4u;
+                return false;
+            }
+            __nanosleep(32);
+        }
+    }
+    return true;
+}
+
+// Raise this rank's flag for epoch E in every rank's flag array (itself
+// included), after its earlier writes are visible to the peers.
+__device__ __forceinline__ void tp_signal(const TpComm& c, unsigned E)
+{
+    __threadfence_system();
+    for (int p = 0; p < c.size; ++p)
+    {
+        volatile unsigned* f = c.flags[p] + 4 * c.rank;
+        *f = E;
+    }
+}
 
 struct GemvParams
 {
@@ -96,6 +157,14 @@ struct GemvParams
     const float* attn_part;
     int attn_S, attn_pstride;
     int l2_hint; // stream the weights with the L2 evict-first policy
+    // tensor parallel (zero otherwise): PRO_TP_RMSNORM waits for epoch
+    // *tp_epoch + tp_wait_phase + 1 and adds partial buffer tp_buf; a
+    // partial-writing GEMV (tp_sig) raises epoch *tp_epoch + tp_sig_phase + 1
+    // in every rank once its last CTA is done (tp_counter: last-CTA count)
+    TpComm tpc;
+    const unsigned* tp_epoch;
+    unsigned* tp_counter;
+    int tp_wait_phase, tp_buf, tp_sig, tp_sig_phase;
     // scales can be staged as aligned u32 pairs (even scales per row, 4-byte
     // aligned array)
     bool scale_pairs;
@@ -297,7 +366,7 @@ template <int NM, int EPI, int S = GEMV_WARPS>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* rb, int group, int lane,
                                               float post = 1.0f, const EpiCache* ec = nullptr, int gl = 0)
 {
-    if constexpr (EPI == EPI_STORE || EPI == EPI_ACCUM || EPI == EPI_RESIDUAL)
+    if constexpr (EPI == EPI_STORE || EPI == EPI_ACCUM || EPI == EPI_RESIDUAL || EPI == EPI_TP_PUSH)
     {
         for (int idx = lane; idx < NM * 16; idx += 32)
         {
@@ -309,6 +378,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
             for (int ss = 0; ss < S; ++ss)
                 v += rb[(m * S + ss) * 16 + rr];
             v *= post; // the RMSNorm factor of the warp-built operand (1: exact no-op)
+            if constexpr (EPI == EPI_TP_PUSH)
+            {
+                // this rank's slot of its own receive buffer (the kernel's last
+                // CTA then copies the whole partial to the other ranks)
+                p.tpc.recv[p.tpc.rank][((size_t)p.tpc.rank * 2 + p.tp_buf) * p.tpc.dim + row] = v;
+                continue;
+            }
             float* yp = p.y + (size_t)m * p.ldc + row;
             if constexpr (EPI == EPI_STORE)
                 *yp = v;

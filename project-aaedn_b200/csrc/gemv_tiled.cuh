@@ -20,10 +20,12 @@
 // interleaved as four independent accumulator chains.
 #pragma once
 
-#include "gemv_tma.cuh"
+#include "gemv_q4.cuh"
 
 namespace aaedn_dev
 {
+
+constexpr uint64_t GEMV_WAIT_LIMIT_NS = 2000000000ull; // 2 s: bound of every mbarrier wait
 
 constexpr int GT_CONSUMERS = 16;
 constexpr int GT_THREADS = (GT_CONSUMERS + 1) * 32;
@@ -45,193 +47,6 @@ inline size_t tiled_bytes(size_t N, size_t K) { return N * K / 2 + N * K / 32 * 
 // Repacks row-major codes/scales ([N][K], K % 128 == 0, N % 16 == 0).
 void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t K, uint8_t* out);
 
-inline size_t gemv_tiled_smem_bytes(int ntile)
-{
-    return (size_t)GT_STAGES * GT_STAGE_BYTES + (size_t)GT_STAGES * 16 + (size_t)(ntile + 1) * 512 +
-           (size_t)ntile * 16 + (size_t)2 * GT_CONSUMERS * 16 * 4 + 64 * 4;
-}
-
-template <int PRO, int EPI>
-__global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_kernel(const GemvParams p)
-{
-    constexpr int NS = GT_STAGES;
-    constexpr int NC = GT_CONSUMERS;
-    constexpr int NCT = NC * 32;
-    constexpr int CT = GT_CHUNK_TILES;
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int ntile = p.K >> 7; // the whole K: tiled weights are only used unchunked
-    const int nchunk = (ntile + CT - 1) / CT;
-    uint8_t* ring = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GT_STAGE_BYTES); // full[NS], empty[NS]
-    uint4* frag = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + (size_t)NS * 16);
-    float* tb = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) + (size_t)(ntile + 1) * 512);
-    float* red = tb + (size_t)ntile * 4; // [2][NC][16]
-    float* misc = red + 2 * NC * 16;
-    __shared__ int s_abort_mem;
-    volatile int& s_abort = s_abort_mem;
-
-    pdl_launch_dependents();
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_groups = p.N >> 4;
-    const int my_groups = blockIdx.x < n_groups ? (n_groups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const uint32_t ring_a = smem_addr(ring);
-    const uint32_t full_a = smem_addr(bars), empty_a = full_a + NS * 8;
-    const size_t group_bytes = (size_t)ntile * GT_TILE_BYTES;
-
-    if (tid == 0)
-    {
-        for (int i = 0; i < NS; ++i)
-        {
-            mbar_init(full_a + 8 * i, 1);
-            mbar_init(empty_a + 8 * i, NC);
-        }
-        mbar_init_fence();
-        s_abort = 0;
-    }
-    __syncthreads();
-
-    if (warp == NC)
-    {
-        // ---------------- producer warp: one bulk copy per chunk ----------------
-        uint32_t q = 0;
-        bool ok = true;
-        for (int gl = 0; gl < my_groups && ok; ++gl)
-        {
-            const uint8_t* gsrc = p.w + (size_t)(blockIdx.x + gl * gridDim.x) * group_bytes;
-            for (int c = 0; c < nchunk; ++c, ++q)
-            {
-                const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-                const uint32_t stage = q % NS, use = q / NS;
-                if (use > 0 && !mbar_wait_bounded(empty_a + 8 * stage, (use - 1) & 1, GEMV_WAIT_LIMIT_NS))
-                {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0)
-                {
-                    const uint32_t bytes = (uint32_t)tiles * GT_TILE_BYTES;
-                    mbar_arrive_expect_tx(full_a + 8 * stage, bytes);
-                    bulk_g2s(ring_a + stage * GT_STAGE_BYTES, gsrc + (size_t)c * CT * GT_TILE_BYTES, bytes,
-                             full_a + 8 * stage);
-                }
-                __syncwarp();
-            }
-        }
-        if (!ok)
-        {
-            s_abort = 1;
-            if (lane == 0 && p.state)
-                p.state->err = 2u;
-        }
-        // drain: every issued chunk has landed before the CTA may exit
-        for (uint32_t k = (q > NS ? q - NS : 0); k < q; ++k)
-            mbar_wait_bounded(full_a + 8 * (k % NS), (k / NS) & 1, GEMV_WAIT_LIMIT_NS);
-        return;
-    }
-
-    // ---------------- consumer warps ----------------
-    pdl_wait();
-    gemv_build_frags<1, PRO, NCT>(p, frag, tb, misc, ntile);
-    if (tid < 32)
-        frag[(size_t)ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
-    named_bar_sync(1, NCT);
-
-    const int g = lane >> 2, t = lane & 3;
-    const bool bact = (g >> 1) == t;
-    const int la = 2 * t + (g & 1);
-    const uint32_t f_base = bact ? smem_addr(frag) + (uint32_t)la * 16 : smem_addr(frag) + (uint32_t)ntile * 512;
-    const uint32_t f_step = bact ? 512u : 0u;
-    const uint32_t tb_base = smem_addr(tb) + (uint32_t)t * 4;
-    bool ok = true;
-    uint32_t q = 0;
-    for (int gl = 0; gl < my_groups; ++gl)
-    {
-        const int group = blockIdx.x + gl * gridDim.x;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        for (int c = 0; c < nchunk && ok; ++c, ++q)
-        {
-            const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-            const uint32_t stage = q % NS;
-            if (!mbar_wait_bounded(full_a + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
-            {
-                ok = false;
-                s_abort = 1;
-                break;
-            }
-            if (warp < tiles)
-            {
-                const uint32_t st = ring_a + stage * GT_STAGE_BYTES;
-                const bool two = warp + NC < tiles;
-                const int ia = warp, ib = two ? warp + NC : warp;
-                uint4 w0[2], w1[2];
-                uint16_t sh0[2], sh1[2];
-                uint32_t fa[2];
-                float tbv[2];
-#pragma unroll
-                for (int k = 0; k < 2; ++k)
-                {
-                    const int i = k ? ib : ia, tt = c * CT + i;
-                    w0[k] = lds128(st + i * 1024 + lane * 16);
-                    w1[k] = lds128(st + i * 1024 + 512 + lane * 16);
-                    const uint32_t sa = st + tiles * 1024 + i * 128 + lane * 2; // u16 scales
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh0[k]) : "r"(sa));
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh1[k]) : "r"(sa + 64));
-                    fa[k] = f_base + (uint32_t)tt * f_step;
-                    tbv[k] = ldsf(tb_base + (uint32_t)tt * 16);
-                }
-                float d[2][2][4] = {}; // [tile][even/odd k-step][accumulator]
-#pragma unroll
-                for (int qq = 0; qq < 4; ++qq)
-                {
-#pragma unroll
-                    for (int k = 0; k < 2; ++k)
-                    {
-                        const uint32_t wa = u4get(w0[k], qq), wb = u4get(w1[k], qq);
-                        const uint4 b = lds128(fa[k] + qq * 128);
-                        float* dd = d[k][qq & 1];
-                        mma_bf16_16816(dd[0], dd[1], dd[2], dd[3], nib_e0(wa), nib_e0(wb), nib_e1(wa), nib_e1(wb),
-                                       b.x, b.y);
-                        mma_bf16_16816(dd[0], dd[1], dd[2], dd[3], nib_e2(wa), nib_e2(wb), nib_e3(wa), nib_e3(wb),
-                                       b.z, b.w);
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < 2; ++k)
-                {
-                    if (k == 1 && !two)
-                        break;
-                    const float sc0 = decode_scale<AAEDN_SCALE_F16>(sh0[k]);
-                    const float sc1 = decode_scale<AAEDN_SCALE_F16>(sh1[k]);
-                    acc0 = fmaf(sc0, ((d[k][0][0] + d[k][1][0]) + (d[k][0][1] + d[k][1][1])) - tbv[k], acc0);
-                    acc1 = fmaf(sc1, ((d[k][0][2] + d[k][1][2]) + (d[k][0][3] + d[k][1][3])) - tbv[k], acc1);
-                }
-            }
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(empty_a + 8 * stage);
-        }
-        float* rb = red + (size_t)(gl & 1) * NC * 16;
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-        if (t == 0)
-        {
-            rb[warp * 16 + g] = acc0;
-            rb[warp * 16 + g + 8] = acc1;
-        }
-        named_bar_sync(1, NCT);
-        if (!ok || s_abort)
-        {
-            if (lane == 0 && p.state)
-                p.state->err = 2u;
-            break;
-        }
-        if (warp == (gl & (NC - 1)))
-            gemv_epilogue<1, EPI, NC>(p, rb, group, lane);
-    }
-}
-
 // ---------------------------------------------------------------------------
 // Integer dot-product engine.
 //
@@ -246,224 +61,6 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_kernel(const GemvPar
 // digit) pairs, so one mma yields digits (0,1) and a second digits (2,3),
 // and four k-steps complete the tile's 4 blocks with nothing rounded.
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d)
-{
-    return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) |
-           ((uint32_t)(d & 0xFF) << 24);
-}
-
-// Base-128 digits of v, |v| <= 127.5.
-__device__ __forceinline__ void digits4(float v, int (&d)[4])
-{
-    float r = fminf(fmaxf(rintf(v), -127.0f), 127.0f);
-    d[0] = (int)r;
-    r = (v - r) * 128.0f; // exact: |v - rint(v)| <= 1/2 (plus the clamp)
-#pragma unroll
-    for (int i = 1; i < 4; ++i)
-    {
-        const float q = rintf(r);
-        d[i] = (int)q;
-        r = (r - q) * 128.0f;
-    }
-}
-
-// Writes the B operands of tiles [0, ntile) to frag[tile][word s][lane g][4
-// words] (16 B; the active lanes are g = 2*tb + j for block tb of the tile
-// and digit parity j: words (digit j even-code elements, digit j odd, digit
-// 2+j even, digit 2+j odd)) and the zero tile after them; misc[0] receives
-// the output factor max|x| / (127 * 128). NTH threads (named barrier 1).
-//
-// One pass over x: item it = tid + NTH * k is 8 consecutive elements (one
-// code word of one block); a thread parks its items' raw values in the very
-// 32 bytes of frag their digits will occupy, so between the reduction (sum
-// of squares, max) and the digits the activation stays on chip, it crosses
-// L2 once and the CTA synchronises twice.
-template <int PRO, int NTH>
-__device__ __forceinline__ void gemv_build_i8(const GemvParams& p, uint4* frag, float* misc, int ntile)
-{
-    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* src = p.x;
-    if constexpr (PRO == PRO_EMBED_RMSNORM)
-    {
-        const uint32_t pos = p.state->pos;
-        const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
-        src = p.embedding + (size_t)tok * p.K;
-    }
-    const int items = ntile * 16;
-    float ss = 0.0f, mx = 0.0f;
-    bool finite = true;
-    for (int it = tid; it < items; it += NTH)
-    {
-        const int tile = it >> 4, tb = (it >> 2) & 3, s = it & 3;
-        const int k0 = tile * 128 + tb * 32 + s * 8;
-        float4 a, b;
-        if constexpr (PRO == PRO_ATTN_COMBINE)
-        {
-            // elements k0..k0+7 of head h: the merge of its S split results,
-            // in split order, as the attention kernel's own merge does; all
-            // loads of up to SU splits are issued at once
-            constexpr int SU = 16;
-            const int hd = p.head_dim, h = k0 / hd, d0 = k0 - h * hd, S = p.attn_S, ps = p.attn_pstride;
-            const float* pb = p.attn_part + (size_t)h * S * ps;
-            float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, den = 0.0f;
-            if (S <= SU)
-            {
-                float ms[SU], ls[SU];
-#pragma unroll
-                for (int s2 = 0; s2 < SU; ++s2)
-                {
-                    const float2 ml = s2 < S ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)s2 * ps + hd))
-                                             : make_float2(-INFINITY, 0.0f);
-                    ms[s2] = ml.x;
-                    ls[s2] = ml.y;
-                }
-                float M = -INFINITY;
-#pragma unroll
-                for (int s2 = 0; s2 < SU; ++s2)
-                    M = fmaxf(M, ms[s2]);
-#pragma unroll
-                for (int s2 = 0; s2 < SU; ++s2)
-                    if (s2 < S)
-                    {
-                        const float* pv = pb + (size_t)s2 * ps + d0;
-                        const float4 va = __ldcg(reinterpret_cast<const float4*>(pv));
-                        const float4 vb = __ldcg(reinterpret_cast<const float4*>(pv + 4));
-                        const float w = (ms[s2] == -INFINITY) ? 0.0f : expf(ms[s2] - M);
-                        num[0] = fmaf(va.x, w, num[0]);
-                        num[1] = fmaf(va.y, w, num[1]);
-                        num[2] = fmaf(va.z, w, num[2]);
-                        num[3] = fmaf(va.w, w, num[3]);
-                        num[4] = fmaf(vb.x, w, num[4]);
-                        num[5] = fmaf(vb.y, w, num[5]);
-                        num[6] = fmaf(vb.z, w, num[6]);
-                        num[7] = fmaf(vb.w, w, num[7]);
-                        den = fmaf(ls[s2], w, den);
-                    }
-            }
-            else
-            {
-                float M = -INFINITY;
-                for (int s2 = 0; s2 < S; ++s2)
-                    M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
-                for (int s2 = 0; s2 < S; ++s2)
-                {
-                    const float* pv = pb + (size_t)s2 * ps;
-                    const float ms = __ldcg(pv + hd);
-                    const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        num[c] = fmaf(__ldcg(pv + d0 + c), w, num[c]);
-                    den = fmaf(__ldcg(pv + hd + 1), w, den);
-                }
-            }
-            float o[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                o[c] = den > 0.0f ? num[c] / den : 0.0f;
-            a = make_float4(o[0], o[1], o[2], o[3]);
-            b = make_float4(o[4], o[5], o[6], o[7]);
-        }
-        else
-        {
-            // L2 loads: in the persistent step kernel x was written by other
-            // CTAs after this SM may have cached an older copy in L1
-            a = __ldcg(reinterpret_cast<const float4*>(src + k0));
-            b = __ldcg(reinterpret_cast<const float4*>(src + k0 + 4));
-        }
-        if constexpr (PRO == PRO_EMBED_RMSNORM)
-            if (blockIdx.x == 0)
-            {
-                *reinterpret_cast<float4*>(p.hidden_out + k0) = a;
-                *reinterpret_cast<float4*>(p.hidden_out + k0 + 4) = b;
-            }
-        float4* park = reinterpret_cast<float4*>(frag + ((size_t)tile * 4 + s) * 8 + 2 * tb);
-        park[0] = a;
-        park[1] = b;
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-        if constexpr (NORM)
-        {
-            const float4 ga = __ldg(reinterpret_cast<const float4*>(p.gain + k0));
-            const float4 gb = __ldg(reinterpret_cast<const float4*>(p.gain + k0 + 4));
-            gv[0] = ga.x, gv[1] = ga.y, gv[2] = ga.z, gv[3] = ga.w;
-            gv[4] = gb.x, gv[5] = gb.y, gv[6] = gb.z, gv[7] = gb.w;
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-        {
-            if constexpr (NORM)
-                ss = fmaf(v[c], v[c], ss);
-            const float a8 = fabsf(v[c] * gv[c]);
-            finite = finite && (a8 <= 3.0e38f);
-            mx = fmaxf(mx, a8);
-        }
-    }
-    // one reduction round for both: warp, then the NTH/32 warp results in
-    // fixed order (deterministic)
-    ss = warp_sum(ss);
-    mx = warp_max(finite ? mx : __int_as_float(0x7f800000));
-    if (lane == 0)
-    {
-        misc[8 + warp] = ss;
-        misc[8 + NTH / 32 + warp] = mx;
-    }
-    named_bar_sync(1, NTH);
-    float tss = 0.0f, tmx = 0.0f;
-    for (int i = 0; i < NTH / 32; ++i)
-    {
-        tss += misc[8 + i];
-        tmx = fmaxf(tmx, misc[8 + NTH / 32 + i]);
-    }
-    float rms = 1.0f;
-    if constexpr (NORM)
-        rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tss, (float)p.K), p.eps)); // src/rmsnorm.cpp:34
-    tmx *= rms;
-    const bool bad = !(tmx <= 3.0e38f);
-    const float inv = (tmx > 0.0f && !bad) ? 127.0f / tmx : 0.0f;
-    for (int it = tid; it < items; it += NTH)
-    {
-        const int tile = it >> 4, tb = (it >> 2) & 3, s = it & 3;
-        const int k0 = tile * 128 + tb * 32 + s * 8;
-        uint4* dst = frag + ((size_t)tile * 4 + s) * 8 + 2 * tb;
-        const float4 a = reinterpret_cast<const float4*>(dst)[0];
-        const float4 b = reinterpret_cast<const float4*>(dst)[1];
-        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        if constexpr (NORM)
-        {
-            const float4 ga = __ldg(reinterpret_cast<const float4*>(p.gain + k0));
-            const float4 gb = __ldg(reinterpret_cast<const float4*>(p.gain + k0 + 4));
-            const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                v[c] = __fmul_rn(__fmul_rn(v[c], rms), gv[c]); // src/rmsnorm.cpp:42-43
-        }
-        // words of lane 2*tb (digits 0 and 2) and lane 2*tb+1 (digits 1 and
-        // 3): [even, odd] element bytes, packed as they are made
-        uint32_t w0[4] = {0u, 0u, 0u, 0u}, w1[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-        {
-            // even elements as y, odd ones as y/16 (their codes enter as 16*c)
-            const float y = __fmul_rn(v[c], inv) * ((c & 1) ? 0.0625f : 1.0f);
-            int d[4];
-            digits4(y, d);
-            const int sh = 8 * (c >> 1), e = c & 1;
-            w0[e] |= (uint32_t)(d[0] & 0xFF) << sh;
-            w0[2 + e] |= (uint32_t)(d[2] & 0xFF) << sh;
-            w1[e] |= (uint32_t)(d[1] & 0xFF) << sh;
-            w1[2 + e] |= (uint32_t)(d[3] & 0xFF) << sh;
-        }
-        dst[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-        dst[1] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-    }
-    if (tid < 32)
-        frag[(size_t)ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
-    if (tid == 0)
-        misc[0] = bad ? __int_as_float(0x7fc00000) : tmx / (127.0f * 128.0f);
-    named_bar_sync(1, NTH);
-}
 
 inline size_t gemv_tiled_i8_smem_bytes(int ntile)
 {
@@ -526,139 +123,6 @@ __device__ __forceinline__ void tiled_drain(const TiledRing& r, uint32_t q)
         mbar_wait_bounded(r.full + 8 * (k % NS), (k / NS) & 1, GEMV_WAIT_LIMIT_NS);
 }
 
-// Consumer warps (16): the row groups of one tiled GEMV in the producer's
-// order, with the activation already built into frag (gemv_build_i8) and its
-// output factor in out_scale; the epilogue EPI of each group runs on one
-// warp. Returns false on a timed-out wait or an abort (s_abort).
-template <int EPI>
-__device__ __forceinline__ bool tiled_i8_consume(const GemvParams& p, const TiledRing& r, uint32_t& q,
-                                                 const uint4* frag, float* red, float out_scale, int cta, int ncta,
-                                                 volatile int& s_abort, unsigned long long* wait_cycles = nullptr)
-{
-    constexpr int NS = GT_STAGES;
-    constexpr int NC = GT_CONSUMERS;
-    constexpr int NCT = NC * 32;
-    constexpr int CT = GT_CHUNK_TILES;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ntile = p.K >> 7, nchunk = (ntile + CT - 1) / CT, n_groups = p.N >> 4;
-    const int g = lane >> 2, t = lane & 3;
-    const bool bact = (g >> 1) == t;
-    // active lanes read their own 16 B of every (tile, word) row of the
-    // fragments; the others read the zero tile
-    const uint32_t f_base = bact ? smem_addr(frag) + (uint32_t)g * 16 : smem_addr(frag) + (uint32_t)ntile * 512;
-    const uint32_t f_step = bact ? 512u : 0u;
-    const uint32_t f_sstep = bact ? 128u : 0u;
-    bool ok = true;
-    int gl = 0;
-    for (int group = cta; group < n_groups; group += ncta, ++gl)
-    {
-        float acc0 = 0.0f, acc1 = 0.0f;
-        for (int c = 0; c < nchunk && ok; ++c, ++q)
-        {
-            const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-            const uint32_t stage = q % NS;
-            const long long c0 = wait_cycles ? clock64() : 0;
-            if (!mbar_wait_bounded(r.full + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
-            {
-                ok = false;
-                s_abort = 1;
-                break;
-            }
-            if (wait_cycles)
-                *wait_cycles += (unsigned long long)(clock64() - c0);
-            if (warp < tiles)
-            {
-                const uint32_t st = r.ring + stage * GT_STAGE_BYTES;
-                const bool two = warp + NC < tiles;
-                const int ia = warp, ib = two ? warp + NC : warp;
-                uint4 w0[2], w1[2];
-                uint16_t sh0[2], sh1[2];
-                uint32_t fa[2];
-#pragma unroll
-                for (int k = 0; k < 2; ++k)
-                {
-                    const int i = k ? ib : ia, tt = c * CT + i;
-                    w0[k] = lds128(st + i * 1024 + lane * 16);
-                    w1[k] = lds128(st + i * 1024 + 512 + lane * 16);
-                    const uint32_t sa = st + tiles * 1024 + i * 128 + lane * 2; // u16 scales
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh0[k]) : "r"(sa));
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(sh1[k]) : "r"(sa + 64));
-                    fa[k] = f_base + (uint32_t)tt * f_step;
-                }
-                int dp[2][4] = {}, dq[2][4] = {}; // [tile][accumulator]: digits (0,1) and (2,3)
-#pragma unroll
-                for (int s = 0; s < 4; ++s)
-                {
-#pragma unroll
-                    for (int k = 0; k < 2; ++k)
-                    {
-                        const uint32_t wa = u4get(w0[k], s), wb = u4get(w1[k], s);
-                        const uint32_t a0 = wa & 0x0F0F0F0Fu, a1 = wb & 0x0F0F0F0Fu;
-                        const uint32_t a2 = wa & 0xF0F0F0F0u, a3 = wb & 0xF0F0F0F0u;
-                        const uint4 b = lds128(fa[k] + (uint32_t)s * f_sstep);
-                        mma_u8s8_16832(dp[k][0], dp[k][1], dp[k][2], dp[k][3], a0, a1, a2, a3, b.x, b.y);
-                        mma_u8s8_16832(dq[k][0], dq[k][1], dq[k][2], dq[k][3], a0, a1, a2, a3, b.z, b.w);
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < 2; ++k)
-                {
-                    if (k == 1 && !two)
-                        break;
-                    // lane (g, t) holds block t of the tile for rows g and g + 8:
-                    // digits (0,1) in dp, (2,3) in dq; |dp[0]*128 + dp[1]| < 2^24
-                    const float r0 = fmaf((float)(dq[k][0] * 128 + dq[k][1]), 1.0f / 16384.0f,
-                                          (float)(dp[k][0] * 128 + dp[k][1]));
-                    const float r1 = fmaf((float)(dq[k][2] * 128 + dq[k][3]), 1.0f / 16384.0f,
-                                          (float)(dp[k][2] * 128 + dp[k][3]));
-                    acc0 = fmaf(decode_scale<AAEDN_SCALE_F16>(sh0[k]), r0, acc0);
-                    acc1 = fmaf(decode_scale<AAEDN_SCALE_F16>(sh1[k]), r1, acc1);
-                }
-            }
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(r.empty + 8 * stage);
-        }
-        if (!ok)
-            break;
-        // this warp's share of the group into buffer gl % RB; the warp that
-        // brings the count to NC runs the epilogue (buffer gl % RB is free
-        // again by the time any warp reaches group gl + RB: warps are at most
-        // GT_STAGES chunks apart)
-        const int b = gl & (GT_RB - 1);
-        float* rb = red + (size_t)b * NC * 16;
-        unsigned* cnt = reinterpret_cast<unsigned*>(red + (size_t)GT_RB * NC * 16);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-        if (t == 0)
-        {
-            rb[warp * 16 + g] = acc0 * out_scale;
-            rb[warp * 16 + g + 8] = acc1 * out_scale;
-        }
-        __syncwarp();
-        unsigned last = 0;
-        if (lane == 0)
-        {
-            __threadfence_block();
-            last = atomicAdd(cnt + b, 1u) == (unsigned)NC - 1 ? 1u : 0u;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last)
-        {
-            __threadfence_block();
-            gemv_epilogue<1, EPI, NC>(p, rb, group, lane);
-            __syncwarp();
-            if (lane == 0)
-                cnt[b] = 0u;
-        }
-    }
-    // the threads decide together (a thread that returned alone would strand
-    // the others at the next barrier)
-    return !named_bar_or(1, NCT, !ok);
-}
-
 // ---------------------------------------------------------------------------
 // Warp-built operand (the persistent step kernel's GEMVs).
 //
@@ -676,10 +140,11 @@ __device__ __forceinline__ bool tiled_i8_consume(const GemvParams& p, const Tile
 // wss[warp]. zero16: a 16-byte zero in shared memory (B of inactive lanes).
 template <int PRO>
 __device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, float* bscale, float* wss,
-                                              unsigned long long* pass_a_cycles = nullptr)
+                                              unsigned long long* pass_a_cycles = nullptr,
+                                              volatile unsigned* cta_flag = nullptr)
 {
     const long long c_start = pass_a_cycles ? clock64() : 0;
-    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
+    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM || PRO == PRO_TP_RMSNORM;
     constexpr int NC = GT_CONSUMERS, CT = GT_CHUNK_TILES;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // the CTA's warps start on different tiles (CTA c shifts by c): 148 CTAs
@@ -692,6 +157,31 @@ __device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, 
         const uint32_t pos = p.state->pos;
         const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
         src = p.embedding + (size_t)tok * p.K;
+    }
+    if constexpr (PRO == PRO_TP_RMSNORM)
+    {
+        // the ranks' partials of the previous GEMV are in this rank's receive
+        // buffer once their flags show its epoch: warp 0 waits on the flags,
+        // the other warps on warp 0 (bounded waits; a timeout is reported
+        // through DecodeState::err)
+        if (lane == 0)
+        {
+            const unsigned E = *p.tp_epoch + (unsigned)p.tp_wait_phase + 1u;
+            if (warp == 0)
+            {
+                tp_wait_flags(p.tpc, E, p.state);
+                __threadfence_system();
+                *cta_flag = E;
+            }
+            else
+            {
+                const uint64_t t0 = globaltimer_ns();
+                while (*cta_flag < E && globaltimer_ns() - t0 < TP_WAIT_LIMIT_NS)
+                    __nanosleep(32);
+                __threadfence_system();
+            }
+        }
+        __syncwarp();
     }
     const int item = lane & 15, tb = item >> 2, s = item & 3;
     float ss = 0.0f;
@@ -777,8 +267,26 @@ __device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, 
                 // other CTAs after this SM may have cached an older copy in L1
                 a = __ldcg(reinterpret_cast<const float4*>(src + k0));
                 b = __ldcg(reinterpret_cast<const float4*>(src + k0 + 4));
+                if constexpr (PRO == PRO_TP_RMSNORM)
+                {
+                    // residual + the ranks' partials (this rank's receive
+                    // buffer), summed in rank order: the same value on every
+                    // rank
+                    float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
+                    const float* rb = p.tpc.recv[p.tpc.rank] + (size_t)p.tp_buf * p.tpc.dim + k0;
+                    for (int w = 0; w < p.tpc.size; ++w)
+                    {
+                        const float* pw = rb + (size_t)w * 2 * p.tpc.dim;
+                        const float4 pa = __ldcg(reinterpret_cast<const float4*>(pw));
+                        const float4 pb = __ldcg(reinterpret_cast<const float4*>(pw + 4));
+                        sa.x += pa.x, sa.y += pa.y, sa.z += pa.z, sa.w += pa.w;
+                        sb.x += pb.x, sb.y += pb.y, sb.z += pb.z, sb.w += pb.w;
+                    }
+                    a = make_float4(a.x + sa.x, a.y + sa.y, a.z + sa.z, a.w + sa.w);
+                    b = make_float4(b.x + sb.x, b.y + sb.y, b.z + sb.z, b.w + sb.w);
+                }
                 v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-                if constexpr (PRO == PRO_EMBED_RMSNORM)
+                if constexpr (PRO == PRO_EMBED_RMSNORM || PRO == PRO_TP_RMSNORM)
                     if (blockIdx.x == 0)
                     {
                         *reinterpret_cast<float4*>(p.hidden_out + k0) = a;
@@ -892,7 +400,7 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
                                                  uint32_t zero16, float* red, float* ecache, int cta, int ncta,
                                                  volatile int& s_abort, unsigned long long* wait_cycles = nullptr)
 {
-    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM;
+    constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM || PRO == PRO_TP_RMSNORM;
     constexpr int NS = GT_STAGES;
     constexpr int NC = GT_CONSUMERS;
     constexpr int NCT = NC * 32;
@@ -1051,8 +559,8 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
     return !named_bar_or(1, NCT, !ok);
 }
 
-// Same CTA shape, ring and layout as gemv_tiled_kernel; the consumers use the
-// integer engine above.
+// The decode GEMV kernel: one producer warp streaming the CTA's chunks, 16
+// consumer warps with warp-built integer operands.
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
 {
@@ -1091,6 +599,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
         reinterpret_cast<unsigned*>(red + (size_t)GT_RB * NC * 16)[tid] = 0u;
     if (tid < 4)
         misc[48 + tid] = 0.0f;
+    if (tid == 0)
+        reinterpret_cast<unsigned*>(misc)[60] = 0u; // tensor parallel: the epoch warp 0 has seen
     __syncthreads();
 
     if (warp == NC)
@@ -1108,12 +618,50 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
     }
 
     pdl_wait();
-    warp_build_i8<PRO>(p, frag, bscale, misc + 32);
+    warp_build_i8<PRO>(p, frag, bscale, misc + 32, nullptr, reinterpret_cast<volatile unsigned*>(misc + 60));
     uint32_t q = 0;
     if (!tiled_wb_consume<PRO, EPI>(p, r, q, frag, bscale, misc + 32, smem_addr(misc + 48), red, ecache,
                                     blockIdx.x, gridDim.x, s_abort))
+    {
         if (lane == 0 && p.state)
             p.state->err = 2u;
+    }
+    else if (p.tp_sig)
+    {
+        // tensor parallel: the last CTA to finish copies this rank's partial
+        // (complete: every CTA counted itself after a fence) into every other
+        // rank's receive buffer, then raises this GEMV's epoch there
+        volatile unsigned* last = reinterpret_cast<volatile unsigned*>(misc) + 61;
+        __threadfence(); // every thread: its rows before the CTA counts itself
+        named_bar_sync(1, NC * 32);
+        if (tid == 0)
+        {
+            const bool l = atomicAdd(p.tp_counter, 1u) == gridDim.x - 1;
+            if (l)
+            {
+                *p.tp_counter = 0u;
+                __threadfence(); // the other CTAs' rows before the copy reads them
+            }
+            *last = l ? 1u : 0u;
+        }
+        named_bar_sync(1, NC * 32);
+        if (*last)
+        {
+            const size_t off = ((size_t)p.tpc.rank * 2 + p.tp_buf) * p.tpc.dim;
+            const float4* src = reinterpret_cast<const float4*>(p.tpc.recv[p.tpc.rank] + off);
+            const int n4 = p.tpc.dim >> 2;
+            for (int q = 0; q < p.tpc.size; ++q)
+                if (q != p.tpc.rank)
+                {
+                    float4* dst = reinterpret_cast<float4*>(p.tpc.recv[q] + off);
+                    for (int i = tid; i < n4; i += NC * 32)
+                        dst[i] = __ldcg(src + i);
+                }
+            named_bar_sync(1, NC * 32);
+            if (tid == 0)
+                tp_signal(p.tpc, *p.tp_epoch + (unsigned)p.tp_sig_phase + 1u); // fences at system scope first
+        }
+    }
 }
 
 } // namespace aaedn_dev

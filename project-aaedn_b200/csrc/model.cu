@@ -24,7 +24,6 @@
 #include "gemv_tiled.cuh"
 #include "mega.cuh"
 #include "tp.cuh"
-#include "gemv_tma.cuh"
 
 namespace aaedn_dev
 {
@@ -336,32 +335,11 @@ struct DevLayer
     float *k, *v; // [n_pages][n_kv][P][hd]
 };
 
-// Shapes the TMA-fed kernel covers: whole 16-row groups, K and the row
-// pitch in whole 256-code chunks, 16-byte aligned codes and scales.
-inline bool tma_ok(const GemvParams& p)
-{
-    return (p.N % 16) == 0 && (p.K % 256) == 0 && (p.ldb % 256) == 0 && (p.kt0 % 2) == 0 &&
-           ((p.kt1 - p.kt0) % 2) == 0 && (reinterpret_cast<uintptr_t>(p.w) & 15) == 0 &&
-           (reinterpret_cast<uintptr_t>(p.s) & 15) == 0;
-}
-
-bool use_tma()
-{
-    static int v = -1;
-    if (v < 0)
-    {
-        const char* e = std::getenv("AAEDN_GEMV_TMA");
-        v = (e && e[0] == '1') ? 1 : 0;
-    }
-    return v == 1;
-}
-
 constexpr size_t TILED_SMEM_MAX = 226 * 1024; // under the 227 KB opt-in maximum of one CTA (static smem too)
 
 inline bool tiles_ok(size_t N, size_t K)
 {
-    return N % 16 == 0 && K % 128 == 0 && K > 0 && gemv_tiled_smem_bytes((int)(K / 128)) <= TILED_SMEM_MAX &&
-           gemv_tiled_i8_smem_bytes((int)(K / 128)) <= TILED_SMEM_MAX;
+    return N % 16 == 0 && K % 128 == 0 && K > 0 && gemv_tiled_i8_smem_bytes((int)(K / 128)) <= TILED_SMEM_MAX;
 }
 
 template <int PRO, int EPI>
@@ -369,34 +347,19 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 {
     if (tiled)
     {
-        static int i8 = -1;
-        if (i8 < 0)
-        {
-            const char* ev = std::getenv("AAEDN_I8");
-            i8 = ev ? std::atoi(ev) != 0 : 1;
-        }
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
-        cudaError_t e = i8 ? launch_kernel(gemv_tiled_i8_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
-                                           gemv_tiled_i8_smem_bytes(p.K / 128), st, pdl, p)
-                           : launch_kernel(gemv_tiled_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
-                                           gemv_tiled_smem_bytes(p.K / 128), st, pdl, p);
+        cudaError_t e = launch_kernel(gemv_tiled_i8_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
+                                      gemv_tiled_i8_smem_bytes(p.K / 128), st, pdl, p);
         if (e != cudaSuccess)
-            return set_error(AAEDN_ECUDA, "launch of gemv_tiled_kernel failed: %s", cudaGetErrorString(e));
+            return set_error(AAEDN_ECUDA, "launch of gemv_tiled_i8_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
         return AAEDN_OK;
     }
-    if (use_tma() && tma_ok(p))
+    if constexpr (PRO == PRO_TP_RMSNORM)
+        return set_error(AAEDN_EUNSUPPORTED, "tensor parallel GEMV needs the tile-major layout");
+    else
     {
-        const int groups = p.N / 16;
-        const int grid = groups < sm_count() ? groups : sm_count();
-        cudaError_t e = launch_kernel(gemv_tma_kernel<PRO, EPI>, dim3(grid), dim3(GEMV_TMA_THREADS),
-                                      gemv_tma_smem_bytes(p.kt1 - p.kt0), st, pdl, p);
-        if (e != cudaSuccess)
-            return set_error(AAEDN_ECUDA, "launch of gemv_tma_kernel failed: %s", cudaGetErrorString(e));
-        count_launch();
-        return AAEDN_OK;
-    }
     auto kern = (p.full_shape && p.scale_pairs) ? gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>
                                                 : gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>;
     static int per_sm = -1;
@@ -413,6 +376,7 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
         return set_error(AAEDN_ECUDA, "launch of gemv_q4_kernel(model) failed: %s", cudaGetErrorString(e));
     count_launch();
     return AAEDN_OK;
+    }
 }
 
 // Opt every model kernel into large dynamic shared memory once, before any
@@ -420,14 +384,13 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 template <int PRO, int EPI>
 int set_gemv_attrs()
 {
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tma_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)TILED_SMEM_MAX));
+    if constexpr (PRO != PRO_TP_RMSNORM)
+    {
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    }
     AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_i8_kernel<PRO, EPI>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TILED_SMEM_MAX));
     return AAEDN_OK;
@@ -443,7 +406,11 @@ int set_model_kernel_attrs()
     if (!rc)
         rc = set_gemv_attrs<PRO_RMSNORM, EPI_SWIGLU>();
     if (!rc)
-        rc = set_gemv_attrs<PRO_PLAIN, EPI_STORE>();
+        rc = set_gemv_attrs<PRO_PLAIN, EPI_TP_PUSH>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_QKV_ROPE>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_SWIGLU>();
     return rc;
 }
 
@@ -478,6 +445,7 @@ struct aaedn_model
     uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
     bool weights_set = false;
     bool pdl = true;   // programmatic dependent launch inside the decode graph
+    bool tp_fuse = false; // tensor parallel: the next GEMV adds the ranks' partials (else a reduce kernel)
     bool tiled = true; // tile-major repacking of the matrices whose shape allows it
     bool l2_hint = true; // weight streams with the L2 evict-first policy
     // tensor parallelism: cfg holds this rank's dims (heads, ffn rows and
@@ -492,6 +460,8 @@ struct aaedn_model
     TpComm tp{};
     bool tp_ready = false;
     unsigned* tp_epoch = nullptr;
+    unsigned* tp_counter = nullptr; // last-CTA count of a partial-writing GEMV
+    float* hidden2 = nullptr;       // residual ping-pong: qkv folds into hidden2, gate/up into hidden
     // the whole step as one persistent kernel (decode_step_kernel)
     bool mega = false;
     int mega_S = 1, mega_ctas = 0, mega_R = 1;
@@ -559,6 +529,8 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->d_attn = m->take<AttnParams>((size_t)c.n_layers * sizeof(AttnParams));
     m->mega_bar = m->take<unsigned>((size_t)c.n_layers * 5 * 4);
     m->tp_epoch = m->take<unsigned>(64);
+    m->tp_counter = m->take<unsigned>(64);
+    m->hidden2 = m->take<float>(D * 4); // tensor parallel: the other residual buffer
     m->dbg_hidden = m->take<float>((size_t)c.n_layers * D * 4);
     return align_up(m->used, 256);
 }
@@ -613,6 +585,17 @@ static GemvParams qkv_params(const aaedn_model* m, uint32_t l)
     q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
     q.scale_pairs = ((D >> 5) & 1) == 0;
     q.l2_hint = m->l2_hint;
+    if (m->tp_size > 1 && m->tp_fuse)
+    {
+        // residual = hidden + the ranks' down partials of layer l - 1, into
+        // hidden2 (layer 0: the embedding row into hidden2)
+        q.tpc = m->tp;
+        q.tp_epoch = m->tp_epoch;
+        q.tp_counter = m->tp_counter;
+        q.hidden_out = m->hidden2;
+        q.tp_buf = 1;
+        q.tp_wait_phase = 2 * (int)l - 1;
+    }
     return q;
 }
 
@@ -657,12 +640,21 @@ static GemvParams o_params(const aaedn_model* m, uint32_t l)
     o.kt1 = ((int)m->kpo + 127) / 128;
     o.x = m->attn_out;
     o.lda = (size_t)m->kpo;
-    o.y = m->tp_size > 1 ? m->tp.part[m->tp_rank][0] : m->hidden; // sharded: this rank's partial
+    o.y = m->hidden; // sharded: the rows are pushed to the ranks instead (EPI_TP_PUSH, buffer 0)
     o.ldc = (size_t)D;
     o.state = m->state;
     o.full_shape = (o.N % 16) == 0 && (o.K % 128) == 0;
     o.scale_pairs = ((m->kpo >> 5) & 1) == 0;
     o.l2_hint = m->l2_hint;
+    if (m->tp_size > 1)
+    {
+        o.tpc = m->tp;
+        o.tp_epoch = m->tp_epoch;
+        o.tp_counter = m->tp_counter;
+        o.tp_sig = 1;
+        o.tp_sig_phase = 2 * (int)l;
+        o.tp_buf = 0;
+    }
     return o;
 }
 
@@ -688,6 +680,17 @@ static GemvParams gu_params(const aaedn_model* m, uint32_t l)
     gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
     gu.scale_pairs = ((D >> 5) & 1) == 0;
     gu.l2_hint = m->l2_hint;
+    if (m->tp_size > 1 && m->tp_fuse)
+    {
+        // residual = hidden2 + the ranks' o partials, into hidden
+        gu.x = m->hidden2;
+        gu.tpc = m->tp;
+        gu.tp_epoch = m->tp_epoch;
+        gu.tp_counter = m->tp_counter;
+        gu.hidden_out = m->hidden;
+        gu.tp_buf = 0;
+        gu.tp_wait_phase = 2 * (int)l;
+    }
     return gu;
 }
 
@@ -706,12 +709,21 @@ static GemvParams down_params(const aaedn_model* m, uint32_t l)
     dn.kt1 = ((int)m->kpd + 127) / 128;
     dn.x = m->act;
     dn.lda = (size_t)m->kpd;
-    dn.y = m->tp_size > 1 ? m->tp.part[m->tp_rank][1] : m->hidden;
+    dn.y = m->hidden; // sharded: pushed to the ranks (EPI_TP_PUSH, buffer 1)
     dn.ldc = (size_t)D;
     dn.state = m->state;
     dn.full_shape = (dn.N % 16) == 0 && (dn.K % 128) == 0;
     dn.scale_pairs = ((m->kpd >> 5) & 1) == 0;
     dn.l2_hint = m->l2_hint;
+    if (m->tp_size > 1)
+    {
+        dn.tpc = m->tp;
+        dn.tp_epoch = m->tp_epoch;
+        dn.tp_counter = m->tp_counter;
+        dn.tp_sig = 1;
+        dn.tp_sig_phase = 2 * (int)l + 1;
+        dn.tp_buf = 1;
+    }
     return dn;
 }
 
@@ -871,7 +883,7 @@ static int enqueue_mega(aaedn_model* m, cudaStream_t st, unsigned long long* tra
 }
 
 // hidden += the sum of the ranks' partials in buffer buf (o: 0, down: 1)
-static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase)
+static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool signal)
 {
     if (!m->tp_ready)
         return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
@@ -881,6 +893,7 @@ static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase)
     rp.dim = (int)m->cfg.dim;
     rp.buf = buf;
     rp.phase = phase;
+    rp.signal = signal ? 1 : 0;
     rp.epoch = m->tp_epoch;
     rp.state = m->state;
     const int blocks = std::max(1, std::min(32, (int)(m->cfg.dim + 255) / 256));
@@ -917,8 +930,10 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         const DevLayer& L = m->layers[l];
         // --- QKV (+RMSNorm prologue, +RoPE/KV-append epilogue)
         const GemvParams q = qkv_params(m, l);
+        const bool fuse = m->tp_size > 1 && m->tp_fuse;
         rc = !(mask & K_QKV) ? AAEDN_OK
              : (l == 0)      ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
+             : fuse          ? model_gemv<PRO_TP_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
                              : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv);
         if (rc)
             return rc;
@@ -935,11 +950,11 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         // --- O projection + residual (sharded: this rank's partial, then the
         // reduction over the ranks adds the sum to the residual)
         const GemvParams o = o_params(m, l);
-        if (m->tp_size > 1)
+        if (m->tp_size > 1) // its partial; the ranks' sum is folded in by gate/up (or a reduce kernel)
         {
-            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_STORE>(o, st, pdl, L.to) : AAEDN_OK;
-            if (!rc && (mask & K_O))
-                rc = tp_reduce(m, st, 0, 2 * (int)l);
+            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to) : AAEDN_OK;
+            if (!rc && (mask & K_O) && !fuse)
+                rc = tp_reduce(m, st, 0, 2 * (int)l, false);
         }
         else
             rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
@@ -949,18 +964,20 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         // --- gate/up (+RMSNorm prologue, SwiGLU epilogue)
         const GemvParams gu = gu_params(m, l);
-        rc = (mask & K_GU) ? model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu) : AAEDN_OK;
+        rc = !(mask & K_GU) ? AAEDN_OK
+             : fuse         ? model_gemv<PRO_TP_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu)
+                            : model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu);
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- down + residual
         const GemvParams dn = down_params(m, l);
-        if (m->tp_size > 1)
+        if (m->tp_size > 1) // its partial; the next qkv (or the final reduction) folds the sum in
         {
-            rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_STORE>(dn, st, pdl, L.td) : AAEDN_OK;
-            if (!rc && (mask & K_DOWN))
-                rc = tp_reduce(m, st, 1, 2 * (int)l + 1);
+            rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(dn, st, pdl, L.td) : AAEDN_OK;
+            if (!rc && (mask & K_DOWN) && (!fuse || l + 1 == c.n_layers))
+                rc = tp_reduce(m, st, 1, 2 * (int)l + 1, false);
         }
         else
             rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
@@ -1103,9 +1120,10 @@ extern "C" int aaedn_tp_plan_get(const aaedn_model_config* cfg, uint32_t tp_rank
     if (tp_size != 1 && tp_size != 2 && tp_size != 4 && tp_size != 8)
         return set_error(AAEDN_EINVAL, "tensor parallel size must be 1, 2, 4 or 8");
     if (tp_rank >= tp_size || fc.n_kv_heads == 0 || fc.n_kv_heads % tp_size || fc.n_heads % tp_size ||
-        fc.ffn_dim % (32 * tp_size) || fc.vocab < tp_size)
+        fc.ffn_dim % (32 * tp_size) || fc.vocab < tp_size || (tp_size > 1 && fc.dim % 128))
         return set_error(AAEDN_EINVAL,
-                         "rank %u of %u: n_heads, n_kv_heads and ffn_dim / 32 must divide by the tensor-parallel size",
+                         "rank %u of %u: n_heads, n_kv_heads and ffn_dim / 32 must divide by the tensor-parallel "
+                         "size (and dim be a multiple of 128)",
                          tp_rank, tp_size);
     aaedn_tp_plan p{};
     p.n_heads = fc.n_heads / tp_size;
@@ -1176,6 +1194,8 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         m->tiled = !(t && t[0] == '0');
         const char* h = std::getenv("AAEDN_L2HINT");
         m->l2_hint = !(h && h[0] == '0');
+        const char* f = std::getenv("AAEDN_TP_FUSE");
+        m->tp_fuse = f && f[0] == '1'; // measured slower on 2 GPUs: opt-in
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
@@ -1252,6 +1272,10 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     rc = setup_mega(m);
     if (rc)
         return fail(rc);
+    if (m->tp_size > 1)
+        for (const DevLayer& L : m->layers)
+            if (!(L.tqkv && L.to && L.tgu && L.td))
+                return fail(set_error(AAEDN_EUNSUPPORTED, "tensor parallel decode needs every matrix tile-major"));
     *out = m;
     return AAEDN_OK;
 }
@@ -1268,10 +1292,11 @@ extern "C" int aaedn_model_create_tp(const aaedn_model_config* cfg, uint32_t tp_
     if (rc || tp_size == 1)
         return rc;
     aaedn_model* m = *out;
-    // the peer-visible region: partials [2][dim], flags [TP_MAX][4], argmax
-    // slots [TP_MAX] (one cudaMalloc: an IPC handle covers it)
+    // the peer-visible region: receive buffers [TP_MAX sources][2][dim],
+    // flags [TP_MAX][4], argmax slots [TP_MAX] (one cudaMalloc: an IPC handle
+    // covers it)
     const size_t part = (size_t)m->cfg.dim * 4;
-    m->tp_region_bytes = 2 * part + TP_MAX * 16 + TP_MAX * 8 + 256;
+    m->tp_region_bytes = (size_t)TP_MAX * 2 * part + TP_MAX * 16 + TP_MAX * 8 + 256;
     if (cudaMalloc(reinterpret_cast<void**>(&m->tp_region), m->tp_region_bytes) != cudaSuccess ||
         cudaMemset(m->tp_region, 0, m->tp_region_bytes) != cudaSuccess)
     {
@@ -1285,12 +1310,11 @@ extern "C" int aaedn_model_create_tp(const aaedn_model_config* cfg, uint32_t tp_
 }
 
 // addresses inside a rank's region
-static void tp_layout(uint8_t* base, size_t dim, float*& p0, float*& p1, unsigned*& flags, float2*& best)
+static void tp_layout(uint8_t* base, size_t dim, float*& recv, unsigned*& flags, float2*& best)
 {
-    p0 = reinterpret_cast<float*>(base);
-    p1 = p0 + dim;
-    flags = reinterpret_cast<unsigned*>(base + 2 * dim * 4);
-    best = reinterpret_cast<float2*>(base + 2 * dim * 4 + TP_MAX * 16);
+    recv = reinterpret_cast<float*>(base);
+    flags = reinterpret_cast<unsigned*>(base + (size_t)TP_MAX * 2 * dim * 4);
+    best = reinterpret_cast<float2*>(base + (size_t)TP_MAX * 2 * dim * 4 + TP_MAX * 16);
 }
 
 extern "C" int aaedn_model_tp_handle(aaedn_model* m, uint8_t* h_handle)
@@ -1325,9 +1349,10 @@ extern "C" int aaedn_model_tp_connect(aaedn_model* m, const uint8_t* h_handles)
             m->tp_peer[r] = p;
             base = static_cast<uint8_t*>(p);
         }
-        tp_layout(base, dim, m->tp.part[r][0], m->tp.part[r][1], m->tp.flags[r], m->tp.best[r]);
+        tp_layout(base, dim, m->tp.recv[r], m->tp.flags[r], m->tp.best[r]);
     }
     m->tp.my_flags = m->tp.flags[m->tp_rank];
+    m->tp.dim = (int)dim;
     m->tp_ready = true;
     return AAEDN_OK;
 }
@@ -1666,6 +1691,8 @@ extern "C" int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n)
 extern "C" int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* h_hidden, float* h_logits)
 {
     MODEL_OK(m);
+    if (m->tp_size > 1) // the residual of a layer is complete only inside the next layer's kernels
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_forward_debug: not for tensor-parallel models");
     const aaedn_model_config& c = m->cfg;
     if (token >= m->full.vocab)
         return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", token, m->full.vocab);
@@ -1769,6 +1796,8 @@ extern "C" int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t ca
 extern "C" int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32_t cap)
 {
     MODEL_OK(m);
+    if (m->tp_size > 1) // a part alone would wait for partials its peers never send
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_profile_parts: not for tensor-parallel models");
     static const int masks[8] = {K_ALL, K_QKV | K_O | K_GU | K_DOWN, K_QKV, K_ATTN, K_O, K_GU, K_DOWN, K_LM};
     if (!h_ms || cap < 8 || reps == 0)
         return set_error(AAEDN_EINVAL, "aaedn_model_profile_parts: need 8 outputs and reps > 0");

@@ -4,13 +4,17 @@
 // of the KV cache), rows [r F/T, (r+1) F/T) of gate and up, the matching
 // input columns of o and down (row-parallel), and lm_head rows [r V/T, ...).
 // After o and down each rank has a partial sum of the full hidden-size
-// output; instead of a library all-reduce, every rank writes its partial to
-// a buffer the other ranks map (CUDA IPC over NVLink), raises a flag in each
-// peer's memory, and one small kernel per rank then reads the T partials
-// straight from the peers, adds them in rank order (the same sum, bit for
-// bit, on every rank) and adds the result to the residual stream. The
-// greedy argmax is exchanged the same way, so all ranks feed the same token
-// to the next step.
+// output; instead of a library all-reduce, the GEMV's epilogue stores its rows
+// in this rank's slot of its own receive buffer, and the GEMV's last CTA copies
+// the whole slot into every other rank's receive buffer (CUDA IPC over
+// NVLink) and raises a flag in each rank's memory. tp_reduce_kernel then
+// waits for all flags and adds the T partials (read from its own memory, in
+// rank order: the same sum, bit for bit, on every rank) to the residual.
+// Opt-in (AAEDN_TP_FUSE=1), the next GEMV does that addition while it builds
+// its operand instead (PRO_TP_RMSNORM); measured slower on 2 GPUs (417 against
+// 560 tok/s at the 7B widths), since every CTA of the next GEMV then waits for
+// the flags. The greedy argmax is exchanged the same way, so all ranks feed
+// the same token to the next step.
 //
 // Flags carry an epoch, E = tp_epoch + phase + 1, that only grows (phase:
 // 2 per layer, then the argmax); tp_epoch advances by one step's worth in a
@@ -29,21 +33,6 @@
 namespace aaedn_dev
 {
 
-constexpr int TP_MAX = 8;
-constexpr uint64_t TP_WAIT_LIMIT_NS = 2000000000ull; // 2 s
-
-// The peer-visible region of one rank (one cudaMalloc, exported by IPC):
-// partials [2][dim] floats, flags [TP_MAX] (one per writer rank, 16-byte
-// apart), argmax slots [TP_MAX] (value, index).
-struct TpComm
-{
-    float* part[TP_MAX][2];       // partial buffers of every rank (own included)
-    unsigned* flags[TP_MAX];      // flag words of every rank: flags[p][4 * w] = epoch written by w
-    float2* best[TP_MAX];         // argmax slots of every rank: best[p][w] = (value, index) of w
-    unsigned* my_flags;           // == flags[rank]
-    int rank, size;
-};
-
 struct TpReduceParams
 {
     TpComm c;
@@ -51,40 +40,10 @@ struct TpReduceParams
     int dim;
     int buf;             // 0: o partials, 1: down partials
     int phase;           // epoch offset of this reduction within the step
+    int signal;          // also raise this rank's flag (0: the GEMV did)
     const unsigned* epoch;
     DecodeState* state;
 };
-
-__device__ __forceinline__ bool tp_wait_flags(const TpComm& c, unsigned E, DecodeState* st)
-{
-    const uint64_t t0 = globaltimer_ns();
-    for (int w = 0; w < c.size; ++w)
-    {
-        volatile unsigned* f = c.my_flags + 4 * w;
-        while (*f < E)
-        {
-            if (globaltimer_ns() - t0 > TP_WAIT_LIMIT_NS)
-            {
-                st->err = 4u;
-                return false;
-            }
-            __nanosleep(32);
-        }
-    }
-    return true;
-}
-
-// Raise this rank's flag for epoch E in every rank's flag array (itself
-// included), after its earlier writes are visible to the peers.
-__device__ __forceinline__ void tp_signal(const TpComm& c, unsigned E)
-{
-    __threadfence_system();
-    for (int p = 0; p < c.size; ++p)
-    {
-        volatile unsigned* f = c.flags[p] + 4 * c.rank;
-        *f = E;
-    }
-}
 
 // hidden[i] += sum over ranks (in rank order) of part[rank][buf][i]. Launched
 // right after the GEMV that wrote this rank's partial (stream order: that
@@ -95,18 +54,19 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p)
     const unsigned E = *p.epoch + (unsigned)p.phase + 1u;
     if (threadIdx.x == 0)
     {
-        if (blockIdx.x == 0)
+        if (blockIdx.x == 0 && p.signal)
             tp_signal(p.c, E);
         s_ok = tp_wait_flags(p.c, E, p.state) ? 1 : 0;
     }
     __syncthreads();
     if (!s_ok)
         return;
+    const float* rb = p.c.recv[p.c.rank] + (size_t)p.buf * p.dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.dim; i += gridDim.x * blockDim.x)
     {
         float s = 0.0f;
         for (int w = 0; w < p.c.size; ++w) // fixed order: the same sum on every rank
-            s += __ldcv(p.c.part[w][p.buf] + i);
+            s += __ldcg(rb + (size_t)w * 2 * p.dim + i);
         p.hidden[i] = __ldcg(p.hidden + i) + s; // residual (src/transformer.cpp:214)
     }
 }

@@ -1,8 +1,8 @@
-"""Tensor-parallel decode on 2 GPUs against the oracle: two processes, one
+"""Tensor-parallel decode on 2, 4 and 8 GPUs against the oracle: one process
 per GPU, each with its share of the model (aaedn_model_create_tp), partial
 sums added through each other's memory. The greedy tokens must equal the
 oracle's and the assembled logits must agree within 1e-4 (the same bars as
-the single-GPU model tests). Needs two GPUs; skipped otherwise."""
+the single-GPU model tests). Needs 2 (4, 8) GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -25,10 +25,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, size, port, cfg, seed, n_prompt, n_new, q):
+def _rank(rank, size, port, cfg, seed, n_prompt, n_new, fuse, q):
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), AAEDN_TP_FUSE=fuse)
     torch.cuda.set_device(rank)
     from datetime import timedelta
     dist.init_process_group("gloo", rank=rank, world_size=size, timeout=timedelta(seconds=120))
@@ -49,14 +49,14 @@ def _rank(rank, size, port, cfg, seed, n_prompt, n_new, q):
         dist.destroy_process_group()
 
 
-def _run(cfg, seed, n_prompt, n_new, size=2):
+def _run(cfg, seed, n_prompt, n_new, size=2, fuse="0"):
     import torch
     if torch.cuda.device_count() < size:
         pytest.skip(f"needs {size} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, size, port, cfg, seed, n_prompt, n_new, q)) for r in range(size)]
+    procs = [ctx.Process(target=_rank, args=(r, size, port, cfg, seed, n_prompt, n_new, fuse, q)) for r in range(size)]
     for pr in procs:
         pr.start()
     res = sorted(q.get(timeout=600) for _ in range(size))
@@ -72,10 +72,19 @@ def _run(cfg, seed, n_prompt, n_new, size=2):
     return toks[0], logits
 
 
-@pytest.mark.parametrize("cfg,seed,n_prompt,n_new", [(GQA, 77, 9, 120), (W7B, 2024, 4, 64)])
-def test_tp2_greedy_identical_to_oracle(oracle, cfg, seed, n_prompt, n_new):
+@pytest.mark.parametrize("cfg,seed,n_prompt,n_new,size,fuse", [
+    (GQA, 77, 9, 120, 2, "1"),
+    (GQA, 77, 9, 120, 2, "0"),
+    (W7B, 2024, 4, 64, 2, "1"),
+    (W7B, 2024, 4, 64, 2, "0"),
+    (W7B, 31, 5, 40, 4, "0"),
+    (W7B, 31, 5, 40, 8, "0"),
+])
+def test_tp_greedy_identical_to_oracle(oracle, cfg, seed, n_prompt, n_new, size, fuse):
+    """fuse "1": the next GEMV adds the ranks' partials while it builds its
+    operand; "0": a separate reduction kernel after o and down."""
     import pyoracle
-    got, logits = _run(cfg, seed, n_prompt, n_new)
+    got, logits = _run(cfg, seed, n_prompt, n_new, size=size, fuse=fuse)
     w = ab.synthetic_weights(cfg, seed)
     om = pyoracle.OracleModel(oracle, cfg, w)
     want, wl = om.generate(ab.synth_tokens(seed, 0, cfg["vocab"], n_prompt), n_new)
