@@ -265,6 +265,16 @@ int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32
  * 0's clock when it reached / left each grid barrier. The position is left
  * where it was. */
 int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase, size_t cap_phase);
+/* Tracing of the per-kernel decode step: one step replayed with globaltimer
+ * stamps (ns) per CTA; h_stamps [5 * n_layers + 1][1024][4]: per launch (qkv,
+ * attention, o, gate/up, down of each layer, then lm_head) and CTA slot c <
+ * 160: entry, operand ready, [GEMV: previous kernel complete; attention: its
+ * token loop done], exit (0 where a kernel records no such event); GEMV
+ * launches also hold, from slot 160 on, consumer warp 0's (arrived, released)
+ * stamps of chunks 0..23 of CTAs 0..7 (48 words per CTA); h_grid [5 *
+ * n_layers + 1]: CTAs per launch (0: not traced). Single-GPU models only; the
+ * position is left where it was. No counterpart in the reference. */
+int aaedn_model_trace_kernels(aaedn_model* m, uint64_t* h_stamps, size_t cap, uint32_t* h_grid, size_t cap_grid);
 /* Synchronises and reports the sticky device-side error of the decode state
  * (AAEDN_ESTATE: a position past the cache; AAEDN_ETIMEOUT: a bounded device
  * wait ran out). forward and generate check it themselves; decode_steps does

@@ -13,7 +13,8 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libaaedn_b200.so")
+# AAEDN_B200_LIB: another build of the library (same C ABI) to load instead
+LIB_PATH = os.environ.get("AAEDN_B200_LIB") or os.path.join(HERE, "libaaedn_b200.so")
 
 OK = 0
 EINVAL, ECUDA, ETIMEOUT, EFORMAT, ENOMEM, EUNSUPPORTED, ESTATE = -1, -2, -3, -4, -5, -6, -7
@@ -130,6 +131,7 @@ def lib():
         "aaedn_model_profile_parts": ([_vp, _u32, _vp, _u32], _int),
         "aaedn_model_profile_step": ([_vp, _vp, _u32, ctypes.POINTER(_u32)], _int),
         "aaedn_model_trace_step": ([_vp, _vp, _sz, _vp, _sz], _int),
+        "aaedn_model_trace_kernels": ([_vp, _vp, _sz, _vp, _sz], _int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -474,6 +476,16 @@ class Model:
         ph = np.zeros((self.cfg["n_layers"] * 5 + 1) * 2, np.int64)
         check(lib().aaedn_model_trace_step(self.h, _p(cta), cta.size, _p(ph), ph.size))
         return cta.reshape(-1, 8), ph.reshape(-1, 2)
+
+    def trace_kernels(self):
+        """globaltimer stamps (ns) of one decode step of the per-kernel graph:
+        (stamps [5 * n_layers + 1][1024][4], grid [5 * n_layers + 1]); per
+        launch and CTA: entry, operand ready, first weights, exit."""
+        nk = self.cfg["n_layers"] * 5 + 1
+        st = np.zeros(nk * 1024 * 4, np.uint64)
+        grid = np.zeros(nk, np.uint32)
+        check(lib().aaedn_model_trace_kernels(self.h, _p(st), st.size, _p(grid), grid.size))
+        return st.reshape(nk, 1024, 4), grid
 
     def forward_debug(self, token):
         hidden = np.empty((self.cfg["n_layers"], self.cfg["dim"]), np.float32)

@@ -51,6 +51,7 @@ struct AttnParams
     int nseg;
     uint32_t seg_start[ATTN_MAX_SEG];
     uint32_t seg_off[ATTN_MAX_SEG + 1]; // prefix sums of the lengths
+    unsigned long long* trace; // per-CTA timeline of a traced step, or null
 };
 
 // Shared memory: per-warp running max and sum [8][G] each, per-warp V sums
@@ -103,8 +104,10 @@ __device__ __forceinline__ int attn_len(const AttnParams& p)
 // 0..255 within the group) that synchronise on named barrier bar_id: the
 // split's partial result, and the merge of all S splits by the group that
 // finishes a kv head last. asmem: attn_smem_bytes; s_last: one word of
-// shared memory.
-template <int MODE, int G, int HDM>
+// shared memory. PDLW: the item waits for the previous kernel itself, after
+// it has requested its first batch of K/V rows (decode mode: every row but
+// the current position's was written by earlier steps).
+template <int MODE, int G, int HDM, bool PDLW = false>
 __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int split, int tid, float* asmem,
                                           unsigned* s_last, int bar_id)
 {
@@ -122,13 +125,14 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
     float* wacc = wl + ATTN_WARPS * G;   // [8][G][hd]
 
     // batch loader: tokens tb0 + 8j, j < TB, K and V slices of this lane
+    // (not token `skip`)
     float4 kr[TB][NCH], vr[TB][NCH];
-    auto load_batch = [&](int tb0) {
+    auto load_batch = [&](int tb0, int skip) {
 #pragma unroll
         for (int j = 0; j < TB; ++j)
         {
             const int t = tb0 + ATTN_WARPS * j;
-            const bool live = t < t1;
+            const bool live = t < t1 && t != skip;
             const size_t ro = live ? attn_row<MODE>(p, t, kvh) : 0;
 #pragma unroll
             for (int c = 0; c < NCH; ++c)
@@ -148,8 +152,32 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
         }
     };
     // the first batch's rows are requested before q: their latencies overlap
+    // (PDLW: before the wait for the kernel that writes q and row L - 1)
+    const int tcur = (MODE == 1 && PDLW) ? L - 1 : -1;
     if (t0 + warp < t1)
-        load_batch(t0 + warp);
+        load_batch(t0 + warp, tcur);
+    if constexpr (PDLW)
+    {
+        pdl_wait();
+        if (tid == 0)
+            trace_mark(p.trace, split * p.n_kv + kvh, 1);
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+            if (t0 + warp + ATTN_WARPS * j == tcur && tcur < t1)
+            {
+                const size_t ro = attn_row<MODE>(p, tcur, kvh);
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    const int ch = lane + 32 * c;
+                    if (ch < hd4)
+                    {
+                        kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                        vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                    }
+                }
+            }
+    }
     // lane slices of q (scaled once: s = (q*scale).k would round differently,
     // so the scale is applied to the dot as src/attention.cpp:42 does)
     float4 qv[G][NCH];
@@ -179,7 +207,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
     for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
     {
         if (tb0 != t0 + warp)
-            load_batch(tb0);
+            load_batch(tb0, -1);
 #pragma unroll
         for (int gi = 0; gi < G; ++gi)
         {
@@ -241,6 +269,8 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
         }
     }
 
+    if (tid == 0)
+        trace_mark(p.trace, split * p.n_kv + kvh, 2);
     // merge the 8 warps (fixed order) into this split's partial result
 #pragma unroll
     for (int gi = 0; gi < G; ++gi)
@@ -302,16 +332,40 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
         const int gi = i / hd, d = i - gi * hd;
         const int h = kvh * G + gi;
         const float* pb = p.part + (size_t)h * S * ps;
+        // splits in batches of SU with the loads unrolled (one L2 round trip
+        // per batch, not per split); the sums still run in split order
+        constexpr int SU = 8;
         float M = -INFINITY;
-        for (int s2 = 0; s2 < S; ++s2)
-            M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
-        float num = 0.0f, den = 0.0f;
-        for (int s2 = 0; s2 < S; ++s2)
+        for (int sb = 0; sb < S; sb += SU)
         {
-            const float ms = __ldcg(pb + (size_t)s2 * ps + hd);
-            const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            num = fmaf(__ldcg(pb + (size_t)s2 * ps + d), w, num);
-            den = fmaf(__ldcg(pb + (size_t)s2 * ps + hd + 1), w, den);
+            float mv[SU];
+#pragma unroll
+            for (int u = 0; u < SU; ++u)
+                mv[u] = sb + u < S ? __ldcg(pb + (size_t)(sb + u) * ps + hd) : -INFINITY;
+#pragma unroll
+            for (int u = 0; u < SU; ++u)
+                M = fmaxf(M, mv[u]);
+        }
+        float num = 0.0f, den = 0.0f;
+        for (int sb = 0; sb < S; sb += SU)
+        {
+            float mv[SU], vv[SU], lv[SU];
+#pragma unroll
+            for (int u = 0; u < SU; ++u)
+            {
+                const bool live = sb + u < S;
+                const float* pv = pb + (size_t)(sb + u) * ps;
+                mv[u] = live ? __ldcg(pv + hd) : -INFINITY;
+                vv[u] = live ? __ldcg(pv + d) : 0.0f;
+                lv[u] = live ? __ldcg(pv + hd + 1) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < SU; ++u)
+            {
+                const float w = (mv[u] == -INFINITY) ? 0.0f : expf(mv[u] - M);
+                num = fmaf(vv[u], w, num);
+                den = fmaf(lv[u], w, den);
+            }
         }
         p.out[(size_t)h * hd + d] = den > 0.0f ? num / den : 0.0f;
     }
@@ -327,6 +381,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
     __shared__ unsigned s_last;
     pdl_launch_dependents();
     const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
+    const int lin = split * gridDim.x + kvh;
+    if (tid == 0)
+        trace_mark(p.trace, lin, 0);
     if constexpr (MODE == 1)
     {
         // The position only changes at the end of a decode step (lm_head), so
@@ -346,8 +403,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
             asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
         }
     }
-    pdl_wait();
-    attn_item<MODE, G, HDM>(p, kvh, split, tid, asmem, &s_last, 0);
+    if constexpr (MODE == 1)
+        attn_item<MODE, G, HDM, true>(p, kvh, split, tid, asmem, &s_last, 0); // waits for the previous kernel
+    else
+    {
+        pdl_wait();
+        attn_item<MODE, G, HDM>(p, kvh, split, tid, asmem, &s_last, 0);
+    }
+    if (tid == 0)
+        trace_mark(p.trace, lin, 3);
 }
 
 } // namespace aaedn_dev

@@ -288,6 +288,28 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy()
     return pol;
 }
 
+// Timeline of one traced decode step: up to STEP_TRACE_CTAS CTAs of a launch
+// each write STEP_TRACE_EVENTS globaltimer stamps (0 entry, 1 operand ready,
+// 2 first weights arrived, 3 exit; 0 where a kernel has no such event).
+constexpr int STEP_TRACE_CTAS = 1024;
+constexpr int STEP_TRACE_EVENTS = 4;
+__device__ __forceinline__ void trace_mark(unsigned long long* t, int cta, int e)
+{
+    if (t && cta < STEP_TRACE_CTAS)
+        t[(size_t)cta * STEP_TRACE_EVENTS + e] = globaltimer_ns();
+}
+
+// Per-chunk stamps of a tiled GEMV's first STEP_TRACE_CHUNK_CTAS CTAs (consumer
+// warp 0: chunk arrived, chunk released), after the per-CTA slots of its grid:
+// slot (STEP_TRACE_CHUNK_BASE + cta * 2 * STEP_TRACE_CHUNKS + 2 q + e).
+constexpr int STEP_TRACE_CHUNK_CTAS = 8, STEP_TRACE_CHUNKS = 24;
+constexpr int STEP_TRACE_CHUNK_BASE = 160 * STEP_TRACE_EVENTS;
+__device__ __forceinline__ void trace_chunk(unsigned long long* t, int cta, uint32_t q, int e)
+{
+    if (t && cta < STEP_TRACE_CHUNK_CTAS && q < (uint32_t)STEP_TRACE_CHUNKS)
+        t[STEP_TRACE_CHUNK_BASE + (size_t)cta * 2 * STEP_TRACE_CHUNKS + 2 * q + e] = globaltimer_ns();
+}
+
 // bulk_g2s with an L2 cache policy
 __device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar,
                                               uint64_t policy)

@@ -157,6 +157,8 @@ struct GemvParams
     const float* attn_part;
     int attn_S, attn_pstride;
     int l2_hint; // stream the weights with the L2 evict-first policy
+    unsigned long long* trace; // per-CTA timeline of a traced step (tiled kernel), or null
+    int stages;                // ring stages of the tiled kernel (0: GT_STAGES)
     // tensor parallel (zero otherwise): PRO_TP_RMSNORM waits for epoch
     // *tp_epoch + tp_wait_phase + 1 and adds partial buffer tp_buf; a
     // partial-writing GEMV (tp_sig) raises epoch *tp_epoch + tp_sig_phase + 1

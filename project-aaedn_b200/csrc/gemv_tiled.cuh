@@ -29,7 +29,9 @@ constexpr uint64_t GEMV_WAIT_LIMIT_NS = 2000000000ull; // 2 s: bound of every mb
 
 constexpr int GT_CONSUMERS = 16;
 constexpr int GT_THREADS = (GT_CONSUMERS + 1) * 32;
-constexpr int GT_STAGES = 4;
+constexpr int GT_STAGES = 4;     // ring stages of the persistent step kernel; the
+                                 // decode GEMV takes what its shared memory allows
+constexpr int GT_MAX_STAGES = 8;
 constexpr int GT_CHUNK_TILES = 32; // two tiles per consumer warp
 constexpr int GT_TILE_BYTES = 1024 + 128; // codes + scales of one tile (16 rows x 128 codes)
 constexpr int GT_STAGE_BYTES = GT_CHUNK_TILES * GT_TILE_BYTES; // 36 KB
@@ -62,10 +64,19 @@ void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t
 // and four k-steps complete the tile's 4 blocks with nothing rounded.
 // ---------------------------------------------------------------------------
 
-inline size_t gemv_tiled_i8_smem_bytes(int ntile)
+inline size_t gemv_tiled_i8_smem_bytes(int ntile, int stages = GT_STAGES)
 {
-    return (size_t)GT_STAGES * GT_STAGE_BYTES + (size_t)GT_STAGES * 16 + (size_t)ntile * (512 + 16) + GT_RED_BYTES +
+    return (size_t)stages * GT_STAGE_BYTES + (size_t)stages * 16 + (size_t)ntile * (512 + 16) + GT_RED_BYTES +
            64 * 4 + GT_ECACHE_FLOATS * 4;
+}
+
+// The most ring stages (<= GT_MAX_STAGES) whose shared memory fits `budget`.
+inline int gemv_tiled_stages(int ntile, size_t budget)
+{
+    int s = GT_MAX_STAGES;
+    while (s > 2 && gemv_tiled_i8_smem_bytes(ntile, s) > budget)
+        --s;
+    return s;
 }
 
 // The shared-memory ring of a tiled GEMV CTA: stage i at ring + i * 36 KB,
@@ -74,6 +85,7 @@ inline size_t gemv_tiled_i8_smem_bytes(int ntile)
 struct TiledRing
 {
     uint32_t ring, full, empty; // shared-memory addresses
+    uint32_t ns;                // stages
 };
 
 // Producer warp: issues, for every row group this CTA owns (cta, cta + ncta,
@@ -83,16 +95,18 @@ __device__ __forceinline__ bool tiled_produce(const uint8_t* w, int N, int K, co
                                               int cta, int ncta, int lane, unsigned long long* wait_cycles = nullptr,
                                               bool hint = false)
 {
-    constexpr int NS = GT_STAGES, CT = GT_CHUNK_TILES;
+    constexpr int CT = GT_CHUNK_TILES;
+    const uint32_t NS = r.ns;
     const int ntile = K >> 7, nchunk = (ntile + CT - 1) / CT, n_groups = N >> 4;
     const size_t group_bytes = (size_t)ntile * GT_TILE_BYTES;
+    // stage and use of chunk q, advanced without a division per chunk
+    uint32_t stage = q % NS, use = q / NS;
     for (int group = cta; group < n_groups; group += ncta)
     {
         const uint8_t* gsrc = w + (size_t)group * group_bytes;
-        for (int c = 0; c < nchunk; ++c, ++q)
+        for (int c = 0; c < nchunk; ++c, ++q, (++stage == NS) ? (stage = 0, ++use) : 0u)
         {
             const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-            const uint32_t stage = q % NS, use = q / NS;
             const long long c0 = wait_cycles ? clock64() : 0;
             if (use > 0 && !mbar_wait_bounded(r.empty + 8 * stage, (use - 1) & 1, GEMV_WAIT_LIMIT_NS))
                 return false;
@@ -118,7 +132,7 @@ __device__ __forceinline__ bool tiled_produce(const uint8_t* w, int N, int K, co
 // Producer warp before exit: every issued chunk (q of them) has landed.
 __device__ __forceinline__ void tiled_drain(const TiledRing& r, uint32_t q)
 {
-    constexpr int NS = GT_STAGES;
+    const uint32_t NS = r.ns;
     for (uint32_t k = (q > NS ? q - NS : 0); k < q; ++k)
         mbar_wait_bounded(r.full + 8 * (k % NS), (k / NS) & 1, GEMV_WAIT_LIMIT_NS);
 }
@@ -207,29 +221,39 @@ __device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, 
                 const int hd = p.head_dim, h = k0 / hd, d0 = k0 - h * hd, S = p.attn_S, ps = p.attn_pstride;
                 const float* pb = p.attn_part + (size_t)h * S * ps;
                 float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, den = 0.0f;
-                if (S <= SU)
+                // splits in batches of SU, loads unrolled (one L2 round trip
+                // per batch); the sums run in split order
+                float M = -INFINITY;
+                for (int sb = 0; sb < S; sb += SU)
+                {
+                    float mv[SU];
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                        mv[u] = sb + u < S ? __ldcg(pb + (size_t)(sb + u) * ps + hd) : -INFINITY;
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                        M = fmaxf(M, mv[u]);
+                }
+                for (int sb = 0; sb < S; sb += SU)
                 {
                     float ms[SU], ls[SU];
 #pragma unroll
-                    for (int s2 = 0; s2 < SU; ++s2)
+                    for (int u = 0; u < SU; ++u)
                     {
-                        const float2 ml = s2 < S ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)s2 * ps + hd))
-                                                 : make_float2(-INFINITY, 0.0f);
-                        ms[s2] = ml.x;
-                        ls[s2] = ml.y;
+                        const float2 ml = sb + u < S
+                                              ? __ldcg(reinterpret_cast<const float2*>(pb + (size_t)(sb + u) * ps + hd))
+                                              : make_float2(-INFINITY, 0.0f);
+                        ms[u] = ml.x;
+                        ls[u] = ml.y;
                     }
-                    float M = -INFINITY;
 #pragma unroll
-                    for (int s2 = 0; s2 < SU; ++s2)
-                        M = fmaxf(M, ms[s2]);
-#pragma unroll
-                    for (int s2 = 0; s2 < SU; ++s2)
-                        if (s2 < S)
+                    for (int u = 0; u < SU; ++u)
+                        if (sb + u < S)
                         {
-                            const float* pv = pb + (size_t)s2 * ps + d0;
+                            const float* pv = pb + (size_t)(sb + u) * ps + d0;
                             const float4 va = __ldcg(reinterpret_cast<const float4*>(pv));
                             const float4 vb = __ldcg(reinterpret_cast<const float4*>(pv + 4));
-                            const float w = (ms[s2] == -INFINITY) ? 0.0f : expf(ms[s2] - M);
+                            const float w = (ms[u] == -INFINITY) ? 0.0f : expf(ms[u] - M);
                             num[0] = fmaf(va.x, w, num[0]);
                             num[1] = fmaf(va.y, w, num[1]);
                             num[2] = fmaf(va.z, w, num[2]);
@@ -238,24 +262,8 @@ __device__ __forceinline__ void warp_build_i8(const GemvParams& p, uint4* frag, 
                             num[5] = fmaf(vb.y, w, num[5]);
                             num[6] = fmaf(vb.z, w, num[6]);
                             num[7] = fmaf(vb.w, w, num[7]);
-                            den = fmaf(ls[s2], w, den);
+                            den = fmaf(ls[u], w, den);
                         }
-                }
-                else
-                {
-                    float M = -INFINITY;
-                    for (int s2 = 0; s2 < S; ++s2)
-                        M = fmaxf(M, __ldcg(pb + (size_t)s2 * ps + hd));
-                    for (int s2 = 0; s2 < S; ++s2)
-                    {
-                        const float* pv = pb + (size_t)s2 * ps;
-                        const float ms = __ldcg(pv + hd);
-                        const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-#pragma unroll
-                        for (int cc = 0; cc < 8; ++cc)
-                            num[cc] = fmaf(__ldcg(pv + d0 + cc), w, num[cc]);
-                        den = fmaf(__ldcg(pv + hd + 1), w, den);
-                    }
                 }
 #pragma unroll
                 for (int cc = 0; cc < 8; ++cc)
@@ -401,7 +409,7 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
                                                  volatile int& s_abort, unsigned long long* wait_cycles = nullptr)
 {
     constexpr bool NORM = PRO == PRO_RMSNORM || PRO == PRO_EMBED_RMSNORM || PRO == PRO_TP_RMSNORM;
-    constexpr int NS = GT_STAGES;
+    const uint32_t NS = r.ns;
     constexpr int NC = GT_CONSUMERS;
     constexpr int NCT = NC * 32;
     constexpr int CT = GT_CHUNK_TILES;
@@ -448,15 +456,15 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
     }
     bool ok = true;
     int gl = 0;
+    uint32_t stage = q % NS, phase = (q / NS) & 1; // advanced without a division per chunk
     for (int group = cta; group < n_groups; group += ncta, ++gl)
     {
         float acc0 = 0.0f, acc1 = 0.0f;
-        for (int c = 0; c < nchunk && ok; ++c, ++q)
+        for (int c = 0; c < nchunk && ok; ++c, ++q, (++stage == NS) ? (stage = 0, phase ^= 1u) : 0u)
         {
             const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-            const uint32_t stage = q % NS;
             const long long c0 = wait_cycles ? clock64() : 0;
-            if (!mbar_wait_bounded(r.full + 8 * stage, (q / NS) & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
+            if (!mbar_wait_bounded(r.full + 8 * stage, phase, GEMV_WAIT_LIMIT_NS) || s_abort)
             {
                 ok = false;
                 s_abort = 1;
@@ -464,6 +472,8 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
             }
             if (wait_cycles)
                 *wait_cycles += (unsigned long long)(clock64() - c0);
+            if (p.trace && tid == 0)
+                trace_chunk(p.trace, cta, q, 0);
             if (wv < tiles)
             {
                 const uint32_t st = r.ring + stage * GT_STAGE_BYTES;
@@ -516,6 +526,8 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(r.empty + 8 * stage);
+            if (p.trace && tid == 0)
+                trace_chunk(p.trace, cta, q, 1);
         }
         if (!ok)
             break;
@@ -564,7 +576,7 @@ __device__ __forceinline__ bool tiled_wb_consume(const GemvParams& p, const Tile
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
 {
-    constexpr int NS = GT_STAGES;
+    const int NS = p.stages > 0 ? p.stages : GT_STAGES;
     constexpr int NC = GT_CONSUMERS;
     extern __shared__ __align__(16) uint8_t smem[];
     const int ntile = p.K >> 7;
@@ -580,10 +592,13 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
 
     pdl_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 0);
     TiledRing r;
     r.ring = smem_addr(ring);
     r.full = smem_addr(bars);
     r.empty = r.full + NS * 8;
+    r.ns = (uint32_t)NS;
 
     if (tid == 0)
     {
@@ -618,7 +633,11 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
     }
 
     pdl_wait();
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 2);
     warp_build_i8<PRO>(p, frag, bscale, misc + 32, nullptr, reinterpret_cast<volatile unsigned*>(misc + 60));
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 1);
     uint32_t q = 0;
     if (!tiled_wb_consume<PRO, EPI>(p, r, q, frag, bscale, misc + 32, smem_addr(misc + 48), red, ecache,
                                     blockIdx.x, gridDim.x, s_abort))
@@ -662,6 +681,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
                 tp_signal(p.tpc, *p.tp_epoch + (unsigned)p.tp_sig_phase + 1u); // fences at system scope first
         }
     }
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 3);
 }
 
 } // namespace aaedn_dev

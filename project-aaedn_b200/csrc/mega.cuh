@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) decode_step_kernel(const MegaPa
     r.ring = smem_addr(smem);
     r.full = r.ring + NS * GT_STAGE_BYTES;
     r.empty = r.full + NS * 8;
+    r.ns = NS;
     if (tid == 0)
     {
         for (int i = 0; i < NS; ++i)

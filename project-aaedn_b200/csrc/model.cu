@@ -87,6 +87,7 @@ struct LmParams
     int l2_hint;   // stream the rows with the L2 evict-first policy
     int row0;      // token id of row 0 (tensor parallel: this rank's first row)
     int defer;     // leave the per-CTA results (the ranks' argmax exchange finishes)
+    unsigned long long* trace; // per-CTA timeline of a traced step, or null
 };
 
 constexpr int LM_CONSUMERS = 8;
@@ -128,6 +129,8 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
 
     pdl_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 0);
     const int n0 = blockIdx.x * p.rows_per_cta;
     const int nrows = max(0, min(p.vocab, n0 + p.rows_per_cta) - n0);
     const uint32_t ring_a = smem_addr(ring);
@@ -200,6 +203,8 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
     for (int i = tid; i < p.dim; i += NC * 32)
         xs[i] = __fmul_rn(__fmul_rn(p.hidden[i], rms), p.gain[i]);
     named_bar_sync(1, NC * 32);
+    if (tid == 0)
+        trace_mark(p.trace, blockIdx.x, 1);
 
     const int d4 = p.dim >> 2;
     const uint32_t xs_a = smem_addr(xs);
@@ -258,6 +263,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(const LmP
             }
         p.part_val[blockIdx.x] = v;
         p.part_idx[blockIdx.x] = i;
+        trace_mark(p.trace, blockIdx.x, 3);
         s_last = 0u;
         if (!p.defer)
         {
@@ -347,17 +353,26 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 {
     if (tiled)
     {
+        static int max_stages = -1;
+        if (max_stages < 0)
+        {
+            const char* e = std::getenv("AAEDN_GEMV_STAGES");
+            // 4 by default: 5 (what a 4096-wide row group leaves room for) measured slower
+            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : GT_STAGES;
+        }
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
+        GemvParams pp = p;
+        pp.stages = std::min(max_stages, gemv_tiled_stages(p.K / 128, TILED_SMEM_MAX));
         cudaError_t e = launch_kernel(gemv_tiled_i8_kernel<PRO, EPI>, dim3(grid), dim3(GT_THREADS),
-                                      gemv_tiled_i8_smem_bytes(p.K / 128), st, pdl, p);
+                                      gemv_tiled_i8_smem_bytes(p.K / 128, pp.stages), st, pdl, pp);
         if (e != cudaSuccess)
             return set_error(AAEDN_ECUDA, "launch of gemv_tiled_i8_kernel failed: %s", cudaGetErrorString(e));
         count_launch();
         return AAEDN_OK;
     }
-    if constexpr (PRO == PRO_TP_RMSNORM)
-        return set_error(AAEDN_EUNSUPPORTED, "tensor parallel GEMV needs the tile-major layout");
+    if constexpr (PRO == PRO_TP_RMSNORM || PRO == PRO_ATTN_COMBINE)
+        return set_error(AAEDN_EUNSUPPORTED, "this GEMV prologue needs the tile-major layout");
     else
     {
     auto kern = (p.full_shape && p.scale_pairs) ? gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>
@@ -384,7 +399,7 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 template <int PRO, int EPI>
 int set_gemv_attrs()
 {
-    if constexpr (PRO != PRO_TP_RMSNORM)
+    if constexpr (PRO != PRO_TP_RMSNORM && PRO != PRO_ATTN_COMBINE)
     {
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
@@ -411,6 +426,10 @@ int set_model_kernel_attrs()
         rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_QKV_ROPE>();
     if (!rc)
         rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_SWIGLU>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_ATTN_COMBINE, EPI_RESIDUAL>();
+    if (!rc)
+        rc = set_gemv_attrs<PRO_ATTN_COMBINE, EPI_TP_PUSH>();
     return rc;
 }
 
@@ -445,6 +464,7 @@ struct aaedn_model
     uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
     bool weights_set = false;
     bool pdl = true;   // programmatic dependent launch inside the decode graph
+    bool attn_fuse = false; // the o-GEMV merges the attention splits while it builds its operand
     bool tp_fuse = false; // tensor parallel: the next GEMV adds the ranks' partials (else a reduce kernel)
     bool tiled = true; // tile-major repacking of the matrices whose shape allows it
     bool l2_hint = true; // weight streams with the L2 evict-first policy
@@ -902,8 +922,10 @@ static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool s
     return AAEDN_OK;
 }
 
+// trace: a timeline buffer of [5 n_layers + 1][STEP_TRACE_CTAS][STEP_TRACE_EVENTS]
+// stamps (qkv, attention, o, gate/up, down of each layer, then lm_head), or null
 static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::vector<cudaEvent_t>* ev = nullptr,
-                        int mask = K_ALL)
+                        int mask = K_ALL, unsigned long long* trace = nullptr)
 {
     if (m->tp_size > 1 && !m->tp_ready)
         return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
@@ -928,8 +950,28 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     for (uint32_t l = 0; l < c.n_layers; ++l)
     {
         const DevLayer& L = m->layers[l];
+        GemvParams q = qkv_params(m, l), o = o_params(m, l), gu = gu_params(m, l), dn = down_params(m, l);
+        AttnParams a = attn_params(m, l, m->attn_S);
+        const bool afuse = m->attn_fuse && L.to;
+        if (afuse)
+        {
+            // attention leaves its S split results; the o build merges them
+            a.no_combine = 1;
+            o.attn_part = m->attn_part;
+            o.attn_S = m->attn_S;
+            o.attn_pstride = hd + 4;
+            o.head_dim = hd;
+        }
+        if (trace)
+        {
+            const size_t per = (size_t)STEP_TRACE_CTAS * STEP_TRACE_EVENTS, k0 = (size_t)l * 5;
+            q.trace = trace + k0 * per;
+            a.trace = trace + (k0 + 1) * per;
+            o.trace = trace + (k0 + 2) * per;
+            gu.trace = trace + (k0 + 3) * per;
+            dn.trace = trace + (k0 + 4) * per;
+        }
         // --- QKV (+RMSNorm prologue, +RoPE/KV-append epilogue)
-        const GemvParams q = qkv_params(m, l);
         const bool fuse = m->tp_size > 1 && m->tp_fuse;
         rc = !(mask & K_QKV) ? AAEDN_OK
              : (l == 0)      ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
@@ -940,7 +982,6 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if ((rc = mark()))
             return rc;
         // --- attention
-        const AttnParams a = attn_params(m, l, m->attn_S);
         const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
         rc = (mask & K_ATTN) ? attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl) : AAEDN_OK;
         if (rc)
@@ -949,21 +990,23 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         // --- O projection + residual (sharded: this rank's partial, then the
         // reduction over the ranks adds the sum to the residual)
-        const GemvParams o = o_params(m, l);
         if (m->tp_size > 1) // its partial; the ranks' sum is folded in by gate/up (or a reduce kernel)
         {
-            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to) : AAEDN_OK;
+            rc = !(mask & K_O) ? AAEDN_OK
+                 : afuse       ? model_gemv<PRO_ATTN_COMBINE, EPI_TP_PUSH>(o, st, pdl, L.to)
+                               : model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to);
             if (!rc && (mask & K_O) && !fuse)
                 rc = tp_reduce(m, st, 0, 2 * (int)l, false);
         }
         else
-            rc = (mask & K_O) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to) : AAEDN_OK;
+            rc = !(mask & K_O) ? AAEDN_OK
+                 : afuse       ? model_gemv<PRO_ATTN_COMBINE, EPI_RESIDUAL>(o, st, pdl, L.to)
+                               : model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to);
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- gate/up (+RMSNorm prologue, SwiGLU epilogue)
-        const GemvParams gu = gu_params(m, l);
         rc = !(mask & K_GU) ? AAEDN_OK
              : fuse         ? model_gemv<PRO_TP_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu)
                             : model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu);
@@ -972,7 +1015,6 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if ((rc = mark()))
             return rc;
         // --- down + residual
-        const GemvParams dn = down_params(m, l);
         if (m->tp_size > 1) // its partial; the next qkv (or the final reduction) folds the sum in
         {
             rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(dn, st, pdl, L.td) : AAEDN_OK;
@@ -989,7 +1031,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             AAEDN_CUDA_TRY(cudaMemcpyAsync(m->dbg_hidden + (size_t)l * D, m->hidden, (size_t)D * 4,
                                            cudaMemcpyDeviceToDevice, st));
     }
-    const LmParams lp = lm_params(m);
+    LmParams lp = lm_params(m);
+    if (trace)
+        lp.trace = trace + (size_t)c.n_layers * 5 * STEP_TRACE_CTAS * STEP_TRACE_EVENTS;
     if (mask & K_LM)
     {
         cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(LM_THREADS),
@@ -1194,6 +1238,8 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         m->tiled = !(t && t[0] == '0');
         const char* h = std::getenv("AAEDN_L2HINT");
         m->l2_hint = !(h && h[0] == '0');
+        const char* af = std::getenv("AAEDN_ATTN_FUSE");
+        m->attn_fuse = af && af[0] == '1'; // measured slower (every CTA merges all heads): opt-in
         const char* f = std::getenv("AAEDN_TP_FUSE");
         m->tp_fuse = f && f[0] == '1'; // measured slower on 2 GPUs: opt-in
     }
@@ -1201,7 +1247,10 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
     // about two attention CTAs per SM (a CTA walks its token range in
     // batches, so any split count covers any context length)
-    int S = std::max(1, (2 * sm_count() + (int)c.n_kv_heads - 1) / (int)c.n_kv_heads);
+    int per_sm = 2;
+    if (const char* e = std::getenv("AAEDN_ATTN_CTAS_PER_SM"))
+        per_sm = std::max(1, std::min(4, std::atoi(e)));
+    int S = std::max(1, (per_sm * sm_count() + (int)c.n_kv_heads - 1) / (int)c.n_kv_heads);
     S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
     S = std::min(S, 64);
     m->attn_S = S;
@@ -1894,6 +1943,68 @@ extern "C" int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t ca
         rc = write_state(m, m->h_pos, m->h_pos); // the traced step does not count
     if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess)
         rc = set_error(AAEDN_ECUDA, "trace step sync");
+    return rc;
+}
+
+extern "C" int aaedn_model_trace_kernels(aaedn_model* m, uint64_t* h_stamps, size_t cap, uint32_t* h_grid,
+                                         size_t cap_grid)
+{
+    MODEL_OK(m);
+    const aaedn_model_config& c = m->cfg;
+    const size_t nk = (size_t)c.n_layers * 5 + 1, per = (size_t)STEP_TRACE_CTAS * STEP_TRACE_EVENTS;
+    if (m->mega)
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_kernels: the model runs the persistent kernel");
+    if (m->tp_size > 1)
+        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_kernels: not for a tensor-parallel model");
+    if (!h_stamps || !h_grid || cap < nk * per || cap_grid < nk)
+        return set_error(AAEDN_EINVAL, "aaedn_model_trace_kernels: need %zu stamps and %zu grid sizes", nk * per, nk);
+    if (m->h_pos == 0 || (size_t)m->h_pos + 2 > c.max_seq)
+        return set_error(AAEDN_ESTATE, "aaedn_model_trace_kernels: sequence empty or full");
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        const DevLayer& L = m->layers[l];
+        const GemvParams g[4] = {qkv_params(m, l), o_params(m, l), gu_params(m, l), down_params(m, l)};
+        const bool t[4] = {L.tqkv, L.to, L.tgu, L.td};
+        const int slot[4] = {0, 2, 3, 4};
+        for (int i = 0; i < 4; ++i)
+            h_grid[(size_t)l * 5 + slot[i]] =
+                t[i] ? (uint32_t)std::min(g[i].N / 16, sm_count()) : 0u; // 0: not traced (row-major GEMV)
+        h_grid[(size_t)l * 5 + 1] = (uint32_t)(c.n_kv_heads * m->attn_S);
+    }
+    h_grid[nk - 1] = (uint32_t)m->lm_ctas;
+    unsigned long long* d = nullptr;
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    AAEDN_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d), nk * per * 8));
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    int rc = AAEDN_OK;
+    cudaError_t e = cudaMemsetAsync(d, 0, nk * per * 8, m->stream);
+    if (e == cudaSuccess)
+        e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess)
+    {
+        rc = enqueue_step(m, m->stream, false, nullptr, K_ALL, d);
+        e = cudaStreamEndCapture(m->stream, &g);
+    }
+    if (!rc && e == cudaSuccess)
+        e = cudaGraphInstantiate(&ge, g, 0);
+    if (!rc && e == cudaSuccess)
+        e = cudaGraphLaunch(ge, m->stream);
+    if (!rc && e == cudaSuccess)
+        e = cudaMemcpyAsync(h_stamps, d, nk * per * 8, cudaMemcpyDeviceToHost, m->stream);
+    if (!rc && e == cudaSuccess)
+        e = cudaStreamSynchronize(m->stream);
+    if (!rc && e != cudaSuccess)
+        rc = set_error(AAEDN_ECUDA, "trace kernels: %s", cudaGetErrorString(e));
+    if (ge)
+        cudaGraphExecDestroy(ge);
+    if (g)
+        cudaGraphDestroy(g);
+    cudaFree(d);
+    if (!rc)
+        rc = write_state(m, m->h_pos, m->h_pos); // the traced step does not count
+    if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess)
+        rc = set_error(AAEDN_ECUDA, "trace kernels sync");
     return rc;
 }
 

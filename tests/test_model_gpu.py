@@ -125,3 +125,23 @@ def test_7b_width_two_layers_vs_oracle():
     np.testing.assert_array_equal(got, want)
     assert _rel_err(gm.logits(), wl) < 1e-4
     gm.close()
+
+
+@pytest.mark.parametrize("env", [
+    {"AAEDN_ATTN_FUSE": "1"},                 # the o build merges the attention splits
+    {"AAEDN_ATTN_CTAS_PER_SM": "4"},          # more attention splits (S > 16: batched merges)
+    {"AAEDN_PDL": "0", "AAEDN_L2HINT": "0"},  # plain launches, no L2 policy
+])
+def test_launch_options_same_tokens(env, monkeypatch):
+    """The model's launch options (read when it is created) change timing
+    only: the 7B widths, two layers, against the oracle."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    cfg = dict(ab.LLAMA2_7B, n_layers=2, max_seq=256)
+    w, om, gm = _pair(cfg, seed=99)
+    prompt = ab.synth_tokens(99, 0, cfg["vocab"], 5)
+    want, wl = om.generate(prompt, 48)
+    got = gm.generate(prompt, 48)
+    np.testing.assert_array_equal(got, want)
+    assert _rel_err(gm.logits(), wl) < 1e-4
+    gm.close()
