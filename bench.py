@@ -12,8 +12,10 @@ there is no dataset (data: synthetic).
 
 Ours: W untimed device-resident decode steps, then exactly K timed steps
 (CUDA events on the model's stream, barrier + synchronize on both sides, max
-over ranks). Under torchrun each rank runs an independent replica on its
-own GPU (weak scaling; the decode path of one sequence is not sharded yet).
+over ranks). Under torchrun the N ranks decode ONE sequence tensor-parallel
+(heads, FFN rows and lm_head rows sharded; partial sums added through peer
+memory over NVLink; strong scaling), or with --mode replicas N independent
+sequences (weak scaling).
 The line also carries the end-to-end rate through the reference-facing
 call (transformer_forward semantics: host token in, host logits out, host
 argmax), the roofline of the dequant-GEMV kernels from CUDA events, the SM
