@@ -107,7 +107,11 @@ __device__ __forceinline__ int attn_len(const AttnParams& p)
 // shared memory. PDLW: the item waits for the previous kernel itself, after
 // it has requested its first batch of K/V rows (decode mode: every row but
 // the current position's was written by earlier steps).
-template <int MODE, int G, int HDM, bool PDLW = false>
+// CL: the S splits of a kv head are one thread-block cluster (split = the
+// CTA's rank in it); each CTA leaves its partial result in its own shared
+// memory (after the attn_smem_bytes block) and rank 0 merges the S of them
+// through distributed shared memory. No global partials, counters or atomics.
+template <int MODE, int G, int HDM, bool PDLW = false, bool CL = false>
 __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int split, int tid, float* asmem,
                                           unsigned* s_last, int bar_id)
 {
@@ -304,13 +308,63 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
             den = fmaf(wl[w * G + gi], f, den);
         }
         const int h = kvh * G + gi;
-        float* pp = p.part + ((size_t)h * S + split) * ps;
+        float* pp = CL ? wacc + (size_t)ATTN_WARPS * G * hd + (size_t)gi * (hd + 2)
+                       : p.part + ((size_t)h * S + split) * ps;
         pp[d] = o;
         if (d == 0)
         {
             pp[hd] = M;
             pp[hd + 1] = den;
         }
+    }
+
+    if constexpr (CL)
+    {
+        // merge the cluster's S partials in split order (the same arithmetic
+        // as the global merge below); the second barrier keeps every CTA's
+        // shared memory alive until rank 0 has read it
+        cluster_sync_all();
+        if (split == 0)
+            for (int i = tid; i < G * hd; i += ATTN_THREADS)
+            {
+                const int gi = i / hd, d = i - gi * hd;
+                const uint32_t cb = smem_addr(wacc + (size_t)ATTN_WARPS * G * hd + (size_t)gi * (hd + 2));
+                constexpr int SU = 8;
+                float M = -INFINITY;
+                for (int sb = 0; sb < S; sb += SU)
+                {
+                    float mv[SU];
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                        mv[u] = sb + u < S ? ld_dsmem_f32(cb + hd * 4, sb + u) : -INFINITY;
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                        M = fmaxf(M, mv[u]);
+                }
+                float num = 0.0f, den = 0.0f;
+                for (int sb = 0; sb < S; sb += SU)
+                {
+                    float mv[SU], vv[SU], lv[SU];
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                    {
+                        const bool live = sb + u < S;
+                        mv[u] = live ? ld_dsmem_f32(cb + hd * 4, sb + u) : -INFINITY;
+                        vv[u] = live ? ld_dsmem_f32(cb + d * 4, sb + u) : 0.0f;
+                        lv[u] = live ? ld_dsmem_f32(cb + (hd + 1) * 4, sb + u) : 0.0f;
+                    }
+#pragma unroll
+                    for (int u = 0; u < SU; ++u)
+                    {
+                        const float w = (mv[u] == -INFINITY) ? 0.0f : expf(mv[u] - M);
+                        num = fmaf(vv[u], w, num);
+                        den = fmaf(lv[u], w, den);
+                    }
+                }
+                p.out[(size_t)(kvh * G + gi) * hd + d] = den > 0.0f ? num / den : 0.0f;
+            }
+        cluster_sync_all();
+        return;
     }
 
     if (p.no_combine)
@@ -374,7 +428,10 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
 }
 
 
-template <int MODE, int G, int HDM>
+// CL (decode mode): launched as clusters of gridDim.y CTAs, one per split of
+// a kv head, which merge their partials in distributed shared memory
+// (attn_cluster_smem_bytes of dynamic shared memory).
+template <int MODE, int G, int HDM, bool CL = false>
 __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_split_kernel(const AttnParams p)
 {
     extern __shared__ __align__(16) float asmem[];
@@ -404,7 +461,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
         }
     }
     if constexpr (MODE == 1)
-        attn_item<MODE, G, HDM, true>(p, kvh, split, tid, asmem, &s_last, 0); // waits for the previous kernel
+        attn_item<MODE, G, HDM, true, CL>(p, kvh, split, tid, asmem, &s_last, 0); // waits for the previous kernel
     else
     {
         pdl_wait();
@@ -423,6 +480,92 @@ template <int MODE, int G, int HDM>
 inline cudaError_t attn_launch_one(const AttnParams& p, dim3 grid, size_t smem, cudaStream_t st, bool pdl)
 {
     return launch_kernel(attn_split_kernel<MODE, G, HDM>, grid, dim3(ATTN_THREADS), smem, st, pdl, p);
+}
+
+// Shared memory of the cluster variant: the per-warp block plus this CTA's
+// partial result (G x (hd + 2) floats) that the cluster reads.
+inline size_t attn_cluster_smem_bytes(int G, int hd)
+{
+    return attn_smem_bytes(G, hd, 0) + (size_t)G * (hd + 2) * 4;
+}
+
+// Decode attention as clusters of grid.y CTAs (the splits of one kv head).
+template <int G, int HDM>
+inline cudaError_t attn_launch_cluster_one(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, p.head_dim);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = grid.y;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, attn_split_kernel<1, G, HDM, true>, p);
+}
+
+inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
+{
+    const int G = p.n_heads / p.n_kv;
+    const bool big = p.head_dim > 128;
+    if ((int)grid.y != p.S || p.S > 16)
+        return set_error(AAEDN_EINVAL, "clustered attention: %u CTAs per cluster for %d splits", grid.y, p.S);
+    cudaError_t e;
+    switch (G)
+    {
+    case 1: e = big ? attn_launch_cluster_one<1, 256>(p, grid, st, pdl) : attn_launch_cluster_one<1, 128>(p, grid, st, pdl); break;
+    case 2: e = big ? attn_launch_cluster_one<2, 256>(p, grid, st, pdl) : attn_launch_cluster_one<2, 128>(p, grid, st, pdl); break;
+    case 4: e = big ? attn_launch_cluster_one<4, 256>(p, grid, st, pdl) : attn_launch_cluster_one<4, 128>(p, grid, st, pdl); break;
+    case 8: e = big ? attn_launch_cluster_one<8, 256>(p, grid, st, pdl) : attn_launch_cluster_one<8, 128>(p, grid, st, pdl); break;
+    default: return set_error(AAEDN_EUNSUPPORTED, "attention: %d query heads per kv head (1, 2, 4 or 8)", G);
+    }
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of clustered attn_split_kernel failed: %s", cudaGetErrorString(e));
+    return AAEDN_OK;
+}
+
+// Clusters of `S` CTAs that can be resident at once for head group G and
+// head_dim hd (0: the variant can not run here).
+template <int G, int HDM>
+inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_kv, S);
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, hd);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_split_kernel<1, G, HDM, true>, &cfg) != cudaSuccess)
+    {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+inline int attn_cluster_capacity(int G, int hd, int S, int n_kv)
+{
+    const bool big = hd > 128;
+    switch (G)
+    {
+    case 1: return big ? attn_cluster_capacity_one<1, 256>(S, hd, n_kv) : attn_cluster_capacity_one<1, 128>(S, hd, n_kv);
+    case 2: return big ? attn_cluster_capacity_one<2, 256>(S, hd, n_kv) : attn_cluster_capacity_one<2, 128>(S, hd, n_kv);
+    case 4: return big ? attn_cluster_capacity_one<4, 256>(S, hd, n_kv) : attn_cluster_capacity_one<4, 128>(S, hd, n_kv);
+    case 8: return big ? attn_cluster_capacity_one<8, 256>(S, hd, n_kv) : attn_cluster_capacity_one<8, 128>(S, hd, n_kv);
+    default: return 0;
+    }
 }
 
 // Launches the instantiation for G = n_heads / n_kv (1, 2, 4 or 8).
@@ -453,6 +596,18 @@ inline int attn_set_attrs_g()
                                         200 * 1024));
     AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<MODE, G, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         200 * 1024));
+    if constexpr (MODE == 1)
+    {
+        // the clustered variant: up to 16 CTAs per cluster
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 128, true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 256, true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 128, true>,
+                                            cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 256, true>,
+                                            cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    }
     return AAEDN_OK;
 }
 

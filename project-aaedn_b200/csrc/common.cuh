@@ -310,6 +310,25 @@ __device__ __forceinline__ void trace_chunk(unsigned long long* t, int cta, uint
         t[STEP_TRACE_CHUNK_BASE + (size_t)cta * 2 * STEP_TRACE_CHUNKS + 2 * q + e] = globaltimer_ns();
 }
 
+// Thread-block cluster barrier (every thread of every CTA of the cluster,
+// convergent): the CTAs' shared-memory writes before it are visible to the
+// cluster's reads after it.
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A float in the shared memory of CTA `rank` of this cluster, at the offset of
+// the local shared address `laddr`.
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t laddr, uint32_t rank)
+{
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(laddr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
 // bulk_g2s with an L2 cache policy
 __device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar,
                                               uint64_t policy)

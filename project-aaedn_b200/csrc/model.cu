@@ -457,6 +457,7 @@ struct aaedn_model
     float* dbg_hidden = nullptr;
     int page_size = 64, n_pages = 0;
     int attn_S = 1, attn_max_tok = 1;
+    int attn_cS = 0; // splits of the clustered decode attention (0: splits merged through global memory)
     int lm_ctas = 1, lm_rows = 8, lm_stages = 8, lm_consumers = 8;
     cudaGraphExec_t graph_exec = nullptr;
     uint32_t kernels_per_step = 0;
@@ -951,7 +952,8 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     {
         const DevLayer& L = m->layers[l];
         GemvParams q = qkv_params(m, l), o = o_params(m, l), gu = gu_params(m, l), dn = down_params(m, l);
-        AttnParams a = attn_params(m, l, m->attn_S);
+        const int aS = m->attn_cS ? m->attn_cS : m->attn_S;
+        AttnParams a = attn_params(m, l, aS);
         const bool afuse = m->attn_fuse && L.to;
         if (afuse)
         {
@@ -983,7 +985,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         // --- attention
         const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
-        rc = (mask & K_ATTN) ? attn_launch<1>(a, dim3(KV, m->attn_S), asmem, st, pdl) : AAEDN_OK;
+        rc = !(mask & K_ATTN) ? AAEDN_OK
+             : m->attn_cS     ? attn_launch_cluster(a, dim3(KV, aS), st, pdl)
+                              : attn_launch<1>(a, dim3(KV, aS), asmem, st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -1315,6 +1319,22 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     rc = attn_set_attrs<1>();
     if (rc)
         return fail(rc);
+    if (!m->attn_fuse)
+    {
+        // decode attention as clusters of Sc splits per kv head (a power of
+        // two <= 8 by default, <= max_seq / 8) merging in distributed shared
+        // memory, when this GPU can hold such a cluster (7B, one B200: 8
+        // splits 562 tok/s, 16 splits 520, the global merge over 10 splits
+        // 552); AAEDN_ATTN_CLUSTER=0 keeps the global merge, =n caps Sc at n
+        const char* ce = std::getenv("AAEDN_ATTN_CLUSTER");
+        int cap = ce ? std::atoi(ce) : 8;
+        int Sc = 16;
+        while (Sc > 1 && (Sc > cap || Sc > (int)(c.max_seq / 8)))
+            Sc >>= 1;
+        const int G = (int)(c.n_heads / c.n_kv_heads);
+        if (Sc >= 2 && attn_cluster_capacity(G, (int)c.head_dim, Sc, (int)c.n_kv_heads) >= 1)
+            m->attn_cS = Sc;
+    }
     rc = set_model_kernel_attrs();
     if (rc)
         return fail(rc);
@@ -1969,7 +1989,7 @@ extern "C" int aaedn_model_trace_kernels(aaedn_model* m, uint64_t* h_stamps, siz
         for (int i = 0; i < 4; ++i)
             h_grid[(size_t)l * 5 + slot[i]] =
                 t[i] ? (uint32_t)std::min(g[i].N / 16, sm_count()) : 0u; // 0: not traced (row-major GEMV)
-        h_grid[(size_t)l * 5 + 1] = (uint32_t)(c.n_kv_heads * m->attn_S);
+        h_grid[(size_t)l * 5 + 1] = (uint32_t)(c.n_kv_heads * (m->attn_cS ? m->attn_cS : m->attn_S));
     }
     h_grid[nk - 1] = (uint32_t)m->lm_ctas;
     unsigned long long* d = nullptr;

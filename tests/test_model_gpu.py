@@ -129,7 +129,8 @@ def test_7b_width_two_layers_vs_oracle():
 
 @pytest.mark.parametrize("env", [
     {"AAEDN_ATTN_FUSE": "1"},                 # the o build merges the attention splits
-    {"AAEDN_ATTN_CTAS_PER_SM": "4"},          # more attention splits (S > 16: batched merges)
+    {"AAEDN_ATTN_CLUSTER": "0", "AAEDN_ATTN_CTAS_PER_SM": "4"},  # splits merged in global memory, S > 16
+    {"AAEDN_ATTN_CLUSTER": "16"},             # clusters of 16 splits (non-portable size)
     {"AAEDN_PDL": "0", "AAEDN_L2HINT": "0"},  # plain launches, no L2 policy
 ])
 def test_launch_options_same_tokens(env, monkeypatch):
