@@ -527,6 +527,7 @@ inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, 
     }
     if (e != cudaSuccess)
         return set_error(AAEDN_ECUDA, "launch of clustered attn_split_kernel failed: %s", cudaGetErrorString(e));
+    count_launch();
     return AAEDN_OK;
 }
 

@@ -146,3 +146,17 @@ def test_launch_options_same_tokens(env, monkeypatch):
     np.testing.assert_array_equal(got, want)
     assert _rel_err(gm.logits(), wl) < 1e-4
     gm.close()
+
+
+def test_launch_count_per_step():
+    """Every kernel of the decode step is counted (the bench reports the
+    count): 5 per layer (qkv, attention, o, gate/up, down) and the lm_head."""
+    cfg = GQA_SMALL
+    w, om, gm = _pair(cfg, seed=5)
+    gm.forward(ab.synth_tokens(5, 0, cfg["vocab"], 3), want_logits=False)
+    assert gm.kernels_per_step() == 5 * cfg["n_layers"] + 1
+    n0 = ab.kernel_launches()
+    gm.decode_steps(2)
+    gm.status()
+    assert ab.kernel_launches() - n0 == 2 * (5 * cfg["n_layers"] + 1)
+    gm.close()
