@@ -154,7 +154,7 @@ def test_launch_count_per_step():
     cfg = GQA_SMALL
     w, om, gm = _pair(cfg, seed=5)
     gm.forward(ab.synth_tokens(5, 0, cfg["vocab"], 3), want_logits=False)
-    assert gm.kernels_per_step() == 5 * cfg["n_layers"] + 1
+    assert gm.kernels_per_step == 5 * cfg["n_layers"] + 1
     n0 = ab.kernel_launches()
     gm.decode_steps(2)
     gm.status()
