@@ -141,6 +141,19 @@ int aaedn_cu_ffn_swiglu(const float* d_in, float* d_out, size_t batch, size_t hi
                         const uint16_t* d_gate_scales, const uint16_t* d_up_scales, const uint16_t* d_down_scales,
                         int semantics, void* stream);
 
+/* Next-token sampling (docs/mpd.md:539-554; src/main.cpp:214-247 is the
+ * reference's softmax-and-draw without temperature or top-p, walking ids in
+ * index order where this walks them in the spec's sorted order):
+ * temperature T, nucleus top_p, multinomial draw with the caller's uniform
+ * variate u in [0, 1) (the reference's rand() / RAND_MAX). T <= 0 is greedy
+ * (argmax, ties to the lowest id). Otherwise p_i = exp((l_i - max) / T); the
+ * tokens sorted by p descending (ties: lower id first) are kept up to and
+ * including the first whose cumulative sum reaches top_p * sum(p); the token
+ * returned is the first kept one whose cumulative sum reaches u times the
+ * kept mass. Masses are summed in fp64. Writes one uint32 to d_token. */
+int aaedn_cu_sample(const float* d_logits, uint32_t vocab, float temperature, float top_p, float u,
+                    uint32_t* d_token, void* stream);
+
 /* No counterpart in the reference. The same attention as
  * aaedn_cu_attention for callers that cannot let a library allocate device
  * memory (for example an application that hands all device memory to one

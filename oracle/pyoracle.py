@@ -232,3 +232,54 @@ class OracleModel:
         if rc != 0:
             raise RuntimeError("or_model_generate failed")
         return out, logits
+
+
+def sample_ref(logits, temperature, top_p, u):
+    """Next-token sampling as the reference specifies it (docs/mpd.md:539-554),
+    sorting explicitly (src/main.cpp:214-247, the reference's plain softmax
+    draw, walks ids in index order instead; sample_main_ref restates it): temperature <= 0 is the argmax (ties to the lowest id);
+    otherwise p = exp((l - max) * (1/T)) in fp32, tokens sorted by p
+    descending (stable: lower id first), kept up to and including the first
+    whose cumulative sum reaches top_p * sum(p), then the first kept token
+    whose cumulative sum reaches u times the kept mass. Cumulative sums in
+    fp64. Returns (token, margin): margin is the smallest relative distance
+    of a threshold from a cumulative sum it was compared with (decisions
+    closer than fp32 rounding of p can differ between implementations)."""
+    lg = np.asarray(logits, np.float32)
+    if not temperature > 0:
+        return int(np.argmax(lg)), np.inf
+    mx = lg.max()
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    p = np.exp((lg - mx) * inv_t).astype(np.float32)
+    order = np.argsort(-p, kind="stable")
+    cs = np.cumsum(p[order].astype(np.float64))
+    z = cs[-1]
+    t1 = float(top_p) * z
+    k = int(np.searchsorted(cs, t1, side="left"))
+    k = min(k, cs.size - 1)  # rounding can leave t1 above the total: keep all
+    w = cs[k]
+    t2 = float(u) * w
+    j = int(np.searchsorted(cs, t2, side="left"))
+    margin = np.inf
+    for t, i in ((t1, k), (t2, j)):
+        for c in (cs[i], cs[i - 1] if i > 0 else None):
+            if c is not None and t > 0:
+                margin = min(margin, abs(c - t) / t)
+    return int(order[j]), margin
+
+
+def sample_main_ref(logits, r):
+    """src/main.cpp:216-246 as written: softmax in fp32 (expf(l - max), sum,
+    divide), then the first id whose running fp32 sum reaches r."""
+    lg = np.asarray(logits, np.float32)
+    e = np.exp(lg - lg.max()).astype(np.float32)
+    s = np.float32(0)
+    for v in e:
+        s = np.float32(s + v)
+    pr = (e / s).astype(np.float32)
+    c = np.float32(0)
+    for i, v in enumerate(pr):
+        c = np.float32(c + v)
+        if r <= c:
+            return i
+    return 0

@@ -102,6 +102,7 @@ def lib():
         "aaedn_cu_attention_noalloc": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
         "aaedn_cu_ffn_swiglu": ([_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp], _int),
         "aaedn_memcpy_d2d": ([_vp, _vp, _sz, _vp], _int),
+        "aaedn_cu_sample": ([_vp, _u32, ctypes.c_float, ctypes.c_float, ctypes.c_float, _vp, _vp], _int),
         "aaedn_abn_read_header": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader)], _int),
         "aaedn_abn_read_payload": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader), _vp, _vp], _int),
         "aaedn_model_create": ([ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], _int),
@@ -245,6 +246,16 @@ def ffn_swiglu(d_in, d_out, batch, hidden, ffn, d_gate, d_up, d_down, d_gs, d_us
     scales, silu(g)*u; FFN_REFERENCE: what src/ffn.cpp computes)."""
     check(lib().aaedn_cu_ffn_swiglu(_p(d_in), _p(d_out), batch, hidden, ffn, _p(d_gate), _p(d_up), _p(d_down),
                                     _p(d_gs), _p(d_us), _p(d_ds), semantics, stream))
+
+
+def sample(d_logits, vocab, temperature, top_p, u, d_token, stream=None):
+    """Next token from device logits on the device (docs/mpd.md:539-554;
+    src/main.cpp:214-247 is the reference's plain softmax draw): temperature
+    (<= 0: greedy), nucleus top_p in
+    (0, 1], multinomial draw with the caller's uniform u in [0, 1); the
+    token id goes to the uint32 at d_token."""
+    check(lib().aaedn_cu_sample(_p(d_logits), int(vocab), float(temperature), float(top_p), float(u), _p(d_token),
+                                stream))
 
 
 def abn_read(path):
