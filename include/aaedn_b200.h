@@ -91,6 +91,7 @@ int aaedn_abn_read_header(const char* path, aaedn_abn_header* h_out);
  * checksum mismatch. */
 int aaedn_abn_read_payload(const char* path, const aaedn_abn_header* h_hdr, uint8_t* h_data, uint16_t* h_scales);
 
+
 /* ---- kernels (device pointers) ------------------------------------------ */
 /* include/dequant.hpp:10 dequant_4bit (src/dequant.cpp:7-28): out[i] =
  * code(i) * scale(i/32); all-zero output when data/scales are null or
@@ -236,6 +237,25 @@ int aaedn_model_set_layer(aaedn_model* m, uint32_t layer, const aaedn_layer_host
 /* embedding [vocab][dim], final_norm [dim], lm_head [vocab][dim], fp32 host. */
 int aaedn_model_set_globals(aaedn_model* m, const float* h_embedding, const float* h_final_norm,
                             const float* h_lm_head);
+/* Whole-model files: the per-layer layout of docs/mpd.md:497-499 (RMSNorm
+ * scale fp32 [dim] | QKV weight | QKV bias fp32 | O weight | FFN gate | FFN
+ * up | FFN down | RMSNorm 2 scale fp32 [dim]; a weight = row-major 4-bit
+ * codes then its u16 fp16-bit scales; QKV rows are the q heads, then k, then
+ * v), followed by the final-norm gain fp32 [dim], the embedding and the
+ * lm_head fp32 [vocab][dim]. The reference's converter does not write it yet
+ * (tools/convert_model.py:121-126 writes one matrix), so the header marks it
+ * version 3 and keeps what the documented header lacks in its reserved
+ * bytes: n_kv_heads (u32, offset 49), rope_theta (f32, 53), eps (f32, 57).
+ * Reads and checks the header and returns the model shape (max_seq 0: the
+ * caller chooses the context). AAEDN_EFORMAT when the file is rejected. */
+int aaedn_abn_model_read_header(const char* path, aaedn_abn_header* h_out, aaedn_model_config* cfg_out);
+/* Every weight of a whole-model file (aaedn_abn_model_read_header) into a
+ * model of the same shape (a tensor-parallel rank keeps its share): the
+ * FNV-1a checksum of the payload is checked first, then the layers are read
+ * one at a time. A nonzero QKV bias is AAEDN_EUNSUPPORTED (the model has
+ * none, src/transformer.cpp:112-117). No counterpart in the reference (its
+ * transformer_init fills weights with constants and rand()). */
+int aaedn_model_load_abn(aaedn_model* m, const char* path);
 /* Fill every weight from the seeded generator (N(0,0.02) linear weights
  * quantized with the block quantizer; fp32 embedding and lm_head; norm gains
  * 1.0). Tensor ids: embedding 0, lm_head 1, layer l: 16 + 8l + {q,k,v,o,g,u,d}.

@@ -118,6 +118,9 @@ def lib():
         "aaedn_model_arena_bytes": ([_vp], _sz),
         "aaedn_model_set_layer": ([_vp, _u32, ctypes.POINTER(LayerHost)], _int),
         "aaedn_model_set_globals": ([_vp, _vp, _vp, _vp], _int),
+        "aaedn_abn_model_read_header": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader), ctypes.POINTER(ModelConfig)],
+                                        _int),
+        "aaedn_model_load_abn": ([_vp, ctypes.c_char_p], _int),
         "aaedn_model_synthesize": ([_vp, _u64], _int),
         "aaedn_model_reset": ([_vp], _int),
         "aaedn_model_pos": ([_vp], _u32),
@@ -256,6 +259,16 @@ def sample(d_logits, vocab, temperature, top_p, u, d_token, stream=None):
     token id goes to the uint32 at d_token."""
     check(lib().aaedn_cu_sample(_p(d_logits), int(vocab), float(temperature), float(top_p), float(u), _p(d_token),
                                 stream))
+
+
+def abn_model_config(path, max_seq=4096):
+    """The model shape of a whole-model .abn file (aaedn_abn_model_read_header)
+    as a config dict, with the caller's context length."""
+    h, c = AbnHeader(), ModelConfig()
+    check(lib().aaedn_abn_model_read_header(str(path).encode(), ctypes.byref(h), ctypes.byref(c)))
+    d = c.as_dict()
+    d["max_seq"] = max_seq
+    return d
 
 
 def abn_read(path):
@@ -429,6 +442,10 @@ class Model:
 
     def synthesize(self, seed):
         check(lib().aaedn_model_synthesize(self.h, seed))
+
+    def load_abn(self, path):
+        """Every weight from a whole-model .abn file of this model's shape."""
+        check(lib().aaedn_model_load_abn(self.h, str(path).encode()))
 
     def reset(self):
         check(lib().aaedn_model_reset(self.h))

@@ -364,8 +364,16 @@ void transformer_init(Transformer* tf, Arena* arena, const char* model_path)
     c.rope_theta = 10000.0f;
     c.eps = 1e-6f;
     aaedn_abn_header h{};
-    if (model_path && aaedn_abn_read_header(model_path, &h) == AAEDN_OK && h.n_layers && h.n_heads && h.head_dim &&
-        h.vocab_size && h.hidden_dim && h.ffn_dim)
+    aaedn_model_config fc{};
+    const bool whole = model_path && aaedn_abn_model_read_header(model_path, &h, &fc) == AAEDN_OK;
+    if (whole)
+    {
+        // a whole-model file: its shape and, below, its weights
+        fc.max_seq = c.max_seq;
+        c = fc;
+    }
+    else if (model_path && aaedn_abn_read_header(model_path, &h) == AAEDN_OK && h.n_layers && h.n_heads &&
+             h.head_dim && h.vocab_size && h.hidden_dim && h.ffn_dim)
     {
         c.dim = h.hidden_dim;
         c.n_layers = h.n_layers;
@@ -377,7 +385,7 @@ void transformer_init(Transformer* tf, Arena* arena, const char* model_path)
     aaedn_model* m = nullptr;
     if (aaedn_model_create(&c, &m) != AAEDN_OK)
         return;
-    if (aaedn_model_synthesize(m, 1234) != AAEDN_OK)
+    if ((whole ? aaedn_model_load_abn(m, model_path) : aaedn_model_synthesize(m, 1234)) != AAEDN_OK)
     {
         aaedn_model_destroy(m);
         return;

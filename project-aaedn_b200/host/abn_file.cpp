@@ -1,11 +1,13 @@
 // abn_file.cpp — the .abn v2 model-file reader behind quant_load
-// (src/quant.cpp:31-119; the writer is tools/convert_model.py:130-150).
+// (src/quant.cpp:31-119; the writer is tools/convert_model.py:130-150), and
+// the reader of whole-model files (at the end of this file).
 //
 // The header is read field by field, little-endian, in the order of the
 // format string "<8sIQI6IB15s" (64 bytes). The checks are the reference's:
 // magic "AAEDNMDL", version 2, payload_size == hidden^2/2 + hidden^2/16 (one
 // hidden x hidden block-quantized matrix: codes, then u16 scales), and the
 // FNV-1a 32 checksum of codes followed by scales.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -35,10 +37,11 @@ struct File
 uint32_t le32(const uint8_t* p) { return (uint32_t)p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24; }
 uint64_t le64(const uint8_t* p) { return (uint64_t)le32(p) | (uint64_t)le32(p + 4) << 32; }
 
-int parse(File& file, aaedn_abn_header* h)
+// The 64 header bytes, unchecked beyond the magic; raw keeps them (the full
+// model format keeps more fields in the reserved bytes).
+int parse_raw(File& file, aaedn_abn_header* h, uint8_t* raw)
 {
-    uint8_t raw[64];
-    if (!file.read(raw, sizeof raw))
+    if (!file.read(raw, 64))
         return set_error(AAEDN_EFORMAT, "abn: header shorter than 64 bytes");
     if (std::memcmp(raw, "AAEDNMDL", 8) != 0)
         return set_error(AAEDN_EFORMAT, "abn: bad magic");
@@ -52,6 +55,14 @@ int parse(File& file, aaedn_abn_header* h)
     h->hidden_dim = le32(raw + 40);
     h->ffn_dim = le32(raw + 44);
     h->quant_type = raw[48];
+    return AAEDN_OK;
+}
+
+int parse(File& file, aaedn_abn_header* h)
+{
+    uint8_t raw[64];
+    if (int rc = parse_raw(file, h, raw))
+        return rc;
     if (h->version != kAbnVersion)
         return set_error(AAEDN_EFORMAT, "abn: version %u (want %u)", h->version, kAbnVersion);
     const uint64_t hd = h->hidden_dim;
@@ -99,4 +110,179 @@ extern "C" int aaedn_abn_read_payload(const char* path, const aaedn_abn_header* 
     if (c != h.payload_checksum)
         return set_error(AAEDN_EFORMAT, "abn: checksum %08x, header says %08x", c, h.payload_checksum);
     return AAEDN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Full-model files: the layout of docs/mpd.md:497-499 (per layer, in order:
+// RMSNorm scale, QKV weight, QKV bias, O weight, FFN gate, FFN up, FFN down,
+// RMSNorm 2 scale; a weight is its row-major 4-bit codes, then its u16
+// scales), which the reference's converter does not write yet
+// (tools/convert_model.py:121-126 writes one matrix). Stored as version 3
+// with what the documented header lacks in its reserved bytes, and the
+// model's remaining tensors after the layers.
+namespace
+{
+
+constexpr uint32_t kAbnModelVersion = 3;
+
+struct ModelDims
+{
+    uint64_t D, qkv, qdim, F, V;
+};
+
+ModelDims dims_of(const aaedn_model_config& c)
+{
+    return {c.dim, (uint64_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim, (uint64_t)c.n_heads * c.head_dim,
+            c.ffn_dim, c.vocab};
+}
+
+uint64_t q4_bytes(uint64_t rows, uint64_t cols) { return rows * cols / 2 + rows * cols / 32 * 2; }
+
+uint64_t layer_bytes(const ModelDims& d)
+{
+    return d.D * 4 + q4_bytes(d.qkv, d.D) + d.qkv * 4 + q4_bytes(d.D, d.qdim) + 2 * q4_bytes(d.F, d.D) +
+           q4_bytes(d.D, d.F) + d.D * 4;
+}
+
+uint64_t model_payload_bytes(const aaedn_model_config& c)
+{
+    const ModelDims d = dims_of(c);
+    return (uint64_t)c.n_layers * layer_bytes(d) + d.D * 4 + 2 * d.V * d.D * 4;
+}
+
+float lef32(const uint8_t* p)
+{
+    const uint32_t u = le32(p);
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+int parse_model(File& file, aaedn_abn_header* h, aaedn_model_config* c)
+{
+    uint8_t raw[64];
+    if (int rc = parse_raw(file, h, raw))
+        return rc;
+    if (h->version != kAbnModelVersion)
+        return set_error(AAEDN_EFORMAT, "abn: version %u is not a full-model file (%u)", h->version,
+                         kAbnModelVersion);
+    if (h->quant_type != 0)
+        return set_error(AAEDN_EUNSUPPORTED, "abn: quant_type %u (only 0, 4-bit blocks)", h->quant_type);
+    *c = aaedn_model_config{};
+    c->dim = h->hidden_dim;
+    c->n_layers = h->n_layers;
+    c->n_heads = h->n_heads;
+    c->n_kv_heads = le32(raw + 49);
+    c->head_dim = h->head_dim;
+    c->ffn_dim = h->ffn_dim;
+    c->vocab = h->vocab_size;
+    c->rope_theta = lef32(raw + 53);
+    c->eps = lef32(raw + 57);
+    if (!c->dim || !c->n_layers || !c->n_heads || !c->n_kv_heads || !c->head_dim || !c->ffn_dim || !c->vocab ||
+        c->n_heads % c->n_kv_heads || c->dim % 32 || c->ffn_dim % 32 || (c->n_heads * c->head_dim) % 32 ||
+        !(c->rope_theta > 0.0f) || !(c->eps > 0.0f))
+        return set_error(AAEDN_EFORMAT, "abn: model dimensions in the header do not describe a model");
+    if (h->payload_size != model_payload_bytes(*c))
+        return set_error(AAEDN_EFORMAT, "abn: payload_size %llu, the header's dimensions need %llu",
+                         (unsigned long long)h->payload_size, (unsigned long long)model_payload_bytes(*c));
+    return AAEDN_OK;
+}
+
+} // namespace
+
+extern "C" int aaedn_abn_model_read_header(const char* path, aaedn_abn_header* h_out, aaedn_model_config* cfg_out)
+{
+    if (!path || !h_out || !cfg_out)
+        return set_error(AAEDN_EINVAL, "aaedn_abn_model_read_header: null argument");
+    std::memset(h_out, 0, sizeof *h_out);
+    File file(path);
+    if (!file.f)
+        return set_error(AAEDN_EFORMAT, "abn: cannot open %s", path);
+    return parse_model(file, h_out, cfg_out);
+}
+
+extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
+{
+    if (!m || !path)
+        return set_error(AAEDN_EINVAL, "aaedn_model_load_abn: null argument");
+    aaedn_model_config mc{}, fc{};
+    if (int rc = aaedn_model_config_get(m, &mc))
+        return rc;
+    aaedn_abn_header h{};
+    {
+        File file(path);
+        if (!file.f)
+            return set_error(AAEDN_EFORMAT, "abn: cannot open %s", path);
+        if (int rc = parse_model(file, &h, &fc))
+            return rc;
+        if (fc.dim != mc.dim || fc.n_layers != mc.n_layers || fc.n_heads != mc.n_heads ||
+            fc.n_kv_heads != mc.n_kv_heads || fc.head_dim != mc.head_dim || fc.ffn_dim != mc.ffn_dim ||
+            fc.vocab != mc.vocab)
+            return set_error(AAEDN_EINVAL, "aaedn_model_load_abn: the file's model shape differs from the model's");
+        // pass 1: the checksum, before any weight reaches the model
+        std::vector<uint8_t> buf(64u << 20);
+        uint32_t c = 0x811C9DC5u;
+        for (uint64_t left = h.payload_size; left > 0;)
+        {
+            const size_t n = (size_t)std::min<uint64_t>(left, buf.size());
+            if (!file.read(buf.data(), n))
+                return set_error(AAEDN_EFORMAT, "abn: payload shorter than %llu bytes",
+                                 (unsigned long long)h.payload_size);
+            c = aaedn_fnv1a32(buf.data(), n, c);
+            left -= n;
+        }
+        if (c != h.payload_checksum)
+            return set_error(AAEDN_EFORMAT, "abn: checksum %08x, header says %08x", c, h.payload_checksum);
+    }
+    // pass 2: layer by layer into the model
+    File file(path);
+    aaedn_abn_header h2{};
+    if (!file.f || parse_model(file, &h2, &fc) || h2.payload_checksum != h.payload_checksum)
+        return set_error(AAEDN_EFORMAT, "abn: %s changed while it was read", path);
+    const ModelDims d = dims_of(fc);
+    const uint64_t qrows = d.qdim, krows = (uint64_t)fc.n_kv_heads * fc.head_dim;
+    std::vector<float> an(d.D), fn(d.D), bias(d.qkv);
+    std::vector<uint8_t> qkv_c(d.qkv * d.D / 2), o_c(d.D * d.qdim / 2), g_c(d.F * d.D / 2), u_c(d.F * d.D / 2),
+        d_c(d.D * d.F / 2);
+    std::vector<uint16_t> qkv_s(d.qkv * d.D / 32), o_s(d.D * d.qdim / 32), g_s(d.F * d.D / 32), u_s(d.F * d.D / 32),
+        d_s(d.D * d.F / 32);
+    auto rd = [&](void* dst, size_t n) { return file.read(dst, n); };
+    for (uint32_t l = 0; l < fc.n_layers; ++l)
+    {
+        const bool ok = rd(an.data(), d.D * 4) && rd(qkv_c.data(), qkv_c.size()) && rd(qkv_s.data(), qkv_s.size() * 2) &&
+                        rd(bias.data(), d.qkv * 4) && rd(o_c.data(), o_c.size()) && rd(o_s.data(), o_s.size() * 2) &&
+                        rd(g_c.data(), g_c.size()) && rd(g_s.data(), g_s.size() * 2) && rd(u_c.data(), u_c.size()) &&
+                        rd(u_s.data(), u_s.size() * 2) && rd(d_c.data(), d_c.size()) &&
+                        rd(d_s.data(), d_s.size() * 2) && rd(fn.data(), d.D * 4);
+        if (!ok)
+            return set_error(AAEDN_EFORMAT, "abn: layer %u cut short", l);
+        for (float b : bias)
+            if (b != 0.0f) // decision D8: the model has no bias (src/transformer.cpp:112-117 zeroes it)
+                return set_error(AAEDN_EUNSUPPORTED, "abn: layer %u has a nonzero QKV bias", l);
+        // QKV rows are q, then k, then v: each matrix is a contiguous run of
+        // the codes and of the scales
+        aaedn_layer_host w{};
+        w.wq = qkv_c.data();
+        w.wk = qkv_c.data() + qrows * d.D / 2;
+        w.wv = qkv_c.data() + (qrows + krows) * d.D / 2;
+        w.sq = qkv_s.data();
+        w.sk = qkv_s.data() + qrows * d.D / 32;
+        w.sv = qkv_s.data() + (qrows + krows) * d.D / 32;
+        w.wo = o_c.data();
+        w.so = o_s.data();
+        w.wg = g_c.data();
+        w.sg = g_s.data();
+        w.wu = u_c.data();
+        w.su = u_s.data();
+        w.wd = d_c.data();
+        w.sd = d_s.data();
+        w.attn_norm = an.data();
+        w.ffn_norm = fn.data();
+        if (int rc = aaedn_model_set_layer(m, l, &w))
+            return rc;
+    }
+    std::vector<float> final_norm(d.D), emb(d.V * d.D), lm(d.V * d.D);
+    if (!rd(final_norm.data(), d.D * 4) || !rd(emb.data(), emb.size() * 4) || !rd(lm.data(), lm.size() * 4))
+        return set_error(AAEDN_EFORMAT, "abn: embedding or lm_head cut short");
+    return aaedn_model_set_globals(m, emb.data(), final_norm.data(), lm.data());
 }

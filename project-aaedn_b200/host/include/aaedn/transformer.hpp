@@ -1,12 +1,14 @@
 // transformer.hpp — mirror of the reference include/transformer.hpp.
 //
-// transformer_init takes the model dimensions from the .abn header at
-// model_path (src/quant.cpp's checks; the reference's hard-coded shape,
-// src/transformer.cpp:37-43, when the file is missing or rejected) and builds
-// a device-resident model whose weights are seeded N(0, 0.02) values
-// quantized with the reference quantizer (the reference fills its weights
-// with rand() and constants, src/transformer.cpp:54-121; real weights go in
-// through aaedn_model_set_layer). transformer_forward runs the token loop on
+// transformer_init builds a device-resident model from the file at
+// model_path: a whole-model .abn file (aaedn_abn_model_read_header) gives the
+// shape and every weight; otherwise the shape comes from an .abn v2 header
+// (src/quant.cpp's checks; the reference's hard-coded shape,
+// src/transformer.cpp:37-43, when the file is missing or rejected) and the
+// weights are seeded N(0, 0.02) values quantized with the reference
+// quantizer (the reference fills its weights with rand() and constants,
+// src/transformer.cpp:54-121; real weights also go in through
+// aaedn_model_set_layer). The context is 16384 tokens. transformer_forward runs the token loop on
 // the B200 for all seq_len tokens at the model's current position and copies
 // the last token's logits to the HOST array `logits` (vocab_size floats).
 // kv_cache and rope_tables stay null: the model keeps its paged cache and

@@ -114,3 +114,41 @@ def test_abn_reader_matches_oracle(oracle, tmp_path, case):
         assert h.version == 2 and h.hidden_dim == 64 and h.vocab_size == 1000
         np.testing.assert_array_equal(data, codes)
         np.testing.assert_array_equal(sc, scales)
+
+
+WHOLE = dict(dim=256, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=32, ffn_dim=512, vocab=1000, max_seq=200,
+             rope_theta=500000.0, eps=1e-6)
+
+
+def test_whole_model_file_header_round_trip(tmp_path):
+    import abn_model_file
+    w = ab.synthetic_weights(WHOLE, 31)
+    path = tmp_path / "m.abn"
+    n = abn_model_file.write(path, WHOLE, w)
+    cfg = ab.abn_model_config(path, max_seq=200)
+    assert cfg == {**WHOLE, "rope_theta": np.float32(WHOLE["rope_theta"]), "eps": np.float32(WHOLE["eps"])}
+    assert path.stat().st_size == 64 + n
+
+
+def test_whole_model_file_rejections(tmp_path):
+    import abn_model_file
+    w = ab.synthetic_weights(WHOLE, 31)
+    good = tmp_path / "good.abn"
+    abn_model_file.write(good, WHOLE, w)
+    raw = good.read_bytes()
+    cases = {
+        "short": raw[:40],
+        "magic": b"X" + raw[1:],
+        "v2": raw[:8] + (2).to_bytes(4, "little") + raw[12:],               # a one-matrix file's version
+        "size": raw[:12] + (len(raw) - 65).to_bytes(8, "little") + raw[20:],  # payload_size off by one
+        "kv": raw[:49] + (3).to_bytes(4, "little") + raw[53:],               # 8 heads over 3 kv heads
+    }
+    for name, blob in cases.items():
+        p = tmp_path / f"{name}.abn"
+        p.write_bytes(blob)
+        with pytest.raises(ab.AaednError) as e:
+            ab.abn_model_config(p)
+        assert e.value.rc == ab.EFORMAT, name
+    # the one-matrix reader keeps rejecting whole-model files (version 3)
+    with pytest.raises(ab.AaednError):
+        ab.abn_read(good)

@@ -161,3 +161,37 @@ def test_launch_count_per_step():
     gm.status()
     assert ab.kernel_launches() - n0 == 2 * (5 * cfg["n_layers"] + 1)
     gm.close()
+
+
+def test_model_from_whole_model_file(tmp_path):
+    """aaedn_model_load_abn: a whole-model .abn file gives the same greedy
+    tokens and logits as the same weights handed over in memory (the oracle's);
+    a corrupted payload or a nonzero QKV bias is refused before any weight of
+    the model changes."""
+    import abn_model_file
+    cfg = GQA_SMALL
+    w = ab.synthetic_weights(cfg, 41)
+    path = tmp_path / "m.abn"
+    abn_model_file.write(path, cfg, w)
+    gm = ab.Model(ab.abn_model_config(path, max_seq=cfg["max_seq"]))
+    gm.load_abn(path)
+    om = pyoracle.OracleModel(pyoracle.Oracle(), cfg, w)
+    prompt = ab.synth_tokens(41, 0, cfg["vocab"], 6)
+    want, wl = om.generate(prompt, 40)
+    np.testing.assert_array_equal(gm.generate(prompt, 40), want)
+    assert _rel_err(gm.logits(), wl) < 1e-4
+    raw = bytearray(path.read_bytes())
+    raw[-1] ^= 1
+    bad = tmp_path / "bad.abn"
+    bad.write_bytes(bytes(raw))
+    with pytest.raises(ab.AaednError) as e:
+        gm.load_abn(bad)
+    assert e.value.rc == ab.EFORMAT
+    biased = tmp_path / "bias.abn"
+    abn_model_file.write(biased, cfg, w, bias=np.full((cfg["n_heads"] + 2 * cfg["n_kv_heads"]) * cfg["head_dim"], 0.5))
+    with pytest.raises(ab.AaednError) as e:
+        gm.load_abn(biased)
+    assert e.value.rc == ab.EUNSUPPORTED
+    gm.reset()
+    np.testing.assert_array_equal(gm.generate(prompt, 40), want)  # the refused files changed nothing
+    gm.close()
