@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -68,6 +69,27 @@ inline std::vector<uint8_t> valid_model(const Dims& d, std::vector<uint8_t>* cod
     if (scales_out)
         *scales_out = scales;
     return out;
+}
+
+// A whole-model file (the layout aaedn_abn_model_read_header documents):
+// version 3, n_kv_heads / rope_theta / eps in the reserved bytes, then the
+// given payload.
+inline std::vector<uint8_t> whole_model_header(const Dims& d, uint32_t n_kv_heads, float theta, float eps,
+                                               const std::vector<uint8_t>& payload)
+{
+    std::vector<uint8_t> out = header(3, payload.size(), fnv1a(payload.data(), payload.size()), d);
+    auto put = [&](size_t at, const void* v) { std::memcpy(out.data() + at, v, 4); };
+    put(49, &n_kv_heads);
+    put(53, &theta);
+    put(57, &eps);
+    return out;
+}
+
+template <typename T>
+inline void append(std::vector<uint8_t>& out, const std::vector<T>& v)
+{
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(v.data());
+    out.insert(out.end(), p, p + v.size() * sizeof(T));
 }
 
 inline void write_file(const std::string& path, const std::vector<uint8_t>& data)

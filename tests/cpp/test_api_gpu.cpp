@@ -369,6 +369,100 @@ int main(int argc, char** argv)
         CHECK(tf.model == nullptr);
     }
 
+    // ---- transformer_init from a whole-model file: the same logits as the
+    // same weights handed to a model through the C ABI
+    {
+        abn_test::Dims md;
+        md.n_layers = 2, md.n_heads = 4, md.head_dim = 32, md.vocab = 1000, md.hidden = 128, md.ffn = 256;
+        const uint32_t KV = 2, D = md.hidden, F = md.ffn, V = md.vocab, QR = md.n_heads * md.head_dim,
+                       KR = KV * md.head_dim;
+        auto q4 = [&](size_t rows, size_t cols, std::vector<uint8_t>& c, std::vector<uint16_t>& s) {
+            std::vector<float> x(rows * cols);
+            for (auto& v : x)
+                v = 0.02f * frand();
+            c.resize(rows * cols / 2);
+            s.resize(rows * cols / 32);
+            aaedn_quantize_q4(x.data(), x.size(), c.data(), s.data());
+        };
+        struct Layer
+        {
+            std::vector<uint8_t> c[7];
+            std::vector<uint16_t> s[7];
+            std::vector<float> an, fn;
+        };
+        const size_t rows[7] = {QR, KR, KR, D, F, F, D}, cols[7] = {D, D, D, QR, D, D, F};
+        std::vector<Layer> L(md.n_layers);
+        std::vector<uint8_t> payload;
+        for (auto& l : L)
+        {
+            for (int i = 0; i < 7; ++i)
+                q4(rows[i], cols[i], l.c[i], l.s[i]);
+            l.an.assign(D, 1.0f);
+            l.fn.assign(D, 1.0f);
+            for (size_t i = 0; i < D; ++i)
+                l.an[i] += 0.1f * frand(), l.fn[i] += 0.1f * frand();
+            abn_test::append(payload, l.an);
+            for (int i = 0; i < 3; ++i) // QKV codes: q rows, k rows, v rows
+                abn_test::append(payload, l.c[i]);
+            for (int i = 0; i < 3; ++i) // then their scales
+                abn_test::append(payload, l.s[i]);
+            abn_test::append(payload, std::vector<float>(QR + 2 * KR, 0.0f)); // QKV bias
+            for (int i = 3; i < 7; ++i)
+            {
+                abn_test::append(payload, l.c[i]);
+                abn_test::append(payload, l.s[i]);
+            }
+            abn_test::append(payload, l.fn);
+        }
+        std::vector<float> fnorm(D, 1.0f), emb((size_t)V * D), lm((size_t)V * D);
+        for (auto& v : emb)
+            v = 0.02f * frand();
+        for (auto& v : lm)
+            v = 0.02f * frand();
+        abn_test::append(payload, fnorm);
+        abn_test::append(payload, emb);
+        abn_test::append(payload, lm);
+        std::vector<uint8_t> file = abn_test::whole_model_header(md, KV, 10000.0f, 1e-6f, payload);
+        file.insert(file.end(), payload.begin(), payload.end());
+        abn_test::write_file(dir + "/whole.abn", file);
+
+        aaedn::Transformer tf;
+        aaedn::transformer_init(&tf, &arena, (dir + "/whole.abn").c_str());
+        const bool shaped = tf.model && tf.n_layers == 2 && tf.hidden_dim == D && tf.vocab_size == V;
+        CHECK(shaped);
+        aaedn_model_config c{};
+        aaedn_model_config_get(tf.model, &c);
+        CHECK(c.n_kv_heads == KV && c.rope_theta == 10000.0f);
+        if (!shaped || c.n_kv_heads != KV) // the weights below only fit that shape
+        {
+            aaedn::transformer_destroy(&tf);
+            aaedn::arena_destroy(&arena);
+            std::printf("FAILED\n");
+            return 1;
+        }
+        const uint32_t ids[3] = {3, 141, 592};
+        std::vector<float> got(V), want(V);
+        aaedn::transformer_forward(&tf, ids, 3, got.data());
+        aaedn_model* m2 = nullptr;
+        CHECK(aaedn_model_create(&c, &m2) == AAEDN_OK);
+        for (uint32_t li = 0; li < md.n_layers; ++li)
+        {
+            const Layer& l = L[li];
+            aaedn_layer_host w{};
+            w.wq = l.c[0].data(), w.wk = l.c[1].data(), w.wv = l.c[2].data(), w.wo = l.c[3].data();
+            w.wg = l.c[4].data(), w.wu = l.c[5].data(), w.wd = l.c[6].data();
+            w.sq = l.s[0].data(), w.sk = l.s[1].data(), w.sv = l.s[2].data(), w.so = l.s[3].data();
+            w.sg = l.s[4].data(), w.su = l.s[5].data(), w.sd = l.s[6].data();
+            w.attn_norm = l.an.data(), w.ffn_norm = l.fn.data();
+            CHECK(aaedn_model_set_layer(m2, li, &w) == AAEDN_OK);
+        }
+        CHECK(aaedn_model_set_globals(m2, emb.data(), fnorm.data(), lm.data()) == AAEDN_OK);
+        CHECK(aaedn_model_forward(m2, ids, 3, want.data()) == AAEDN_OK);
+        CHECK(got == want);
+        aaedn_model_destroy(m2);
+        aaedn::transformer_destroy(&tf);
+    }
+
     aaedn::arena_destroy(&arena);
     std::printf("%s\n", fails ? "FAILED" : "PASSED");
     return fails ? 1 : 0;
