@@ -82,7 +82,7 @@ def _rank(rank, size, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("size", [2])
+@pytest.mark.parametrize("size", [2, 4])
 def test_tp_shares_recombine_to_the_whole_layer(size):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
