@@ -114,3 +114,23 @@ def test_tp_plan_rejects_shapes_that_do_not_divide():
         ab.tp_plan(CFG, 0, 3)
     p = ab.tp_plan(dict(ab.LLAMA2_7B), 7, 8)
     assert p["ffn_dim"] == 1376 and p["down_k"] == 1408 and p["o_k"] == 512 and p["vocab0"] == 28000
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_tp_plan_7b_shares(size):
+    """The 7B shape splits at 2, 4 and 8 ranks: heads, kv heads, FFN rows and
+    vocabulary rows tile the whole without overlap, and the row-parallel
+    input widths (o, down) are padded to whole 128-code tiles (11008 / 4 =
+    2752 FFN columns per rank -> 2816), which the tile-major GEMV needs."""
+    cfg = dict(ab.LLAMA2_7B)
+    plans = [ab.tp_plan(cfg, r, size) for r in range(size)]
+    assert sum(p["n_heads"] for p in plans) == cfg["n_heads"]
+    assert sum(p["n_kv_heads"] for p in plans) == cfg["n_kv_heads"]
+    assert sum(p["ffn_dim"] for p in plans) == cfg["ffn_dim"]
+    assert sum(p["vocab"] for p in plans) == cfg["vocab"]
+    for r, p in enumerate(plans):
+        assert p["q_head0"] == r * p["n_heads"] and p["kv_head0"] == r * p["n_kv_heads"]
+        assert p["ffn_row0"] == r * p["ffn_dim"]
+        assert p["o_k"] % 128 == 0 and p["o_k"] >= p["n_heads"] * cfg["head_dim"]
+        assert p["down_k"] % 128 == 0 and p["down_k"] >= p["ffn_dim"] and p["down_k"] - p["ffn_dim"] < 128
+    assert [p["vocab0"] for p in plans] == list(np.cumsum([0] + [p["vocab"] for p in plans[:-1]]))
