@@ -649,7 +649,7 @@ static AttnParams attn_params(const aaedn_model* m, uint32_t l, int S)
 static GemvParams o_params(const aaedn_model* m, uint32_t l)
 {
     const aaedn_model_config& c = m->cfg;
-    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads;
+    const int D = (int)c.dim;
     const DevLayer& L = m->layers[l];
     GemvParams o{};
     o.w = L.wo;
@@ -718,7 +718,7 @@ static GemvParams gu_params(const aaedn_model* m, uint32_t l)
 static GemvParams down_params(const aaedn_model* m, uint32_t l)
 {
     const aaedn_model_config& c = m->cfg;
-    const int D = (int)c.dim, F = (int)c.ffn_dim;
+    const int D = (int)c.dim;
     const DevLayer& L = m->layers[l];
     GemvParams dn{};
     dn.w = L.wd;
