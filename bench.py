@@ -25,7 +25,15 @@ restatement on the host cores, rank 0 only).
 Reference arm (--impl reference): the reference's CPU token loop cannot run
 end to end (src/transformer.cpp:156 overflows a static buffer), so the arm
 times the CPU restatement of that loop (oracle/, built with the reference's
-own flags) on all host threads, on a bounded sample of the same workload.
+own flags) on all host threads, on a bounded sample of the same workload:
+the same weights (the oracle's restatement of the seeded generator and of
+the block quantizer), decode steps from the same first position. It loads
+nothing of this repository's CUDA library.
+
+Parity: when the workload is the full 7B model with the 128-token prompt,
+the first 32 greedy tokens of the run (every N, tensor parallel included)
+are compared with the oracle's (tests/golden/llama2_7b_seed1234.npz) and the
+line carries "parity": true/false.
 """
 import argparse
 import json
@@ -44,6 +52,12 @@ METRIC = "decode tok/s (7B-shape, bs1, 1 GPU) + dequant-GEMV GB/s vs HBM peak"
 SEED = 1234
 PROMPT = 128
 FALLBACK_HBM_GBS = 6650.0
+# the Llama-2-7B-shaped model (both arms; the reference arm must not import
+# the CUDA library's package for it)
+LLAMA2_7B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, head_dim=128, ffn_dim=11008, vocab=32000,
+                 max_seq=4096, rope_theta=10000.0, eps=1e-6)
+PARITY_FIXTURE = os.path.join(ROOT, "tests", "golden", "llama2_7b_seed1234.npz")
+PARITY_TOKENS = 32
 
 
 def parse():
@@ -67,8 +81,7 @@ def parse():
 
 
 def model_cfg(args=None):
-    import aaedn_b200 as ab
-    cfg = dict(ab.LLAMA2_7B)
+    cfg = dict(LLAMA2_7B)
     if args is not None and args.layers:
         cfg["n_layers"] = args.layers
     if args is not None and args.ctx:
@@ -174,63 +187,120 @@ def gpu_identity(dev_index):
     return str(dev_index)
 
 
-def host_weights(cfg):
-    import aaedn_b200 as ab
-    return ab.synthetic_weights(cfg, SEED)
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
-def cpu_decode_sample(cfg, w, seconds, steps_cap=None):
+def oracle_weights(cfg):
+    """The seeded synthetic model built by the oracle alone (bit-identical to
+    the library's aaedn_model_synthesize, tests/test_oracle_golden.py)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    o = pyoracle.Oracle()
+    o.set_threads(host_cores())
+    return pyoracle.synthetic_weights(cfg, SEED, o)
+
+
+def cpu_decode_sample(cfg, w, seconds, pos0, steps_cap=None, warmup=1):
     """Times greedy decode steps of the CPU restatement (oracle/, reference
-    flags, all host threads) after a 2-token prompt; returns (tok/s, steps,
+    flags, every host core) from position pos0 (the cache below it filled by
+    the oracle's seek), `warmup` untimed steps first; returns (tok/s, steps,
     threads, description)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle
-    import aaedn_b200 as ab
     orc = pyoracle.Oracle(fast=True)
-    c = dict(cfg, max_seq=256)
+    # torch.distributed.run exports OMP_NUM_THREADS=1: the CPU arm sets its
+    # thread count itself
+    orc.set_threads(host_cores())
+    n_ctx = pos0 + warmup + (steps_cap or 256) + 2
+    c = dict(cfg, max_seq=min(cfg["max_seq"], max(256, n_ctx)))
     om = pyoracle.OracleModel(orc, c, w)
-    prompt = ab.synth_tokens(SEED, 0, cfg["vocab"], 2)
-    logits = None
-    for t in prompt:
-        logits = om.step(t)
+    om.seek(pos0)
+    tok = int(orc.synth_tokens(SEED, 0, cfg["vocab"], 1)[0])
+    for _ in range(max(1, warmup)):
+        tok = int(np.argmax(om.step(tok)))
     t0 = time.perf_counter()
-    tok = int(np.argmax(logits))
     logits = om.step(tok)
     first = time.perf_counter() - t0
-    n = max(1, min(int(seconds / max(first, 1e-3)), steps_cap or 10 ** 9, 256 - 10))
+    n = max(1, min(int(seconds / max(first, 1e-3)), steps_cap or 10 ** 9, c["max_seq"] - om.pos - 1))
     t0 = time.perf_counter()
     for _ in range(n):
         tok = int(np.argmax(logits))
         logits = om.step(tok)
     dt = time.perf_counter() - t0
-    desc = (f"{n} greedy decode steps of the full 7B-shape model at positions 3..{2 + n} after a 2-token prompt "
-            f"(oracle built -O3 -mavx2 -mfma -ffast-math, OpenMP over GEMV rows and heads)")
+    p1 = om.pos
+    desc = (f"{n} greedy decode steps of the full {cfg['n_layers']}-layer 7B-shape model at positions "
+            f"{p1 - n}..{p1 - 1} (the GPU arm's first timed position {pos0}; K/V below it from the oracle's "
+            f"seek), oracle built -O3 -mavx2 -mfma -ffast-math, OpenMP over GEMV rows and heads on "
+            f"{orc.threads()} threads")
+    cpu_decode_sample.last_positions = [p1 - n, p1]
     return n / dt, n, orc.threads(), desc
+
+
+def workload_config(cfg, args, positions=None, parallelism="single GPU"):
+    full = (cfg["n_layers"], args.prompt) == (32, PROMPT)
+    return {"workload": ("llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode" if full else
+                         f"profiling case: {cfg['n_layers']} layers, {args.prompt}-token prompt"),
+            "dim": cfg["dim"], "n_layers": cfg["n_layers"], "n_heads": cfg["n_heads"],
+            "head_dim": cfg["head_dim"], "ffn_dim": cfg["ffn_dim"], "vocab": cfg["vocab"],
+            "ctx": cfg["max_seq"], "prompt": args.prompt,
+            "positions": positions if positions is not None else [args.prompt + max(3, args.warmup),
+                                                                  args.prompt + max(3, args.warmup) + args.steps],
+            "weights": "4-bit codes, fp16 scale per 32, fp32 embedding/lm_head",
+            "l2": "inputs larger than L2: 4.1 GB of weights streamed per step",
+            "parallelism": parallelism}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cfg = model_cfg()
+    cfg = model_cfg(args)
     if not os.path.exists(os.path.join(ROOT, "oracle", "build", "liboracle_fast.so")):
         subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=True, capture_output=True)
-    w = host_weights(cfg)
-    # each step is one decode token; the count is bounded so the run stays
-    # within a few minutes of CPU time
+    w = oracle_weights(cfg)
+    # the GPU arm's timed region starts after the prompt and W warm-up steps;
+    # each step here is one decode token from there, the count bounded so the
+    # run stays within a few minutes of CPU time
+    W = max(3, args.warmup)
+    pos0 = args.prompt + W
     cap = max(1, args.steps)
-    value, n, threads, desc = cpu_decode_sample(cfg, w, seconds=max(5.0, args.cpu_seconds), steps_cap=cap)
+    value, n, threads, desc = cpu_decode_sample(cfg, w, seconds=max(5.0, args.cpu_seconds), pos0=pos0,
+                                                steps_cap=cap)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": n, "warmup": 1, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+        "steps": n, "warmup": 1, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 else "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "llama2-7b-shape q4 greedy decode bs1 (CPU restatement of the reference loop)",
-                   "dim": cfg["dim"], "n_layers": cfg["n_layers"], "vocab": cfg["vocab"]},
+        "config": dict(workload_config(cfg, args, positions=cpu_decode_sample.last_positions,
+                                       parallelism=f"CPU, {threads} threads"),
+                       sample=f"{n} decode steps against the GPU arm's {args.steps}, from its first timed "
+                              f"position {pos0} (+ the warm-up step)"),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def parity_check(model, cfg, args, tp):
+    """The run's first greedy tokens against the oracle fixture of the full 7B
+    model (None when the workload is not that model)."""
+    if (cfg["n_layers"], args.prompt) != (32, PROMPT) or not os.path.exists(PARITY_FIXTURE):
+        return None
+    fx = np.load(PARITY_FIXTURE)
+    want = fx["tokens"][:PARITY_TOKENS]
+    have = model.pos - args.prompt + 1  # greedy tokens produced since the prompt
+    if have < PARITY_TOKENS:
+        model.decode_steps(PARITY_TOKENS - have)
+    got = model.tokens(PARITY_TOKENS)
+    bad = np.nonzero(got != want)[0]
+    return {"match": bool(bad.size == 0), "tokens": PARITY_TOKENS,
+            "first_mismatch": int(bad[0]) if bad.size else None,
+            "against": "tests/golden/llama2_7b_seed1234.npz (strict oracle, seed 1234)"}
 
 
 def run_ours(args):
@@ -257,9 +327,8 @@ def run_ours(args):
         raise SystemExit(f"steps+warmup too large for ctx {cfg['max_seq']}")
 
     tp = world > 1 and args.mode == "tp"
-    w = host_weights(cfg)
     model = ab.Model(cfg, tp=(rank, world) if tp else None)
-    model.set_weights(w)
+    model.synthesize(SEED)  # the seeded synthetic model, generated and quantized on the host, uploaded
     if tp:
         model.connect_tp()
     stream = torch.cuda.ExternalStream(model.stream)
@@ -286,6 +355,9 @@ def run_ours(args):
     launches = ab.kernel_launches() - launches0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    # the run's first greedy tokens against the oracle (outside the timed
+    # region; every rank takes the same steps)
+    parity = parity_check(model, cfg, args, tp)
     t = torch.tensor([ms], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -358,7 +430,7 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            v, n, threads, desc = cpu_decode_sample(cfg, w, args.cpu_seconds)
+            v, n, threads, desc = cpu_decode_sample(cfg, oracle_weights(cfg), args.cpu_seconds, pos0=pos0)
             cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
         except Exception as ex:  # the GPU number stands without it
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
@@ -369,16 +441,12 @@ def run_ours(args):
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": ("llama2-7b-shape q4 greedy decode bs1: 128-token prompt, then decode"
-                                    if (cfg["n_layers"], args.prompt) == (32, 128) else
-                                    f"profiling case: {cfg['n_layers']} layers, {args.prompt}-token prompt"),
-                       "dim": cfg["dim"], "n_layers": cfg["n_layers"], "n_heads": cfg["n_heads"],
-                       "head_dim": cfg["head_dim"], "ffn_dim": cfg["ffn_dim"], "vocab": cfg["vocab"],
-                       "ctx": cfg["max_seq"], "prompt": args.prompt, "positions": [pos0, pos1],
-                       "weights": "4-bit codes, fp16 scale per 32, fp32 embedding/lm_head",
-                       "l2": "inputs larger than L2: 4.1 GB of weights streamed per step",
-                       "parallelism": (f"tp{world} (heads, ffn rows, lm_head rows; partials added over NVLink "
-                                       "peer memory)" if tp else f"replicas x{world}" if world > 1 else "single GPU")},
+            "config": workload_config(cfg, args, positions=[pos0, pos1],
+                                      parallelism=(f"tp{world} (heads, ffn rows, lm_head rows; partials added "
+                                                   "over NVLink peer memory)" if tp else
+                                                   f"replicas x{world}" if world > 1 else "single GPU")),
+            "parity": None if parity is None else parity["match"],
+            "parity_detail": parity,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "gemv_tiled_i8_kernel (the 4 dequant-GEMVs of every layer, M=1)",

@@ -83,8 +83,13 @@ void or_quantize_q4(const float* x, size_t n, uint8_t* data, uint16_t* scales)
     const size_t BS = 32; /* convert_model.py:12 */
     size_t n_blocks = (n + BS - 1) / BS;
     memset(data, 0, (n + 1) / 2); /* pack_nibbles_unsigned zero-initialises, :25 */
-    for (size_t b = 0; b < n_blocks; ++b)
+    /* blocks own disjoint bytes (32 codes = 16 bytes): the loop runs over
+     * them in parallel with the same results as the sequential order */
+    long long NB = (long long)n_blocks;
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long long bb = 0; bb < NB; ++bb)
     {
+        size_t b = (size_t)bb;
         size_t start = b * BS, end = start + BS < n ? start + BS : n;
         /* :47 max_val = float(np.max(np.abs(block))) -- max taken in fp32 */
         float mx = 0.0f;
@@ -618,4 +623,79 @@ int or_model_generate(or_model* m, const uint32_t* prompt, size_t n_prompt, size
         memcpy(last_logits, logits, m->c.vocab * sizeof(float));
     free(logits);
     return rc;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Seeded synthetic inputs                                                    */
+/* ------------------------------------------------------------------------ */
+/* The counter-based generator the library's synthetic models are built from
+ * (its aaedn_synth_normal / aaedn_synth_tokens), restated here so that a test
+ * or the CPU baseline builds the same weights and prompts without loading
+ * the library: splitmix64 keyed by (seed, tensor id), one 64-bit draw per
+ * element pair, Box-Muller in fp64. */
+static uint64_t or_splitmix64(uint64_t x)
+{
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static uint64_t or_stream_key(uint64_t seed, uint64_t id)
+{
+    return or_splitmix64(seed ^ or_splitmix64(id + 0x632BE59BD9B4E019ull));
+}
+
+void or_synth_normal(uint64_t seed, uint64_t id, float std_dev, float* out, size_t n)
+{
+    const uint64_t key = or_stream_key(seed, id);
+    const double two_pi = 6.283185307179586476925286766559;
+    long long pairs = (long long)((n + 1) / 2);
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long long pp = 0; pp < pairs; ++pp)
+    {
+        size_t i = (size_t)pp * 2;
+        uint64_t h = or_splitmix64(key + (uint64_t)pp * 0x9E3779B97F4A7C15ull);
+        double u1 = ((double)(h >> 40) + 1.0) * (1.0 / 16777216.0); /* (0, 1] */
+        double u2 = (double)(h & 0xFFFFFFull) * (1.0 / 16777216.0);  /* [0, 1) */
+        double r = sqrt(-2.0 * log(u1));
+        double t = two_pi * u2;
+        out[i] = (float)(std_dev * r * cos(t));
+        if (i + 1 < n)
+            out[i + 1] = (float)(std_dev * r * sin(t));
+    }
+}
+
+void or_synth_tokens(uint64_t seed, uint64_t id, uint32_t vocab, uint32_t* out, size_t n)
+{
+    const uint64_t key = or_stream_key(seed, id ^ 0x746F6B656E73ull);
+    for (size_t i = 0; i < n; ++i)
+        out[i] = (uint32_t)(or_splitmix64(key + i * 0x9E3779B97F4A7C15ull) % vocab);
+}
+
+/* Timing aid of the CPU baseline: move the sequence to position pos with
+ * every cached K/V row below it filled from a fixed pattern, so a decode step
+ * at pos does the work of one at that position (the attention reads pos + 1
+ * rows) without the pos prompt steps before it. The logits that follow are
+ * not those of any prompt. Returns -1 when pos is outside the cache. */
+int or_model_seek(or_model* m, uint32_t pos)
+{
+    const or_config* c = &m->c;
+    if (pos >= c->max_seq)
+        return -1;
+    const size_t kd = (size_t)c->n_kv_heads * c->head_dim;
+    long long L = (long long)c->n_layers;
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long long l = 0; l < L; ++l)
+    {
+        size_t base = (size_t)l * c->max_seq * kd;
+        for (size_t i = 0; i < (size_t)pos * kd; ++i)
+        {
+            uint64_t h = or_splitmix64((uint64_t)l * 0x100000000ull + i);
+            m->k_cache[base + i] = (float)((double)(h >> 40) * (1.0 / 16777216.0) - 0.5);
+            m->v_cache[base + i] = (float)((double)(h & 0xFFFFFFull) * (1.0 / 16777216.0) - 0.5);
+        }
+    }
+    m->pos = pos;
+    return 0;
 }

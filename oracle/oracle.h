@@ -136,6 +136,15 @@ uint32_t or_argmax(const float* v, size_t n);
 /* Prompt then greedy decode; out_tokens receives n_new ids. Returns 0 ok. */
 int or_model_generate(or_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_new,
                       uint32_t* out_tokens, float* last_logits);
+/* The library's seeded synthetic generator, restated (N(0, std) fp32 from
+ * splitmix64 + Box-Muller keyed by (seed, tensor id, index); uniform token
+ * ids in [0, vocab)). Identical outputs to aaedn_synth_normal /
+ * aaedn_synth_tokens, so tests and the CPU baseline need not load the
+ * library to build the same model. */
+void or_synth_normal(uint64_t seed, uint64_t id, float std_dev, float* out, size_t n);
+void or_synth_tokens(uint64_t seed, uint64_t id, uint32_t vocab, uint32_t* out, size_t n);
+/* Timing aid: jump to position pos with synthetic K/V rows below it. */
+int or_model_seek(or_model* m, uint32_t pos);
 /* Threads the OpenMP loops may use (0 = library default). */
 void or_set_threads(int n);
 int or_get_threads(void);

@@ -52,6 +52,7 @@ class Oracle:
     """One of the two oracle builds: strict (parity) or fast (timed baseline)."""
 
     def __init__(self, fast=False):
+        self.fast = bool(fast)
         name = "liboracle_fast.so" if fast else "liboracle.so"
         path = os.path.join(HERE, "build", name)
         if not os.path.exists(path):
@@ -91,6 +92,10 @@ class Oracle:
         L.or_model_generate.restype = ctypes.c_int
         L.or_set_threads.argtypes = [ctypes.c_int]
         L.or_get_threads.restype = ctypes.c_int
+        L.or_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, _vp, _sz]
+        L.or_synth_tokens.argtypes = [ctypes.c_uint64, ctypes.c_uint64, _u32, _vp, _sz]
+        L.or_model_seek.argtypes = [_vp, _u32]
+        L.or_model_seek.restype = ctypes.c_int
 
     # -- primitives -------------------------------------------------------
     def quantize(self, x):
@@ -161,11 +166,58 @@ class Oracle:
         b = np.frombuffer(bytes(blob), np.uint8)
         return bool(self.lib.or_abn_v2_accepts(ptr(b), b.size))
 
+    def synth_normal(self, seed, tensor_id, n, std=0.02):
+        out = np.empty(n, np.float32)
+        self.lib.or_synth_normal(seed, tensor_id, std, ptr(out), n)
+        return out
+
+    def synth_tokens(self, seed, stream_id, vocab, n):
+        out = np.empty(n, np.uint32)
+        self.lib.or_synth_tokens(seed, stream_id, vocab, ptr(out), n)
+        return out
+
     def set_threads(self, n):
         self.lib.or_set_threads(int(n))
 
     def threads(self):
         return self.lib.or_get_threads()
+
+
+LAYER_MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
+
+
+def layer_shapes(cfg):
+    D, hd, H, KV, F = cfg["dim"], cfg["head_dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["ffn_dim"]
+    return {"wq": (H * hd, D), "wk": (KV * hd, D), "wv": (KV * hd, D), "wo": (D, H * hd), "wg": (F, D),
+            "wu": (F, D), "wd": (D, F)}
+
+
+def synthetic_weights(cfg, seed, oracle=None):
+    """The seeded synthetic model built on the oracle side alone: the same
+    tensors as the library's synthetic model (tensor ids: embedding 0,
+    lm_head 1, layer l: 16 + 8l + index in (q, k, v, o, g, u, d); N(0, 0.02)
+    linear weights quantized with the oracle's restatement of
+    tools/convert_model.py:36-55; fp32 embedding/lm_head; gains 1.0). The
+    strict build generates and quantizes (bit-exact with the library)."""
+    o = oracle if (oracle is not None and not getattr(oracle, "fast", False)) else Oracle()
+    L, D, V = cfg["n_layers"], cfg["dim"], cfg["vocab"]
+    shapes = layer_shapes(cfg)
+    w = {k: [] for k in LAYER_MATS}
+    w["attn_norm"] = [np.ones(D, np.float32) for _ in range(L)]
+    w["ffn_norm"] = [np.ones(D, np.float32) for _ in range(L)]
+    for l in range(L):
+        for i, name in enumerate(LAYER_MATS):
+            r, c = shapes[name]
+            w[name].append(o.quantize(o.synth_normal(seed, 16 + 8 * l + i, r * c)))
+    w["embedding"] = o.synth_normal(seed, 0, V * D).reshape(V, D)
+    w["lm_head"] = o.synth_normal(seed, 1, V * D).reshape(V, D)
+    w["final_norm"] = np.ones(D, np.float32)
+    return w
+
+
+def synth_tokens(seed, stream_id, vocab, n):
+    """The library's seeded prompt ids, from the oracle's restatement."""
+    return Oracle().synth_tokens(seed, stream_id, vocab, n)
 
 
 class OracleModel:
@@ -215,6 +267,11 @@ class OracleModel:
     @property
     def pos(self):
         return self.o.lib.or_model_pos(self.h)
+
+    def seek(self, pos):
+        """Timing aid: jump to position pos with synthetic cached K/V rows."""
+        if self.o.lib.or_model_seek(self.h, int(pos)) != 0:
+            raise ValueError(f"seek to {pos} outside the cache")
 
     def step(self, token, want_hidden=False):
         logits = np.empty(self.cfg["vocab"], np.float32)

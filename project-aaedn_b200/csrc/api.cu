@@ -132,12 +132,14 @@ static int gemv_dispatch(const GemvParams& p, int first_chunk, cudaStream_t st)
                                     : gemv_q4_kernel<NM, PRO_PLAIN, EPI_STORE, SK, false>)
                             : (full ? gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK, true>
                                     : gemv_q4_kernel<NM, PRO_PLAIN, EPI_ACCUM, SK, false>);
-    static bool attr_done[2][2] = {{false, false}, {false, false}};
-    if (!attr_done[first_chunk][full])
-    {
+    // per device (the attribute is set on the current device only)
+    static PerDeviceOnce attr_done[2][2];
+    const int arc = attr_done[first_chunk][full].run([&]() -> int {
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_done[first_chunk][full] = true;
-    }
+        return AAEDN_OK;
+    });
+    if (arc)
+        return arc;
     const int groups = (p.N + 15) / 16;
     const int grid = groups < sm_count() ? groups : sm_count();
     const size_t smem = gemv_smem_bytes(NM, p.kt1 - p.kt0);
@@ -293,7 +295,7 @@ extern "C" int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, cons
         const int nm = (int)((M - m0) < 8 ? (M - m0) : 8);
         // tiles per chunk so that ring + activation fragments fit in 200 KB
         const size_t fixed = gemv_smem_bytes(nm, 0);
-        const int max_tiles = (int)((200 * 1024 - fixed) / ((size_t)nm * 528));
+        const int max_tiles = (int)((200 * 1024 - fixed) / ((size_t)nm * (GEMV_FRAG_TILE_BYTES + 16)));
         for (int kt0 = 0; kt0 < ntile_total; kt0 += max_tiles)
         {
             GemvParams p{};
@@ -364,6 +366,9 @@ extern "C" int aaedn_cu_rope_apply(float* d_q, float* d_k, size_t seq_len, size_
     return AAEDN_OK;
 }
 
+// the attention kernels' shared-memory attribute, set once per device
+static PerDeviceOnce g_attn_api_attrs;
+
 extern "C" int aaedn_cu_attention(const float* d_q, const float* d_k, const float* d_v, const uint32_t* h_segments,
                                   size_t num_segments, float* d_out, size_t n_heads, size_t head_dim, float scale,
                                   void* stream)
@@ -433,13 +438,11 @@ extern "C" int aaedn_cu_attention(const float* d_q, const float* d_k, const floa
     AAEDN_CUDA_TRY(cudaMemsetAsync(counters, 0, n_heads * sizeof(unsigned), st));
     p.part = part;
     p.counters = counters;
-    static bool attr = false;
-    if (!attr)
+    int arc = g_attn_api_attrs.run([]() { return attn_set_attrs_g<0, 1>(); });
+    if (arc)
     {
-        int arc = attn_set_attrs_g<0, 1>();
-        if (arc)
-            return arc;
-        attr = true;
+        cudaFreeAsync(part, st);
+        return arc;
     }
     int lrc = attn_launch<0>(p, dim3((unsigned)n_heads, (unsigned)S), smem, st);
     AAEDN_CUDA_TRY(cudaFreeAsync(part, st));
@@ -562,13 +565,8 @@ extern "C" int aaedn_cu_attention_noalloc(const float* d_q, const float* d_k, co
     // the array keeps whatever the last call left: the split counters must
     // start at zero (the partials are written before they are read)
     AAEDN_CUDA_TRY(cudaMemsetAsync(p.counters, 0, n_heads * sizeof(unsigned), st));
-    static bool attr = false;
-    if (!attr)
-    {
-        int arc = attn_set_attrs_g<0, 1>();
-        if (arc)
-            return arc;
-        attr = true;
-    }
+    const int arc = g_attn_api_attrs.run([]() { return attn_set_attrs_g<0, 1>(); });
+    if (arc)
+        return arc;
     return attn_launch<0>(p, dim3((unsigned)n_heads, (unsigned)S), smem, st);
 }

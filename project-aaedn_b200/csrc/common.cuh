@@ -7,6 +7,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 #include <utility>
 
 #include "../../include/aaedn_b200.h"
@@ -58,6 +59,39 @@ inline int sm_count()
     }
     return cache[dev];
 }
+
+// A set-up step that must run once on every device a process uses, such as
+// cudaFuncSetAttribute (it acts on the current device only). Thread-safe:
+// the first caller on a device runs it under the lock; later callers, and
+// callers on devices where it already succeeded, return at once.
+class PerDeviceOnce
+{
+  public:
+    template <typename Fn>
+    int run(Fn&& fn)
+    {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess)
+            return set_error(AAEDN_ECUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+        if (dev < 0 || dev >= 64)
+            return set_error(AAEDN_EUNSUPPORTED, "device ordinal %d >= 64", dev);
+        const uint64_t bit = 1ull << dev;
+        if (done_.load(std::memory_order_acquire) & bit)
+            return AAEDN_OK;
+        std::lock_guard<std::mutex> lk(mu_);
+        if (done_.load(std::memory_order_relaxed) & bit)
+            return AAEDN_OK;
+        const int rc = fn();
+        if (rc == AAEDN_OK)
+            done_.fetch_or(bit, std::memory_order_release);
+        return rc;
+    }
+
+  private:
+    std::mutex mu_;
+    std::atomic<uint64_t> done_{0};
+};
 
 // ---------------------------------------------------------------------------
 // device helpers

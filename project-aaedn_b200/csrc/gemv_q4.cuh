@@ -13,10 +13,12 @@
 //  * codes are turned into bf16 values 16 + c with one shift and one LOP3 per
 //    two codes (exact: 4-bit integers are exact in bf16);
 //  * the tensor core (mma.sync m16n8k16 bf16 -> fp32) is used as the dot
-//    product engine: A = 16 weight rows x 16 codes, B columns = 4 quant
-//    blocks x 2 parts of the activation (x = hi + lo, both bf16, so x is
-//    carried to 2^-18 relative), so each lane's fp32 accumulators hold the
-//    per-(row, block) partial sums its own block needs;
+//    product engine: A = 16 weight rows x 16 codes; the activation is split
+//    into three bf16 parts x = hi + mid + lo (24 significant bits, as many
+//    as fp32 carries), the B columns of one mma are 4 quant blocks x (hi,
+//    mid) and those of a second mma 4 blocks x (lo, 0), so each lane's fp32
+//    accumulators hold the per-(row, block) partial sums its own block
+//    needs;
 //  * the per-block epilogue removes the +16 bias with a precomputed
 //    16*sum(x) per block and applies the block scale in fp32;
 //  * RMSNorm (prologue), RoPE + KV-cache append, SwiGLU and the residual add
@@ -90,6 +92,11 @@ constexpr uint64_t TP_WAIT_LIMIT_NS = 2000000000ull; // 2 s
 
 
 
+// Waits (bounded) until every rank's flag word in this rank's array shows
+// epoch E. On success a system-scope fence follows the flag reads, so the
+// caller's later loads (and those of threads it releases through a barrier)
+// see what the peers wrote before raising their flags (tp_signal fences at
+// system scope before its flag stores).
 __device__ __forceinline__ bool tp_wait_flags(const TpComm& c, unsigned E, DecodeState* st)
 {
     const uint64_t t0 = globaltimer_ns();
@@ -106,6 +113,7 @@ __device__ __forceinline__ bool tp_wait_flags(const TpComm& c, unsigned E, Decod
             __nanosleep(32);
         }
     }
+    __threadfence_system();
     return true;
 }
 
@@ -177,12 +185,17 @@ struct GemvParams
 constexpr int GEMV_WARPS = 8;
 constexpr int GEMV_STAGES = 6; // per-thread cp.async ring depth (tiles)
 
+// Activation fragments of one 128-code tile: 4 k-steps x 16 lane slots
+// (8 for the (hi, mid) mma, 8 for the (lo, 0) mma) x 16 B.
+constexpr int GEMV_FRAG_TILE_BYTES = 1024;
+
 // Dynamic shared memory of one CTA: the cp.async ring (6 stages x 256
-// threads x 40 B), the activation fragments, block biases, two reduction
-// buffers.
+// threads x 40 B), the activation fragments (and one zero tile), block
+// biases, two reduction buffers.
 inline size_t gemv_smem_bytes(int nm, int ntile)
 {
-    return (size_t)GEMV_STAGES * GEMV_WARPS * 32 * 40 + (size_t)(nm * ntile + 1) * 512 + (size_t)nm * ntile * 16 +
+    return (size_t)GEMV_STAGES * GEMV_WARPS * 32 * 40 + (size_t)(nm * ntile + 1) * GEMV_FRAG_TILE_BYTES +
+           (size_t)nm * ntile * 16 +
            (size_t)2 * nm * GEMV_WARPS * 16 * 4 + 64 * 4;
 }
 
@@ -225,10 +238,11 @@ __device__ __forceinline__ float block_sum(float v, float* scratch)
 }
 
 // Builds the B-operand fragments of the activations for tiles [kt0, kt1):
-// frag[((m*ntile + tt)*4 + q)*8 + la] holds, for lane slot la = 2*tp + p
-// (block tp of the tile, part p), the 4 bf16x2 registers of mmas 2q and
-// 2q+1: (x[8q+0],x[8q+4]), (x[8q+1],x[8q+5]), (x[8q+2],x[8q+6]),
-// (x[8q+3],x[8q+7]) of that block. tb[(m*ntile+tt)*4+tp] = 16 * sum(hi+lo).
+// frag[((m*ntile + tt)*4 + q)*16 + la] holds, for lane slot la = 2*tp + p
+// (block tp of the tile; p = 0: hi, 1: mid) and la = 8 + 2*tp + p (p = 0:
+// lo, 1: zero), the 4 bf16x2 registers of mmas 2q and 2q+1: (x[8q+0],x[8q+4]),
+// (x[8q+1],x[8q+5]), (x[8q+2],x[8q+6]), (x[8q+3],x[8q+7]) of that part of the
+// block. tb[(m*ntile+tt)*4+tp] = 16 * sum(hi+mid+lo).
 template <int NM, int PRO, int NTH = GEMV_WARPS * 32>
 __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* frag, float* tb, float* misc,
                                                  int ntile)
@@ -323,22 +337,29 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
             for (int c = 0; c < 8; ++c)
                 v[c] = 0.0f;
         }
-        __nv_bfloat16 hi[8], lo[8];
+        // x = hi + mid + lo: each part the bf16 rounding of what the parts
+        // before it leave (the differences are exact in fp32)
+        __nv_bfloat16 hi[8], mid[8], lo[8];
         float tsum = 0.0f;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
         {
             hi[c] = __float2bfloat16_rn(v[c]);
-            lo[c] = __float2bfloat16_rn(v[c] - __bfloat162float(hi[c]));
-            tsum += __bfloat162float(hi[c]) + __bfloat162float(lo[c]);
+            const float r1 = v[c] - __bfloat162float(hi[c]);
+            mid[c] = __float2bfloat16_rn(r1);
+            lo[c] = __float2bfloat16_rn(r1 - __bfloat162float(mid[c]));
+            tsum += (__bfloat162float(hi[c]) + __bfloat162float(mid[c])) + __bfloat162float(lo[c]);
         }
         if (live)
         {
-            uint4* dst = frag + (((size_t)m * ntile + tt) * 4 + q) * 8 + 2 * tp;
+            uint4* dst = frag + (((size_t)m * ntile + tt) * 4 + q) * 16 + 2 * tp;
             dst[0] = make_uint4(pack_bf16(hi[0], hi[4]), pack_bf16(hi[1], hi[5]), pack_bf16(hi[2], hi[6]),
                                 pack_bf16(hi[3], hi[7]));
-            dst[1] = make_uint4(pack_bf16(lo[0], lo[4]), pack_bf16(lo[1], lo[5]), pack_bf16(lo[2], lo[6]),
+            dst[1] = make_uint4(pack_bf16(mid[0], mid[4]), pack_bf16(mid[1], mid[5]), pack_bf16(mid[2], mid[6]),
+                                pack_bf16(mid[3], mid[7]));
+            dst[8] = make_uint4(pack_bf16(lo[0], lo[4]), pack_bf16(lo[1], lo[5]), pack_bf16(lo[2], lo[6]),
                                 pack_bf16(lo[3], lo[7]));
+            dst[9] = make_uint4(0u, 0u, 0u, 0u);
         }
         tsum += __shfl_xor_sync(0xffffffffu, tsum, 1);
         tsum += __shfl_xor_sync(0xffffffffu, tsum, 2);
@@ -476,7 +497,7 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
     // inactive lanes read their (zero) B operand from the fragment area of a
     // tile past the end, which the prologue zero-fills
     const uint32_t f_base = smem_addr(frag) + (uint32_t)la * 16;
-    const uint32_t f_zero = smem_addr(frag) + (uint32_t)NM * ntile * 512;
+    const uint32_t f_zero = smem_addr(frag) + (uint32_t)NM * ntile * GEMV_FRAG_TILE_BYTES;
     const uint32_t tb_base = smem_addr(tb) + (uint32_t)t * 4;
     uint32_t c_off_w = 0, c_off_s = 0;
     for (int gl = 0; gl < my_groups; ++gl)
@@ -486,9 +507,9 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
 #pragma unroll
         for (int m = 0; m < NM; ++m)
             acc0[m] = acc1[m] = 0.0f;
-        uint32_t fa = bact ? f_base + (uint32_t)tA * 512 : f_zero;
-        const uint32_t fstep = bact ? 512u : 0u;
-        const uint32_t mstride = bact ? (uint32_t)ntile * 512 : 0u;
+        uint32_t fa = bact ? f_base + (uint32_t)tA * GEMV_FRAG_TILE_BYTES : f_zero;
+        const uint32_t fstep = bact ? (uint32_t)GEMV_FRAG_TILE_BYTES : 0u;
+        const uint32_t mstride = bact ? (uint32_t)ntile * GEMV_FRAG_TILE_BYTES : 0u;
         uint32_t ta = tb_base + (uint32_t)tA * 16;
         for (int tt = tA; tt < tB; ++tt, fa += fstep, ta += 16)
         {
@@ -502,10 +523,10 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
             c_off_s = (c_off_s == (D - 1) * NT * 8) ? 0u : c_off_s + NT * 8;
             issue();
 
-            float d0[NM], d1[NM], d2[NM], d3[NM];
+            float d0[NM], d1[NM], d2[NM], d3[NM], e0[NM], e1[NM], e2[NM], e3[NM];
 #pragma unroll
             for (int m = 0; m < NM; ++m)
-                d0[m] = d1[m] = d2[m] = d3[m] = 0.0f;
+                d0[m] = d1[m] = d2[m] = d3[m] = e0[m] = e1[m] = e2[m] = e3[m] = 0.0f;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
             {
@@ -515,17 +536,21 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
                 {
-                    const uint4 b = lds128(fa + (uint32_t)m * mstride + (uint32_t)(q * 128));
+                    const uint32_t fq = fa + (uint32_t)m * mstride + (uint32_t)(q * 256);
+                    const uint4 b = lds128(fq), bl = lds128(fq + 128);
                     mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], a0, a1, a2, a3, b.x, b.y);
                     mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], c0, c1, c2, c3, b.z, b.w);
+                    mma_bf16_16816(e0[m], e1[m], e2[m], e3[m], a0, a1, a2, a3, bl.x, bl.y);
+                    mma_bf16_16816(e0[m], e1[m], e2[m], e3[m], c0, c1, c2, c3, bl.z, bl.w);
                 }
             }
 #pragma unroll
             for (int m = 0; m < NM; ++m)
             {
                 const float tbv = ldsf(ta + (uint32_t)(m * ntile * 16));
-                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) - tbv, acc0[m]);
-                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) - tbv, acc1[m]);
+                // column 2t: (hi, lo) parts, column 2t+1: (mid, 0)
+                acc0[m] = fmaf(sc0, ((d0[m] + d1[m]) + e0[m]) - tbv, acc0[m]);
+                acc1[m] = fmaf(sc1, ((d2[m] + d3[m]) + e2[m]) - tbv, acc1[m]);
             }
         }
         float* rb = red + (size_t)(gl & 1) * NM * S * 16;
@@ -569,7 +594,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
     uint32_t* sts = reinterpret_cast<uint32_t*>(smem + (size_t)D * NT * 32);
     uint4* frag = reinterpret_cast<uint4*>(smem + (size_t)D * NT * 40);
     // one zero tile after the fragments: the B operand of inactive lanes
-    float* tb = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) + (size_t)(NM * ntile + 1) * 512);
+    float* tb = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(frag) +
+                                         (size_t)(NM * ntile + 1) * GEMV_FRAG_TILE_BYTES);
     float* red = tb + (size_t)NM * ntile * 4; // [2][NM][S][16]
     float* misc = red + 2 * NM * S * 16;
 
@@ -648,8 +674,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
 
     pdl_wait();
     gemv_build_frags<NM, PRO>(p, frag, tb, misc, ntile);
-    if (tid < 32)
-        frag[(size_t)NM * ntile * 32 + tid] = make_uint4(0, 0, 0, 0);
+    if (tid < GEMV_FRAG_TILE_BYTES / 16)
+        frag[(size_t)NM * ntile * (GEMV_FRAG_TILE_BYTES / 16) + tid] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
     if (FULL)
@@ -669,9 +695,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
 #pragma unroll
         for (int m = 0; m < NM; ++m)
             acc0[m] = acc1[m] = 0.0f;
-        const uint4* fb = frag + (size_t)tA * 32 + la;
+        constexpr int FT = GEMV_FRAG_TILE_BYTES / 16; // uint4 per tile
+        const uint4* fb = frag + (size_t)tA * FT + la;
         const float* tbp = tb + (size_t)tA * 4 + t;
-        for (int tt = tA; tt < tB; ++tt, fb += 32, tbp += 4)
+        for (int tt = tA; tt < tB; ++tt, fb += FT, tbp += 4)
         {
             cp_async_wait<D - 2>(); // this thread's copies of this item have landed
             const uint4* wsl = stw + (size_t)c_slot * NT * 2 + (size_t)tid * 2;
@@ -694,10 +721,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
             // refill the slot consumed in the previous iteration
             issue();
 
-            float d0[NM], d1[NM], d2[NM], d3[NM];
+            float d0[NM], d1[NM], d2[NM], d3[NM], e0[NM], e1[NM], e2[NM], e3[NM];
 #pragma unroll
             for (int m = 0; m < NM; ++m)
-                d0[m] = d1[m] = d2[m] = d3[m] = 0.0f;
+                d0[m] = d1[m] = d2[m] = d3[m] = e0[m] = e1[m] = e2[m] = e3[m] = 0.0f;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
             {
@@ -707,19 +734,24 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
                 {
-                    uint4 b = make_uint4(0, 0, 0, 0);
+                    uint4 b = make_uint4(0, 0, 0, 0), bl = b;
                     if (bact)
-                        b = fb[(size_t)m * ntile * 32 + q * 8];
+                    {
+                        b = fb[(size_t)m * ntile * FT + q * 16];
+                        bl = fb[(size_t)m * ntile * FT + q * 16 + 8];
+                    }
                     mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], a0, a1, a2, a3, b.x, b.y);
                     mma_bf16_16816(d0[m], d1[m], d2[m], d3[m], c0, c1, c2, c3, b.z, b.w);
+                    mma_bf16_16816(e0[m], e1[m], e2[m], e3[m], a0, a1, a2, a3, bl.x, bl.y);
+                    mma_bf16_16816(e0[m], e1[m], e2[m], e3[m], c0, c1, c2, c3, bl.z, bl.w);
                 }
             }
 #pragma unroll
             for (int m = 0; m < NM; ++m)
             {
                 const float tbv = tbp[(size_t)m * ntile * 4];
-                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) - tbv, acc0[m]);
-                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) - tbv, acc1[m]);
+                acc0[m] = fmaf(sc0, ((d0[m] + d1[m]) + e0[m]) - tbv, acc0[m]);
+                acc1[m] = fmaf(sc1, ((d2[m] + d3[m]) + e2[m]) - tbv, acc1[m]);
             }
         }
         float* rb = red + (size_t)(gl & 1) * NM * S * 16;

@@ -209,10 +209,11 @@ extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
     if (int rc = aaedn_model_config_get(m, &mc))
         return rc;
     aaedn_abn_header h{};
+    // one open handle for both passes
+    File file(path);
+    if (!file.f)
+        return set_error(AAEDN_EFORMAT, "abn: cannot open %s", path);
     {
-        File file(path);
-        if (!file.f)
-            return set_error(AAEDN_EFORMAT, "abn: cannot open %s", path);
         if (int rc = parse_model(file, &h, &fc))
             return rc;
         if (fc.dim != mc.dim || fc.n_layers != mc.n_layers || fc.n_heads != mc.n_heads ||
@@ -234,11 +235,13 @@ extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
         if (c != h.payload_checksum)
             return set_error(AAEDN_EFORMAT, "abn: checksum %08x, header says %08x", c, h.payload_checksum);
     }
-    // pass 2: layer by layer into the model
-    File file(path);
-    aaedn_abn_header h2{};
-    if (!file.f || parse_model(file, &h2, &fc) || h2.payload_checksum != h.payload_checksum)
-        return set_error(AAEDN_EFORMAT, "abn: %s changed while it was read", path);
+    // pass 2: layer by layer into the model, from the same handle rewound to
+    // the payload; the checksum is taken again over the bytes this pass
+    // reads, and a file that changed between the passes is refused before
+    // the embedding and lm_head are set (the layers already set then hold a
+    // mix: reload the model)
+    if (std::fseek(file.f, 64, SEEK_SET) != 0)
+        return set_error(AAEDN_EFORMAT, "abn: cannot rewind %s", path);
     const ModelDims d = dims_of(fc);
     const uint64_t qrows = d.qdim, krows = (uint64_t)fc.n_kv_heads * fc.head_dim;
     std::vector<float> an(d.D), fn(d.D), bias(d.qkv);
@@ -246,7 +249,13 @@ extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
         d_c(d.D * d.F / 2);
     std::vector<uint16_t> qkv_s(d.qkv * d.D / 32), o_s(d.D * d.qdim / 32), g_s(d.F * d.D / 32), u_s(d.F * d.D / 32),
         d_s(d.D * d.F / 32);
-    auto rd = [&](void* dst, size_t n) { return file.read(dst, n); };
+    uint32_t c2 = 0x811C9DC5u;
+    auto rd = [&](void* dst, size_t n) {
+        if (!file.read(dst, n))
+            return false;
+        c2 = aaedn_fnv1a32(static_cast<const uint8_t*>(dst), n, c2);
+        return true;
+    };
     for (uint32_t l = 0; l < fc.n_layers; ++l)
     {
         const bool ok = rd(an.data(), d.D * 4) && rd(qkv_c.data(), qkv_c.size()) && rd(qkv_s.data(), qkv_s.size() * 2) &&
@@ -284,5 +293,8 @@ extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
     std::vector<float> final_norm(d.D), emb(d.V * d.D), lm(d.V * d.D);
     if (!rd(final_norm.data(), d.D * 4) || !rd(emb.data(), emb.size() * 4) || !rd(lm.data(), lm.size() * 4))
         return set_error(AAEDN_EFORMAT, "abn: embedding or lm_head cut short");
+    if (c2 != h.payload_checksum)
+        return set_error(AAEDN_EFORMAT, "abn: %s changed while it was read (checksum %08x, header says %08x)", path,
+                         c2, h.payload_checksum);
     return aaedn_model_set_globals(m, emb.data(), final_norm.data(), lm.data());
 }

@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures that pin the oracle to the reference.
 
-Run in a container that has the reference checkout (default
-/root/reference, override with AAEDN_REF) and oracle/_ref built
-(``make -C oracle``). Writes two small files next to this script:
+Run where the reference checkout exists, named by the AAEDN_REF environment
+variable (required), with oracle/_ref built from it
+(``make -C oracle AAEDN_REF=...``). Writes two small files next to this
+script:
 
 * ``quant_golden.npz`` — inputs and outputs of the reference's own block
   quantizer ``quantize_block_4bit_unsigned`` (tools/convert_model.py:36-55),
@@ -32,7 +33,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("AAEDN_REF", "/root/reference")
+REF = os.environ.get("AAEDN_REF")  # the reference project's root: required
 
 
 def load_reference_quantizer():
@@ -211,6 +212,8 @@ def make_ref_kernels_golden(lib, rng):
 
 
 def main():
+    if not REF or not os.path.isdir(os.path.join(REF, "src")):
+        raise SystemExit("set AAEDN_REF to the reference project's root (the directory holding src/ and tools/)")
     rng = np.random.default_rng(20261201)
     mod = load_reference_quantizer()
     q = make_quant_golden(mod, rng)

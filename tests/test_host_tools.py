@@ -152,3 +152,38 @@ def test_whole_model_file_rejections(tmp_path):
     # the one-matrix reader keeps rejecting whole-model files (version 3)
     with pytest.raises(ab.AaednError):
         ab.abn_read(good)
+
+
+def test_oracle_generator_matches_the_library(oracle):
+    """The oracle's restatement of the seeded generator (what bench.py's CPU
+    arm and the fixture script build their weights from) gives the library's
+    synthetic tensors and prompts bit for bit, and its quantizer the
+    library's codes and scales."""
+    import pyoracle
+    for seed, tid, n in ((1234, 0, 1001), (7, 16 + 8 * 3 + 6, 300001), (1, 1, 5)):
+        a = ab.synth_normal(seed, tid, n)
+        b = oracle.synth_normal(seed, tid, n)
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    np.testing.assert_array_equal(ab.synth_tokens(1234, 0, 32000, 128), oracle.synth_tokens(1234, 0, 32000, 128))
+    cfg = dict(ab.TINY, n_layers=2)
+    w1, w2 = ab.synthetic_weights(cfg, 1234), pyoracle.synthetic_weights(cfg, 1234, oracle)
+    for k in ab.LAYER_MATS:
+        for l in range(2):
+            for i in range(2):
+                np.testing.assert_array_equal(w1[k][l][i], w2[k][l][i])
+    np.testing.assert_array_equal(w1["embedding"], w2["embedding"])
+    np.testing.assert_array_equal(w1["lm_head"], w2["lm_head"])
+
+
+def test_oracle_seek_fills_the_cache_below_the_position(oracle):
+    """The CPU baseline's timing aid: after seek(p) the next step runs at
+    position p (its logits are finite; attention reads p + 1 rows)."""
+    import pyoracle
+    cfg = dict(ab.TINY, n_layers=1, max_seq=64)
+    om = pyoracle.OracleModel(oracle, cfg, pyoracle.synthetic_weights(cfg, 3, oracle))
+    om.seek(40)
+    assert om.pos == 40
+    lg = om.step(5)
+    assert om.pos == 41 and np.isfinite(lg).all()
+    with pytest.raises(ValueError):
+        om.seek(64)
