@@ -318,6 +318,12 @@ int aaedn_model_status(aaedn_model* m);
 int aaedn_model_next_token(aaedn_model* m, uint32_t* h_token);
 /* Kernels launched by one decode step. */
 uint32_t aaedn_model_kernels_per_step(const aaedn_model* m);
+/* Prompt tokens one prefill chunk takes through the tensor-core GEMMs
+ * (forward / generate with more than one token); 0 when the model runs its
+ * prompt as one decode step per token (tensor-parallel ranks, and matrix
+ * shapes without the tile-major layout: K % 128 or N % 16 nonzero). No
+ * counterpart in the reference (src/transformer.cpp:146 processes one token). */
+uint32_t aaedn_model_prefill_rows(const aaedn_model* m);
 /* Copy the last step's logits ([vocab]) / the greedy tokens generated so far. */
 int aaedn_model_logits(aaedn_model* m, float* h_logits);
 int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n);

@@ -128,6 +128,7 @@ def lib():
         "aaedn_model_generate": ([_vp, _vp, _sz, _sz, _vp], _int),
         "aaedn_model_decode_steps": ([_vp, _sz], _int),
         "aaedn_model_kernels_per_step": ([_vp], _u32),
+        "aaedn_model_prefill_rows": ([_vp], _u32),
         "aaedn_model_logits": ([_vp, _vp], _int),
         "aaedn_model_tokens": ([_vp, _vp, _sz], _int),
         "aaedn_model_forward_debug": ([_vp, _u32, _vp, _vp], _int),
@@ -418,6 +419,12 @@ class Model:
     @property
     def kernels_per_step(self):
         return int(lib().aaedn_model_kernels_per_step(self.h))
+
+    @property
+    def prefill_rows(self):
+        """Prompt tokens per tensor-core prefill chunk (0: one decode step per
+        prompt token)."""
+        return int(lib().aaedn_model_prefill_rows(self.h))
 
     def set_weights(self, w):
         keep = []

@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "gemm_tc.h"
 #include "gemv_q4.cuh"
 
 namespace aaedn_dev
@@ -234,7 +235,7 @@ extern "C" int aaedn_stream_sync(void* stream)
 extern "C" int aaedn_device_sync(void)
 {
     AAEDN_CUDA_TRY(cudaDeviceSynchronize());
-    return AAEDN_OK;
+    return tc_api_err_check();
 }
 
 extern "C" int aaedn_cu_dequant_4bit(const uint8_t* d_data, const uint16_t* d_scales, float* d_out, size_t n,
@@ -288,8 +289,33 @@ extern "C" int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, cons
     CHECK_DEV(d_out);
     if ((reinterpret_cast<uintptr_t>(d_w) & 15) || ((ldb / 2) & 15))
         return set_error(AAEDN_EINVAL, "aaedn_cu_fused_matmul: weights must be 16-byte aligned rows");
-    const int ntile_total = (int)((K + 127) / 128);
     cudaStream_t st = as_stream(stream);
+    if (M > 8 && scale_kind == AAEDN_SCALE_F16 && (K % 64) == 0 && M <= (size_t)INT32_MAX)
+    {
+        // many rows: the tensor-core GEMM (each weight read once per 128 x
+        // up-to-128 tile instead of once per 8 rows)
+        TcGemmArgs a{};
+        a.x = d_in;
+        a.lda = lda;
+        a.M = (int)M;
+        a.N = (int)N;
+        a.K = (int)K;
+        a.w = d_w;
+        a.s = d_scales;
+        a.ldb = ldb;
+        a.w_layout = TC_W_ROWMAJOR;
+        a.out = d_out;
+        a.ldc = ldc;
+        a.err = tc_api_err_word();
+        if (!a.err)
+            return set_error(AAEDN_ECUDA, "aaedn_cu_fused_matmul: error word allocation failed");
+        a.workspace_bytes = tc_gemm_workspace_bytes(a.M, a.N, a.K);
+        AAEDN_CUDA_TRY(cudaMallocAsync(&a.workspace, a.workspace_bytes, st));
+        const int rc = tc_gemm(a, st);
+        AAEDN_CUDA_TRY(cudaFreeAsync(a.workspace, st));
+        return rc;
+    }
+    const int ntile_total = (int)((K + 127) / 128);
     for (size_t m0 = 0; m0 < M; m0 += 8)
     {
         const int nm = (int)((M - m0) < 8 ? (M - m0) : 8);

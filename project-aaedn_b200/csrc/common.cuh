@@ -179,6 +179,15 @@ __device__ __forceinline__ uint32_t nib_e0(uint32_t w) { return lop3_bias(w << 3
 __device__ __forceinline__ uint32_t nib_e1(uint32_t w) { return lop3_bias(w >> 1); }
 __device__ __forceinline__ uint32_t nib_e2(uint32_t w) { return lop3_bias(w >> 5); }
 __device__ __forceinline__ uint32_t nib_e3(uint32_t w) { return lop3_bias(w >> 9); }
+// (16 + c) - 16 = c on both halves of a bf16x2 word: exact (4-bit integers
+// are exact in bf16), so the codes enter the product without a bias to
+// remove after the accumulation.
+__device__ __forceinline__ uint32_t unbias16(uint32_t v)
+{
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(0x41804180u));
+    return r;
+}
 
 // D += A (16x32 u8, row) * B (32x8 s8, col) with s32 accumulators: the dot
 // product engine of the integer GEMV (exact: no rounding anywhere).

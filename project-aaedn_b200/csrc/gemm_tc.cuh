@@ -1,0 +1,536 @@
+// gemm_tc.cuh — the block-quantized matrix product on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory), for more than
+// eight activation rows: prefill and the fused_matmul API at M > 8.
+//
+// Replaces the intended product of src/fused_matmul.cpp:70-169 (out[m][n] =
+// sum_k in[m][k] * code(n, k) * scale(n, k / 32)) for many rows at once.
+//
+// Roles: D[n][m] = sum_k W[n][k] * X[m][k], with the weights as the MMA's A
+// operand (128 weight rows per CTA tile, UMMA M = 128) and the activations
+// as B (BN activation rows per tile, UMMA N = BN); the fp32 accumulator tile
+// [128 lanes = weight rows][BN columns = activation rows] lives in TMEM.
+//
+// Precision: the MMA takes bf16 operands. A dequantized weight code * scale
+// (a 4-bit integer times an fp16 value: at most 15 significant bits) is
+// exactly w_hi + w_lo with both parts bf16; the fp32 activation is split into
+// three bf16 parts x_hi + x_mid + x_lo (24 significant bits, what fp32
+// carries). The accumulator receives the five products whose magnitude is
+// above 2^-24 of the leading one (x_hi w_hi, x_mid w_hi, x_lo w_hi, x_hi w_lo,
+// x_mid w_lo), so the product is fp32-accurate: the tensor pipe does 5 bf16
+// MMAs per fp32 multiply-add of the product. The tensor core rounds each
+// MMA's sum into its accumulator with an error of up to one unit in the last
+// place of the accumulator, so the four small products go to a second
+// accumulator (2^-8 of the first's magnitude): the leading accumulator takes
+// K / 16 additions instead of 5 K / 16; the epilogue adds the two in fp32.
+//
+// Data movement, per stage of 64 K:
+//   * the activation parts (prepared once per call in global memory as bf16
+//     [3][M_pad][K]) arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle:
+//     the canonical K-major layout the MMA reads), issued by warp 4;
+//   * the weights' 4-bit codes and fp16 scales are read from global memory by
+//     warps 0-3 (one weight row per thread, 32 bytes of codes per stage,
+//     loaded two stages ahead), dequantized in registers and written as the
+//     two bf16 parts into the same swizzled layout (fence.proxy.async before
+//     the stage is marked full);
+//   * warp 5 issues the 20 MMAs of the stage (4 k-steps x 5 part products)
+//     from one thread and commits them to the stage's "empty" barrier.
+// Epilogue: warps 0-3 read their 32 TMEM lanes (tcgen05.ld 32x32b) and store
+// out[m][n] (a warp writes 32 consecutive n of one m: coalesced).
+//
+// Every wait is bounded (globaltimer): a wait that runs out sets *err, the
+// kernel drains what it issued, frees its TMEM and returns.
+#pragma once
+
+#include <cuda.h> // CUtensorMap
+
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace aaedn_dev
+{
+
+constexpr int TC_BM = 128;     // weight rows per tile (UMMA M)
+constexpr int TC_BK = 64;      // K per stage: one 128-byte swizzle row of bf16
+constexpr int TC_XP = 3;       // bf16 parts of the activation
+constexpr int TC_WP = 2;       // bf16 parts of a dequantized weight (exact)
+constexpr int TC_THREADS = 192; // warps 0-3 dequant + epilogue, 4 TMA, 5 MMA
+constexpr uint64_t TC_WAIT_LIMIT_NS = 2000000000ull;
+
+struct TcGemmParams
+{
+    const uint8_t* w;  // codes (and, tiled, scales)
+    const uint16_t* s; // row-major scales
+    size_t ldb;        // row-major: codes per weight row
+    int w_layout;
+    int N, K, M;       // weight rows, reduction length, activation rows
+    int k_per_split;   // K handled by the CTAs of one blockIdx.z (a multiple of 64)
+    float* out;        // blockIdx.z == s writes out + s * split_stride
+    size_t ldc, split_stride;
+    unsigned* err;     // set to 1 when a bounded wait ran out
+    TcEpi e;           // the model's epilogues
+};
+
+template <int BN, int STAGES>
+struct TcSmem
+{
+    static constexpr size_t W_PART = (size_t)TC_BM * 128; // 16 KB
+    static constexpr size_t X_PART = (size_t)BN * 128;
+    static constexpr size_t STAGE = TC_WP * W_PART + TC_XP * X_PART;
+    static constexpr size_t BARS = 1024; // after the stages: mbarriers, TMEM address
+    static constexpr size_t BYTES = STAGES * STAGE + BARS + 1024; // + alignment slack
+    static constexpr uint32_t TMEM_COLS = 2 * BN; // leading + small-product accumulators (a power of two)
+};
+
+// ---- tcgen05 / TMA primitives ----------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), leading offset unused (16 B), sm100 version 1.
+__device__ __forceinline__ uint64_t tc_desc_sw128(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B, fp32 D, both K-major,
+// M = 128, N = n.
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(int n)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+                 : "memory");
+}
+
+// Arrives once on the mbarrier when every MMA this thread issued so far is done.
+__device__ __forceinline__ void tc_commit(uint32_t mbar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t mbar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+                 "[%4];" ::"r"(dst),
+                 "l"(tmap), "r"(x), "r"(y), "r"(mbar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8])
+{
+    uint32_t r[8];
+    // one statement: the registers are read only after the wait
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        v[i] = __uint_as_float(r[i]);
+}
+
+// 16 bytes of codes (32 weights of one quant block) dequantized with scale
+// sc into their bf16 parts, stored at byte offset (4 * kb + j) * 16 of a
+// 128-byte swizzled row (j = 0..3: 8 weights each).
+__device__ __forceinline__ void tc_dequant_block(uint4 codes, float sc, uint32_t w0_row, uint32_t w1_row, int kb,
+                                                 int r7)
+{
+    const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+    {
+        // 8 weights: bytes 0..3 of word j, low nibble first
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+        {
+            const uint32_t byte = (cw[j] >> (8 * b)) & 0xFFu;
+            const float wa = (float)(byte & 0xFu) * sc, wb = (float)(byte >> 4) * sc; // exact in fp32
+            const __nv_bfloat16 ha = __float2bfloat16_rn(wa), hb = __float2bfloat16_rn(wb);
+            const __nv_bfloat16 la = __float2bfloat16_rn(wa - __bfloat162float(ha));
+            const __nv_bfloat16 lb = __float2bfloat16_rn(wb - __bfloat162float(hb));
+            hi[b] = pack_bf16(ha, hb);
+            lo[b] = pack_bf16(la, lb);
+        }
+        const uint32_t chunk = (uint32_t)(((4 * kb + j) ^ r7) * 16);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(w0_row + chunk), "r"(hi[0]), "r"(hi[1]),
+                     "r"(hi[2]), "r"(hi[3])
+                     : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(w1_row + chunk), "r"(lo[0]), "r"(lo[1]),
+                     "r"(lo[2]), "r"(lo[3])
+                     : "memory");
+    }
+}
+
+// Address of the 32 code bytes and two scales of weight row `row`, quant
+// blocks b0, b0 + 1 (b0 even).
+__device__ __forceinline__ void tc_w_addr(const TcGemmParams& p, int row, int b0, const uint8_t*& codes,
+                                          const uint16_t*& scales)
+{
+    if (p.w_layout == TC_W_TILED)
+    {
+        const int ntile = p.K >> 7, group = row >> 4, r16 = row & 15, h = r16 >> 3, g = r16 & 7;
+        const int tile = b0 >> 2, t = b0 & 3, c = tile >> 5, ti = tile & 31;
+        const int tiles_in_chunk = min(32, ntile - 32 * c);
+        const uint8_t* chunk = p.w + (size_t)group * ntile * 1152 + (size_t)c * 32 * 1152;
+        codes = chunk + (size_t)(ti * 2 + h) * 512 + (4 * g + t) * 16;
+        scales = reinterpret_cast<const uint16_t*>(chunk + (size_t)tiles_in_chunk * 1024 + (ti * 2 + h) * 64 +
+                                                   (4 * g + t) * 2);
+    }
+    else
+    {
+        codes = p.w + (size_t)row * (p.ldb >> 1) + (size_t)b0 * 16;
+        scales = p.s + (size_t)row * (p.ldb >> 5) + b0;
+    }
+}
+
+// Epilogue of 8 activation rows (columns c0.. of the accumulator) of weight
+// row `row` (thread = TMEM lane), values v. Every lane of the warp calls it
+// (the paired epilogues exchange values between lanes r and r + 8).
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue8(const TcGemmParams& p, float* out, int row, bool live, int m_first,
+                                             const float (&v)[8])
+{
+    if constexpr (EPI == TC_EPI_STORE || EPI == TC_EPI_RESID)
+    {
+        if (!live)
+            return;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            const int m = m_first + j;
+            if (m < p.M)
+            {
+                float* o = out + (size_t)m * p.ldc + row;
+                if constexpr (EPI == TC_EPI_STORE)
+                    *o = v[j];
+                else
+                    *o = v[j] + *o; // src/transformer.cpp:214, 227 (tmp + hidden)
+            }
+        }
+    }
+    else
+    {
+        float u[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            u[j] = __shfl_down_sync(0xffffffffu, v[j], 8); // row + 8 of the same 16-row group
+        const int jj = row & 15, rbase = row & ~15;
+        if (!live || jj >= 8)
+            return;
+        const TcEpi& e = p.e;
+        if constexpr (EPI == TC_EPI_SWIGLU)
+        {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                const int m = m_first + j;
+                if (m < p.M)
+                    e.act[(size_t)m * e.ld_act + (rbase >> 1) + jj] = __fmul_rn(silu_f(v[j]), u[j]); // D6
+            }
+        }
+        else
+        {
+            const int hd = e.head_dim, half = hd >> 1;
+            const bool isq = rbase < e.q_rows, isk = !isq && rbase < e.q_rows + e.kv_rows;
+            const int rel = isq ? rbase : (isk ? rbase - e.q_rows : rbase - e.q_rows - e.kv_rows);
+            const int h = rel / hd;
+            const int i = ((rel % hd) >> 4) * 8 + jj; // rope pair (i, i + half)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                const int m = m_first + j;
+                if (m >= p.M)
+                    continue;
+                const int pos = e.pos0 + m;
+                const int page = e.page_table[pos / e.page_size], slot = pos % e.page_size;
+                float* kv = nullptr;
+                if (!isq)
+                    kv = (isk ? e.k_layer : e.v_layer) + (((size_t)page * e.n_kv + h) * e.page_size + slot) * hd;
+                if (isq || isk)
+                {
+                    // rotate-half at the absolute position (D3, src/rope.cpp:53-54)
+                    const float c = e.rope_cos[(size_t)pos * half + i], sn = e.rope_sin[(size_t)pos * half + i];
+                    const float o0 = __fsub_rn(__fmul_rn(c, v[j]), __fmul_rn(sn, u[j]));
+                    const float o1 = __fadd_rn(__fmul_rn(sn, v[j]), __fmul_rn(c, u[j]));
+                    float* dst = isq ? e.qrows + (size_t)m * e.ldq + (size_t)h * hd : kv;
+                    dst[i] = o0;
+                    dst[i + half] = o1;
+                }
+                else
+                {
+                    const int d = rel % hd + jj;
+                    kv[d] = v[j];
+                    kv[d + 8] = u[j];
+                }
+            }
+        }
+    }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmParams p,
+                                                                    const __grid_constant__ CUtensorMap xmap)
+{
+    using SM = TcSmem<BN, STAGES>;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    // 1024-byte alignment: the 128-byte swizzle pattern is taken from address bits
+    const uint32_t raw_a = smem_addr(smem_raw);
+    const uint32_t base = (raw_a + 1023u) & ~1023u;
+    const uint32_t bar0 = base + (uint32_t)(STAGES * SM::STAGE);
+    // barriers: full_x[S], full_w[S], empty[S], accum; then the TMEM address
+    auto full_x = [&](int s) { return bar0 + 8u * s; };
+    auto full_w = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto empty = [&](int s) { return bar0 + 8u * (2 * STAGES + s); };
+    const uint32_t accum = bar0 + 8u * (3 * STAGES);
+    const uint32_t tmem_slot = bar0 + 8u * (3 * STAGES + 1);
+    __shared__ int s_abort_mem;
+    volatile int& s_abort = s_abort_mem;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * TC_BM, m0 = blockIdx.y * BN;
+    const int kb0 = blockIdx.z * (p.k_per_split / TC_BK); // first 64-wide K block of this CTA
+    const int nk = min(p.K - blockIdx.z * p.k_per_split, p.k_per_split) / TC_BK;
+    float* out = p.out + (size_t)blockIdx.z * p.split_stride;
+    const uint32_t M_pad = (uint32_t)((p.M + BN - 1) / BN * BN);
+
+    if (tid == 0)
+    {
+        for (int s = 0; s < STAGES; ++s)
+        {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_w(s), 128);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(accum, 1);
+        mbar_init_fence();
+        s_abort = 0;
+    }
+    if (warp == 5)
+    {
+        // two accumulators of BN fp32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                     "r"(SM::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = lds32(tmem_slot);
+
+    auto w_part = [&](int s, int j) { return base + (uint32_t)(s * SM::STAGE + j * SM::W_PART); };
+    auto x_part = [&](int s, int i) { return base + (uint32_t)(s * SM::STAGE + TC_WP * SM::W_PART + i * SM::X_PART); };
+    auto fail = [&]() {
+        s_abort = 1;
+        if (p.err)
+            atomicExch(p.err, 1u);
+    };
+
+    if (warp == 4)
+    {
+        // ---- TMA producer of the activation parts
+        int issued = 0;
+        if (lane == 0)
+        {
+            for (int kb = 0; kb < nk; ++kb)
+            {
+                const int s = kb % STAGES, use = kb / STAGES;
+                if (use > 0 && !mbar_wait_bounded(empty(s), (use - 1) & 1, TC_WAIT_LIMIT_NS))
+                {
+                    fail();
+                    break;
+                }
+                if (s_abort)
+                    break;
+                mbar_arrive_expect_tx(full_x(s), (uint32_t)(TC_XP * SM::X_PART));
+                for (int i = 0; i < TC_XP; ++i)
+                    tma_load_2d(x_part(s, i), &xmap, (kb0 + kb) * TC_BK, (int)(i * M_pad) + m0, full_x(s));
+                ++issued;
+            }
+            // the copies it issued have landed before the CTA may exit
+            for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb)
+                mbar_wait_bounded(full_x(kb % STAGES), (kb / STAGES) & 1, TC_WAIT_LIMIT_NS);
+        }
+        __syncwarp();
+    }
+    else if (warp == 5)
+    {
+        // ---- MMA issuer (one thread)
+        if (lane == 0)
+        {
+            constexpr uint32_t idesc = tc_idesc_bf16(BN);
+            // (x part, w part) products, largest first
+            const int px[5] = {0, 1, 0, 2, 1}, pw[5] = {0, 0, 1, 0, 1};
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; ++kb)
+            {
+                const int s = kb % STAGES;
+                const uint32_t ph = (uint32_t)(kb / STAGES) & 1;
+                if (!mbar_wait_bounded(full_x(s), ph, TC_WAIT_LIMIT_NS) ||
+                    !mbar_wait_bounded(full_w(s), ph, TC_WAIT_LIMIT_NS) || s_abort)
+                {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < TC_BK / 16; ++k)
+#pragma unroll
+                    for (int q = 0; q < 5; ++q)
+                        // q = 0 into columns [0, BN), the rest into [BN, 2 BN); the first
+                        // product into each overwrites it
+                        tc_mma(tmem + (q ? (uint32_t)BN : 0u), tc_desc_sw128(w_part(s, pw[q]) + k * 32),
+                               tc_desc_sw128(x_part(s, px[q]) + k * 32), idesc,
+                               (kb | k | (q > 1 ? 1 : 0)) != 0 ? 1u : 0u);
+                tc_commit(empty(s)); // the stage's smem is free once these MMAs are done
+            }
+            // always: the epilogue (and the TMEM release) waits for every MMA
+            // issued, on success or not
+            tc_commit(accum);
+        }
+        __syncwarp();
+    }
+    else
+    {
+        // ---- warps 0-3: weight rows n0 + tid, dequantized into the stages
+        const int row = n0 + tid;
+        const bool live = row < p.N;
+        const uint32_t r7 = (uint32_t)(tid & 7);
+        uint4 ca[2] = {}, cb[2] = {};
+        uint32_t sp[2] = {};
+        auto load = [&](int kb, int slot) {
+            if (live && kb < nk)
+            {
+                const uint8_t* c;
+                const uint16_t* sc;
+                tc_w_addr(p, row, (kb0 + kb) * 2, c, sc);
+                ca[slot] = __ldg(reinterpret_cast<const uint4*>(c));
+                cb[slot] = __ldg(reinterpret_cast<const uint4*>(c) + 1);
+                sp[slot] = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 1) << 16);
+            }
+            else
+            {
+                ca[slot] = cb[slot] = make_uint4(0, 0, 0, 0);
+                sp[slot] = 0;
+            }
+        };
+        load(0, 0);
+        load(1, 1);
+        for (int kb = 0; kb < nk; ++kb)
+        {
+            const int s = kb % STAGES, use = kb / STAGES, slot = kb & 1;
+            if (use > 0 && !mbar_wait_bounded(empty(s), (use - 1) & 1, TC_WAIT_LIMIT_NS))
+            {
+                fail();
+                break;
+            }
+            if (s_abort)
+                break;
+            const uint32_t w0 = w_part(s, 0) + (uint32_t)tid * 128, w1 = w_part(s, 1) + (uint32_t)tid * 128;
+            const float s0 = __half2float(__ushort_as_half((uint16_t)(sp[slot] & 0xFFFFu)));
+            const float s1 = __half2float(__ushort_as_half((uint16_t)(sp[slot] >> 16)));
+            tc_dequant_block(ca[slot], s0, w0, w1, 0, (int)r7);
+            tc_dequant_block(cb[slot], s1, w0, w1, 1, (int)r7);
+            load(kb + 2, slot); // two stages ahead
+            // generic-proxy stores, then visible to the tensor core's reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(full_w(s));
+        }
+        // ---- epilogue: this warp's 32 TMEM lanes = weight rows n0 + 32 w + lane
+        if (mbar_wait_bounded(accum, 0, TC_WAIT_LIMIT_NS) && !s_abort)
+        {
+            tc_fence_after();
+            const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
+            for (int c0 = 0; c0 < BN; c0 += 8)
+            {
+                float v[8], w[8];
+                tc_ld8(t_row + (uint32_t)c0, v);
+                tc_ld8(t_row + (uint32_t)(BN + c0), w);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    v[j] += w[j];
+                tc_epilogue8<EPI>(p, out, row, live, m0 + c0, v);
+            }
+        }
+        else
+            fail();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5)
+    {
+        // every MMA issued has completed before its accumulator is released
+        if (lane == 0)
+            mbar_wait_bounded(accum, 0, TC_WAIT_LIMIT_NS);
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(SM::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// Splits fp32 activation rows into the three bf16 parts the GEMM reads:
+// parts[i][m][k] for m < M_pad (rows M..M_pad-1 zero).
+__global__ void tc_split_kernel(const float* __restrict__ x, size_t lda, int M, int M_pad, int K,
+                                __nv_bfloat16* __restrict__ parts)
+{
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; // 4 elements per thread
+    const size_t per_row = (size_t)K / 4;
+    if (i >= (size_t)M_pad * per_row)
+        return;
+    const int m = (int)(i / per_row), k = (int)(i - (size_t)m * per_row) * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (m < M)
+    {
+        const float* src = x + (size_t)m * lda + k;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            v[j] = src[j];
+    }
+    __nv_bfloat16 h[3][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+    {
+        h[0][j] = __float2bfloat16_rn(v[j]);
+        const float r1 = v[j] - __bfloat162float(h[0][j]);
+        h[1][j] = __float2bfloat16_rn(r1);
+        h[2][j] = __float2bfloat16_rn(r1 - __bfloat162float(h[1][j]));
+    }
+    const size_t plane = (size_t)M_pad * K;
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+    {
+        uint2 w;
+        w.x = pack_bf16(h[q][0], h[q][1]);
+        w.y = pack_bf16(h[q][2], h[q][3]);
+        *reinterpret_cast<uint2*>(parts + q * plane + (size_t)m * K + k) = w;
+    }
+}
+
+// out[m][n] = (accumulate ? out[m][n] : 0) + the sum over s of part[s][m][n]
+// (splits summed in order: deterministic).
+__global__ void tc_splitk_reduce_kernel(const float* __restrict__ part, int splits, size_t split_stride, int M, int N,
+                                        float* __restrict__ out, size_t ldc, int accumulate)
+{
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)M * N)
+        return;
+    const int m = (int)(i / N), n = (int)(i - (size_t)m * N);
+    float v = 0.0f;
+    for (int s = 0; s < splits; ++s)
+        v += part[(size_t)s * split_stride + (size_t)m * N + n];
+    float* o = out + (size_t)m * ldc + n;
+    *o = accumulate ? v + *o : v;
+}
+
+} // namespace aaedn_dev

@@ -11,7 +11,10 @@
 //    16-byte non-temporal loads; each lane of a quad reads one whole block of
 //    its two rows (g, g+8), so every load is a full aligned 16-byte vector;
 //  * codes are turned into bf16 values 16 + c with one shift and one LOP3 per
-//    two codes (exact: 4-bit integers are exact in bf16);
+//    two codes, then c with one bf16x2 subtraction (exact: 4-bit integers are
+//    exact in bf16), so no bias has to be removed after the accumulation
+//    (that would lose the low bits of blocks whose large activations meet
+//    zero codes);
 //  * the tensor core (mma.sync m16n8k16 bf16 -> fp32) is used as the dot
 //    product engine: A = 16 weight rows x 16 codes; the activation is split
 //    into three bf16 parts x = hi + mid + lo (24 significant bits, as many
@@ -19,8 +22,7 @@
 //    mid) and those of a second mma 4 blocks x (lo, 0), so each lane's fp32
 //    accumulators hold the per-(row, block) partial sums its own block
 //    needs;
-//  * the per-block epilogue removes the +16 bias with a precomputed
-//    16*sum(x) per block and applies the block scale in fp32;
+//  * the per-block epilogue applies the block scale in fp32;
 //  * RMSNorm (prologue), RoPE + KV-cache append, SwiGLU and the residual add
 //    (epilogues) are fused for the decode path.
 #pragma once
@@ -242,7 +244,7 @@ __device__ __forceinline__ float block_sum(float v, float* scratch)
 // (block tp of the tile; p = 0: hi, 1: mid) and la = 8 + 2*tp + p (p = 0:
 // lo, 1: zero), the 4 bf16x2 registers of mmas 2q and 2q+1: (x[8q+0],x[8q+4]),
 // (x[8q+1],x[8q+5]), (x[8q+2],x[8q+6]), (x[8q+3],x[8q+7]) of that part of the
-// block. tb[(m*ntile+tt)*4+tp] = 16 * sum(hi+mid+lo).
+// block.
 template <int NM, int PRO, int NTH = GEMV_WARPS * 32>
 __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* frag, float* tb, float* misc,
                                                  int ntile)
@@ -340,7 +342,6 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
         // x = hi + mid + lo: each part the bf16 rounding of what the parts
         // before it leave (the differences are exact in fp32)
         __nv_bfloat16 hi[8], mid[8], lo[8];
-        float tsum = 0.0f;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
         {
@@ -348,7 +349,6 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
             const float r1 = v[c] - __bfloat162float(hi[c]);
             mid[c] = __float2bfloat16_rn(r1);
             lo[c] = __float2bfloat16_rn(r1 - __bfloat162float(mid[c]));
-            tsum += (__bfloat162float(hi[c]) + __bfloat162float(mid[c])) + __bfloat162float(lo[c]);
         }
         if (live)
         {
@@ -361,10 +361,6 @@ __device__ __forceinline__ void gemv_build_frags(const GemvParams& p, uint4* fra
                                 pack_bf16(lo[3], lo[7]));
             dst[9] = make_uint4(0u, 0u, 0u, 0u);
         }
-        tsum += __shfl_xor_sync(0xffffffffu, tsum, 1);
-        tsum += __shfl_xor_sync(0xffffffffu, tsum, 2);
-        if (live && q == 0)
-            tb[((size_t)m * ntile + tt) * 4 + tp] = 16.0f * tsum;
     }
 }
 
@@ -498,7 +494,6 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
     // tile past the end, which the prologue zero-fills
     const uint32_t f_base = smem_addr(frag) + (uint32_t)la * 16;
     const uint32_t f_zero = smem_addr(frag) + (uint32_t)NM * ntile * GEMV_FRAG_TILE_BYTES;
-    const uint32_t tb_base = smem_addr(tb) + (uint32_t)t * 4;
     uint32_t c_off_w = 0, c_off_s = 0;
     for (int gl = 0; gl < my_groups; ++gl)
     {
@@ -510,8 +505,7 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
         uint32_t fa = bact ? f_base + (uint32_t)tA * GEMV_FRAG_TILE_BYTES : f_zero;
         const uint32_t fstep = bact ? (uint32_t)GEMV_FRAG_TILE_BYTES : 0u;
         const uint32_t mstride = bact ? (uint32_t)ntile * GEMV_FRAG_TILE_BYTES : 0u;
-        uint32_t ta = tb_base + (uint32_t)tA * 16;
-        for (int tt = tA; tt < tB; ++tt, fa += fstep, ta += 16)
+        for (int tt = tA; tt < tB; ++tt, fa += fstep)
         {
             cp_async_wait<D - 2>();
             const uint4 wa4 = lds128(w_base + c_off_w);
@@ -531,8 +525,10 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
             for (int q = 0; q < 4; ++q)
             {
                 const uint32_t wa = u4get(wa4, q), wb = u4get(wb4, q);
-                const uint32_t a0 = nib_e0(wa), a1 = nib_e0(wb), a2 = nib_e1(wa), a3 = nib_e1(wb);
-                const uint32_t c0 = nib_e2(wa), c1 = nib_e2(wb), c2 = nib_e3(wa), c3 = nib_e3(wb);
+                const uint32_t a0 = unbias16(nib_e0(wa)), a1 = unbias16(nib_e0(wb));
+                const uint32_t a2 = unbias16(nib_e1(wa)), a3 = unbias16(nib_e1(wb));
+                const uint32_t c0 = unbias16(nib_e2(wa)), c1 = unbias16(nib_e2(wb));
+                const uint32_t c2 = unbias16(nib_e3(wa)), c3 = unbias16(nib_e3(wb));
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
                 {
@@ -547,10 +543,9 @@ __device__ __forceinline__ void gemv_lean_loop(const GemvParams& p, uint4* stw, 
 #pragma unroll
             for (int m = 0; m < NM; ++m)
             {
-                const float tbv = ldsf(ta + (uint32_t)(m * ntile * 16));
-                // column 2t: (hi, lo) parts, column 2t+1: (mid, 0)
-                acc0[m] = fmaf(sc0, ((d0[m] + d1[m]) + e0[m]) - tbv, acc0[m]);
-                acc1[m] = fmaf(sc1, ((d2[m] + d3[m]) + e2[m]) - tbv, acc1[m]);
+                // columns 2t / 2t+1 of the first mma: (hi, mid); column 2t of the second: lo
+                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) + e0[m], acc0[m]);
+                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) + e2[m], acc1[m]);
             }
         }
         float* rb = red + (size_t)(gl & 1) * NM * S * 16;
@@ -697,8 +692,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
             acc0[m] = acc1[m] = 0.0f;
         constexpr int FT = GEMV_FRAG_TILE_BYTES / 16; // uint4 per tile
         const uint4* fb = frag + (size_t)tA * FT + la;
-        const float* tbp = tb + (size_t)tA * 4 + t;
-        for (int tt = tA; tt < tB; ++tt, fb += FT, tbp += 4)
+        for (int tt = tA; tt < tB; ++tt, fb += FT)
         {
             cp_async_wait<D - 2>(); // this thread's copies of this item have landed
             const uint4* wsl = stw + (size_t)c_slot * NT * 2 + (size_t)tid * 2;
@@ -729,8 +723,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
             for (int q = 0; q < 4; ++q)
             {
                 const uint32_t wa = u4get(wa4, q), wb = u4get(wb4, q);
-                const uint32_t a0 = nib_e0(wa), a1 = nib_e0(wb), a2 = nib_e1(wa), a3 = nib_e1(wb);
-                const uint32_t c0 = nib_e2(wa), c1 = nib_e2(wb), c2 = nib_e3(wa), c3 = nib_e3(wb);
+                const uint32_t a0 = unbias16(nib_e0(wa)), a1 = unbias16(nib_e0(wb));
+                const uint32_t a2 = unbias16(nib_e1(wa)), a3 = unbias16(nib_e1(wb));
+                const uint32_t c0 = unbias16(nib_e2(wa)), c1 = unbias16(nib_e2(wb));
+                const uint32_t c2 = unbias16(nib_e3(wa)), c3 = unbias16(nib_e3(wb));
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
                 {
@@ -749,9 +745,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_q4_kernel(const GemvP
 #pragma unroll
             for (int m = 0; m < NM; ++m)
             {
-                const float tbv = tbp[(size_t)m * ntile * 4];
-                acc0[m] = fmaf(sc0, ((d0[m] + d1[m]) + e0[m]) - tbv, acc0[m]);
-                acc1[m] = fmaf(sc1, ((d2[m] + d3[m]) + e2[m]) - tbv, acc1[m]);
+                acc0[m] = fmaf(sc0, (d0[m] + d1[m]) + e0[m], acc0[m]);
+                acc1[m] = fmaf(sc1, (d2[m] + d3[m]) + e2[m], acc1[m]);
             }
         }
         float* rb = red + (size_t)(gl & 1) * NM * S * 16;

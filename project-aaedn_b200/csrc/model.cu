@@ -20,9 +20,11 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "gemm_tc.h"
 #include "gemv_q4.cuh"
 #include "gemv_tiled.cuh"
 #include "mega.cuh"
+#include "prefill.cuh"
 #include "tp.cuh"
 
 namespace aaedn_dev
@@ -490,6 +492,13 @@ struct aaedn_model
     GemvParams* d_gemv = nullptr; // [n_layers][4]
     AttnParams* d_attn = nullptr; // [n_layers]
     unsigned* mega_bar = nullptr; // [5 * n_layers]
+    // prefill: chunks of up to pf_rows prompt tokens through the tensor-core
+    // GEMM (0: the prompt runs as decode steps)
+    int pf_rows = 0;
+    float *pf_hidden = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_act = nullptr;
+    void* pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
+    unsigned* pf_err = nullptr;
 
     template <typename T>
     T* take(size_t bytes)
@@ -553,6 +562,21 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->tp_counter = m->take<unsigned>(64);
     m->hidden2 = m->take<float>(D * 4); // tensor parallel: the other residual buffer
     m->dbg_hidden = m->take<float>((size_t)c.n_layers * D * 4);
+    if (m->pf_rows)
+    {
+        const size_t P = (size_t)m->pf_rows;
+        m->pf_hidden = m->take<float>(P * D * 4);
+        m->pf_q = m->take<float>(P * H * hd * 4);
+        m->pf_attn = m->take<float>(P * m->kpo * 4);
+        m->pf_act = m->take<float>(P * m->kpd * 4);
+        size_t ws = 0;
+        for (const auto& nk : {std::make_pair(qkv_rows, D), std::make_pair(D, (size_t)m->kpo),
+                               std::make_pair(2 * F, D), std::make_pair(D, (size_t)m->kpd)})
+            ws = std::max(ws, tc_gemm_workspace_bytes((int)P, (int)nk.first, (int)nk.second));
+        m->pf_ws_bytes = ws;
+        m->pf_ws = m->take<uint8_t>(ws);
+        m->pf_err = m->take<unsigned>(64);
+    }
     return align_up(m->used, 256);
 }
 
@@ -1133,7 +1157,11 @@ static int device_status(aaedn_model* m)
 {
     uint32_t* w = m->pinned + m->cfg.max_seq + 4;
     AAEDN_CUDA_TRY(cudaMemcpyAsync(w, &m->state->err, 4, cudaMemcpyDeviceToHost, m->stream));
+    if (m->pf_err)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(w + 1, m->pf_err, 4, cudaMemcpyDeviceToHost, m->stream));
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    if (m->pf_err && w[1] != 0u && *w == 0u)
+        return set_error(AAEDN_ETIMEOUT, "a bounded wait of a prefill GEMM ran out");
     switch (*w)
     {
     case 0: return AAEDN_OK;
@@ -1149,6 +1177,129 @@ static int put_tokens(aaedn_model* m, const uint32_t* h_tokens, size_t n)
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     std::memcpy(m->pinned, h_tokens, n * 4);
     AAEDN_CUDA_TRY(cudaMemcpyAsync(m->prompt + m->h_pos, m->pinned, n * 4, cudaMemcpyHostToDevice, m->stream));
+    return AAEDN_OK;
+}
+
+// One chunk of n prompt tokens at positions pos0.. (tokens already in
+// m->prompt): embedding rows, then per layer RMSNorm -> QKV GEMM (RoPE, K/V
+// appended to the cache) -> causal attention -> O GEMM (+residual) ->
+// RMSNorm -> gate/up GEMM (SwiGLU) -> down GEMM (+residual). The last row of
+// the residual stream goes to m->hidden for the lm_head when `last`.
+static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
+{
+    cudaStream_t st = m->stream;
+    const aaedn_model_config& c = m->cfg;
+    const int D = (int)c.dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads, hd = (int)c.head_dim, F = (int)c.ffn_dim;
+    const int M_pad = tc_m_pad(n);
+    __nv_bfloat16* parts = static_cast<__nv_bfloat16*>(tc_gemm_parts(m->pf_ws));
+    pf_embed_kernel<<<n, 256, 0, st>>>(m->prompt + pos0, n, m->embedding, D, m->pf_hidden);
+    AAEDN_LAUNCH_CHECK("pf_embed_kernel");
+    count_launch();
+    TcGemmArgs base{};
+    base.x = nullptr; // parts written into the workspace by the kernel before
+    base.M = n;
+    base.w_layout = TC_W_TILED;
+    base.workspace = m->pf_ws;
+    base.workspace_bytes = m->pf_ws_bytes;
+    base.err = m->pf_err;
+    int rc;
+    for (uint32_t l = 0; l < c.n_layers; ++l)
+    {
+        const DevLayer& L = m->layers[l];
+        // ---- attention block
+        pf_rmsnorm_split_kernel<<<M_pad, 256, 0, st>>>(m->pf_hidden, D, n, M_pad, L.attn_norm, c.eps, parts);
+        AAEDN_LAUNCH_CHECK("pf_rmsnorm_split_kernel");
+        count_launch();
+        TcGemmArgs q = base;
+        q.N = (H + 2 * KV) * hd;
+        q.K = D;
+        q.w = L.wqkv;
+        q.epi = TC_EPI_QKV;
+        q.e.qrows = m->pf_q;
+        q.e.ldq = (size_t)H * hd;
+        q.e.k_layer = L.k;
+        q.e.v_layer = L.v;
+        q.e.page_table = m->page_table;
+        q.e.page_size = m->page_size;
+        q.e.n_kv = KV;
+        q.e.head_dim = hd;
+        q.e.q_rows = H * hd;
+        q.e.kv_rows = KV * hd;
+        q.e.pos0 = (int)pos0;
+        q.e.rope_cos = m->rope_cos;
+        q.e.rope_sin = m->rope_sin;
+        if ((rc = tc_gemm(q, st)))
+            return rc;
+        attn_prefill_kernel<<<dim3(H, (n + PF_ATTN_WARPS - 1) / PF_ATTN_WARPS), PF_ATTN_WARPS * 32, 0, st>>>(
+            m->pf_q, (size_t)H * hd, L.k, L.v, m->page_table, m->page_size, H, KV, hd, (int)pos0, n,
+            1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo);
+        AAEDN_LAUNCH_CHECK("attn_prefill_kernel");
+        count_launch();
+        if ((rc = tc_split(m->pf_attn, m->kpo, n, (int)m->kpo, m->pf_ws, st)))
+            return rc;
+        TcGemmArgs o = base;
+        o.N = D;
+        o.K = (int)m->kpo;
+        o.w = L.wo;
+        o.epi = TC_EPI_RESID;
+        o.out = m->pf_hidden;
+        o.ldc = (size_t)D;
+        if ((rc = tc_gemm(o, st)))
+            return rc;
+        // ---- feed-forward block
+        pf_rmsnorm_split_kernel<<<M_pad, 256, 0, st>>>(m->pf_hidden, D, n, M_pad, L.ffn_norm, c.eps, parts);
+        AAEDN_LAUNCH_CHECK("pf_rmsnorm_split_kernel");
+        count_launch();
+        TcGemmArgs gu = base;
+        gu.N = 2 * F;
+        gu.K = D;
+        gu.w = L.wgu;
+        gu.epi = TC_EPI_SWIGLU;
+        gu.e.act = m->pf_act;
+        gu.e.ld_act = m->kpd;
+        if ((rc = tc_gemm(gu, st)))
+            return rc;
+        if ((rc = tc_split(m->pf_act, m->kpd, n, (int)m->kpd, m->pf_ws, st)))
+            return rc;
+        TcGemmArgs dn = base;
+        dn.N = D;
+        dn.K = (int)m->kpd;
+        dn.w = L.wd;
+        dn.epi = TC_EPI_RESID;
+        dn.out = m->pf_hidden;
+        dn.ldc = (size_t)D;
+        if ((rc = tc_gemm(dn, st)))
+            return rc;
+    }
+    if (last)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(m->hidden, m->pf_hidden + (size_t)(n - 1) * D, (size_t)D * 4,
+                                       cudaMemcpyDeviceToDevice, st));
+    return AAEDN_OK;
+}
+
+// n prompt tokens (already in m->prompt at h_pos) through prefill chunks,
+// then the lm_head step of the last one: the decode state ends as after n
+// decode steps (position h_pos + n, the greedy token of the last logits).
+static int prefill(aaedn_model* m, size_t n)
+{
+    const uint32_t p0 = m->h_pos;
+    int rc = AAEDN_OK;
+    for (size_t c0 = 0; c0 < n && !rc; c0 += (size_t)m->pf_rows)
+    {
+        const int nc = (int)std::min<size_t>((size_t)m->pf_rows, n - c0);
+        rc = prefill_chunk(m, p0 + (uint32_t)c0, nc, c0 + (size_t)nc == n);
+    }
+    if (rc)
+        return rc;
+    // the lm_head of the last prompt token as the decode step does it
+    if ((rc = write_state(m, p0 + (uint32_t)n - 1, p0 + (uint32_t)n)))
+        return rc;
+    LmParams lp = lm_params(m);
+    cudaError_t e = launch_kernel(lm_head_argmax_kernel, dim3(m->lm_ctas), dim3(LM_THREADS),
+                                  lm_smem_bytes((int)m->cfg.dim, m->lm_stages), m->stream, false, lp);
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of lm_head_argmax_kernel failed: %s", cudaGetErrorString(e));
+    count_launch();
     return AAEDN_OK;
 }
 
@@ -1272,6 +1423,17 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
                                               (200 * 1024 - (size_t)c.dim * 4 - 1024) / ((size_t)c.dim * 4));
         m->lm_consumers = fit >= LM_CONSUMERS ? LM_CONSUMERS : (fit >= 4 ? 4 : (fit >= 2 ? 2 : 1));
         m->lm_stages = fit / m->lm_consumers * m->lm_consumers;
+    }
+    {
+        // prefill through the tensor-core GEMM: every matrix in the tile-major
+        // layout (K % 128, N % 16), one GPU, head_dim a multiple of 32
+        const size_t D = c.dim, hd = c.head_dim, F = c.ffn_dim;
+        const size_t qkv_rows = (size_t)(c.n_heads + 2 * c.n_kv_heads) * hd;
+        const bool ok = m->tp_size == 1 && m->tiled && tiles_ok(qkv_rows, D) && tiles_ok(D, m->kpo) &&
+                        tiles_ok(2 * F, D) && tiles_ok(D, m->kpd) && hd % 32 == 0 && hd <= 256;
+        const char* pe = std::getenv("AAEDN_PREFILL_ROWS");
+        const int rows = pe ? std::atoi(pe) : 256;
+        m->pf_rows = ok && rows > 1 ? (int)std::min<uint32_t>((uint32_t)rows, c.max_seq) : 0;
     }
     const size_t bytes = plan_arena(m, false);
     cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&m->arena), bytes);
@@ -1461,6 +1623,8 @@ extern "C" int aaedn_model_config_get(const aaedn_model* m, aaedn_model_config* 
 extern "C" void* aaedn_model_stream(aaedn_model* m) { return m ? (void*)m->stream : nullptr; }
 extern "C" size_t aaedn_model_arena_bytes(const aaedn_model* m) { return m ? m->arena_bytes : 0; }
 extern "C" uint32_t aaedn_model_pos(aaedn_model* m) { return m ? m->h_pos : 0; }
+extern "C" uint32_t aaedn_model_prefill_rows(const aaedn_model* m) { return m ? (uint32_t)m->pf_rows : 0u; }
+
 extern "C" uint32_t aaedn_model_kernels_per_step(const aaedn_model* m)
 {
     return m ? 5u * m->cfg.n_layers + 1u : 0u;
@@ -1685,7 +1849,7 @@ extern "C" int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, siz
     if (!rc)
         rc = write_state(m, m->h_pos, m->h_pos + (uint32_t)n);
     if (!rc)
-        rc = run_steps(m, n);
+        rc = (n > 1 && m->pf_rows) ? prefill(m, n) : run_steps(m, n);
     if (rc)
         return rc;
     m->h_pos += (uint32_t)n;
@@ -1711,11 +1875,26 @@ extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, si
     int rc = put_tokens(m, h_prompt, n_prompt);
     if (!rc)
         rc = write_state(m, m->h_pos, m->h_pos + (uint32_t)n_prompt);
-    if (!rc)
+    if (!rc && n_prompt > 1 && m->pf_rows)
+    {
+        // the prompt through the tensor-core prefill, then the decode steps
+        rc = prefill(m, n_prompt);
+        if (!rc)
+        {
+            m->h_pos += (uint32_t)n_prompt;
+            rc = run_steps(m, steps - n_prompt);
+            if (!rc)
+                m->h_pos += (uint32_t)(steps - n_prompt);
+        }
+    }
+    else if (!rc)
+    {
         rc = run_steps(m, steps);
+        if (!rc)
+            m->h_pos += (uint32_t)steps;
+    }
     if (rc)
         return rc;
-    m->h_pos += (uint32_t)steps;
     if (n_new)
         AAEDN_CUDA_TRY(cudaMemcpyAsync(h_out, m->out_tokens, n_new * 4, cudaMemcpyDeviceToHost, m->stream));
     return device_status(m);
