@@ -256,6 +256,14 @@ int aaedn_abn_model_read_header(const char* path, aaedn_abn_header* h_out, aaedn
  * none, src/transformer.cpp:112-117). No counterpart in the reference (its
  * transformer_init fills weights with constants and rand()). */
 int aaedn_model_load_abn(aaedn_model* m, const char* path);
+/* Writes a whole-model file in the layout aaedn_model_load_abn reads, from
+ * host tensors: layers[n_layers] (quantized with aaedn_quantize_q4, fp16
+ * scales; null norm gains are written as 1.0), the fp32 embedding and lm_head
+ * [vocab][dim] and the final-norm gain [dim] (null: 1.0); the QKV bias is
+ * written as zeros. The converter role of tools/convert_model.py:121-150
+ * (which writes one matrix in the version-2 header) for the whole model. */
+int aaedn_abn_model_write(const char* path, const aaedn_model_config* cfg, const aaedn_layer_host* layers,
+                          const float* h_embedding, const float* h_final_norm, const float* h_lm_head);
 /* Fill every weight from the seeded generator (N(0,0.02) linear weights
  * quantized with the block quantizer; fp32 embedding and lm_head; norm gains
  * 1.0). Tensor ids: embedding 0, lm_head 1, layer l: 16 + 8l + {q,k,v,o,g,u,d}.

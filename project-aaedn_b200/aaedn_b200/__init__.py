@@ -121,6 +121,8 @@ def lib():
         "aaedn_abn_model_read_header": ([ctypes.c_char_p, ctypes.POINTER(AbnHeader), ctypes.POINTER(ModelConfig)],
                                         _int),
         "aaedn_model_load_abn": ([_vp, ctypes.c_char_p], _int),
+        "aaedn_abn_model_write": ([ctypes.c_char_p, ctypes.POINTER(ModelConfig), ctypes.POINTER(LayerHost), _vp, _vp,
+                                   _vp], _int),
         "aaedn_model_synthesize": ([_vp, _u64], _int),
         "aaedn_model_reset": ([_vp], _int),
         "aaedn_model_pos": ([_vp], _u32),
@@ -379,6 +381,11 @@ class Model:
         hs = [None] * self.tp[1]
         dist.all_gather_object(hs, self.tp_handle(), group=group)
         self.tp_connect(hs)
+
+    def tp_share(self):
+        """(first token id, count) of this rank's lm_head rows / logits slice."""
+        p = tp_plan(self.cfg, self.tp[0], self.tp[1])
+        return p["vocab0"], p["vocab"]
 
     def next_token(self):
         """The greedy token of the last step (synchronises)."""

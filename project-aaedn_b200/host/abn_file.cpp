@@ -298,3 +298,119 @@ extern "C" int aaedn_model_load_abn(aaedn_model* m, const char* path)
                          c2, h.payload_checksum);
     return aaedn_model_set_globals(m, emb.data(), final_norm.data(), lm.data());
 }
+
+// ---------------------------------------------------------------------------
+// Writer of whole-model files (the layout aaedn_model_load_abn reads): the
+// header is written last, once the payload's FNV-1a checksum is known.
+namespace
+{
+
+struct WFile
+{
+    FILE* f = nullptr;
+    uint32_t hash = 0x811C9DC5u;
+    uint64_t bytes = 0;
+    explicit WFile(const char* path) : f(path ? std::fopen(path, "wb") : nullptr) {}
+    ~WFile()
+    {
+        if (f)
+            std::fclose(f);
+    }
+    bool put(const void* p, size_t n)
+    {
+        if (!n)
+            return true;
+        if (std::fwrite(p, 1, n, f) != n)
+            return false;
+        hash = aaedn_fnv1a32(static_cast<const uint8_t*>(p), n, hash);
+        bytes += n;
+        return true;
+    }
+    bool zeros(size_t n)
+    {
+        static const uint8_t z[4096] = {};
+        for (size_t left = n; left > 0;)
+        {
+            const size_t k = std::min(left, sizeof z);
+            if (!put(z, k))
+                return false;
+            left -= k;
+        }
+        return true;
+    }
+};
+
+void le32w(uint8_t* p, uint32_t v)
+{
+    for (int i = 0; i < 4; ++i)
+        p[i] = (uint8_t)(v >> (8 * i));
+}
+
+} // namespace
+
+extern "C" int aaedn_abn_model_write(const char* path, const aaedn_model_config* cfg, const aaedn_layer_host* layers,
+                                     const float* h_embedding, const float* h_final_norm, const float* h_lm_head)
+{
+    if (!path || !cfg || !layers || !h_embedding || !h_lm_head)
+        return set_error(AAEDN_EINVAL, "aaedn_abn_model_write: null argument");
+    const aaedn_model_config& c = *cfg;
+    if (!c.dim || !c.n_layers || !c.n_heads || !c.n_kv_heads || !c.head_dim || !c.ffn_dim || !c.vocab ||
+        c.n_heads % c.n_kv_heads || c.dim % 32 || c.ffn_dim % 32 || (c.n_heads * c.head_dim) % 32 ||
+        !(c.rope_theta > 0.0f) || !(c.eps > 0.0f))
+        return set_error(AAEDN_EINVAL, "aaedn_abn_model_write: the config does not describe a model");
+    const ModelDims d = dims_of(c);
+    const uint64_t qrows = d.qdim, krows = (uint64_t)c.n_kv_heads * c.head_dim;
+    WFile file(path);
+    if (!file.f)
+        return set_error(AAEDN_EFORMAT, "abn: cannot create %s", path);
+    uint8_t hdr[64] = {};
+    if (std::fwrite(hdr, 1, 64, file.f) != 64) // placeholder, rewritten at the end
+        return set_error(AAEDN_EFORMAT, "abn: write to %s failed", path);
+    std::vector<float> ones(d.D, 1.0f);
+    bool ok = true;
+    for (uint32_t l = 0; l < c.n_layers && ok; ++l)
+    {
+        const aaedn_layer_host& w = layers[l];
+        if (!w.wq || !w.wk || !w.wv || !w.wo || !w.wg || !w.wu || !w.wd || !w.sq || !w.sk || !w.sv || !w.so ||
+            !w.sg || !w.su || !w.sd)
+            return set_error(AAEDN_EINVAL, "aaedn_abn_model_write: layer %u has a null tensor", l);
+        const float* an = w.attn_norm ? w.attn_norm : ones.data();
+        const float* fn = w.ffn_norm ? w.ffn_norm : ones.data();
+        // RMSNorm | QKV codes (q, k, v rows) | QKV scales | QKV bias (zero) |
+        // O | gate | up | down (codes, then scales) | RMSNorm 2
+        ok = file.put(an, d.D * 4) && file.put(w.wq, qrows * d.D / 2) && file.put(w.wk, krows * d.D / 2) &&
+             file.put(w.wv, krows * d.D / 2) && file.put(w.sq, qrows * d.D / 32 * 2) &&
+             file.put(w.sk, krows * d.D / 32 * 2) && file.put(w.sv, krows * d.D / 32 * 2) &&
+             file.zeros(d.qkv * 4) && file.put(w.wo, d.D * d.qdim / 2) && file.put(w.so, d.D * d.qdim / 32 * 2) &&
+             file.put(w.wg, d.F * d.D / 2) && file.put(w.sg, d.F * d.D / 32 * 2) && file.put(w.wu, d.F * d.D / 2) &&
+             file.put(w.su, d.F * d.D / 32 * 2) && file.put(w.wd, d.D * d.F / 2) &&
+             file.put(w.sd, d.D * d.F / 32 * 2) && file.put(fn, d.D * 4);
+    }
+    ok = ok && file.put(h_final_norm ? h_final_norm : ones.data(), d.D * 4) && file.put(h_embedding, d.V * d.D * 4) &&
+         file.put(h_lm_head, d.V * d.D * 4);
+    if (!ok)
+        return set_error(AAEDN_EFORMAT, "abn: write to %s failed", path);
+    if (file.bytes != model_payload_bytes(c))
+        return set_error(AAEDN_EFORMAT, "abn: wrote %llu payload bytes, the layout has %llu",
+                         (unsigned long long)file.bytes, (unsigned long long)model_payload_bytes(c));
+    // "<8sIQI6IB15s": magic, version 3, payload size, checksum, the six dims,
+    // quant_type 0; reserved bytes: n_kv_heads, rope_theta, eps
+    std::memcpy(hdr, "AAEDNMDL", 8);
+    le32w(hdr + 8, kAbnModelVersion);
+    le32w(hdr + 12, (uint32_t)file.bytes);
+    le32w(hdr + 16, (uint32_t)(file.bytes >> 32));
+    le32w(hdr + 20, file.hash);
+    const uint32_t dims6[6] = {c.n_layers, c.n_heads, c.head_dim, c.vocab, c.dim, c.ffn_dim};
+    for (int i = 0; i < 6; ++i)
+        le32w(hdr + 24 + 4 * i, dims6[i]);
+    hdr[48] = 0;
+    le32w(hdr + 49, c.n_kv_heads);
+    uint32_t tb, eb;
+    std::memcpy(&tb, &c.rope_theta, 4);
+    std::memcpy(&eb, &c.eps, 4);
+    le32w(hdr + 53, tb);
+    le32w(hdr + 57, eb);
+    if (std::fseek(file.f, 0, SEEK_SET) != 0 || std::fwrite(hdr, 1, 64, file.f) != 64 || std::fflush(file.f) != 0)
+        return set_error(AAEDN_EFORMAT, "abn: header write to %s failed", path);
+    return AAEDN_OK;
+}
