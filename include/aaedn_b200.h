@@ -299,13 +299,6 @@ int aaedn_model_profile_step(aaedn_model* m, float* h_ms, uint32_t cap, uint32_t
  * attention, o, gate/up, down, lm_head. Leaves the KV cache and hidden state
  * undefined (rewind or reset afterwards). */
 int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h_ms, uint32_t cap);
-/* Tracing of the persistent step kernel (when the model runs it): one step
- * with cycle counters; h_cta [n_ctas][8]: consumer waits for weights,
- * grid-barrier waits, producer waits for free stages, total, attention,
- * activation builds, lm_head (SM cycles); h_phase [5 * n_layers + 1][2]: CTA
- * 0's clock when it reached / left each grid barrier. The position is left
- * where it was. */
-int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase, size_t cap_phase);
 /* Tracing of the per-kernel decode step: one step replayed with globaltimer
  * stamps (ns) per CTA; h_stamps [5 * n_layers + 1][1024][4]: per launch (qkv,
  * attention, o, gate/up, down of each layer, then lm_head) and CTA slot c <

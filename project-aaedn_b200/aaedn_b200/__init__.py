@@ -137,7 +137,6 @@ def lib():
         "aaedn_model_rewind": ([_vp, _u32], _int),
         "aaedn_model_profile_parts": ([_vp, _u32, _vp, _u32], _int),
         "aaedn_model_profile_step": ([_vp, _vp, _u32, ctypes.POINTER(_u32)], _int),
-        "aaedn_model_trace_step": ([_vp, _vp, _sz, _vp, _sz], _int),
         "aaedn_model_trace_kernels": ([_vp, _vp, _sz, _vp, _sz], _int),
     }
     for name, (args, res) in sig.items():
@@ -507,17 +506,6 @@ class Model:
         out = np.empty(8, np.float32)
         check(lib().aaedn_model_profile_parts(self.h, reps, _p(out), 8))
         return dict(zip(self.PART_NAMES, out.tolist()))
-
-    def trace_step(self, n_ctas=None):
-        """Cycle counters of one step of the persistent kernel: per-CTA
-        [wait weights, wait barriers, producer wait, total, attention, build,
-        lm_head] and CTA 0's barrier arrival / exit clocks."""
-        import os
-        n_ctas = n_ctas or 256
-        cta = np.zeros(n_ctas * 8, np.uint64)
-        ph = np.zeros((self.cfg["n_layers"] * 5 + 1) * 2, np.int64)
-        check(lib().aaedn_model_trace_step(self.h, _p(cta), cta.size, _p(ph), ph.size))
-        return cta.reshape(-1, 8), ph.reshape(-1, 2)
 
     def trace_kernels(self):
         """globaltimer stamps (ns) of one decode step of the per-kernel graph:

@@ -47,7 +47,6 @@ struct AttnParams
     int max_tok;              // unused (kept for the launch interface)
     const int* page_table;
     int page_size;
-    int no_combine; // leave the S partial results for the consumer to merge
     int nseg;
     uint32_t seg_start[ATTN_MAX_SEG];
     uint32_t seg_off[ATTN_MAX_SEG + 1]; // prefix sums of the lengths
@@ -367,8 +366,6 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
         return;
     }
 
-    if (p.no_combine)
-        return;
     // last CTA of this kv head merges the S splits in order
     __threadfence();
     named_bar_sync(bar_id, ATTN_THREADS);

@@ -57,7 +57,6 @@ int tc_launch(const TcGemmParams& p, const CUtensorMap& map, dim3 grid, cudaStre
         return rc;
     q4_gemm_tc_kernel<BN, STAGES, EPI><<<grid, TC_THREADS, smem, st>>>(p, map);
     AAEDN_LAUNCH_CHECK("q4_gemm_tc_kernel");
-    count_launch();
     return AAEDN_OK;
 }
 
@@ -99,7 +98,6 @@ int tc_split(const float* x, size_t lda, int M, int K, void* workspace, cudaStre
     tc_split_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(
         x, lda, M, M_pad, K, reinterpret_cast<__nv_bfloat16*>(tc_gemm_parts(workspace)));
     AAEDN_LAUNCH_CHECK("tc_split_kernel");
-    count_launch();
     return AAEDN_OK;
 }
 
@@ -151,7 +149,6 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t st)
         const size_t work = (size_t)M_pad * (a.K / 4);
         tc_split_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a.x, a.lda, a.M, M_pad, a.K, parts);
         AAEDN_LAUNCH_CHECK("tc_split_kernel");
-        count_launch();
     }
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)TC_XP * M_pad};
@@ -204,7 +201,6 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t st)
         tc_splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
             partial, splits, (size_t)a.M * a.N, a.M, a.N, a.out, a.ldc, a.epi == TC_EPI_RESID ? 1 : 0);
         AAEDN_LAUNCH_CHECK("tc_splitk_reduce_kernel");
-        count_launch();
     }
     return AAEDN_OK;
 }

@@ -170,25 +170,37 @@ __device__ __forceinline__ void tc_dequant_block(uint4 codes, float sc, uint32_t
     }
 }
 
-// Address of the 32 code bytes and two scales of weight row `row`, quant
-// blocks b0, b0 + 1 (b0 even).
-__device__ __forceinline__ void tc_w_addr(const TcGemmParams& p, int row, int b0, const uint8_t*& codes,
-                                          const uint16_t*& scales)
+// The 32 code bytes (quant blocks b0, b0 + 1 in order; b0 even) and their
+// two scales (low half: b0) of weight row `row`.
+__device__ __forceinline__ void tc_w_load(const TcGemmParams& p, int row, int b0, uint4& ca, uint4& cb,
+                                          uint32_t& sp)
 {
     if (p.w_layout == TC_W_TILED)
     {
-        const int ntile = p.K >> 7, group = row >> 4, r16 = row & 15, h = r16 >> 3, g = r16 & 7;
-        const int tile = b0 >> 2, t = b0 & 3, c = tile >> 5, ti = tile & 31;
-        const int tiles_in_chunk = min(32, ntile - 32 * c);
-        const uint8_t* chunk = p.w + (size_t)group * ntile * 1152 + (size_t)c * 32 * 1152;
-        codes = chunk + (size_t)(ti * 2 + h) * 512 + (4 * g + t) * 16;
-        scales = reinterpret_cast<const uint16_t*>(chunk + (size_t)tiles_in_chunk * 1024 + (ti * 2 + h) * 64 +
-                                                   (4 * g + t) * 2);
+        // the decode GEMV's layout (gemv_tiled.cuh): chunks of 16 tiles;
+        // blocks b0, b0 + 1 are pair P = (b0 % 4) / 2 of their tile, whose 64
+        // code bytes for rows g and g + 8 sit in lanes 4g..4g+3, word (H, r)
+        // of lane 4g + t = bytes [8H + 4(t & 1), +4) of block b' = t >> 1
+        constexpr int CT = 16;
+        const int ntile = p.K >> 7, group = row >> 4, r16 = row & 15, r = r16 >> 3, g = r16 & 7;
+        const int tile = b0 >> 2, P = (b0 >> 1) & 1, c = tile / CT, ti = tile % CT;
+        const int tiles_in_chunk = min(CT, ntile - CT * c);
+        const uint8_t* chunk = p.w + (size_t)group * ntile * 1152 + (size_t)c * CT * 1152;
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(chunk + (size_t)ti * 1024 + P * 512 + (4 * g) * 16);
+        // lane t' = 4g + t: words (H0 r0, H0 r1, H1 r0, H1 r1) at q[4 t' ..]
+        ca = make_uint4(__ldg(q + 0 + r), __ldg(q + 4 + r), __ldg(q + 2 + r), __ldg(q + 6 + r));
+        cb = make_uint4(__ldg(q + 8 + r), __ldg(q + 12 + r), __ldg(q + 10 + r), __ldg(q + 14 + r));
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(chunk + (size_t)tiles_in_chunk * 1024 + ti * 128) +
+                             ((P * 8 + g) * 2) * 2 + r;
+        sp = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 2) << 16);
     }
     else
     {
-        codes = p.w + (size_t)row * (p.ldb >> 1) + (size_t)b0 * 16;
-        scales = p.s + (size_t)row * (p.ldb >> 5) + b0;
+        const uint8_t* c = p.w + (size_t)row * (p.ldb >> 1) + (size_t)b0 * 16;
+        const uint16_t* sc = p.s + (size_t)row * (p.ldb >> 5) + b0;
+        ca = __ldg(reinterpret_cast<const uint4*>(c));
+        cb = __ldg(reinterpret_cast<const uint4*>(c) + 1);
+        sp = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 1) << 16);
     }
 }
 
@@ -410,14 +422,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
         uint32_t sp[2] = {};
         auto load = [&](int kb, int slot) {
             if (live && kb < nk)
-            {
-                const uint8_t* c;
-                const uint16_t* sc;
-                tc_w_addr(p, row, (kb0 + kb) * 2, c, sc);
-                ca[slot] = __ldg(reinterpret_cast<const uint4*>(c));
-                cb[slot] = __ldg(reinterpret_cast<const uint4*>(c) + 1);
-                sp[slot] = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 1) << 16);
-            }
+                tc_w_load(p, row, (kb0 + kb) * 2, ca[slot], cb[slot], sp[slot]);
             else
             {
                 ca[slot] = cb[slot] = make_uint4(0, 0, 0, 0);

@@ -37,13 +37,6 @@ enum
     PRO_PLAIN = 0,
     PRO_RMSNORM = 1,
     PRO_EMBED_RMSNORM = 2,
-    // x = the attention output, merged here from the per-split partial
-    // results (max, sum, unnormalised sum of V rows) of every head
-    PRO_ATTN_COMBINE = 3,
-    // tensor parallel: x = p.x + the sum over ranks of their partials
-    // (read from the peers once their flags show them complete), then the
-    // RMSNorm; CTA 0 stores the summed x to hidden_out
-    PRO_TP_RMSNORM = 4,
 };
 
 
@@ -162,21 +155,17 @@ struct GemvParams
     const float* rope_sin;
     // SwiGLU epilogue
     float* act;
-    // PRO_ATTN_COMBINE: partials [n_heads][attn_S][attn_pstride] (head_dim
-    // sums, max, sum; attn_pstride a multiple of 4)
-    const float* attn_part;
-    int attn_S, attn_pstride;
     int l2_hint; // stream the weights with the L2 evict-first policy
     unsigned long long* trace; // per-CTA timeline of a traced step (tiled kernel), or null
     int stages;                // ring stages of the tiled kernel (0: GT_STAGES)
-    // tensor parallel (zero otherwise): PRO_TP_RMSNORM waits for epoch
-    // *tp_epoch + tp_wait_phase + 1 and adds partial buffer tp_buf; a
-    // partial-writing GEMV (tp_sig) raises epoch *tp_epoch + tp_sig_phase + 1
-    // in every rank once its last CTA is done (tp_counter: last-CTA count)
+    // tensor parallel (zero otherwise): a partial-writing GEMV (tp_sig)
+    // stores its rows in partial buffer tp_buf and raises epoch *tp_epoch +
+    // tp_sig_phase + 1 in every rank once its last CTA is done (tp_counter:
+    // last-CTA count)
     TpComm tpc;
     const unsigned* tp_epoch;
     unsigned* tp_counter;
-    int tp_wait_phase, tp_buf, tp_sig, tp_sig_phase;
+    int tp_buf, tp_sig, tp_sig_phase;
     // scales can be staged as aligned u32 pairs (even scales per row, 4-byte
     // aligned array)
     bool scale_pairs;

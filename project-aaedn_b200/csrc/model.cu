@@ -23,7 +23,6 @@
 #include "gemm_tc.h"
 #include "gemv_q4.cuh"
 #include "gemv_tiled.cuh"
-#include "mega.cuh"
 #include "prefill.cuh"
 #include "tp.cuh"
 
@@ -31,6 +30,10 @@ namespace aaedn_dev
 {
 void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t K, uint8_t* out)
 {
+    // the layout of gemv_tiled.cuh: per row group, chunks of <= 16 tiles;
+    // tile codes [P][lane 4g + t][H0 r0, H0 r1, H1 r0, H1 r1] (4 bytes each:
+    // bytes [8H + 4(t & 1), +4) of block 2P + (t >> 1) of row g + 8r), then
+    // the chunk's tile scales [P][g][b'][r]
     const size_t ntile = K / 128, nchunk = (ntile + GT_CHUNK_TILES - 1) / GT_CHUNK_TILES;
     const size_t group_bytes = ntile * GT_TILE_BYTES;
     aaedn_host::parallel_for(N / 16, 1, [&](size_t g0, size_t g1) {
@@ -40,24 +43,36 @@ void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t
             for (size_t c = 0; c < nchunk; ++c)
             {
                 const size_t tiles = std::min<size_t>(GT_CHUNK_TILES, ntile - c * GT_CHUNK_TILES);
-                for (size_t i = 0; i < tiles; ++i) // codes in A-fragment order
-                    for (int h = 0; h < 2; ++h)
+                for (size_t i = 0; i < tiles; ++i)
+                {
+                    const size_t tile = c * GT_CHUNK_TILES + i;
+                    for (int P = 0; P < 2; ++P)
                         for (int l = 0; l < 32; ++l)
                         {
-                            const size_t row = gi * 16 + (l >> 2) + 8 * h;
-                            const size_t blk = (c * GT_CHUNK_TILES + i) * 4 + (l & 3);
-                            std::memcpy(o, codes + row * (K / 2) + blk * 16, 16);
-                            o += 16;
+                            const int g = l >> 2, t = l & 3;
+                            const size_t blk = tile * 4 + 2 * P + (t >> 1);
+                            for (int H = 0; H < 2; ++H)
+                                for (int r = 0; r < 2; ++r)
+                                {
+                                    const size_t row = gi * 16 + g + 8 * r;
+                                    std::memcpy(o, codes + row * (K / 2) + blk * 16 + 8 * H + 4 * (t & 1), 4);
+                                    o += 4;
+                                }
                         }
-                for (size_t i = 0; i < tiles; ++i) // then the scales, same order
-                    for (int h = 0; h < 2; ++h)
-                        for (int l = 0; l < 32; ++l)
-                        {
-                            const size_t row = gi * 16 + (l >> 2) + 8 * h;
-                            const size_t blk = (c * GT_CHUNK_TILES + i) * 4 + (l & 3);
-                            std::memcpy(o, scales + row * (K / 32) + blk, 2);
-                            o += 2;
-                        }
+                }
+                for (size_t i = 0; i < tiles; ++i)
+                {
+                    const size_t tile = c * GT_CHUNK_TILES + i;
+                    for (int P = 0; P < 2; ++P)
+                        for (int g = 0; g < 8; ++g)
+                            for (int b = 0; b < 2; ++b)
+                                for (int r = 0; r < 2; ++r)
+                                {
+                                    const size_t row = gi * 16 + g + 8 * r;
+                                    std::memcpy(o, scales + row * (K / 32) + tile * 4 + 2 * P + b, 2);
+                                    o += 2;
+                                }
+                }
             }
         }
     });
@@ -359,8 +374,8 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
         if (max_stages < 0)
         {
             const char* e = std::getenv("AAEDN_GEMV_STAGES");
-            // 4 by default: 5 (what a 4096-wide row group leaves room for) measured slower
-            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : GT_STAGES;
+            // default: as many 18 KB stages as the shared memory holds (<= 12)
+            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : GT_MAX_STAGES;
         }
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
@@ -373,9 +388,6 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
         count_launch();
         return AAEDN_OK;
     }
-    if constexpr (PRO == PRO_TP_RMSNORM || PRO == PRO_ATTN_COMBINE)
-        return set_error(AAEDN_EUNSUPPORTED, "this GEMV prologue needs the tile-major layout");
-    else
     {
     auto kern = (p.full_shape && p.scale_pairs) ? gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>
                                                 : gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>;
@@ -401,13 +413,10 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 template <int PRO, int EPI>
 int set_gemv_attrs()
 {
-    if constexpr (PRO != PRO_TP_RMSNORM && PRO != PRO_ATTN_COMBINE)
-    {
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    }
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_q4_kernel<1, PRO, EPI, AAEDN_SCALE_F16, true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     AAEDN_CUDA_TRY(cudaFuncSetAttribute(gemv_tiled_i8_kernel<PRO, EPI>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TILED_SMEM_MAX));
     return AAEDN_OK;
@@ -424,14 +433,6 @@ int set_model_kernel_attrs()
         rc = set_gemv_attrs<PRO_RMSNORM, EPI_SWIGLU>();
     if (!rc)
         rc = set_gemv_attrs<PRO_PLAIN, EPI_TP_PUSH>();
-    if (!rc)
-        rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_QKV_ROPE>();
-    if (!rc)
-        rc = set_gemv_attrs<PRO_TP_RMSNORM, EPI_SWIGLU>();
-    if (!rc)
-        rc = set_gemv_attrs<PRO_ATTN_COMBINE, EPI_RESIDUAL>();
-    if (!rc)
-        rc = set_gemv_attrs<PRO_ATTN_COMBINE, EPI_TP_PUSH>();
     return rc;
 }
 
@@ -467,8 +468,6 @@ struct aaedn_model
     uint32_t* pinned = nullptr; // host staging: [max_seq] tokens + state words
     bool weights_set = false;
     bool pdl = true;   // programmatic dependent launch inside the decode graph
-    bool attn_fuse = false; // the o-GEMV merges the attention splits while it builds its operand
-    bool tp_fuse = false; // tensor parallel: the next GEMV adds the ranks' partials (else a reduce kernel)
     bool tiled = true; // tile-major repacking of the matrices whose shape allows it
     bool l2_hint = true; // weight streams with the L2 evict-first policy
     // tensor parallelism: cfg holds this rank's dims (heads, ffn rows and
@@ -485,13 +484,6 @@ struct aaedn_model
     unsigned* tp_epoch = nullptr;
     unsigned* tp_counter = nullptr; // last-CTA count of a partial-writing GEMV
     float* hidden2 = nullptr;       // residual ping-pong: qkv folds into hidden2, gate/up into hidden
-    // the whole step as one persistent kernel (decode_step_kernel)
-    bool mega = false;
-    int mega_S = 1, mega_ctas = 0, mega_R = 1;
-    size_t mega_smem = 0;
-    GemvParams* d_gemv = nullptr; // [n_layers][4]
-    AttnParams* d_attn = nullptr; // [n_layers]
-    unsigned* mega_bar = nullptr; // [5 * n_layers]
     // prefill: chunks of up to pf_rows prompt tokens through the tensor-core
     // GEMM (0: the prompt runs as decode steps)
     int pf_rows = 0;
@@ -550,14 +542,11 @@ static size_t plan_arena(aaedn_model* m, bool carve)
     m->attn_out = m->take<float>(std::max<size_t>(H * hd, m->kpo) * 4); // padding stays zero
     m->act = m->take<float>(std::max<size_t>(F, m->kpd) * 4);
     m->logits = m->take<float>(V * 4);
-    m->attn_part = m->take<float>(H * (size_t)std::max(m->attn_S, m->mega_S) * (hd + 4) * 4);
+    m->attn_part = m->take<float>(H * (size_t)m->attn_S * (hd + 4) * 4);
     m->attn_counters = m->take<unsigned>(KV * 4);
     const size_t lm_parts = (size_t)std::max(m->lm_ctas, sm_count());
     m->lm_part_val = m->take<float>(lm_parts * 4);
     m->lm_part_idx = m->take<int>(lm_parts * 4);
-    m->d_gemv = m->take<GemvParams>((size_t)c.n_layers * 4 * sizeof(GemvParams));
-    m->d_attn = m->take<AttnParams>((size_t)c.n_layers * sizeof(AttnParams));
-    m->mega_bar = m->take<unsigned>((size_t)c.n_layers * 5 * 4);
     m->tp_epoch = m->take<unsigned>(64);
     m->tp_counter = m->take<unsigned>(64);
     m->hidden2 = m->take<float>(D * 4); // tensor parallel: the other residual buffer
@@ -630,17 +619,6 @@ static GemvParams qkv_params(const aaedn_model* m, uint32_t l)
     q.full_shape = (q.N % 16) == 0 && (q.K % 128) == 0;
     q.scale_pairs = ((D >> 5) & 1) == 0;
     q.l2_hint = m->l2_hint;
-    if (m->tp_size > 1 && m->tp_fuse)
-    {
-        // residual = hidden + the ranks' down partials of layer l - 1, into
-        // hidden2 (layer 0: the embedding row into hidden2)
-        q.tpc = m->tp;
-        q.tp_epoch = m->tp_epoch;
-        q.tp_counter = m->tp_counter;
-        q.hidden_out = m->hidden2;
-        q.tp_buf = 1;
-        q.tp_wait_phase = 2 * (int)l - 1;
-    }
     return q;
 }
 
@@ -725,17 +703,6 @@ static GemvParams gu_params(const aaedn_model* m, uint32_t l)
     gu.full_shape = (gu.N % 16) == 0 && (gu.K % 128) == 0;
     gu.scale_pairs = ((D >> 5) & 1) == 0;
     gu.l2_hint = m->l2_hint;
-    if (m->tp_size > 1 && m->tp_fuse)
-    {
-        // residual = hidden2 + the ranks' o partials, into hidden
-        gu.x = m->hidden2;
-        gu.tpc = m->tp;
-        gu.tp_epoch = m->tp_epoch;
-        gu.tp_counter = m->tp_counter;
-        gu.hidden_out = m->hidden;
-        gu.tp_buf = 0;
-        gu.tp_wait_phase = 2 * (int)l;
-    }
     return gu;
 }
 
@@ -797,136 +764,6 @@ static LmParams lm_params(const aaedn_model* m)
     return lp;
 }
 
-// decode_step_kernel instantiation for G query heads per kv head and head_dim
-template <int HDM>
-static void* mega_kernel_for(int G)
-{
-    switch (G)
-    {
-    case 1: return reinterpret_cast<void*>(decode_step_kernel<1, HDM>);
-    case 2: return reinterpret_cast<void*>(decode_step_kernel<2, HDM>);
-    case 4: return reinterpret_cast<void*>(decode_step_kernel<4, HDM>);
-    case 8: return reinterpret_cast<void*>(decode_step_kernel<8, HDM>);
-    default: return nullptr;
-    }
-}
-
-static void* mega_kernel(const aaedn_model* m)
-{
-    const int G = (int)(m->cfg.n_heads / m->cfg.n_kv_heads);
-    return m->cfg.head_dim > 128 ? mega_kernel_for<256>(G) : mega_kernel_for<128>(G);
-}
-
-static MegaParams mega_params(const aaedn_model* m)
-{
-    const aaedn_model_config& c = m->cfg;
-    MegaParams P{};
-    P.gemv = m->d_gemv;
-    P.attn = m->d_attn;
-    P.state = m->state;
-    P.bar = m->mega_bar;
-    P.n_layers = (int)c.n_layers;
-    P.attn_items = (int)c.n_kv_heads * m->mega_S;
-    P.lm.hidden = m->hidden;
-    P.lm.gain = m->final_norm;
-    P.lm.w = m->lm_head;
-    P.lm.logits = m->logits;
-    P.lm.part_val = m->lm_part_val;
-    P.lm.part_idx = m->lm_part_idx;
-    P.lm.out_tokens = m->out_tokens;
-    P.lm.eps = c.eps;
-    P.lm.dim = (int)c.dim;
-    P.lm.vocab = (int)c.vocab;
-    P.lm.max_seq = (int)c.max_seq;
-    P.lm.rows_per_cta = ((int)c.vocab + m->mega_ctas - 1) / m->mega_ctas;
-    P.lm.rows_per_chunk = m->mega_R;
-    return P;
-}
-
-// Decides whether this model runs as the persistent step kernel and uploads
-// its per-layer parameter arrays. Called once the arena is carved.
-static int setup_mega(aaedn_model* m)
-{
-    m->mega = false;
-    const char* e = std::getenv("AAEDN_MEGA");
-    if (!(e && e[0] == '1') || m->tp_size > 1)
-        return AAEDN_OK;
-    const aaedn_model_config& c = m->cfg;
-    for (const DevLayer& L : m->layers)
-        if (!(L.tqkv && L.to && L.tgu && L.td))
-            return AAEDN_OK; // every matrix must be tile-major
-    const int G = (int)(c.n_heads / c.n_kv_heads);
-    void* kern = mega_kernel(m);
-    if (!kern || c.head_dim > 256)
-        return AAEDN_OK;
-    // lm_head rows per ring stage: a power of two, every warp slice whole
-    int R = 16;
-    while (R > 1 && (size_t)R * c.dim * 4 > (size_t)GT_STAGE_BYTES)
-        R >>= 1;
-    if ((size_t)c.dim * 4 > (size_t)GT_STAGE_BYTES || ((c.dim / 4) % (GT_CONSUMERS / R)) != 0 || c.dim % 4)
-        return AAEDN_OK;
-    const int max_ntile = (int)(std::max({c.dim, c.n_heads * c.head_dim, c.ffn_dim}) / 128);
-    const size_t work = mega_work_bytes(max_ntile, attn_smem_bytes(G, (int)c.head_dim, 0), (int)c.dim);
-    const size_t smem = mega_smem_bytes(work);
-    if (smem > TILED_SMEM_MAX)
-        return AAEDN_OK;
-    int dev = 0, coop = 0, nb = 0;
-    AAEDN_CUDA_TRY(cudaGetDevice(&dev));
-    AAEDN_CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
-    if (!coop)
-        return AAEDN_OK;
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TILED_SMEM_MAX));
-    AAEDN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, GT_THREADS, smem));
-    if (nb < 1)
-        return AAEDN_OK;
-    m->mega_ctas = sm_count();
-    m->mega_R = R;
-    m->mega_smem = smem;
-    std::vector<GemvParams> gp((size_t)c.n_layers * 4);
-    std::vector<AttnParams> ap(c.n_layers);
-    for (uint32_t l = 0; l < c.n_layers; ++l)
-    {
-        gp[4 * l + 0] = qkv_params(m, l);
-        gp[4 * l + 1] = o_params(m, l);
-        gp[4 * l + 1].attn_part = m->attn_part; // the o build merges the attention splits
-        gp[4 * l + 1].attn_S = m->mega_S;
-        gp[4 * l + 1].attn_pstride = (int)c.head_dim + 4;
-        gp[4 * l + 1].head_dim = (int)c.head_dim;
-        gp[4 * l + 2] = gu_params(m, l);
-        gp[4 * l + 3] = down_params(m, l);
-        ap[l] = attn_params(m, l, m->mega_S);
-        ap[l].no_combine = 1;
-    }
-    AAEDN_CUDA_TRY(cudaMemcpy(m->d_gemv, gp.data(), gp.size() * sizeof(GemvParams), cudaMemcpyHostToDevice));
-    AAEDN_CUDA_TRY(cudaMemcpy(m->d_attn, ap.data(), ap.size() * sizeof(AttnParams), cudaMemcpyHostToDevice));
-    m->mega = true;
-    return AAEDN_OK;
-}
-
-static int enqueue_mega(aaedn_model* m, cudaStream_t st, unsigned long long* trace_cta = nullptr,
-                        long long* trace_phase = nullptr)
-{
-    MegaParams P = mega_params(m);
-    P.trace_cta = trace_cta;
-    P.trace_phase = trace_phase;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)m->mega_ctas);
-    cfg.blockDim = dim3(GT_THREADS);
-    cfg.dynamicSmemBytes = m->mega_smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeCooperative;
-    at[0].val.cooperative = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    const void* args[1] = {&P};
-    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel(m), const_cast<void**>(args));
-    if (e != cudaSuccess)
-        return set_error(AAEDN_ECUDA, "launch of decode_step_kernel failed: %s", cudaGetErrorString(e));
-    count_launch();
-    return AAEDN_OK;
-}
-
 // hidden += the sum of the ranks' partials in buffer buf (o: 0, down: 1)
 static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool signal)
 {
@@ -954,8 +791,6 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
 {
     if (m->tp_size > 1 && !m->tp_ready)
         return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
-    if (m->mega && !debug && !ev && mask == K_ALL)
-        return enqueue_mega(m, st);
     // programmatic dependent launches between consecutive kernels (not when
     // events or copies sit between them)
     const bool pdl = m->pdl && !ev && !debug;
@@ -978,16 +813,6 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         GemvParams q = qkv_params(m, l), o = o_params(m, l), gu = gu_params(m, l), dn = down_params(m, l);
         const int aS = m->attn_cS ? m->attn_cS : m->attn_S;
         AttnParams a = attn_params(m, l, aS);
-        const bool afuse = m->attn_fuse && L.to;
-        if (afuse)
-        {
-            // attention leaves its S split results; the o build merges them
-            a.no_combine = 1;
-            o.attn_part = m->attn_part;
-            o.attn_S = m->attn_S;
-            o.attn_pstride = hd + 4;
-            o.head_dim = hd;
-        }
         if (trace)
         {
             const size_t per = (size_t)STEP_TRACE_CTAS * STEP_TRACE_EVENTS, k0 = (size_t)l * 5;
@@ -998,10 +823,8 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             dn.trace = trace + (k0 + 4) * per;
         }
         // --- QKV (+RMSNorm prologue, +RoPE/KV-append epilogue)
-        const bool fuse = m->tp_size > 1 && m->tp_fuse;
         rc = !(mask & K_QKV) ? AAEDN_OK
              : (l == 0)      ? model_gemv<PRO_EMBED_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
-             : fuse          ? model_gemv<PRO_TP_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv)
                              : model_gemv<PRO_RMSNORM, EPI_QKV_ROPE>(q, st, pdl, L.tqkv);
         if (rc)
             return rc;
@@ -1018,35 +841,29 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             return rc;
         // --- O projection + residual (sharded: this rank's partial, then the
         // reduction over the ranks adds the sum to the residual)
-        if (m->tp_size > 1) // its partial; the ranks' sum is folded in by gate/up (or a reduce kernel)
+        if (m->tp_size > 1) // its partial, then the ranks' sum into the residual
         {
-            rc = !(mask & K_O) ? AAEDN_OK
-                 : afuse       ? model_gemv<PRO_ATTN_COMBINE, EPI_TP_PUSH>(o, st, pdl, L.to)
-                               : model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to);
-            if (!rc && (mask & K_O) && !fuse)
+            rc = !(mask & K_O) ? AAEDN_OK : model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to);
+            if (!rc && (mask & K_O))
                 rc = tp_reduce(m, st, 0, 2 * (int)l, false);
         }
         else
-            rc = !(mask & K_O) ? AAEDN_OK
-                 : afuse       ? model_gemv<PRO_ATTN_COMBINE, EPI_RESIDUAL>(o, st, pdl, L.to)
-                               : model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to);
+            rc = !(mask & K_O) ? AAEDN_OK : model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to);
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- gate/up (+RMSNorm prologue, SwiGLU epilogue)
-        rc = !(mask & K_GU) ? AAEDN_OK
-             : fuse         ? model_gemv<PRO_TP_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu)
-                            : model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu);
+        rc = !(mask & K_GU) ? AAEDN_OK : model_gemv<PRO_RMSNORM, EPI_SWIGLU>(gu, st, pdl, L.tgu);
         if (rc)
             return rc;
         if ((rc = mark()))
             return rc;
         // --- down + residual
-        if (m->tp_size > 1) // its partial; the next qkv (or the final reduction) folds the sum in
+        if (m->tp_size > 1) // its partial, then the ranks' sum into the residual
         {
             rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(dn, st, pdl, L.td) : AAEDN_OK;
-            if (!rc && (mask & K_DOWN) && (!fuse || l + 1 == c.n_layers))
+            if (!rc && (mask & K_DOWN))
                 rc = tp_reduce(m, st, 1, 2 * (int)l + 1, false);
         }
         else
@@ -1194,7 +1011,6 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
     __nv_bfloat16* parts = static_cast<__nv_bfloat16*>(tc_gemm_parts(m->pf_ws));
     pf_embed_kernel<<<n, 256, 0, st>>>(m->prompt + pos0, n, m->embedding, D, m->pf_hidden);
     AAEDN_LAUNCH_CHECK("pf_embed_kernel");
-    count_launch();
     TcGemmArgs base{};
     base.x = nullptr; // parts written into the workspace by the kernel before
     base.M = n;
@@ -1209,7 +1025,6 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
         // ---- attention block
         pf_rmsnorm_split_kernel<<<M_pad, 256, 0, st>>>(m->pf_hidden, D, n, M_pad, L.attn_norm, c.eps, parts);
         AAEDN_LAUNCH_CHECK("pf_rmsnorm_split_kernel");
-        count_launch();
         TcGemmArgs q = base;
         q.N = (H + 2 * KV) * hd;
         q.K = D;
@@ -1234,7 +1049,6 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
             m->pf_q, (size_t)H * hd, L.k, L.v, m->page_table, m->page_size, H, KV, hd, (int)pos0, n,
             1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo);
         AAEDN_LAUNCH_CHECK("attn_prefill_kernel");
-        count_launch();
         if ((rc = tc_split(m->pf_attn, m->kpo, n, (int)m->kpo, m->pf_ws, st)))
             return rc;
         TcGemmArgs o = base;
@@ -1249,7 +1063,6 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
         // ---- feed-forward block
         pf_rmsnorm_split_kernel<<<M_pad, 256, 0, st>>>(m->pf_hidden, D, n, M_pad, L.ffn_norm, c.eps, parts);
         AAEDN_LAUNCH_CHECK("pf_rmsnorm_split_kernel");
-        count_launch();
         TcGemmArgs gu = base;
         gu.N = 2 * F;
         gu.K = D;
@@ -1393,10 +1206,6 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         m->tiled = !(t && t[0] == '0');
         const char* h = std::getenv("AAEDN_L2HINT");
         m->l2_hint = !(h && h[0] == '0');
-        const char* af = std::getenv("AAEDN_ATTN_FUSE");
-        m->attn_fuse = af && af[0] == '1'; // measured slower (every CTA merges all heads): opt-in
-        const char* f = std::getenv("AAEDN_TP_FUSE");
-        m->tp_fuse = f && f[0] == '1'; // measured slower on 2 GPUs: opt-in
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
@@ -1410,10 +1219,6 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     S = std::min(S, 64);
     m->attn_S = S;
     m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
-    // the persistent step kernel runs two attention items per CTA at once:
-    // at most 2 * SMs items
-    m->mega_S = std::max(1, std::min<int>(64, 2 * sm_count() / (int)c.n_kv_heads));
-    m->mega_S = std::max(1, std::min<int>(m->mega_S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
     // lm_head: one CTA per SM, each streaming one contiguous run of rows
     m->lm_rows = std::max(1, (int)((c.vocab + sm_count() - 1) / sm_count()));
     m->lm_ctas = (int)((c.vocab + m->lm_rows - 1) / m->lm_rows);
@@ -1481,7 +1286,6 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     rc = attn_set_attrs<1>();
     if (rc)
         return fail(rc);
-    if (!m->attn_fuse)
     {
         // decode attention as clusters of Sc splits per kv head (a power of
         // two <= 8 by default, <= max_seq / 8) merging in distributed shared
@@ -1498,9 +1302,6 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
             m->attn_cS = Sc;
     }
     rc = set_model_kernel_attrs();
-    if (rc)
-        return fail(rc);
-    rc = setup_mega(m);
     if (rc)
         return fail(rc);
     if (m->tp_size > 1)
@@ -2103,56 +1904,12 @@ extern "C" int aaedn_model_profile_parts(aaedn_model* m, uint32_t reps, float* h
     return rc;
 }
 
-extern "C" int aaedn_model_trace_step(aaedn_model* m, uint64_t* h_cta, size_t cap_cta, int64_t* h_phase,
-                                      size_t cap_phase)
-{
-    MODEL_OK(m);
-    if (!m->mega)
-        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_step: the model does not run the persistent kernel");
-    const aaedn_model_config& c = m->cfg;
-    const size_t ncta = (size_t)m->mega_ctas * MEGA_TRACE_CTA, nph = ((size_t)c.n_layers * 5 + 1) * 2;
-    if (!h_cta || !h_phase || cap_cta < ncta || cap_phase < nph)
-        return set_error(AAEDN_EINVAL, "aaedn_model_trace_step: need %zu + %zu outputs", ncta, nph);
-    if (m->h_pos == 0 || (size_t)m->h_pos + 2 > c.max_seq)
-        return set_error(AAEDN_ESTATE, "aaedn_model_trace_step: sequence empty or full");
-    unsigned long long* d_cta = nullptr;
-    long long* d_ph = nullptr;
-    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
-    AAEDN_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&d_cta), ncta * 8));
-    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&d_ph), nph * 8);
-    if (e == cudaSuccess)
-        e = cudaMemsetAsync(d_cta, 0, ncta * 8, m->stream);
-    if (e == cudaSuccess)
-        e = cudaMemsetAsync(d_ph, 0, nph * 8, m->stream);
-    int rc = e == cudaSuccess ? enqueue_mega(m, m->stream, d_cta, d_ph)
-                              : set_error(AAEDN_ECUDA, "trace buffers: %s", cudaGetErrorString(e));
-    if (!rc)
-    {
-        e = cudaMemcpyAsync(h_cta, d_cta, ncta * 8, cudaMemcpyDeviceToHost, m->stream);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(h_phase, d_ph, nph * 8, cudaMemcpyDeviceToHost, m->stream);
-        if (e == cudaSuccess)
-            e = cudaStreamSynchronize(m->stream);
-        if (e != cudaSuccess)
-            rc = set_error(AAEDN_ECUDA, "trace step: %s", cudaGetErrorString(e));
-    }
-    cudaFree(d_cta);
-    cudaFree(d_ph);
-    if (!rc)
-        rc = write_state(m, m->h_pos, m->h_pos); // the traced step does not count
-    if (!rc && cudaStreamSynchronize(m->stream) != cudaSuccess)
-        rc = set_error(AAEDN_ECUDA, "trace step sync");
-    return rc;
-}
-
 extern "C" int aaedn_model_trace_kernels(aaedn_model* m, uint64_t* h_stamps, size_t cap, uint32_t* h_grid,
                                          size_t cap_grid)
 {
     MODEL_OK(m);
     const aaedn_model_config& c = m->cfg;
     const size_t nk = (size_t)c.n_layers * 5 + 1, per = (size_t)STEP_TRACE_CTAS * STEP_TRACE_EVENTS;
-    if (m->mega)
-        return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_kernels: the model runs the persistent kernel");
     if (m->tp_size > 1)
         return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_trace_kernels: not for a tensor-parallel model");
     if (!h_stamps || !h_grid || cap < nk * per || cap_grid < nk)

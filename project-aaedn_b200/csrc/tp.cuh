@@ -10,10 +10,7 @@
 // NVLink) and raises a flag in each rank's memory. tp_reduce_kernel then
 // waits for all flags and adds the T partials (read from its own memory, in
 // rank order: the same sum, bit for bit, on every rank) to the residual.
-// Opt-in (AAEDN_TP_FUSE=1), the next GEMV does that addition while it builds
-// its operand instead (PRO_TP_RMSNORM); measured slower on 2 GPUs (417 against
-// 560 tok/s at the 7B widths), since every CTA of the next GEMV then waits for
-// the flags. The greedy argmax is exchanged the same way, so all ranks feed
+// The greedy argmax is exchanged the same way, so all ranks feed
 // the same token to the next step.
 //
 // Flags carry an epoch, E = tp_epoch + phase + 1, that only grows (phase:

@@ -3,8 +3,10 @@ restated with numpy on the CPU: the activation of each 32-element block is
 scaled to y = x * (127 / max|x|) in fp32, each y becomes the integer
 Y = rint(y * 2^21) (odd elements: rint(y * 2^17), the high nibble carries a
 factor 16), Y is split into four balanced base-128 digits, the 4-bit codes
-meet the digits in exact integer dot products (the tensor-core MMAs), and
-the digits' sums are recombined and scaled in fp32 as the epilogue does.
+meet the digits in exact integer dot products (the tensor-core MMAs: each
+covers two blocks and gives all four digit sums of both), and the digit
+pairs' sums are scaled in fp32 by the lanes that hold them, digits (0, 1) at
+weight 1 and digits (2, 3) at 2^-14, then added, as the kernel does.
 This pins the engine's precision: the error of an element is below
 |w| * max|x of its block| * 1e-7 (the digits keep 2^-22 of the block's scale,
 odd elements 2^-18 of y / 16), plus fp32 accumulation; on the normally
@@ -29,7 +31,8 @@ def engine_dot(codes, scales, x):
     """One output row: codes uint8 [K] (0..15, the weight's nibbles), fp16
     scales [K/32], x fp32 [K]. Mirrors the kernel's roundings."""
     K = x.size
-    acc = np.float32(0)
+    acc_hi = np.float32(0)  # the lanes holding digits (0, 1)
+    acc_lo = np.float32(0)  # the lanes holding digits (2, 3)
     for b in range(K // 32):
         xb = x[32 * b:32 * b + 32].astype(np.float32)
         cb = codes[32 * b:32 * b + 32].astype(np.int64)
@@ -41,11 +44,12 @@ def engine_dot(codes, scales, x):
         a = np.where(np.arange(32) % 2 == 0, cb, 16 * cb)  # low nibble c, high nibble 16 c
         d0, d1, d2, d3 = _digits(Y)
         p0, p1, q0, q1 = (int(np.dot(a, d)) for d in (d0, d1, d2, d3))
-        r = np.float32(np.float32(q0 * 128 + q1) * np.float32(1.0 / 16384.0) + np.float32(p0 * 128 + p1))
         bsc = np.float32(mx / np.float32(127.0 * 128.0))
         sw = np.float32(np.float16(scales[b]).astype(np.float32))
-        acc = np.float32(acc + np.float32(sw * bsc) * r)
-    return acc
+        acc_hi = np.float32(acc_hi + np.float32(sw * bsc) * np.float32(p0 * 128 + p1))
+        acc_lo = np.float32(acc_lo + np.float32(sw * np.float32(bsc * np.float32(1.0 / 16384.0))) *
+                            np.float32(q0 * 128 + q1))
+    return np.float32(acc_hi + acc_lo)
 
 
 @pytest.mark.parametrize("seed,dist", [(0, "normal"), (1, "wide"), (2, "sparse"), (3, "tiny")])

@@ -25,10 +25,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, size, port, cfg, seed, n_prompt, n_new, fuse, q):
+def _rank(rank, size, port, cfg, seed, n_prompt, n_new, q):
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), AAEDN_TP_FUSE=fuse)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     from datetime import timedelta
     dist.init_process_group("gloo", rank=rank, world_size=size, timeout=timedelta(seconds=120))
@@ -49,14 +49,14 @@ def _rank(rank, size, port, cfg, seed, n_prompt, n_new, fuse, q):
         dist.destroy_process_group()
 
 
-def _run(cfg, seed, n_prompt, n_new, size=2, fuse="0"):
+def _run(cfg, seed, n_prompt, n_new, size=2):
     import torch
     if torch.cuda.device_count() < size:
         pytest.skip(f"needs {size} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, size, port, cfg, seed, n_prompt, n_new, fuse, q)) for r in range(size)]
+    procs = [ctx.Process(target=_rank, args=(r, size, port, cfg, seed, n_prompt, n_new, q)) for r in range(size)]
     for pr in procs:
         pr.start()
     res = sorted(q.get(timeout=600) for _ in range(size))
@@ -72,19 +72,15 @@ def _run(cfg, seed, n_prompt, n_new, size=2, fuse="0"):
     return toks[0], logits
 
 
-@pytest.mark.parametrize("cfg,seed,n_prompt,n_new,size,fuse", [
-    (GQA, 77, 9, 120, 2, "1"),
-    (GQA, 77, 9, 120, 2, "0"),
-    (W7B, 2024, 4, 64, 2, "1"),
-    (W7B, 2024, 4, 64, 2, "0"),
-    (W7B, 31, 5, 40, 4, "0"),
-    (W7B, 31, 5, 40, 8, "0"),
+@pytest.mark.parametrize("cfg,seed,n_prompt,n_new,size", [
+    (GQA, 77, 9, 120, 2),
+    (W7B, 2024, 4, 64, 2),
+    (W7B, 31, 5, 40, 4),
+    (W7B, 31, 5, 40, 8),
 ])
-def test_tp_greedy_identical_to_oracle(oracle, cfg, seed, n_prompt, n_new, size, fuse):
-    """fuse "1": the next GEMV adds the ranks' partials while it builds its
-    operand; "0": a separate reduction kernel after o and down."""
+def test_tp_greedy_identical_to_oracle(oracle, cfg, seed, n_prompt, n_new, size):
     import pyoracle
-    got, logits = _run(cfg, seed, n_prompt, n_new, size=size, fuse=fuse)
+    got, logits = _run(cfg, seed, n_prompt, n_new, size=size)
     w = ab.synthetic_weights(cfg, seed)
     om = pyoracle.OracleModel(oracle, cfg, w)
     want, wl = om.generate(ab.synth_tokens(seed, 0, cfg["vocab"], n_prompt), n_new)
