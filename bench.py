@@ -71,6 +71,11 @@ def parse():
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-microbench", action="store_true", help="skip the dequant-GEMV/GEMM microbenchmark")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batched"],
+                    help="decode: the headline 7B bs1 decode; batched: the 8B-GQA batched decode (its own line)")
+    ap.add_argument("--batch", type=int, default=32, help="batched workload: streams")
+    ap.add_argument("--batch-prompt", type=int, default=2048, help="batched workload: prompt tokens per stream")
     ap.add_argument("--mode", default="tp", choices=["tp", "replicas"],
                     help="N > 1 GPUs: one sequence tensor-parallel over the N GPUs (strong scaling), or N "
                          "independent replicas (weak scaling)")
@@ -311,6 +316,46 @@ def prefill_report(cfg, n, ms, shards, chunk_rows):
                      "one decode step per prompt token")}
 
 
+def microbench(reps=20):
+    """The dequant-GEMV / GEMM microbenchmark on the block-quant format
+    (weights N(0, 0.02) quantized, activations N(0, 1) fp32) through the
+    fused_matmul entry point: shapes 4096x4096, 11008x4096, 4096x11008 at
+    M = 1 and 8 (GEMV engine; GB/s of codes + scales + activations against
+    the HBM peak) and M = 64 (tcgen05 GEMM; TFLOP/s, 2 M N K). Enough weight
+    copies rotate that every call reads HBM (more than the 126 MB of L2)."""
+    import torch
+    import aaedn_b200 as ab
+    peak, _ = measured_peaks()
+    out = []
+    for N, K in ((4096, 4096), (11008, 4096), (4096, 11008)):
+        wbytes = N * K // 2 + N * K // 16
+        copies = max(2, int(400e6 // wbytes) + 1)
+        d, sc = ab.quantize_q4(ab.synth_normal(77, N + K, N * K))
+        wd = torch.from_numpy(d).cuda()
+        ws = torch.from_numpy(sc.view(np.int16)).cuda()
+        W = [(wd.clone(), ws.clone()) for _ in range(copies)]
+        for M in (1, 8, 64):
+            x = torch.from_numpy(ab.synth_normal(78, M, M * K, std=1.0)).cuda()
+            y = torch.empty(M * N, dtype=torch.float32, device="cuda")
+            for i in range(3):
+                ab.fused_matmul(x, W[i % copies][0], W[i % copies][1], y, M, N, K)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(reps):
+                ab.fused_matmul(x, W[i % copies][0], W[i % copies][1], y, M, N, K)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            byts = gemv_bytes(N, K, M)
+            row = {"N": N, "K": K, "M": M, "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9,
+                   "hbm_frac": byts / (ms / 1e3) / 1e9 / peak, "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12,
+                   "engine": "tcgen05 GEMM" if M > 8 else "GEMV (mma.sync bf16, three activation parts)"}
+            out.append(row)
+        del W
+    return out
+
+
 def parity_check(model, cfg, args, tp, prompt_logits):
     """The run's first greedy tokens and its logits after the prompt against
     the oracle fixture of the full 7B model (None when the workload is not
@@ -474,6 +519,13 @@ def run_ours(args):
     sb = step_bytes(cfg, mean_pos) * share  # per GPU
     step_gbs = sb / (ms_max / K / 1000.0) / 1e9
 
+    micro = None
+    if rank == 0 and world == 1 and not args.no_microbench:
+        try:
+            micro = microbench()
+        except Exception as ex:  # the decode number stands without it
+            micro = [{"failed": str(ex)}]
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -504,6 +556,7 @@ def run_ours(args):
             "decode_step": {"algorithmic_bytes": sb, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
                             **kernel_split},
             "prefill": prefill_report(cfg, args.prompt, prefill_ms, world if tp else 1, model.prefill_rows),
+            "microbench": micro,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12,
                     "d2h_bytes_per_step": (4 * ab.tp_plan(cfg, rank, world)["vocab"] + 4) if tp else 4 * cfg["vocab"],
@@ -521,10 +574,87 @@ def run_ours(args):
     return 0
 
 
+LLAMA3_8B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336, vocab=128256,
+                 max_seq=4096, rope_theta=500000.0, eps=1e-6)
+
+
+def run_batched(args):
+    """The Llama-3-8B-shaped GQA model with a batch of streams (default 32),
+    each prefilled with its own seeded random prompt (default 2048 tokens),
+    then decoded together at batch width (default 256 steps): one GPU, the
+    batched model (shared paged KV pool, tensor-core GEMMs over the batch).
+    Prints one JSON line of its own (not the headline metric)."""
+    import torch
+    import aaedn_b200 as ab
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    B, T, K, W = args.batch, args.batch_prompt, args.steps, max(3, args.warmup)
+    cfg = dict(LLAMA3_8B, max_seq=T + W + K + 8)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    model = ab.BatchedModel(cfg, max_seqs=B, kv_tokens=B * (cfg["max_seq"] + 64))
+    t0 = time.time()
+    model.synthesize(SEED)
+    synth_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(model.stream)
+    seqs, nxt = [], []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(B):
+        s = model.open()
+        _, n = model.prefill(s, ab.synth_tokens(SEED, 100 + i, cfg["vocab"], T), want_logits=False)
+        seqs.append(s)
+        nxt.append(n)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    for _ in range(W):
+        _, out = model.step(seqs, nxt, want_logits=False)
+        nxt = [int(v) for v in out]
+    torch.cuda.synchronize()
+    clocks = ClockSampler(gpu_identity(int(os.environ.get("LOCAL_RANK", "0"))))
+    time.sleep(0.3)
+    e0.record(stream)
+    for _ in range(K):
+        _, out = model.step(seqs, nxt, want_logits=False)
+        nxt = [int(v) for v in out]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    peak, kind = measured_peaks()
+    L = cfg["n_layers"]
+    wbytes = sum(gemv_bytes(n, k, B) for n, k in gemv_shapes(cfg).values()) * L + cfg["vocab"] * cfg["dim"] * 4
+    mean_pos = T + W + (K - 1) / 2.0
+    kv = L * 2 * B * (mean_pos + 1) * cfg["n_kv_heads"] * cfg["head_dim"] * 4
+    step_s = ms / K / 1000.0
+    line = {
+        "metric": "batched decode tok/s (Llama-3-8B shape, GQA, 1 GPU)", "value": B * K / (ms / 1000.0),
+        "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": f"llama3-8b-shape q4, {B} streams x {T}-token prompt, then {K} batched decode steps",
+                   "dim": cfg["dim"], "n_layers": L, "n_heads": cfg["n_heads"], "n_kv_heads": cfg["n_kv_heads"],
+                   "ffn_dim": cfg["ffn_dim"], "vocab": cfg["vocab"], "batch": B, "prompt": T,
+                   "kv": "fp32 pages of 64 tokens in a shared pool"},
+        "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": wbytes + kv,
+                     "achieved": (wbytes + kv) / step_s / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": (wbytes + kv) / step_s / 1e9 / peak, "peak_kind": kind},
+        "prefill": {"tokens": B * T, "ms": prefill_ms, "tok_s": B * T / (prefill_ms / 1000.0),
+                    "linear_tflops": 2.0 * B * T * sum(n * k for n, k in gemv_shapes(cfg).values()) * L /
+                    (prefill_ms / 1000.0) / 1e12},
+        "synthesize_s": synth_s, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    model.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "batched":
+        return run_batched(args)
     return run_ours(args)
 
 

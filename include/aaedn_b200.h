@@ -332,6 +332,48 @@ int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n);
  * layer to h_hidden [n_layers][dim] and the logits to h_logits. */
 int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* h_hidden, float* h_logits);
 
+/* ---- batched sequences over a shared, paged KV cache -----------------------
+ * The per-agent view of the reference's cache (src/kvcache.cpp:15-60:
+ * segment_tables per agent) and its branch protocol (docs/sdd.md:206-215:
+ * a child branch continues from its parent's tokens, a pruned branch's
+ * storage is released; src/agent.cpp:107-140 agent_diverge / agent_merge)
+ * on the device. A batched model holds up to max_seqs sequences whose K/V
+ * rows live in one pool of pages of 64 tokens (kv_tokens tokens in all); a
+ * sequence is a page table. aaedn_seq_fork gives the child the parent's
+ * pages (shared, counted, nothing copied); the first append of either into a
+ * page they share copies that page first (copy on write); aaedn_seq_close
+ * releases the pages no other sequence holds. aaedn_model_step_batch runs
+ * one token of each listed sequence through one pass: every matrix product
+ * is the tensor-core GEMM over the batch's rows, attention reads each row's
+ * own pages. Weights go in with aaedn_model_set_layer / set_globals /
+ * synthesize / load_abn as for aaedn_model_create; the single-sequence calls
+ * (forward, generate, decode_steps) are not available on a batched model. No
+ * counterpart in the reference beyond the cited bookkeeping (its
+ * transformer_forward runs one token of one sequence). */
+int aaedn_model_create_batched(const aaedn_model_config* cfg, uint32_t max_seqs, uint64_t kv_tokens,
+                               aaedn_model** out);
+/* A new empty sequence (AAEDN_ENOMEM when max_seqs are open). */
+int aaedn_seq_open(aaedn_model* m, uint32_t* seq);
+/* A new sequence that continues from parent's tokens, sharing its pages. */
+int aaedn_seq_fork(aaedn_model* m, uint32_t parent, uint32_t* child);
+/* Closes the sequence (prune): its pages go back to the pool unless another
+ * sequence still holds them. */
+int aaedn_seq_close(aaedn_model* m, uint32_t seq);
+int aaedn_seq_len(aaedn_model* m, uint32_t seq, uint32_t* len);
+/* Pages in the pool and how many are free. */
+int aaedn_model_kv_pages(aaedn_model* m, uint32_t* total, uint32_t* free_pages);
+/* n tokens appended to one sequence through the prefill path; h_logits
+ * [vocab] (may be NULL) and h_next (may be NULL) receive the last token's
+ * logits and greedy next token. Synchronises. */
+int aaedn_seq_prefill(aaedn_model* m, uint32_t seq, const uint32_t* h_tokens, size_t n, float* h_logits,
+                      uint32_t* h_next);
+/* One token for each of n distinct open sequences h_seqs[i] (h_tokens[i] at
+ * the sequence's next position), all in one batched pass; h_logits
+ * [n][vocab] and h_next [n] (either may be NULL) receive each row's logits
+ * and greedy token. Synchronises. */
+int aaedn_model_step_batch(aaedn_model* m, const uint32_t* h_seqs, const uint32_t* h_tokens, size_t n,
+                           float* h_logits, uint32_t* h_next);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,6 +131,14 @@ def lib():
         "aaedn_model_decode_steps": ([_vp, _sz], _int),
         "aaedn_model_kernels_per_step": ([_vp], _u32),
         "aaedn_model_prefill_rows": ([_vp], _u32),
+        "aaedn_model_create_batched": ([ctypes.POINTER(ModelConfig), _u32, _u64, ctypes.POINTER(_vp)], _int),
+        "aaedn_seq_open": ([_vp, ctypes.POINTER(_u32)], _int),
+        "aaedn_seq_fork": ([_vp, _u32, ctypes.POINTER(_u32)], _int),
+        "aaedn_seq_close": ([_vp, _u32], _int),
+        "aaedn_seq_len": ([_vp, _u32, ctypes.POINTER(_u32)], _int),
+        "aaedn_model_kv_pages": ([_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32)], _int),
+        "aaedn_seq_prefill": ([_vp, _u32, _vp, _sz, _vp, _vp], _int),
+        "aaedn_model_step_batch": ([_vp, _vp, _vp, _sz, _vp, _vp], _int),
         "aaedn_model_logits": ([_vp, _vp], _int),
         "aaedn_model_tokens": ([_vp, _vp, _sz], _int),
         "aaedn_model_forward_debug": ([_vp, _u32, _vp, _vp], _int),
@@ -522,3 +530,59 @@ class Model:
         logits = np.empty(self.cfg["vocab"], np.float32)
         check(lib().aaedn_model_forward_debug(self.h, int(token), _p(hidden), _p(logits)))
         return hidden, logits
+
+
+class BatchedModel(Model):
+    """A model holding up to max_seqs sequences over one pool of KV pages
+    (kv_tokens cached tokens in all): open / fork / close sequences, prefill
+    one, step many at once (aaedn_model_create_batched)."""
+
+    def __init__(self, cfg, max_seqs, kv_tokens):
+        self.cfg = dict(cfg)
+        c = ModelConfig(**{k: self.cfg[k] for k, _ in ModelConfig._fields_})
+        h = _vp()
+        check(lib().aaedn_model_create_batched(ctypes.byref(c), int(max_seqs), int(kv_tokens), ctypes.byref(h)))
+        self.tp = (0, 1)
+        self.h = h
+        self.max_seqs = int(max_seqs)
+
+    def open(self):
+        s = _u32()
+        check(lib().aaedn_seq_open(self.h, ctypes.byref(s)))
+        return int(s.value)
+
+    def fork(self, parent):
+        s = _u32()
+        check(lib().aaedn_seq_fork(self.h, int(parent), ctypes.byref(s)))
+        return int(s.value)
+
+    def close_seq(self, seq):
+        check(lib().aaedn_seq_close(self.h, int(seq)))
+
+    def seq_len(self, seq):
+        n = _u32()
+        check(lib().aaedn_seq_len(self.h, int(seq), ctypes.byref(n)))
+        return int(n.value)
+
+    def kv_pages(self):
+        """(pages in the pool, free pages)."""
+        t, f = _u32(), _u32()
+        check(lib().aaedn_model_kv_pages(self.h, ctypes.byref(t), ctypes.byref(f)))
+        return int(t.value), int(f.value)
+
+    def prefill(self, seq, tokens, want_logits=True):
+        """Appends tokens to one sequence; (last logits or None, greedy next)."""
+        t = np.ascontiguousarray(tokens, np.uint32).reshape(-1)
+        logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        nxt = np.zeros(1, np.uint32)
+        check(lib().aaedn_seq_prefill(self.h, int(seq), _p(t), t.size, _p(logits), _p(nxt)))
+        return logits, int(nxt[0])
+
+    def step(self, seqs, tokens, want_logits=True):
+        """One token for each sequence; (logits [n][vocab] or None, greedy next [n])."""
+        sq = np.ascontiguousarray(seqs, np.uint32).reshape(-1)
+        t = np.ascontiguousarray(tokens, np.uint32).reshape(-1)
+        logits = np.empty((sq.size, self.cfg["vocab"]), np.float32) if want_logits else None
+        nxt = np.zeros(sq.size, np.uint32)
+        check(lib().aaedn_model_step_batch(self.h, _p(sq), _p(t), sq.size, _p(logits), _p(nxt)))
+        return logits, nxt

@@ -262,8 +262,9 @@ __device__ __forceinline__ void tc_epilogue8(const TcGemmParams& p, float* out, 
                 const int m = m_first + j;
                 if (m >= p.M)
                     continue;
-                const int pos = e.pos0 + m;
-                const int page = e.page_table[pos / e.page_size], slot = pos % e.page_size;
+                const int pos = e.row_pos ? e.row_pos[m] : e.pos0 + m;
+                const int* pt = e.row_seq ? e.page_table + (size_t)e.row_seq[m] * e.pt_stride : e.page_table;
+                const int page = pt[pos / e.page_size], slot = pos % e.page_size;
                 float* kv = nullptr;
                 if (!isq)
                     kv = (isk ? e.k_layer : e.v_layer) + (((size_t)page * e.n_kv + h) * e.page_size + slot) * hd;

@@ -38,8 +38,15 @@ struct TcEpi
     size_t ldq;
     float* k_layer; // paged cache [page][n_kv][page_size][head_dim]
     float* v_layer;
-    const int* page_table;
+    const int* page_table; // one sequence's, or (row_seq) the base of [sequences][pt_stride]
     int page_size, n_kv, head_dim, q_rows, kv_rows, pos0;
+    // activation rows of different sequences (batched decode): row m is at
+    // position row_pos[m] of sequence row_seq[m], whose page table starts at
+    // page_table + row_seq[m] * pt_stride; null: row m at pos0 + m of the one
+    // sequence of page_table
+    const int* row_pos;
+    const int* row_seq;
+    int pt_stride;
     const float* rope_cos; // [max_seq][head_dim / 2]
     const float* rope_sin;
     float* act; // [M][ld_act]

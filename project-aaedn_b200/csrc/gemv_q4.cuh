@@ -95,14 +95,17 @@ constexpr uint64_t TP_WAIT_LIMIT_NS = 2000000000ull; // 2 s
 __device__ __forceinline__ bool tp_wait_flags(const TpComm& c, unsigned E, DecodeState* st)
 {
     const uint64_t t0 = globaltimer_ns();
+    volatile uint32_t* err = &st->err;
     for (int w = 0; w < c.size; ++w)
     {
         volatile unsigned* f = c.my_flags + 4 * w;
         while (*f < E)
         {
-            if (globaltimer_ns() - t0 > TP_WAIT_LIMIT_NS)
+            // a wait that already ran out in this step (sticky error): the
+            // later ones give up at once instead of waiting their full limit
+            if (*err != 0u || globaltimer_ns() - t0 > TP_WAIT_LIMIT_NS)
             {
-                st->err = 4u;
+                *err = 4u;
                 return false;
             }
             __nanosleep(32);

@@ -324,7 +324,7 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     else if constexpr (EPI == EPI_QKV_ROPE)
     {
         const uint32_t pos = p.state->pos;
-        if ((p.head_dim >> 1) <= GT_ECACHE_FLOATS / 2 - 1 && pos < (uint32_t)p.max_pos)
+        if ((p.head_dim >> 1) <= GT_ECACHE_FLOATS / 2 && pos < (uint32_t)p.max_pos)
         {
             ec.cos = ecache;
             ec.sin = ecache + GT_ECACHE_FLOATS / 2;
@@ -508,26 +508,58 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
     pdl_wait();
     if (tid == 0)
         trace_mark(p.trace, blockIdx.x, 2);
-    gt_build<PRO>(p, frag, bscale, misc + 32);
-    // epilogue inputs staged in shared memory
+    // epilogue inputs for shared memory: loaded into registers first, so
+    // their L2 round trip overlaps the operand build's
+    constexpr int EPRE = GT_ECACHE_FLOATS / NCT; // per thread
+    float epre[EPRE];
+    int n_epre = 0;
     if constexpr (EPI == EPI_RESIDUAL)
     {
         const int n_groups = p.N >> 4, cta = blockIdx.x, ncta = gridDim.x;
         const int my_groups = cta < n_groups ? (n_groups - 1 - cta) / ncta + 1 : 0;
         if (my_groups * 16 <= GT_ECACHE_FLOATS)
-            for (int i = tid; i < my_groups * 16; i += NCT)
-                ecache[i] = __ldcg(p.y + (size_t)(cta + (i >> 4) * ncta) * 16 + (i & 15));
+        {
+            n_epre = my_groups * 16;
+#pragma unroll
+            for (int j = 0; j < EPRE; ++j)
+            {
+                const int i = tid + j * NCT;
+                epre[j] = i < n_epre ? __ldcg(p.y + (size_t)(cta + (i >> 4) * ncta) * 16 + (i & 15)) : 0.0f;
+            }
+        }
     }
     else if constexpr (EPI == EPI_QKV_ROPE)
     {
         const int half = p.head_dim >> 1;
         const uint32_t pos = p.state->pos;
-        if (half <= GT_ECACHE_FLOATS / 2 - 1 && pos < (uint32_t)p.max_pos)
-            for (int i = tid; i < half; i += NCT)
+        if (half <= GT_ECACHE_FLOATS / 2 && pos < (uint32_t)p.max_pos)
+        {
+            n_epre = 2 * half; // cos at [0, half), sin at [half, 2 half) of the staging order
+#pragma unroll
+            for (int j = 0; j < EPRE; ++j)
             {
-                ecache[i] = __ldg(p.rope_cos + (size_t)pos * half + i);
-                ecache[GT_ECACHE_FLOATS / 2 + i] = __ldg(p.rope_sin + (size_t)pos * half + i);
+                const int i = tid + j * NCT;
+                epre[j] = i < half    ? __ldg(p.rope_cos + (size_t)pos * half + i)
+                          : i < n_epre ? __ldg(p.rope_sin + (size_t)pos * half + (i - half))
+                                       : 0.0f;
             }
+        }
+    }
+    gt_build<PRO>(p, frag, bscale, misc + 32);
+#pragma unroll
+    for (int j = 0; j < EPRE; ++j)
+    {
+        const int i = tid + j * NCT;
+        if (i < n_epre)
+        {
+            if constexpr (EPI == EPI_QKV_ROPE)
+            {
+                const int half = p.head_dim >> 1;
+                ecache[i < half ? i : GT_ECACHE_FLOATS / 2 + (i - half)] = epre[j];
+            }
+            else
+                ecache[i] = epre[j];
+        }
     }
     named_bar_sync(1, NCT); // the operand and the staged inputs are complete
     if (tid == 0)

@@ -374,8 +374,9 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
         if (max_stages < 0)
         {
             const char* e = std::getenv("AAEDN_GEMV_STAGES");
-            // default: as many 18 KB stages as the shared memory holds (<= 12)
-            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : GT_MAX_STAGES;
+            // 6 by default (7B, one B200: 6 stages 684.7 tok/s, 8: 660-680,
+            // 12: 651-675; deeper rings slow the operand loads that follow)
+            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : 6;
         }
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
@@ -491,6 +492,25 @@ struct aaedn_model
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
     unsigned* pf_err = nullptr;
+    // batched sequences (aaedn_model_create_batched): the KV pages are a pool
+    // shared by up to max_seqs sequences, each with its own page table; a
+    // page is held by every sequence that lists it (a fork shares the
+    // parent's pages) and copied before a holder writes into it
+    uint32_t max_seqs = 0; // 0: the single-sequence model
+    uint32_t pt_stride = 0; // pages per sequence: its row of seq_pt
+    int* seq_pt = nullptr;  // device [max_seqs][pt_stride]
+    int *b_pos = nullptr, *b_seq = nullptr; // device [max_seqs]: the batch rows
+    uint32_t *b_tokens = nullptr, *b_next = nullptr;
+    float *b_logits = nullptr, *b_norm = nullptr; // [max_seqs][vocab], [max_seqs][dim]
+    struct Seq
+    {
+        bool open = false;
+        uint32_t len = 0;
+        std::vector<int> pages;
+    };
+    std::vector<Seq> seqs;
+    std::vector<int> page_ref, free_pages, h_pt;
+    int* pinned_b = nullptr; // host staging: tokens, positions, sequences of a batch
 
     template <typename T>
     T* take(size_t bytes)
@@ -565,6 +585,17 @@ static size_t plan_arena(aaedn_model* m, bool carve)
         m->pf_ws_bytes = ws;
         m->pf_ws = m->take<uint8_t>(ws);
         m->pf_err = m->take<unsigned>(64);
+    }
+    if (m->max_seqs)
+    {
+        const size_t S = m->max_seqs;
+        m->seq_pt = m->take<int>(S * m->pt_stride * 4);
+        m->b_pos = m->take<int>(S * 4);
+        m->b_seq = m->take<int>(S * 4);
+        m->b_tokens = m->take<uint32_t>(S * 4);
+        m->b_next = m->take<uint32_t>(S * 4);
+        m->b_logits = m->take<float>(S * V * 4);
+        m->b_norm = m->take<float>(S * D * 4);
     }
     return align_up(m->used, 256);
 }
@@ -997,20 +1028,31 @@ static int put_tokens(aaedn_model* m, const uint32_t* h_tokens, size_t n)
     return AAEDN_OK;
 }
 
-// One chunk of n prompt tokens at positions pos0.. (tokens already in
-// m->prompt): embedding rows, then per layer RMSNorm -> QKV GEMM (RoPE, K/V
-// appended to the cache) -> causal attention -> O GEMM (+residual) ->
-// RMSNorm -> gate/up GEMM (SwiGLU) -> down GEMM (+residual). The last row of
-// the residual stream goes to m->hidden for the lm_head when `last`.
-static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
+// Where the rows of a layer pass sit: row t at position pos0 + t of the one
+// sequence whose page table is page_table (a prefill chunk), or, with
+// row_pos / row_seq, at position row_pos[t] of sequence row_seq[t] whose page
+// table starts at page_table + row_seq[t] * pt_stride (batched decode).
+struct RowMap
+{
+    const int* page_table;
+    uint32_t pos0;
+    const int* row_pos;
+    const int* row_seq;
+    int pt_stride;
+};
+
+// The transformer layers over n residual rows in m->pf_hidden (the token
+// loop of src/transformer.cpp:148-228 for many tokens at once): per layer
+// RMSNorm -> QKV GEMM (RoPE, K/V appended to each row's page) -> causal
+// attention -> O GEMM (+residual) -> RMSNorm -> gate/up GEMM (SwiGLU) ->
+// down GEMM (+residual).
+static int layers_pass(aaedn_model* m, int n, const RowMap& rm)
 {
     cudaStream_t st = m->stream;
     const aaedn_model_config& c = m->cfg;
     const int D = (int)c.dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads, hd = (int)c.head_dim, F = (int)c.ffn_dim;
     const int M_pad = tc_m_pad(n);
     __nv_bfloat16* parts = static_cast<__nv_bfloat16*>(tc_gemm_parts(m->pf_ws));
-    pf_embed_kernel<<<n, 256, 0, st>>>(m->prompt + pos0, n, m->embedding, D, m->pf_hidden);
-    AAEDN_LAUNCH_CHECK("pf_embed_kernel");
     TcGemmArgs base{};
     base.x = nullptr; // parts written into the workspace by the kernel before
     base.M = n;
@@ -1034,20 +1076,23 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
         q.e.ldq = (size_t)H * hd;
         q.e.k_layer = L.k;
         q.e.v_layer = L.v;
-        q.e.page_table = m->page_table;
+        q.e.page_table = rm.page_table;
         q.e.page_size = m->page_size;
         q.e.n_kv = KV;
         q.e.head_dim = hd;
         q.e.q_rows = H * hd;
         q.e.kv_rows = KV * hd;
-        q.e.pos0 = (int)pos0;
+        q.e.pos0 = (int)rm.pos0;
+        q.e.row_pos = rm.row_pos;
+        q.e.row_seq = rm.row_seq;
+        q.e.pt_stride = rm.pt_stride;
         q.e.rope_cos = m->rope_cos;
         q.e.rope_sin = m->rope_sin;
         if ((rc = tc_gemm(q, st)))
             return rc;
         attn_prefill_kernel<<<dim3(H, (n + PF_ATTN_WARPS - 1) / PF_ATTN_WARPS), PF_ATTN_WARPS * 32, 0, st>>>(
-            m->pf_q, (size_t)H * hd, L.k, L.v, m->page_table, m->page_size, H, KV, hd, (int)pos0, n,
-            1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo);
+            m->pf_q, (size_t)H * hd, L.k, L.v, rm.page_table, m->page_size, H, KV, hd, (int)rm.pos0, n,
+            1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo, rm.row_pos, rm.row_seq, rm.pt_stride);
         AAEDN_LAUNCH_CHECK("attn_prefill_kernel");
         if ((rc = tc_split(m->pf_attn, m->kpo, n, (int)m->kpo, m->pf_ws, st)))
             return rc;
@@ -1084,10 +1129,17 @@ static int prefill_chunk(aaedn_model* m, uint32_t pos0, int n, bool last)
         if ((rc = tc_gemm(dn, st)))
             return rc;
     }
-    if (last)
-        AAEDN_CUDA_TRY(cudaMemcpyAsync(m->hidden, m->pf_hidden + (size_t)(n - 1) * D, (size_t)D * 4,
-                                       cudaMemcpyDeviceToDevice, st));
     return AAEDN_OK;
+}
+
+// One chunk of n prompt tokens (d_tokens, device) of one sequence at
+// positions pos0..: their residual rows (src/transformer.cpp:144-146), then
+// the layers.
+static int prefill_chunk(aaedn_model* m, const uint32_t* d_tokens, int n, const RowMap& rm)
+{
+    pf_embed_kernel<<<n, 256, 0, m->stream>>>(d_tokens, n, m->embedding, (int)m->cfg.dim, m->pf_hidden);
+    AAEDN_LAUNCH_CHECK("pf_embed_kernel");
+    return layers_pass(m, n, rm);
 }
 
 // n prompt tokens (already in m->prompt at h_pos) through prefill chunks,
@@ -1097,13 +1149,17 @@ static int prefill(aaedn_model* m, size_t n)
 {
     const uint32_t p0 = m->h_pos;
     int rc = AAEDN_OK;
+    size_t last = 0;
     for (size_t c0 = 0; c0 < n && !rc; c0 += (size_t)m->pf_rows)
     {
         const int nc = (int)std::min<size_t>((size_t)m->pf_rows, n - c0);
-        rc = prefill_chunk(m, p0 + (uint32_t)c0, nc, c0 + (size_t)nc == n);
+        rc = prefill_chunk(m, m->prompt + p0 + c0, nc, RowMap{m->page_table, p0 + (uint32_t)c0, nullptr, nullptr, 0});
+        last = (size_t)nc - 1;
     }
     if (rc)
         return rc;
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->hidden, m->pf_hidden + last * m->cfg.dim, (size_t)m->cfg.dim * 4,
+                                   cudaMemcpyDeviceToDevice, m->stream));
     // the lm_head of the last prompt token as the decode step does it
     if ((rc = write_state(m, p0 + (uint32_t)n - 1, p0 + (uint32_t)n)))
         return rc;
@@ -1158,7 +1214,8 @@ extern "C" int aaedn_tp_plan_get(const aaedn_model_config* cfg, uint32_t tp_rank
     return AAEDN_OK;
 }
 
-static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size, aaedn_model** out)
+static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t tp_size, aaedn_model** out,
+                       uint32_t max_seqs = 0, uint64_t kv_tokens = 0)
 {
     if (!cfg || !out)
         return set_error(AAEDN_EINVAL, "aaedn_model_create: null argument");
@@ -1209,6 +1266,14 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
     }
     m->page_size = 64;
     m->n_pages = (int)((c.max_seq + m->page_size - 1) / m->page_size);
+    if (max_seqs)
+    {
+        // batched: a pool of kv_tokens / page_size pages; a sequence's page
+        // table holds up to max_seq tokens
+        m->max_seqs = max_seqs;
+        m->pt_stride = (uint32_t)m->n_pages;
+        m->n_pages = (int)((kv_tokens + m->page_size - 1) / m->page_size);
+    }
     // about two attention CTAs per SM (a CTA walks its token range in
     // batches, so any split count covers any context length)
     int per_sm = 2;
@@ -1239,6 +1304,17 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         const char* pe = std::getenv("AAEDN_PREFILL_ROWS");
         const int rows = pe ? std::atoi(pe) : 256;
         m->pf_rows = ok && rows > 1 ? (int)std::min<uint32_t>((uint32_t)rows, c.max_seq) : 0;
+        if (max_seqs)
+        {
+            if (!ok)
+            {
+                delete m;
+                return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_create_batched: the model's matrices need the "
+                                                     "tile-major layout (K %% 128, N %% 16) and head_dim %% 32");
+            }
+            // a batch of max_seqs rows goes through the same buffers
+            m->pf_rows = std::max<int>(std::max(m->pf_rows, 2), (int)max_seqs);
+        }
     }
     const size_t bytes = plan_arena(m, false);
     cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&m->arena), bytes);
@@ -1259,6 +1335,17 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         return fail(set_error(AAEDN_ECUDA, "stream creation failed"));
     if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), ((size_t)c.max_seq + 16) * 4) != cudaSuccess)
         return fail(set_error(AAEDN_ENOMEM, "pinned staging allocation failed"));
+    if (m->max_seqs)
+    {
+        if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned_b), (size_t)m->max_seqs * 3 * 4) != cudaSuccess)
+            return fail(set_error(AAEDN_ENOMEM, "pinned staging allocation failed"));
+        m->seqs.assign(m->max_seqs, aaedn_model::Seq{});
+        m->page_ref.assign((size_t)m->n_pages, 0);
+        m->free_pages.resize((size_t)m->n_pages);
+        for (int i = 0; i < m->n_pages; ++i)
+            m->free_pages[(size_t)i] = m->n_pages - 1 - i; // handed out from the back: page 0 first
+        m->h_pt.assign((size_t)m->max_seqs * m->pt_stride, 0);
+    }
     if (cudaMemset(m->arena, 0, bytes) != cudaSuccess)
         return fail(set_error(AAEDN_ECUDA, "arena clear failed"));
     // RoPE tables (D3) and the identity page table of the single sequence
@@ -1406,6 +1493,8 @@ extern "C" int aaedn_model_destroy(aaedn_model* m)
         cudaFree(m->arena);
     if (m->pinned)
         cudaFreeHost(m->pinned);
+    if (m->pinned_b)
+        cudaFreeHost(m->pinned_b);
     if (m->stream)
         cudaStreamDestroy(m->stream);
     delete m;
@@ -1629,6 +1718,8 @@ extern "C" int aaedn_model_reset(aaedn_model* m)
 extern "C" int aaedn_model_forward(aaedn_model* m, const uint32_t* h_tokens, size_t n, float* h_logits)
 {
     MODEL_OK(m);
+    if (m->max_seqs)
+        return set_error(AAEDN_EUNSUPPORTED, "a batched model steps its sequences with aaedn_model_step_batch");
     const aaedn_model_config& c = m->cfg;
     const uint32_t V = m->full.vocab;
     if (n == 0 || !h_tokens) // src/transformer.cpp:130-135: zero logits
@@ -1664,6 +1755,8 @@ extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, si
                                     uint32_t* h_out)
 {
     MODEL_OK(m);
+    if (m->max_seqs)
+        return set_error(AAEDN_EUNSUPPORTED, "a batched model steps its sequences with aaedn_model_step_batch");
     const aaedn_model_config& c = m->cfg;
     if (!h_prompt || n_prompt == 0 || (n_new && !h_out))
         return set_error(AAEDN_EINVAL, "aaedn_model_generate: empty prompt or null output");
@@ -1704,6 +1797,8 @@ extern "C" int aaedn_model_generate(aaedn_model* m, const uint32_t* h_prompt, si
 extern "C" int aaedn_model_decode_steps(aaedn_model* m, size_t n_steps)
 {
     MODEL_OK(m);
+    if (m->max_seqs)
+        return set_error(AAEDN_EUNSUPPORTED, "a batched model steps its sequences with aaedn_model_step_batch");
     if (m->h_pos == 0)
         return set_error(AAEDN_ESTATE, "aaedn_model_decode_steps: no token in the sequence yet");
     if ((size_t)m->h_pos + n_steps > m->cfg.max_seq)
@@ -1740,6 +1835,8 @@ extern "C" int aaedn_model_tokens(aaedn_model* m, uint32_t* h_out, size_t n)
 extern "C" int aaedn_model_forward_debug(aaedn_model* m, uint32_t token, float* h_hidden, float* h_logits)
 {
     MODEL_OK(m);
+    if (m->max_seqs)
+        return set_error(AAEDN_EUNSUPPORTED, "a batched model steps its sequences with aaedn_model_step_batch");
     if (m->tp_size > 1) // the residual of a layer is complete only inside the next layer's kernels
         return set_error(AAEDN_EUNSUPPORTED, "aaedn_model_forward_debug: not for tensor-parallel models");
     const aaedn_model_config& c = m->cfg;
@@ -1980,4 +2077,279 @@ extern "C" int aaedn_model_next_token(aaedn_model* m, uint32_t* h_token)
     AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
     *h_token = *w;
     return AAEDN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Batched sequences over a shared, paged KV cache: the per-agent view of
+// src/kvcache.cpp:15-60 (segment_tables[6], one per agent) and the branch
+// protocol of docs/sdd.md:206-215 (diverge: the child continues from the
+// parent's tokens; prune: the branch's storage is released) on the device.
+// A sequence is a page table; fork copies the table (the pages are shared,
+// counted), an append into a shared page copies that page first (copy on
+// write), close releases the pages no other sequence holds.
+// ---------------------------------------------------------------------------
+
+#define BATCHED_OK(m)                                                                                         \
+    do                                                                                                        \
+    {                                                                                                         \
+        MODEL_OK(m);                                                                                          \
+        if (!(m)->max_seqs)                                                                                   \
+            return set_error(AAEDN_EUNSUPPORTED, "not a batched model (aaedn_model_create_batched)");          \
+    } while (0)
+
+static int seq_ok(aaedn_model* m, uint32_t seq)
+{
+    if (seq >= m->max_seqs || !m->seqs[seq].open)
+        return set_error(AAEDN_EINVAL, "sequence %u is not open", seq);
+    return AAEDN_OK;
+}
+
+// Uploads sequence seq's row of the device page table.
+static int upload_pt(aaedn_model* m, uint32_t seq)
+{
+    int* row = m->h_pt.data() + (size_t)seq * m->pt_stride;
+    const auto& pg = m->seqs[seq].pages;
+    std::fill(row, row + m->pt_stride, 0);
+    std::copy(pg.begin(), pg.end(), row);
+    // pageable source: the copy has read it when the call returns
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->seq_pt + (size_t)seq * m->pt_stride, row, (size_t)m->pt_stride * 4,
+                                   cudaMemcpyHostToDevice, m->stream));
+    return AAEDN_OK;
+}
+
+static void release_pages(aaedn_model* m, std::vector<int>& pages)
+{
+    for (int pg : pages)
+        if (--m->page_ref[(size_t)pg] == 0)
+            m->free_pages.push_back(pg);
+    pages.clear();
+}
+
+// Pages for positions [len, len + n) of sequence seq: new pages from the
+// pool, and a copy of the page holding position len when another sequence
+// shares it (its rows below len stay valid in both).
+static int reserve(aaedn_model* m, uint32_t seq, uint32_t n)
+{
+    auto& sq = m->seqs[seq];
+    const uint32_t P = (uint32_t)m->page_size;
+    if ((size_t)sq.len + n > m->cfg.max_seq)
+        return set_error(AAEDN_ESTATE, "sequence %u full: %u + %u tokens > max_seq %u", seq, sq.len, n, m->cfg.max_seq);
+    bool changed = false;
+    if (n && sq.len % P != 0)
+    {
+        const size_t pi = sq.len / P;
+        const int old = sq.pages[pi];
+        if (m->page_ref[(size_t)old] > 1)
+        {
+            if (m->free_pages.empty())
+                return set_error(AAEDN_ENOMEM, "KV page pool exhausted (%d pages)", m->n_pages);
+            const int fresh = m->free_pages.back();
+            m->free_pages.pop_back();
+            const size_t pe = (size_t)m->cfg.n_kv_heads * P * m->cfg.head_dim; // floats per page per layer
+            for (const DevLayer& L : m->layers)
+            {
+                AAEDN_CUDA_TRY(cudaMemcpyAsync(L.k + (size_t)fresh * pe, L.k + (size_t)old * pe, pe * 4,
+                                               cudaMemcpyDeviceToDevice, m->stream));
+                AAEDN_CUDA_TRY(cudaMemcpyAsync(L.v + (size_t)fresh * pe, L.v + (size_t)old * pe, pe * 4,
+                                               cudaMemcpyDeviceToDevice, m->stream));
+            }
+            --m->page_ref[(size_t)old];
+            m->page_ref[(size_t)fresh] = 1;
+            sq.pages[pi] = fresh;
+            changed = true;
+        }
+    }
+    const size_t need = ((size_t)sq.len + n + P - 1) / P;
+    while (sq.pages.size() < need)
+    {
+        if (m->free_pages.empty())
+            return set_error(AAEDN_ENOMEM, "KV page pool exhausted (%d pages)", m->n_pages);
+        const int pg = m->free_pages.back();
+        m->free_pages.pop_back();
+        m->page_ref[(size_t)pg] = 1;
+        sq.pages.push_back(pg);
+        changed = true;
+    }
+    return changed ? upload_pt(m, seq) : AAEDN_OK;
+}
+
+// The final RMSNorm, lm_head and greedy token of n rows of m->pf_hidden
+// starting at row0, into b_logits / b_next rows [0, n).
+static int lm_rows(aaedn_model* m, int row0, int n)
+{
+    cudaStream_t st = m->stream;
+    const int D = (int)m->cfg.dim, V = (int)m->cfg.vocab;
+    pf_rmsnorm_rows_kernel<<<n, 256, 0, st>>>(m->pf_hidden + (size_t)row0 * D, D, m->final_norm, m->cfg.eps,
+                                               m->b_norm);
+    AAEDN_LAUNCH_CHECK("pf_rmsnorm_rows_kernel");
+    lm_rows_kernel<<<dim3((V + LR_TV - 1) / LR_TV, (n + LR_TM - 1) / LR_TM), 256, 0, st>>>(m->b_norm, n, D, m->lm_head,
+                                                                                         V, m->b_logits, (size_t)V);
+    AAEDN_LAUNCH_CHECK("lm_rows_kernel");
+    argmax_rows_kernel<<<n, 256, 0, st>>>(m->b_logits, (size_t)V, V, m->b_next);
+    AAEDN_LAUNCH_CHECK("argmax_rows_kernel");
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_create_batched(const aaedn_model_config* cfg, uint32_t max_seqs, uint64_t kv_tokens,
+                                          aaedn_model** out)
+{
+    if (!cfg || !out)
+        return set_error(AAEDN_EINVAL, "aaedn_model_create_batched: null argument");
+    if (max_seqs == 0 || max_seqs > 256 || kv_tokens == 0 || kv_tokens > (1ull << 26))
+        return set_error(AAEDN_EINVAL, "aaedn_model_create_batched: 1..256 sequences and 1..2^26 cached tokens");
+    return create_impl(cfg, 0, 1, out, max_seqs, kv_tokens);
+}
+
+extern "C" int aaedn_seq_open(aaedn_model* m, uint32_t* seq)
+{
+    BATCHED_OK(m);
+    if (!seq)
+        return set_error(AAEDN_EINVAL, "aaedn_seq_open: null output");
+    for (uint32_t i = 0; i < m->max_seqs; ++i)
+        if (!m->seqs[i].open)
+        {
+            m->seqs[i] = aaedn_model::Seq{};
+            m->seqs[i].open = true;
+            *seq = i;
+            return AAEDN_OK;
+        }
+    return set_error(AAEDN_ENOMEM, "all %u sequences are open", m->max_seqs);
+}
+
+extern "C" int aaedn_seq_fork(aaedn_model* m, uint32_t parent, uint32_t* child)
+{
+    BATCHED_OK(m);
+    if (int rc = seq_ok(m, parent))
+        return rc;
+    uint32_t c = 0;
+    if (int rc = aaedn_seq_open(m, &c))
+        return rc;
+    m->seqs[c].len = m->seqs[parent].len;
+    m->seqs[c].pages = m->seqs[parent].pages;
+    for (int pg : m->seqs[c].pages)
+        ++m->page_ref[(size_t)pg];
+    if (int rc = upload_pt(m, c))
+        return rc;
+    *child = c;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_seq_close(aaedn_model* m, uint32_t seq)
+{
+    BATCHED_OK(m);
+    if (int rc = seq_ok(m, seq))
+        return rc;
+    // stream order: kernels still reading its pages were enqueued before
+    // any later write that reuses them
+    release_pages(m, m->seqs[seq].pages);
+    m->seqs[seq].open = false;
+    m->seqs[seq].len = 0;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_seq_len(aaedn_model* m, uint32_t seq, uint32_t* len)
+{
+    BATCHED_OK(m);
+    if (int rc = seq_ok(m, seq))
+        return rc;
+    if (!len)
+        return set_error(AAEDN_EINVAL, "aaedn_seq_len: null output");
+    *len = m->seqs[seq].len;
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_model_kv_pages(aaedn_model* m, uint32_t* total, uint32_t* free_pages)
+{
+    BATCHED_OK(m);
+    if (total)
+        *total = (uint32_t)m->n_pages;
+    if (free_pages)
+        *free_pages = (uint32_t)m->free_pages.size();
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_seq_prefill(aaedn_model* m, uint32_t seq, const uint32_t* h_tokens, size_t n, float* h_logits,
+                                 uint32_t* h_next)
+{
+    BATCHED_OK(m);
+    if (int rc = seq_ok(m, seq))
+        return rc;
+    if (!h_tokens || n == 0)
+        return set_error(AAEDN_EINVAL, "aaedn_seq_prefill: no tokens");
+    for (size_t i = 0; i < n; ++i)
+        if (h_tokens[i] >= m->cfg.vocab)
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_tokens[i], m->cfg.vocab);
+    if (int rc = reserve(m, seq, (uint32_t)n))
+        return rc;
+    // tokens into the model's prompt buffer (the staging is reused only
+    // after the stream has drained)
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    std::memcpy(m->pinned, h_tokens, n * 4);
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->prompt, m->pinned, n * 4, cudaMemcpyHostToDevice, m->stream));
+    const uint32_t p0 = m->seqs[seq].len;
+    const int* pt = m->seq_pt + (size_t)seq * m->pt_stride;
+    size_t last = 0;
+    for (size_t c0 = 0; c0 < n; c0 += (size_t)m->pf_rows)
+    {
+        const int nc = (int)std::min<size_t>((size_t)m->pf_rows, n - c0);
+        if (int rc = prefill_chunk(m, m->prompt + c0, nc, RowMap{pt, p0 + (uint32_t)c0, nullptr, nullptr, 0}))
+            return rc;
+        last = (size_t)nc - 1;
+    }
+    if (int rc = lm_rows(m, (int)last, 1))
+        return rc;
+    if (h_logits)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->b_logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                       m->stream));
+    if (h_next)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_next, m->b_next, 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->seqs[seq].len += (uint32_t)n;
+    return device_status(m);
+}
+
+extern "C" int aaedn_model_step_batch(aaedn_model* m, const uint32_t* h_seqs, const uint32_t* h_tokens, size_t n,
+                                      float* h_logits, uint32_t* h_next)
+{
+    BATCHED_OK(m);
+    if (!h_seqs || !h_tokens || n == 0 || n > m->max_seqs)
+        return set_error(AAEDN_EINVAL, "aaedn_model_step_batch: 1..%u sequences", m->max_seqs);
+    std::vector<uint8_t> seen(m->max_seqs, 0);
+    for (size_t i = 0; i < n; ++i)
+    {
+        if (int rc = seq_ok(m, h_seqs[i]))
+            return rc;
+        if (seen[h_seqs[i]]++)
+            return set_error(AAEDN_EINVAL, "sequence %u twice in one batch", h_seqs[i]);
+        if (h_tokens[i] >= m->cfg.vocab)
+            return set_error(AAEDN_EINVAL, "token id %u >= vocab %u", h_tokens[i], m->cfg.vocab);
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (int rc = reserve(m, h_seqs[i], 1))
+            return rc;
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream)); // the staging may still feed an earlier copy
+    int* stg = m->pinned_b;
+    for (size_t i = 0; i < n; ++i)
+    {
+        stg[i] = (int)h_tokens[i];
+        stg[m->max_seqs + i] = (int)m->seqs[h_seqs[i]].len;
+        stg[2 * m->max_seqs + i] = (int)h_seqs[i];
+    }
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->b_tokens, stg, n * 4, cudaMemcpyHostToDevice, m->stream));
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->b_pos, stg + m->max_seqs, n * 4, cudaMemcpyHostToDevice, m->stream));
+    AAEDN_CUDA_TRY(cudaMemcpyAsync(m->b_seq, stg + 2 * m->max_seqs, n * 4, cudaMemcpyHostToDevice, m->stream));
+    int rc = prefill_chunk(m, m->b_tokens, (int)n, RowMap{m->seq_pt, 0u, m->b_pos, m->b_seq, (int)m->pt_stride});
+    if (!rc)
+        rc = lm_rows(m, 0, (int)n);
+    if (rc)
+        return rc;
+    if (h_logits)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_logits, m->b_logits, n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                       m->stream));
+    if (h_next)
+        AAEDN_CUDA_TRY(cudaMemcpyAsync(h_next, m->b_next, n * 4, cudaMemcpyDeviceToHost, m->stream));
+    AAEDN_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    for (size_t i = 0; i < n; ++i)
+        ++m->seqs[h_seqs[i]].len;
+    return device_status(m);
 }

@@ -11,6 +11,8 @@
 //     chunk's K/V rows.
 #pragma once
 
+#include <climits>
+
 #include "common.cuh"
 #include "gemv_q4.cuh" // block_sum
 
@@ -66,16 +68,20 @@ __global__ void __launch_bounds__(256) pf_rmsnorm_split_kernel(const float* __re
 
 constexpr int PF_ATTN_WARPS = 4;
 
-// Causal attention of chunk tokens t < n (positions pos0 + t) for query head
-// blockIdx.x: one warp per token. Keys are taken 32 at a time, lane j scoring
-// key s0 + j against q (held in shared memory); the batch's softmax weights
-// then scale the V rows with lanes over the head dims; the softmax is carried
-// online across batches (running max and sum). fp32, expf (D4).
-// out[t][h * hd + d]; head_dim a multiple of 32, <= 256.
+// Causal attention of rows t < n for query head blockIdx.x: one warp per
+// row. Row t is the token at position pos0 + t of the sequence whose pages
+// page_table lists (a prefill chunk), or (row_pos, row_seq: batched decode)
+// the token at position row_pos[t] of sequence row_seq[t], whose page table
+// starts at page_table + row_seq[t] * pt_stride. Keys are taken 32 at a time,
+// lane j scoring key s0 + j against q (held in shared memory); the batch's
+// softmax weights then scale the V rows with lanes over the head dims; the
+// softmax is carried online across batches (running max and sum). fp32,
+// expf (D4). out[t][h * hd + d]; head_dim a multiple of 32, <= 256.
 __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
     const float* __restrict__ q, size_t ldq, const float* __restrict__ k_layer, const float* __restrict__ v_layer,
-    const int* __restrict__ page_table, int page_size, int n_heads, int n_kv, int hd, int pos0, int n, float scale,
-    float* __restrict__ out, size_t ldo)
+    const int* __restrict__ page_table_base, int page_size, int n_heads, int n_kv, int hd, int pos0, int n,
+    float scale, float* __restrict__ out, size_t ldo, const int* __restrict__ row_pos = nullptr,
+    const int* __restrict__ row_seq = nullptr, int pt_stride = 0)
 {
     __shared__ __align__(16) float qs[PF_ATTN_WARPS][256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -83,7 +89,8 @@ __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
     if (t >= n)
         return;
     const int kvh = h / (n_heads / n_kv);
-    const int pos = pos0 + t, nkeys = pos + 1;
+    const int pos = row_pos ? row_pos[t] : pos0 + t, nkeys = pos + 1;
+    const int* page_table = row_seq ? page_table_base + (size_t)row_seq[t] * pt_stride : page_table_base;
     const float* qh = q + (size_t)t * ldq + (size_t)h * hd;
     for (int d = lane; d < hd; d += 32)
         qs[warp][d] = qh[d];
@@ -140,6 +147,130 @@ __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
     for (int i = 0; i < 8; ++i)
         if (i < dpl)
             o[lane + 32 * i] = acc[i] * inv;
+}
+
+// ---------------------------------------------------------------------------
+// lm_head over several rows (batched decode): the final RMSNorm of each row
+// (src/transformer.cpp:230), the fp32 product with the [vocab][dim] lm_head
+// (:232-238) and each row's greedy token (argmax, ties to the lowest id).
+// ---------------------------------------------------------------------------
+
+// out[m][k] = x[m][k] * rms(x[m]) * g[k]; one CTA per row.
+__global__ void __launch_bounds__(256) pf_rmsnorm_rows_kernel(const float* __restrict__ x, int D,
+                                                              const float* __restrict__ gain, float eps,
+                                                              float* __restrict__ out)
+{
+    __shared__ float scratch[64];
+    const float* xr = x + (size_t)blockIdx.x * D;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < D; k += blockDim.x)
+        ss = fmaf(xr[k], xr[k], ss);
+    ss = block_sum(ss, scratch);
+    const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    for (int k = threadIdx.x; k < D; k += blockDim.x)
+        out[(size_t)blockIdx.x * D + k] = __fmul_rn(__fmul_rn(xr[k], rms), gain[k]);
+}
+
+constexpr int LR_TV = 64, LR_TM = 64, LR_TK = 32;
+
+// out[m * ldo + v] = sum_k x[m][k] * w[v][k] for m < M, v < V; a CTA of 256
+// threads owns 64 vocabulary rows x 64 activation rows (4 x 4 per thread),
+// K in slices of 32 staged in shared memory, k ascending in every sum.
+__global__ void __launch_bounds__(256) lm_rows_kernel(const float* __restrict__ x, int M, int D,
+                                                      const float* __restrict__ w, int V, float* __restrict__ out,
+                                                      size_t ldo)
+{
+    __shared__ float ws[LR_TK][LR_TV + 4];
+    __shared__ float xs[LR_TK][LR_TM + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int v0 = blockIdx.x * LR_TV, m0 = blockIdx.y * LR_TM;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < D; k0 += LR_TK)
+    {
+        // 64 x 32 of each operand: 8 floats per thread, k fastest in memory
+        for (int i = tid; i < LR_TV * LR_TK; i += 256)
+        {
+            const int r = i / LR_TK, k = i % LR_TK;
+            const int v = v0 + r, m = m0 + r;
+            ws[k][r] = (v < V && k0 + k < D) ? w[(size_t)v * D + k0 + k] : 0.0f;
+            xs[k][r] = (m < M && k0 + k < D) ? x[(size_t)m * D + k0 + k] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < LR_TK; ++k)
+        {
+            const float4 a = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+    {
+        const int m = m0 + ty * 4 + j;
+        if (m >= M)
+            continue;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            const int v = v0 + tx * 4 + i;
+            if (v < V)
+                out[(size_t)m * ldo + v] = acc[i][j];
+        }
+    }
+}
+
+// next[m] = argmax_v logits[m][v] (ties to the lowest id); one CTA per row.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ logits, size_t ld, int V,
+                                                          uint32_t* __restrict__ next)
+{
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const float* l = logits + (size_t)blockIdx.x * ld;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int v = threadIdx.x; v < V; v += blockDim.x)
+        if (l[v] > bv)
+        {
+            bv = l[v];
+            bi = v;
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi))
+        {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0)
+    {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        bv = sv[0];
+        bi = si[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi))
+            {
+                bv = sv[w];
+                bi = si[w];
+            }
+        next[blockIdx.x] = bi == INT_MAX ? 0u : (uint32_t)bi;
+    }
 }
 
 } // namespace aaedn_dev

@@ -86,3 +86,52 @@ def test_tp_greedy_identical_to_oracle(oracle, cfg, seed, n_prompt, n_new, size)
     want, wl = om.generate(ab.synth_tokens(seed, 0, cfg["vocab"], n_prompt), n_new)
     np.testing.assert_array_equal(got, want)
     assert float(np.abs(logits - wl).max() / np.abs(wl).max()) < 1e-4
+
+
+def _rank_timeout(rank, size, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=size, timeout=timedelta(seconds=120))
+    try:
+        cfg = GQA
+        m = ab.Model(cfg, tp=(rank, size))
+        m.synthesize(7)
+        m.connect_tp()
+        m.generate(ab.synth_tokens(7, 0, cfg["vocab"], 4), 3)  # both ranks step together
+        dist.barrier()
+        rc = ab.OK
+        if rank == 0:
+            # rank 1 launches nothing: rank 0's waits for its partials run out
+            # (bounded) and the step reports it; the GPU stays usable
+            m.decode_steps(1)
+            try:
+                m.status()
+            except ab.AaednError as e:
+                rc = e.rc
+        dist.barrier()  # rank 1 stays mapped until rank 0's step is over
+        m.close()
+        q.put((rank, rc))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_peer_that_does_not_step_times_out():
+    """A rank whose peer never launches its step gets AAEDN_ETIMEOUT from the
+    bounded flag waits (about 2 s), and both ranks shut down cleanly."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_timeout, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for pr in procs:
+        pr.join(timeout=120)
+        assert pr.exitcode == 0
+    assert res[0] == ab.ETIMEOUT and res[1] == ab.OK
