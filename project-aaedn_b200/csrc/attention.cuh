@@ -15,7 +15,9 @@
 // deterministic. All arithmetic is fp32 with expf.
 //
 // In the model the K/V rows of earlier positions do not depend on the
-// previous kernel: a CTA asks L2 for its first rows before waiting for it.
+// previous kernel: a CTA requests its first rows before waiting for it. The
+// decode step's default is attn_decode_kernel (clusters, merge in
+// distributed shared memory).
 #pragma once
 
 #include "gemv_q4.cuh"
@@ -28,7 +30,6 @@ constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_MAX_SEG = 64;
 constexpr int ATTN_MAX_HD = 256;
 constexpr int ATTN_MAX_G = 8; // query heads per kv head (template values 1, 2, 4, 8)
-constexpr int ATTN_PREFETCH_TOKENS = 64; // rows per CTA requested from L2 ahead
 
 struct AttnParams
 {
@@ -51,6 +52,14 @@ struct AttnParams
     uint32_t seg_start[ATTN_MAX_SEG];
     uint32_t seg_off[ATTN_MAX_SEG + 1]; // prefix sums of the lengths
     unsigned long long* trace; // per-CTA timeline of a traced step, or null
+    // attn_decode_kernel over a batch of rows (grid.z = rows; null row_pos:
+    // the one sequence at state->pos): row z is the token at position
+    // row_pos[z] of sequence row_seq[z], whose page table starts at
+    // page_table + row_seq[z] * pt_stride; q + z * ldq, out + z * ldo
+    const int* row_pos;
+    const int* row_seq;
+    int pt_stride;
+    size_t ldq, ldo;
 };
 
 // Shared memory: per-warp running max and sum [8][G] each, per-warp V sums
@@ -74,7 +83,8 @@ __device__ __forceinline__ size_t attn_row(const AttnParams& p, int t, int kvh)
     }
     else
     {
-        const int page = p.page_table[t / p.page_size];
+        // a null page table is the identity (one sequence in pages 0, 1, ...)
+        const int page = p.page_table ? p.page_table[t / p.page_size] : t / p.page_size;
         return (((size_t)page * p.n_kv + kvh) * p.page_size + (t % p.page_size)) * hd;
     }
 }
@@ -106,11 +116,7 @@ __device__ __forceinline__ int attn_len(const AttnParams& p)
 // shared memory. PDLW: the item waits for the previous kernel itself, after
 // it has requested its first batch of K/V rows (decode mode: every row but
 // the current position's was written by earlier steps).
-// CL: the S splits of a kv head are one thread-block cluster (split = the
-// CTA's rank in it); each CTA leaves its partial result in its own shared
-// memory (after the attn_smem_bytes block) and rank 0 merges the S of them
-// through distributed shared memory. No global partials, counters or atomics.
-template <int MODE, int G, int HDM, bool PDLW = false, bool CL = false>
+template <int MODE, int G, int HDM, bool PDLW = false>
 __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int split, int tid, float* asmem,
                                           unsigned* s_last, int bar_id)
 {
@@ -119,7 +125,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
     const int S = p.S;
     const int hd = p.head_dim, hd4 = hd >> 2;
     const int lane = tid & 31, warp = tid >> 5;
-    const int L = attn_len<MODE>(p);
+    int L = attn_len<MODE>(p);
     const int ps = p.pstride ? p.pstride : hd + 2;
     int t0, t1;
     attn_range(L, split, S, t0, t1);
@@ -164,22 +170,35 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
         pdl_wait();
         if (tid == 0)
             trace_mark(p.trace, split * p.n_kv + kvh, 1);
+        const int Lw = attn_len<MODE>(p);
+        if (Lw != L)
+        {
+            // the position was read before the step before had finished
+            // advancing it: take the range again with every row current
+            L = Lw;
+            attn_range(L, split, S, t0, t1);
+            if (t0 + warp < t1)
+                load_batch(t0 + warp, -1);
+        }
+        else
+        {
 #pragma unroll
-        for (int j = 0; j < TB; ++j)
-            if (t0 + warp + ATTN_WARPS * j == tcur && tcur < t1)
-            {
-                const size_t ro = attn_row<MODE>(p, tcur, kvh);
-#pragma unroll
-                for (int c = 0; c < NCH; ++c)
+            for (int j = 0; j < TB; ++j)
+                if (t0 + warp + ATTN_WARPS * j == tcur && tcur < t1)
                 {
-                    const int ch = lane + 32 * c;
-                    if (ch < hd4)
+                    const size_t ro = attn_row<MODE>(p, tcur, kvh);
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c)
                     {
-                        kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
-                        vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                        const int ch = lane + 32 * c;
+                        if (ch < hd4)
+                        {
+                            kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                            vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                        }
                     }
                 }
-            }
+        }
     }
     // lane slices of q (scaled once: s = (q*scale).k would round differently,
     // so the scale is applied to the dot as src/attention.cpp:42 does)
@@ -307,63 +326,13 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
             den = fmaf(wl[w * G + gi], f, den);
         }
         const int h = kvh * G + gi;
-        float* pp = CL ? wacc + (size_t)ATTN_WARPS * G * hd + (size_t)gi * (hd + 2)
-                       : p.part + ((size_t)h * S + split) * ps;
+        float* pp = p.part + ((size_t)h * S + split) * ps;
         pp[d] = o;
         if (d == 0)
         {
             pp[hd] = M;
             pp[hd + 1] = den;
         }
-    }
-
-    if constexpr (CL)
-    {
-        // merge the cluster's S partials in split order (the same arithmetic
-        // as the global merge below); the second barrier keeps every CTA's
-        // shared memory alive until rank 0 has read it
-        cluster_sync_all();
-        if (split == 0)
-            for (int i = tid; i < G * hd; i += ATTN_THREADS)
-            {
-                const int gi = i / hd, d = i - gi * hd;
-                const uint32_t cb = smem_addr(wacc + (size_t)ATTN_WARPS * G * hd + (size_t)gi * (hd + 2));
-                constexpr int SU = 8;
-                float M = -INFINITY;
-                for (int sb = 0; sb < S; sb += SU)
-                {
-                    float mv[SU];
-#pragma unroll
-                    for (int u = 0; u < SU; ++u)
-                        mv[u] = sb + u < S ? ld_dsmem_f32(cb + hd * 4, sb + u) : -INFINITY;
-#pragma unroll
-                    for (int u = 0; u < SU; ++u)
-                        M = fmaxf(M, mv[u]);
-                }
-                float num = 0.0f, den = 0.0f;
-                for (int sb = 0; sb < S; sb += SU)
-                {
-                    float mv[SU], vv[SU], lv[SU];
-#pragma unroll
-                    for (int u = 0; u < SU; ++u)
-                    {
-                        const bool live = sb + u < S;
-                        mv[u] = live ? ld_dsmem_f32(cb + hd * 4, sb + u) : -INFINITY;
-                        vv[u] = live ? ld_dsmem_f32(cb + d * 4, sb + u) : 0.0f;
-                        lv[u] = live ? ld_dsmem_f32(cb + (hd + 1) * 4, sb + u) : 0.0f;
-                    }
-#pragma unroll
-                    for (int u = 0; u < SU; ++u)
-                    {
-                        const float w = (mv[u] == -INFINITY) ? 0.0f : expf(mv[u] - M);
-                        num = fmaf(vv[u], w, num);
-                        den = fmaf(lv[u], w, den);
-                    }
-                }
-                p.out[(size_t)(kvh * G + gi) * hd + d] = den > 0.0f ? num / den : 0.0f;
-            }
-        cluster_sync_all();
-        return;
     }
 
     // last CTA of this kv head merges the S splits in order
@@ -425,10 +394,10 @@ __device__ __forceinline__ void attn_item(const AttnParams& p, int kvh, int spli
 }
 
 
-// CL (decode mode): launched as clusters of gridDim.y CTAs, one per split of
-// a kv head, which merge their partials in distributed shared memory
-// (attn_cluster_smem_bytes of dynamic shared memory).
-template <int MODE, int G, int HDM, bool CL = false>
+// MODE 0: the reference API over a segment list. MODE 1: the model's decode
+// step (splits merged through global memory by the last CTA of a kv head;
+// the clustered kernel below is the default).
+template <int MODE, int G, int HDM>
 __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_split_kernel(const AttnParams p)
 {
     extern __shared__ __align__(16) float asmem[];
@@ -439,31 +408,301 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
     if (tid == 0)
         trace_mark(p.trace, lin, 0);
     if constexpr (MODE == 1)
-    {
-        // The position only changes at the end of a decode step (lm_head), so
-        // it can be read before waiting for the previous kernel; rows of
-        // earlier positions go into L2 while that kernel runs (a prefetch
-        // never returns stale data).
-        const int L = attn_len<MODE>(p), hd = p.head_dim;
-        int t0, t1;
-        attn_range(L, split, p.S, t0, t1);
-        const int pf1 = min(t1, min(L - 1, t0 + ATTN_PREFETCH_TOKENS));
-        const int lines = (hd * 4 + 127) >> 7;
-        for (int i = tid; i < (pf1 - t0) * lines * 2; i += ATTN_THREADS)
-        {
-            const int r = i / (lines * 2), rem = i - r * lines * 2, kv = rem / lines, ln = rem - kv * lines;
-            const size_t ro = attn_row<MODE>(p, t0 + r, kvh);
-            const float* src = (kv ? p.v : p.k) + ro + ln * 32;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
-        }
-    }
-    if constexpr (MODE == 1)
-        attn_item<MODE, G, HDM, true, CL>(p, kvh, split, tid, asmem, &s_last, 0); // waits for the previous kernel
+        attn_item<MODE, G, HDM, true>(p, kvh, split, tid, asmem, &s_last, 0); // waits for the previous kernel
     else
     {
         pdl_wait();
         attn_item<MODE, G, HDM>(p, kvh, split, tid, asmem, &s_last, 0);
     }
+    if (tid == 0)
+        trace_mark(p.trace, lin, 3);
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention as clusters: the S splits of one kv head are one cluster
+// (grid (n_kv, S), cluster (1, S)), CTA rank = split.
+//   1. Before waiting for the kernel that writes q and the current K/V row,
+//      each warp requests the K and V rows of up to TB of its tokens
+//      (t0 + warp + 8 j) straight into registers; no other load precedes
+//      them (a null page table is the identity, so not even a page lookup).
+//      The position is read early and read again after the wait; if it
+//      moved (the step before had not finished advancing it) the rows are
+//      requested again.
+//   2. Online softmax per warp, as attn_item.
+//   3. Each warp rescales its sums to the CTA's running max, the CTA adds
+//      them in warp order: one partial (sums, max, denominator) per CTA in
+//      its shared memory.
+//   4. After a cluster barrier every CTA merges a slice of the outputs over
+//      the S partials (distributed shared memory, split order, one round of
+//      loads), then a second barrier keeps each CTA's shared memory alive
+//      until the others have read it.
+// ---------------------------------------------------------------------------
+// MHA at head_dim <= 128: 64 registers, four CTAs per SM (a cluster then
+// needs fewer free SMs of a GPC while the kernel before drains); wider
+// groups keep their q and V sums for more heads in registers.
+constexpr int attn_decode_min_blocks(int G, int HDM) { return (G == 1 && HDM == 128) ? 4 : (G * HDM >= 1024 ? 1 : 2); }
+
+// Shared memory: wm[8][G], wl[8][G], wacc[8][G][hd], then the CTA's partial
+// [G][hd + 2] (sums, max, denominator).
+__host__ __device__ inline size_t attn_decode_smem_bytes(int G, int hd)
+{
+    return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd + (size_t)G * (hd + 2)) * 4;
+}
+
+template <int G, int HDM>
+__global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) attn_decode_kernel(const AttnParams p)
+{
+    constexpr int NCH = HDM / 128;                // float4 slices per lane
+    constexpr int TB = (G == 2 && NCH == 1) ? 8 : 4; // tokens per warp in flight
+    extern __shared__ __align__(16) float asmem[];
+    pdl_launch_dependents();
+    const int kvh = blockIdx.x, split = blockIdx.y, S = (int)gridDim.y, z = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hd = p.head_dim, hd4 = hd >> 2;
+    // this row's sequence: its page table (null: the identity) and length
+    const int* pt = p.page_table && p.row_seq ? p.page_table + (size_t)p.row_seq[z] * p.pt_stride : p.page_table;
+    auto row_len = [&]() { return p.row_pos ? min(p.row_pos[z] + 1, p.max_len) : attn_len<1>(p); };
+    auto row_of = [&](int t) -> size_t {
+        const int page = pt ? pt[t / p.page_size] : t / p.page_size;
+        return (((size_t)page * p.n_kv + kvh) * p.page_size + (t % p.page_size)) * hd;
+    };
+    const float* qz = p.q + (size_t)z * p.ldq;
+    float* outz = p.out + (size_t)z * p.ldo;
+    float* wm = asmem;                 // [8][G]
+    float* wl = wm + ATTN_WARPS * G;   // [8][G]
+    float* wacc = wl + ATTN_WARPS * G; // [8][G][hd]
+    float* cp = wacc + (size_t)ATTN_WARPS * G * hd; // [G][hd + 2]
+    const int lin = split * gridDim.x + kvh;
+    if (tid == 0)
+        trace_mark(p.trace, lin, 0);
+
+    int L = row_len(), t0, t1;
+    attn_range(L, split, S, t0, t1);
+    float4 kr[TB][NCH], vr[TB][NCH];
+    auto load = [&](int tb0, int skip) {
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+        {
+            const int t = tb0 + ATTN_WARPS * j;
+            const bool live = t < t1 && t != skip;
+            const size_t ro = live ? row_of(t) : 0;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+            {
+                const int ch = lane + 32 * c;
+                if (live && ch < hd4)
+                {
+                    kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                    vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                }
+                else
+                {
+                    kr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
+    };
+    if (t0 + warp < t1)
+        load(t0 + warp, L - 1); // every row but the current position's
+    pdl_wait();
+    if (tid == 0)
+        trace_mark(p.trace, lin, 1);
+    // q, the current row and the position read again, all in flight at once
+    float4 qv[G][NCH];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+        {
+            const int ch = lane + 32 * c;
+            qv[gi][c] = ch < hd4 ? __ldcg(reinterpret_cast<const float4*>(qz + ((size_t)kvh * G + gi) * hd) + ch)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    {
+        const int tcur = L - 1;
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+            if (t0 + warp + ATTN_WARPS * j == tcur && tcur < t1)
+            {
+                const size_t ro = row_of(tcur);
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    const int ch = lane + 32 * c;
+                    if (ch < hd4)
+                    {
+                        kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                        vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
+                    }
+                }
+            }
+        const int Lw = row_len();
+        if (Lw != L)
+        {
+            // the position was read before the step before had finished
+            // advancing it: take the range again with every row current
+            L = Lw;
+            attn_range(L, split, S, t0, t1);
+            if (t0 + warp < t1)
+                load(t0 + warp, -1);
+        }
+    }
+    float m[G], l[G];
+    float4 acc[G][NCH];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+    {
+        m[gi] = -INFINITY;
+        l[gi] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+            acc[gi][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
+    {
+        if (tb0 != t0 + warp)
+            load(tb0, -1);
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi)
+        {
+            float sj[TB];
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+            {
+                float d = 0.0f;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    d = fmaf(qv[gi][c].x, kr[j][c].x, d);
+                    d = fmaf(qv[gi][c].y, kr[j][c].y, d);
+                    d = fmaf(qv[gi][c].z, kr[j][c].z, d);
+                    d = fmaf(qv[gi][c].w, kr[j][c].w, d);
+                }
+                sj[j] = d;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int j = 0; j < TB; ++j)
+                    sj[j] += __shfl_xor_sync(0xffffffffu, sj[j], o);
+            float bm = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+            {
+                sj[j] = (tb0 + ATTN_WARPS * j < t1) ? sj[j] * p.scale : -INFINITY; // src/attention.cpp:42
+                bm = fmaxf(bm, sj[j]);
+            }
+            const float mn = fmaxf(m[gi], bm);
+            if (mn == -INFINITY)
+                continue;
+            const float rs = (m[gi] == -INFINITY) ? 0.0f : expf(m[gi] - mn);
+            m[gi] = mn;
+            l[gi] *= rs;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+            {
+                acc[gi][c].x *= rs;
+                acc[gi][c].y *= rs;
+                acc[gi][c].z *= rs;
+                acc[gi][c].w *= rs;
+            }
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+            {
+                const float e = expf(sj[j] - mn); // 0 for dead slots
+                l[gi] += e;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                {
+                    acc[gi][c].x = fmaf(e, vr[j][c].x, acc[gi][c].x);
+                    acc[gi][c].y = fmaf(e, vr[j][c].y, acc[gi][c].y);
+                    acc[gi][c].z = fmaf(e, vr[j][c].z, acc[gi][c].z);
+                    acc[gi][c].w = fmaf(e, vr[j][c].w, acc[gi][c].w);
+                }
+            }
+        }
+    }
+    if (tid == 0)
+        trace_mark(p.trace, lin, 2);
+
+    // 3. the CTA's partial: warps rescaled to the CTA max, added in warp order
+    if (lane == 0)
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi)
+            wm[warp * G + gi] = m[gi];
+    __syncthreads();
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi)
+    {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < ATTN_WARPS; ++w)
+            M = fmaxf(M, wm[w * G + gi]);
+        const float f = (m[gi] == -INFINITY) ? 0.0f : expf(m[gi] - M);
+        if (lane == 0)
+            wl[warp * G + gi] = l[gi] * f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+        {
+            const int ch = lane + 32 * c;
+            if (ch < hd4)
+                reinterpret_cast<float4*>(wacc + ((size_t)warp * G + gi) * hd)[ch] =
+                    make_float4(acc[gi][c].x * f, acc[gi][c].y * f, acc[gi][c].z * f, acc[gi][c].w * f);
+        }
+        if (tid == gi)
+            cp[gi * (hd + 2) + hd] = M;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * (hd + 1); i += ATTN_THREADS)
+    {
+        const int gi = i / (hd + 1), d = i - gi * (hd + 1);
+        float sum = 0.0f;
+        if (d < hd)
+            for (int w = 0; w < ATTN_WARPS; ++w)
+                sum += wacc[((size_t)w * G + gi) * hd + d];
+        else
+            for (int w = 0; w < ATTN_WARPS; ++w)
+                sum += wl[w * G + gi];
+        cp[gi * (hd + 2) + (d < hd ? d : hd + 1)] = sum;
+    }
+
+    // 4. the cluster merge, a slice of the G * hd outputs per CTA
+    cluster_sync_all();
+    {
+        const int n = G * hd, per = (n + S - 1) / S, i = split * per + tid;
+        if (tid < per && i < n)
+        {
+            const int gi = i / hd, d = i - gi * hd;
+            const uint32_t cb = smem_addr(cp + gi * (hd + 2));
+            constexpr int SM = 16;
+            float mv[SM], vv[SM], lv[SM];
+#pragma unroll
+            for (int r = 0; r < SM; ++r)
+                if (r < S)
+                {
+                    mv[r] = ld_dsmem_f32(cb + hd * 4, r);
+                    vv[r] = ld_dsmem_f32(cb + d * 4, r);
+                    lv[r] = ld_dsmem_f32(cb + (hd + 1) * 4, r);
+                }
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < SM; ++r)
+                if (r < S)
+                    M = fmaxf(M, mv[r]);
+            float num = 0.0f, den = 0.0f;
+#pragma unroll
+            for (int r = 0; r < SM; ++r)
+                if (r < S)
+                {
+                    const float w = (mv[r] == -INFINITY) ? 0.0f : expf(mv[r] - M);
+                    num = fmaf(vv[r], w, num);
+                    den = fmaf(lv[r], w, den);
+                }
+            outz[(size_t)(kvh * G + gi) * hd + d] = den > 0.0f ? num / den : 0.0f;
+        }
+    }
+    cluster_sync_all();
     if (tid == 0)
         trace_mark(p.trace, lin, 3);
 }
@@ -479,12 +718,8 @@ inline cudaError_t attn_launch_one(const AttnParams& p, dim3 grid, size_t smem, 
     return launch_kernel(attn_split_kernel<MODE, G, HDM>, grid, dim3(ATTN_THREADS), smem, st, pdl, p);
 }
 
-// Shared memory of the cluster variant: the per-warp block plus this CTA's
-// partial result (G x (hd + 2) floats) that the cluster reads.
-inline size_t attn_cluster_smem_bytes(int G, int hd)
-{
-    return attn_smem_bytes(G, hd, 0) + (size_t)G * (hd + 2) * 4;
-}
+// Shared memory of the clustered decode kernel.
+inline size_t attn_cluster_smem_bytes(int G, int hd) { return attn_decode_smem_bytes(G, hd); }
 
 // Decode attention as clusters of grid.y CTAs (the splits of one kv head).
 template <int G, int HDM>
@@ -504,7 +739,7 @@ inline cudaError_t attn_launch_cluster_one(const AttnParams& p, dim3 grid, cudaS
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, attn_split_kernel<1, G, HDM, true>, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<G, HDM>, p);
 }
 
 inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
@@ -545,7 +780,7 @@ inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_split_kernel<1, G, HDM, true>, &cfg) != cudaSuccess)
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<G, HDM>, &cfg) != cudaSuccess)
     {
         cudaGetLastError();
         return 0;
@@ -597,13 +832,13 @@ inline int attn_set_attrs_g()
     if constexpr (MODE == 1)
     {
         // the clustered variant: up to 16 CTAs per cluster
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 128, true>,
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 128>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 256, true>,
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 256>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 128, true>,
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 128>,
                                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<1, G, 256, true>,
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 256>,
                                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     }
     return AAEDN_OK;

@@ -260,6 +260,39 @@ __device__ __forceinline__ float ldsf(uint32_t addr)
     return r;
 }
 
+__device__ __forceinline__ float2 lds64f(uint32_t addr)
+{
+    float2 r;
+    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(r.x), "=f"(r.y) : "r"(addr));
+    return r;
+}
+
+// Packed fp32 pairs (sm_100): each component rounds exactly as mul.rn /
+// fma.rn of one float, so these are __fmul_rn / fmaf on two lanes of data
+// in one instruction.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b)
+{
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// a * b + c per component, one rounding (fmaf on each lane of the pair)
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c)
+{
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+        "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // ---- mbarriers and bulk (TMA) copies --------------------------------------
 __device__ __forceinline__ uint64_t globaltimer_ns()
 {

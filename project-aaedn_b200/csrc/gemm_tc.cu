@@ -36,10 +36,11 @@ struct TcShape
 
 TcShape tc_shape(int M)
 {
+    // as many stages as shared memory holds
     if (M <= 32)
-        return {32, 4};
+        return {32, 5};
     if (M <= 64)
-        return {64, 3};
+        return {64, 4};
     return {128, 2};
 }
 
@@ -65,8 +66,8 @@ int tc_launch_bn(int bn, const TcGemmParams& p, const CUtensorMap& map, dim3 gri
 {
     switch (bn)
     {
-    case 32: return tc_launch<32, 4, EPI>(p, map, grid, st);
-    case 64: return tc_launch<64, 3, EPI>(p, map, grid, st);
+    case 32: return tc_launch<32, 5, EPI>(p, map, grid, st);
+    case 64: return tc_launch<64, 4, EPI>(p, map, grid, st);
     default: return tc_launch<128, 2, EPI>(p, map, grid, st);
     }
 }
@@ -94,7 +95,7 @@ void* tc_gemm_parts(void* workspace) { return workspace; }
 int tc_split(const float* x, size_t lda, int M, int K, void* workspace, cudaStream_t st)
 {
     const int M_pad = tc_m_pad(M);
-    const size_t work = (size_t)M_pad * (K / 4);
+    const size_t work = (size_t)M_pad * (K / 8);
     tc_split_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(
         x, lda, M, M_pad, K, reinterpret_cast<__nv_bfloat16*>(tc_gemm_parts(workspace)));
     AAEDN_LAUNCH_CHECK("tc_split_kernel");
@@ -146,7 +147,7 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t st)
     // the activation parts (unless the caller wrote them into the workspace)
     if (a.x)
     {
-        const size_t work = (size_t)M_pad * (a.K / 4);
+        const size_t work = (size_t)M_pad * (a.K / 8);
         tc_split_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a.x, a.lda, a.M, M_pad, a.K, parts);
         AAEDN_LAUNCH_CHECK("tc_split_kernel");
     }

@@ -25,17 +25,20 @@
 //
 // Data movement, per stage of 64 K:
 //   * the activation parts (prepared once per call in global memory as bf16
-//     [3][M_pad][K]) arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle:
-//     the canonical K-major layout the MMA reads), issued by warp 4;
+//     [3][M_pad][K], K in the tc_kpos order) arrive by TMA
+//     (cp.async.bulk.tensor, 128-byte swizzle: the canonical K-major layout
+//     the MMA reads), issued by warp 8;
 //   * the weights' 4-bit codes and fp16 scales are read from global memory by
-//     warps 0-3 (one weight row per thread, 32 bytes of codes per stage,
-//     loaded two stages ahead), dequantized in registers and written as the
-//     two bf16 parts into the same swizzled layout (fence.proxy.async before
-//     the stage is marked full);
-//   * warp 5 issues the 20 MMAs of the stage (4 k-steps x 5 part products)
+//     warps 0-7 (two threads per weight row, one quant block of 16 bytes
+//     each per stage, loaded two stages ahead), dequantized in registers
+//     (bf16x2 and packed fp32 arithmetic, exact) and written as the two bf16
+//     parts into the same swizzled layout (fence.proxy.async before the
+//     stage is marked full);
+//   * warp 9 issues the 20 MMAs of the stage (4 k-steps x 5 part products)
 //     from one thread and commits them to the stage's "empty" barrier.
-// Epilogue: warps 0-3 read their 32 TMEM lanes (tcgen05.ld 32x32b) and store
-// out[m][n] (a warp writes 32 consecutive n of one m: coalesced).
+// Epilogue: warps w and w + 4 read TMEM lanes 32 (w % 4).. (tcgen05.ld
+// 32x32b), half of the columns each, and store out[m][n] (a warp writes 32
+// consecutive n of one m: coalesced).
 //
 // Every wait is bounded (globaltimer): a wait that runs out sets *err, the
 // kernel drains what it issued, frees its TMEM and returns.
@@ -53,7 +56,9 @@ constexpr int TC_BM = 128;     // weight rows per tile (UMMA M)
 constexpr int TC_BK = 64;      // K per stage: one 128-byte swizzle row of bf16
 constexpr int TC_XP = 3;       // bf16 parts of the activation
 constexpr int TC_WP = 2;       // bf16 parts of a dequantized weight (exact)
-constexpr int TC_THREADS = 192; // warps 0-3 dequant + epilogue, 4 TMA, 5 MMA
+constexpr int TC_DQ_WARPS = 8;  // dequant + epilogue warps (two threads per weight row)
+constexpr int TC_TMA_WARP = TC_DQ_WARPS, TC_MMA_WARP = TC_DQ_WARPS + 1;
+constexpr int TC_THREADS = (TC_DQ_WARPS + 2) * 32;
 constexpr uint64_t TC_WAIT_LIMIT_NS = 2000000000ull;
 
 struct TcGemmParams
@@ -78,6 +83,7 @@ struct TcSmem
     static constexpr size_t STAGE = TC_WP * W_PART + TC_XP * X_PART;
     static constexpr size_t BARS = 1024; // after the stages: mbarriers, TMEM address
     static constexpr size_t BYTES = STAGES * STAGE + BARS + 1024; // + alignment slack
+    static_assert(BYTES <= 232448, "GEMM stages exceed the shared memory of a CTA");
     static constexpr uint32_t TMEM_COLS = 2 * BN; // leading + small-product accumulators (a power of two)
 };
 
@@ -138,29 +144,36 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8])
 }
 
 // 16 bytes of codes (32 weights of one quant block) dequantized with scale
-// sc into their bf16 parts, stored at byte offset (4 * kb + j) * 16 of a
-// 128-byte swizzled row (j = 0..3: 8 weights each).
-__device__ __forceinline__ void tc_dequant_block(uint4 codes, float sc, uint32_t w0_row, uint32_t w1_row, int kb,
-                                                 int r7)
+// sc into their two bf16 parts, stored as the 16-byte chunks c0..c0+3 of a
+// 128-byte swizzled row (chunk c at (c ^ r7) * 16). Exact: code * scale has
+// at most 15 significant bits, w_hi = bf16(w) and w_lo = w - w_hi.
+__device__ __forceinline__ void tc_dequant_block(uint4 codes, float sc, uint32_t w0_row, uint32_t w1_row, int c0,
+                                                 uint32_t r7)
 {
     const uint32_t cw[4] = {codes.x, codes.y, codes.z, codes.w};
+    const float2 sc2 = make_float2(sc, sc);
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
     {
-        // 8 weights: bytes 0..3 of word j, low nibble first
         uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
+        for (int i = 0; i < 4; ++i)
         {
-            const uint32_t byte = (cw[j] >> (8 * b)) & 0xFFu;
-            const float wa = (float)(byte & 0xFu) * sc, wb = (float)(byte >> 4) * sc; // exact in fp32
-            const __nv_bfloat16 ha = __float2bfloat16_rn(wa), hb = __float2bfloat16_rn(wb);
-            const __nv_bfloat16 la = __float2bfloat16_rn(wa - __bfloat162float(ha));
-            const __nv_bfloat16 lb = __float2bfloat16_rn(wb - __bfloat162float(hb));
-            hi[b] = pack_bf16(ha, hb);
-            lo[b] = pack_bf16(la, lb);
+            // codes i and i + 4 of the word as bf16 (128 + c) - 128: exact
+            uint32_t cp = ((cw[j] >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+            asm("sub.rn.bf16x2 %0, %0, %1;" : "+r"(cp) : "r"(0x43004300u));
+            const float2 c = make_float2(__uint_as_float(cp << 16), __uint_as_float(cp & 0xFFFF0000u));
+            const float2 w = mul2_rn(c, sc2); // exact
+            const __nv_bfloat162 h = __floats2bfloat162_rn(w.x, w.y);
+            const uint32_t hu = *reinterpret_cast<const uint32_t*>(&h);
+            const float2 hf = make_float2(__uint_as_float(hu << 16), __uint_as_float(hu & 0xFFFF0000u));
+            const float2 r = fma2_rn(hf, neg1, w); // w - w_hi, exact
+            const __nv_bfloat162 l = __floats2bfloat162_rn(r.x, r.y);
+            hi[i] = hu;
+            lo[i] = *reinterpret_cast<const uint32_t*>(&l);
         }
-        const uint32_t chunk = (uint32_t)(((4 * kb + j) ^ r7) * 16);
+        const uint32_t chunk = (((uint32_t)(c0 + j)) ^ r7) * 16u;
         asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(w0_row + chunk), "r"(hi[0]), "r"(hi[1]),
                      "r"(hi[2]), "r"(hi[3])
                      : "memory");
@@ -170,37 +183,32 @@ __device__ __forceinline__ void tc_dequant_block(uint4 codes, float sc, uint32_t
     }
 }
 
-// The 32 code bytes (quant blocks b0, b0 + 1 in order; b0 even) and their
-// two scales (low half: b0) of weight row `row`.
-__device__ __forceinline__ void tc_w_load(const TcGemmParams& p, int row, int b0, uint4& ca, uint4& cb,
-                                          uint32_t& sp)
+// The 16 code bytes of quant block b of weight row `row` and its fp16 scale.
+__device__ __forceinline__ void tc_w_load(const TcGemmParams& p, int row, int b, uint4& ca, uint16_t& sc)
 {
     if (p.w_layout == TC_W_TILED)
     {
         // the decode GEMV's layout (gemv_tiled.cuh): chunks of 16 tiles;
-        // blocks b0, b0 + 1 are pair P = (b0 % 4) / 2 of their tile, whose 64
-        // code bytes for rows g and g + 8 sit in lanes 4g..4g+3, word (H, r)
-        // of lane 4g + t = bytes [8H + 4(t & 1), +4) of block b' = t >> 1
+        // block b is half b' = b % 2 of pair P = (b % 4) / 2 of its tile,
+        // whose code bytes for rows g and g + 8 sit in lanes 4g..4g+3: word
+        // (H, r) of lane 4g + t = bytes [8H + 4(t & 1), +4) of block
+        // 2P + (t >> 1)
         constexpr int CT = 16;
         const int ntile = p.K >> 7, group = row >> 4, r16 = row & 15, r = r16 >> 3, g = r16 & 7;
-        const int tile = b0 >> 2, P = (b0 >> 1) & 1, c = tile / CT, ti = tile % CT;
+        const int tile = b >> 2, P = (b >> 1) & 1, bp = b & 1, c = tile / CT, ti = tile % CT;
         const int tiles_in_chunk = min(CT, ntile - CT * c);
         const uint8_t* chunk = p.w + (size_t)group * ntile * 1152 + (size_t)c * CT * 1152;
-        const uint32_t* q = reinterpret_cast<const uint32_t*>(chunk + (size_t)ti * 1024 + P * 512 + (4 * g) * 16);
-        // lane t' = 4g + t: words (H0 r0, H0 r1, H1 r0, H1 r1) at q[4 t' ..]
-        ca = make_uint4(__ldg(q + 0 + r), __ldg(q + 4 + r), __ldg(q + 2 + r), __ldg(q + 6 + r));
-        cb = make_uint4(__ldg(q + 8 + r), __ldg(q + 12 + r), __ldg(q + 10 + r), __ldg(q + 14 + r));
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(chunk + (size_t)tiles_in_chunk * 1024 + ti * 128) +
-                             ((P * 8 + g) * 2) * 2 + r;
-        sp = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 2) << 16);
+        // lane 4g + 2b' + h: words (H0 r0, H0 r1, H1 r0, H1 r1)
+        const uint32_t* q = reinterpret_cast<const uint32_t*>(chunk + (size_t)ti * 1024 + P * 512 +
+                                                              (4 * g + 2 * bp) * 16);
+        ca = make_uint4(__ldg(q + r), __ldg(q + 4 + r), __ldg(q + 2 + r), __ldg(q + 6 + r));
+        sc = __ldg(reinterpret_cast<const uint16_t*>(chunk + (size_t)tiles_in_chunk * 1024 + ti * 128) +
+                   ((P * 8 + g) * 2 + bp) * 2 + r);
     }
     else
     {
-        const uint8_t* c = p.w + (size_t)row * (p.ldb >> 1) + (size_t)b0 * 16;
-        const uint16_t* sc = p.s + (size_t)row * (p.ldb >> 5) + b0;
-        ca = __ldg(reinterpret_cast<const uint4*>(c));
-        cb = __ldg(reinterpret_cast<const uint4*>(c) + 1);
-        sp = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 1) << 16);
+        ca = __ldg(reinterpret_cast<const uint4*>(p.w + (size_t)row * (p.ldb >> 1) + (size_t)b * 16));
+        sc = __ldg(p.s + (size_t)row * (p.ldb >> 5) + b);
     }
 }
 
@@ -320,14 +328,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
         for (int s = 0; s < STAGES; ++s)
         {
             mbar_init(full_x(s), 1);
-            mbar_init(full_w(s), 128);
+            mbar_init(full_w(s), TC_DQ_WARPS * 32);
             mbar_init(empty(s), 1);
         }
         mbar_init(accum, 1);
         mbar_init_fence();
         s_abort = 0;
     }
-    if (warp == 5)
+    if (warp == TC_MMA_WARP)
     {
         // two accumulators of BN fp32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
@@ -348,7 +356,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
             atomicExch(p.err, 1u);
     };
 
-    if (warp == 4)
+    if (warp == TC_TMA_WARP)
     {
         // ---- TMA producer of the activation parts
         int issued = 0;
@@ -375,7 +383,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
         }
         __syncwarp();
     }
-    else if (warp == 5)
+    else if (warp == TC_MMA_WARP)
     {
         // ---- MMA issuer (one thread)
         if (lane == 0)
@@ -415,49 +423,56 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
     }
     else
     {
-        // ---- warps 0-3: weight rows n0 + tid, dequantized into the stages
-        const int row = n0 + tid;
+        // ---- warps 0-7: thread (half h, row r) = (tid / 128, tid % 128)
+        // dequantizes quant block h of the stage's 64 K of weight row n0 + r
+        const int r = tid & 127, h = tid >> 7;
+        const int row = n0 + r;
         const bool live = row < p.N;
-        const uint32_t r7 = (uint32_t)(tid & 7);
-        uint4 ca[2] = {}, cb[2] = {};
-        uint32_t sp[2] = {};
-        auto load = [&](int kb, int slot) {
+        const uint32_t r7 = (uint32_t)(r & 7);
+        // registers two stages ahead: slot A for even kb, slot B for odd
+        uint4 cwa = make_uint4(0, 0, 0, 0), cwb = make_uint4(0, 0, 0, 0);
+        uint16_t sca = 0, scb = 0;
+        auto load = [&](int kb, uint4& cw, uint16_t& sc) {
             if (live && kb < nk)
-                tc_w_load(p, row, (kb0 + kb) * 2, ca[slot], cb[slot], sp[slot]);
+                tc_w_load(p, row, (kb0 + kb) * 2 + h, cw, sc);
             else
             {
-                ca[slot] = cb[slot] = make_uint4(0, 0, 0, 0);
-                sp[slot] = 0;
+                cw = make_uint4(0, 0, 0, 0);
+                sc = 0;
             }
         };
-        load(0, 0);
-        load(1, 1);
-        for (int kb = 0; kb < nk; ++kb)
-        {
-            const int s = kb % STAGES, use = kb / STAGES, slot = kb & 1;
+        // one stage: false when a wait ran out or the CTA aborts
+        auto stage = [&](int kb, uint4& cw, uint16_t& sc) -> bool {
+            const int s = kb % STAGES, use = kb / STAGES;
             if (use > 0 && !mbar_wait_bounded(empty(s), (use - 1) & 1, TC_WAIT_LIMIT_NS))
             {
                 fail();
-                break;
+                return false;
             }
             if (s_abort)
-                break;
-            const uint32_t w0 = w_part(s, 0) + (uint32_t)tid * 128, w1 = w_part(s, 1) + (uint32_t)tid * 128;
-            const float s0 = __half2float(__ushort_as_half((uint16_t)(sp[slot] & 0xFFFFu)));
-            const float s1 = __half2float(__ushort_as_half((uint16_t)(sp[slot] >> 16)));
-            tc_dequant_block(ca[slot], s0, w0, w1, 0, (int)r7);
-            tc_dequant_block(cb[slot], s1, w0, w1, 1, (int)r7);
-            load(kb + 2, slot); // two stages ahead
+                return false;
+            const uint32_t w0 = w_part(s, 0) + (uint32_t)r * 128, w1 = w_part(s, 1) + (uint32_t)r * 128;
+            tc_dequant_block(cw, __half2float(__ushort_as_half(sc)), w0, w1, 4 * h, r7);
+            load(kb + 2, cw, sc);
             // generic-proxy stores, then visible to the tensor core's reads
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(full_w(s));
-        }
-        // ---- epilogue: this warp's 32 TMEM lanes = weight rows n0 + 32 w + lane
+            return true;
+        };
+        load(0, cwa, sca);
+        load(1, cwb, scb);
+        for (int kb = 0; kb < nk; kb += 2)
+            if (!stage(kb, cwa, sca) || (kb + 1 < nk && !stage(kb + 1, cwb, scb)))
+                break;
+        // ---- epilogue: TMEM lanes 32 (warp % 4) + lane = weight rows, the
+        // warp's half (warp / 4) of the BN activation columns
         if (mbar_wait_bounded(accum, 0, TC_WAIT_LIMIT_NS) && !s_abort)
         {
             tc_fence_after();
-            const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
-            for (int c0 = 0; c0 < BN; c0 += 8)
+            const int erow = n0 + 32 * (warp & 3) + lane;
+            const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+            const int cbeg = (warp >> 2) * (BN / 2);
+            for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += 8)
             {
                 float v[8], w[8];
                 tc_ld8(t_row + (uint32_t)c0, v);
@@ -465,7 +480,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     v[j] += w[j];
-                tc_epilogue8<EPI>(p, out, row, live, m0 + c0, v);
+                tc_epilogue8<EPI>(p, out, erow, erow < p.N, m0 + c0, v);
             }
         }
         else
@@ -473,7 +488,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5)
+    if (warp == TC_MMA_WARP)
     {
         // every MMA issued has completed before its accumulator is released
         if (lane == 0)
@@ -486,40 +501,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) q4_gemm_tc_kernel(const TcGemmP
 }
 
 // Splits fp32 activation rows into the three bf16 parts the GEMM reads:
-// parts[i][m][k] for m < M_pad (rows M..M_pad-1 zero).
+// parts[i][m][tc_kpos(k)] for m < M_pad (rows M..M_pad-1 zero); 8 elements
+// (one group of the K order) per thread.
 __global__ void tc_split_kernel(const float* __restrict__ x, size_t lda, int M, int M_pad, int K,
                                 __nv_bfloat16* __restrict__ parts)
 {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; // 4 elements per thread
-    const size_t per_row = (size_t)K / 4;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t per_row = (size_t)K / 8;
     if (i >= (size_t)M_pad * per_row)
         return;
-    const int m = (int)(i / per_row), k = (int)(i - (size_t)m * per_row) * 4;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const int m = (int)(i / per_row), k = (int)(i - (size_t)m * per_row) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (m < M)
     {
         const float* src = x + (size_t)m * lda + k;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 8; ++j)
             v[j] = src[j];
     }
-    __nv_bfloat16 h[3][4];
+    __nv_bfloat16 h[3][8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 8; ++j)
     {
-        h[0][j] = __float2bfloat16_rn(v[j]);
-        const float r1 = v[j] - __bfloat162float(h[0][j]);
-        h[1][j] = __float2bfloat16_rn(r1);
-        h[2][j] = __float2bfloat16_rn(r1 - __bfloat162float(h[1][j]));
+        const int q = tc_kpos(j);
+        h[0][q] = __float2bfloat16_rn(v[j]);
+        const float r1 = v[j] - __bfloat162float(h[0][q]);
+        h[1][q] = __float2bfloat16_rn(r1);
+        h[2][q] = __float2bfloat16_rn(r1 - __bfloat162float(h[1][q]));
     }
     const size_t plane = (size_t)M_pad * K;
 #pragma unroll
     for (int q = 0; q < 3; ++q)
     {
-        uint2 w;
+        uint4 w;
         w.x = pack_bf16(h[q][0], h[q][1]);
         w.y = pack_bf16(h[q][2], h[q][3]);
-        *reinterpret_cast<uint2*>(parts + q * plane + (size_t)m * K + k) = w;
+        w.z = pack_bf16(h[q][4], h[q][5]);
+        w.w = pack_bf16(h[q][6], h[q][7]);
+        *reinterpret_cast<uint4*>(parts + q * plane + (size_t)m * K + k) = w;
     }
 }
 

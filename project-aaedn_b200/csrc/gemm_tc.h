@@ -11,6 +11,13 @@
 namespace aaedn_dev
 {
 
+// Order of the K elements inside every group of 8 in the GEMM's operands
+// (and so in the activation parts written for it): k = 4 h + j sits at
+// position 2 j + h, the order in which a 32-bit word's 8 codes come out as
+// bf16 pairs (code j, code j + 4). The MMA sums over k, so any order shared
+// by both operands gives the same product.
+__host__ __device__ constexpr int tc_kpos(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
+
 // Weight layouts the GEMM reads.
 enum
 {

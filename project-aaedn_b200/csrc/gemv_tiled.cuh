@@ -38,12 +38,17 @@ constexpr int GT_CONSUMERS = 16;
 constexpr int GT_GROUPS = 4;                             // consumer groups (chunks in flight at once)
 constexpr int GT_GROUP_WARPS = GT_CONSUMERS / GT_GROUPS; // warps of a group
 constexpr int GT_THREADS = (GT_CONSUMERS + 1) * 32;
+// Ring stages: a multiple of the consumer groups (the consumers' waits rely
+// on it: a stage is always refilled for the group that consumed it).
 constexpr int GT_STAGES = 4;     // fewest ring stages a launch takes
 constexpr int GT_MAX_STAGES = 12;
 constexpr int GT_CHUNK_TILES = 16; // four tiles per warp of a group
 constexpr int GT_TILE_BYTES = 1024 + 128; // codes + scales of one tile (16 rows x 128 codes)
 constexpr int GT_STAGE_BYTES = GT_CHUNK_TILES * GT_TILE_BYTES; // 18 KB
 constexpr int GT_FRAG_TILE_BYTES = 512; // activation digits of one tile (B fragments)
+// A block's activation is scaled to |y| <= 119 before its digits are taken:
+// the top digit of odd - even (up to 119 * 17 / 16) then fits a signed byte.
+constexpr float GT_YMAX = 119.0f;
 // Partial sums in flight: slot q % GT_RQ holds chunk q's [4 warps][16 rows];
 // row group counters by group number % GT_RC. Chunks in flight are bounded by
 // the ring (stages + the groups' current chunks), row groups by those over
@@ -83,16 +88,17 @@ void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t
 
 inline size_t gemv_tiled_i8_smem_bytes(int ntile, int stages = GT_STAGES)
 {
-    return (size_t)stages * GT_STAGE_BYTES + (size_t)stages * 16 + (size_t)ntile * (GT_FRAG_TILE_BYTES + 16) +
+    return (size_t)stages * GT_STAGE_BYTES + (size_t)stages * 16 + (size_t)ntile * (GT_FRAG_TILE_BYTES + 32) +
            GT_RED_BYTES + 64 * 4 + GT_ECACHE_FLOATS * 4;
 }
 
-// The most ring stages (<= GT_MAX_STAGES) whose shared memory fits `budget`.
+// The most ring stages (a multiple of GT_GROUPS, <= GT_MAX_STAGES) whose
+// shared memory fits `budget`.
 inline int gemv_tiled_stages(int ntile, size_t budget)
 {
     int s = GT_MAX_STAGES;
-    while (s > 2 && gemv_tiled_i8_smem_bytes(ntile, s) > budget)
-        --s;
+    while (s > GT_STAGES && gemv_tiled_i8_smem_bytes(ntile, s) > budget)
+        s -= GT_GROUPS;
     return s;
 }
 
@@ -158,9 +164,11 @@ __device__ __forceinline__ void tiled_drain(const TiledRing& r, uint32_t q)
 // the mma column g = 4 b' + d (block 2P + b', digit d) and the half h of the
 // block's byte pairs (t & 1 of the consuming lane); the 16 bytes are (H = 0:
 // b0, b1; H = 1: b0, b1), b0 holding digit d of the 4 even elements of those
-// bytes, b1 of the 4 odd ones. bscale[tile * 4 + tb] = the block's unit
-// max / (127 * 128) (the RMSNorm factor stays out: a scalar applied after the
-// dot product, from the per-warp sums of squares in wss).
+// bytes (met by the raw code bytes), b1 digit d of odd - even (met by the
+// high nibbles). bscale[(tile * 4 + t) * 2 + P] = the unit max / (119 * 128)
+// of block 2P + (t >> 1), times 2^-14 for t odd (the lanes holding digits
+// 2 and 3). The RMSNorm factor stays out: a scalar applied after the dot
+// product, from the per-warp sums of squares in wss.
 // ---------------------------------------------------------------------------
 template <int PRO>
 __device__ __forceinline__ void gt_build(const GemvParams& p, uint8_t* frag, float* bscale, float* wss)
@@ -239,17 +247,23 @@ __device__ __forceinline__ void gt_build(const GemvParams& p, uint8_t* frag, flo
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const unsigned bad = __ballot_sync(0xffffffffu, !fin);
         const bool bbad = ((bad >> (lane & ~3)) & 0xFu) != 0;
-        const float inv = (mx > 0.0f && !bbad) ? 127.0f / mx : 0.0f;
+        const float inv = (mx > 0.0f && !bbad) ? GT_YMAX / mx : 0.0f;
         if (item < nitems)
         {
-            // balanced base-128 digits of Y = round(y * 2^21) (odd elements:
-            // of y/16, so Y = round(y * 2^17)), exact integer arithmetic
+            // Y = round(y * 2^21) for an even element, round(y * 2^17) (of
+            // y/16) for an odd one; the mma's raw-byte half meets the even
+            // element's Y, its high-nibble half the difference odd - even:
+            // (lo + 16 hi) Ye + 16 hi (Yo - Ye) = lo Ye + 16 hi Yo. Both as
+            // balanced base-128 digits, exact integer arithmetic.
+            int Yv[8];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+                Yv[cc] = __float2int_rn(__fmul_rn(v[it][cc], inv) * ((cc & 1) ? 131072.0f : 2097152.0f));
             int dg[8][4];
 #pragma unroll
             for (int cc = 0; cc < 8; ++cc)
             {
-                const float y = __fmul_rn(v[it][cc], inv);
-                const int Y = __float2int_rn(y * ((cc & 1) ? 131072.0f : 2097152.0f));
+                const int Y = (cc & 1) ? Yv[cc] - Yv[cc - 1] : Yv[cc];
                 const int d0 = (Y + (1 << 20)) >> 21;
                 const int r0 = Y - (d0 << 21);
                 const int d1 = (r0 + (1 << 13)) >> 14;
@@ -273,8 +287,14 @@ __device__ __forceinline__ void gt_build(const GemvParams& p, uint8_t* frag, flo
 #pragma unroll
             for (int d = 0; d < 4; ++d)
                 *reinterpret_cast<uint2*>(base + (2 * (4 * bp + d) + h) * 16) = make_uint2(pack(0, d), pack(1, d));
-            if (s == 0)
-                bscale[tile * 4 + tb] = bbad ? __int_as_float(0x7fc00000) : mx / (127.0f * 128.0f);
+            // the block's unit, for the consuming lanes t = 2 b' + h (h = 1:
+            // digits (2, 3), weight 2^-14), component P of their pair
+            if (s < 2)
+            {
+                const float u = mx / (GT_YMAX * 128.0f);
+                bscale[(tile * 4 + 2 * bp + s) * 2 + P] =
+                    bbad ? __int_as_float(0x7fc00000) : (s ? __fmul_rn(u, 1.0f / 16384.0f) : u);
+            }
         }
     }
     }
@@ -304,8 +324,7 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     const bool bact = (t >> 1) == (g >> 2);
     const uint32_t f_base = bact ? smem_addr(frag) + (uint32_t)(2 * g + (t & 1)) * 16 : zero16;
     const uint32_t f_tile = bact ? (uint32_t)GT_FRAG_TILE_BYTES : 0u, f_pair = bact ? 256u : 0u;
-    const uint32_t bs_base = smem_addr(bscale) + (uint32_t)(t >> 1) * 4;
-    const float half_w = (t & 1) ? (1.0f / 16384.0f) : 1.0f; // digits (2,3) weigh 2^-14 of digits (0,1)
+    const uint32_t bs_base = smem_addr(bscale) + (uint32_t)t * 8; // (pair 0, pair 1) units of this lane's class
     float* part = red;                                                     // [RQ][4][16]
     unsigned* cnt = reinterpret_cast<unsigned*>(red + GT_RQ * GT_GROUP_WARPS * 16); // [RC]
     float* tmp = reinterpret_cast<float*>(cnt + GT_RC) + warp * 16;          // this warp's 16 sums
@@ -334,12 +353,20 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     }
     const int nq = my_groups * nchunk;
     bool ok = true;
+    // chunk q = grp, grp + 4, ...: its stage, use, row group and chunk within
+    // the row group are advanced without divisions (the ring has >= 4 stages)
+    uint32_t qq = q0 + (uint32_t)grp, stage = qq % NS, use = qq / NS;
+    int gl = grp / nchunk, c = grp - gl * nchunk;
     for (int q = grp; q < nq; q += GT_GROUPS)
     {
-        const uint32_t qq = q0 + (uint32_t)q, stage = qq % NS, phase = (qq / NS) & 1;
-        const int gl = q / nchunk, c = q - gl * nchunk;
         const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-        if (!mbar_wait_bounded(r.full + 8 * stage, phase, GEMV_WAIT_LIMIT_NS) || s_abort)
+        // The ring depth is a multiple of the groups, so the stage's previous
+        // use (chunk qq - NS) was this group's own and has been consumed: the
+        // stage has completed `use` or `use + 1` fills, which the parity of
+        // `use` tells apart. (With other depths the previous use belongs to
+        // another group and may not have landed yet; a parity bit cannot
+        // tell that state from `use + 1`.)
+        if (!mbar_wait_bounded(r.full + 8 * stage, use & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
         {
             ok = false;
             s_abort = 1;
@@ -347,44 +374,55 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
         }
         if (p.trace && tid == 0)
             trace_chunk(p.trace, cta, qq, 0);
-        float acc0 = 0.0f, acc1 = 0.0f;
+        float2 acc = make_float2(0.0f, 0.0f); // rows g, g + 8
         const uint32_t st = r.ring + stage * GT_STAGE_BYTES;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
+        const uint32_t sc = st + (uint32_t)tiles * 1024 + g * 8 + (t >> 1) * 4;
+        const int tt0 = c * CT + 4 * wj; // this warp's first tile within the row
+        // One tile: the raw code bytes meet the even elements' digits, the
+        // high nibbles (x 16) the digits of odd - even; the two halves H of
+        // each block pair chain in one accumulator. A lane's columns are two
+        // adjacent digits of its block: exact integer sums, combined and
+        // scaled in fp32 (two rows per packed instruction).
+        auto tile = [&](int i) {
             const int ti = 4 * wj + i;
-            if (ti < tiles)
-            {
-                const int tt = c * CT + ti; // tile within the row
-                const uint4 w0 = lds128(st + ti * 1024 + lane * 16);
-                const uint4 w1 = lds128(st + ti * 1024 + 512 + lane * 16);
-                const uint32_t sa = st + tiles * 1024 + ti * 128 + g * 8 + (t >> 1) * 4;
-                const uint32_t s0 = lds32(sa), s1 = lds32(sa + 64); // (row g, row g + 8) of pair 0, pair 1
-                const uint4 b0 = lds128(f_base + (uint32_t)tt * f_tile);
-                const uint4 b1 = lds128(f_base + (uint32_t)tt * f_tile + f_pair);
-                const float bu0 = ldsf(bs_base + (uint32_t)tt * 16), bu1 = ldsf(bs_base + (uint32_t)tt * 16 + 8);
-                int d0[4] = {0, 0, 0, 0}, e0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
-                // pair 0: halves H = 0, 1 into separate accumulators (no chain)
-                mma_u8s8_16832(d0[0], d0[1], d0[2], d0[3], w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu,
-                               w0.x & 0xF0F0F0F0u, w0.y & 0xF0F0F0F0u, b0.x, b0.y);
-                mma_u8s8_16832(e0[0], e0[1], e0[2], e0[3], w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu,
-                               w0.z & 0xF0F0F0F0u, w0.w & 0xF0F0F0F0u, b0.z, b0.w);
-                mma_u8s8_16832(d1[0], d1[1], d1[2], d1[3], w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu,
-                               w1.x & 0xF0F0F0F0u, w1.y & 0xF0F0F0F0u, b1.x, b1.y);
-                mma_u8s8_16832(e1[0], e1[1], e1[2], e1[3], w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu,
-                               w1.z & 0xF0F0F0F0u, w1.w & 0xF0F0F0F0u, b1.z, b1.w);
-                // this lane's two digits of its block: exact integers below 2^23
-                const float p0r0 = (float)((d0[0] + e0[0]) * 128 + (d0[1] + e0[1]));
-                const float p0r1 = (float)((d0[2] + e0[2]) * 128 + (d0[3] + e0[3]));
-                const float p1r0 = (float)((d1[0] + e1[0]) * 128 + (d1[1] + e1[1]));
-                const float p1r1 = (float)((d1[2] + e1[2]) * 128 + (d1[3] + e1[3]));
-                const float u0 = bu0 * half_w, u1 = bu1 * half_w;
-                acc0 = fmaf(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s0 & 0xFFFFu)) * u0, p0r0, acc0);
-                acc1 = fmaf(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s0 >> 16)) * u0, p0r1, acc1);
-                acc0 = fmaf(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s1 & 0xFFFFu)) * u1, p1r0, acc0);
-                acc1 = fmaf(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s1 >> 16)) * u1, p1r1, acc1);
-            }
+            const uint32_t tt = (uint32_t)(tt0 + i);
+            const uint4 w0 = lds128(st + ti * 1024 + lane * 16);
+            const uint4 w1 = lds128(st + ti * 1024 + 512 + lane * 16);
+            const uint32_t s0 = lds32(sc + ti * 128), s1 = lds32(sc + ti * 128 + 64);
+            const uint4 b0 = lds128(f_base + tt * f_tile);
+            const uint4 b1 = lds128(f_base + tt * f_tile + f_pair);
+            const float2 bu = lds64f(bs_base + tt * 32);
+            constexpr uint32_t HI = 0xF0F0F0F0u;
+            int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+            mma_u8s8_16832(d0[0], d0[1], d0[2], d0[3], w0.x, w0.y, w0.x & HI, w0.y & HI, b0.x, b0.y);
+            mma_u8s8_16832(d1[0], d1[1], d1[2], d1[3], w1.x, w1.y, w1.x & HI, w1.y & HI, b1.x, b1.y);
+            mma_u8s8_16832(d0[0], d0[1], d0[2], d0[3], w0.z, w0.w, w0.z & HI, w0.w & HI, b0.z, b0.w);
+            mma_u8s8_16832(d1[0], d1[1], d1[2], d1[3], w1.z, w1.w, w1.z & HI, w1.w & HI, b1.z, b1.w);
+            const float2 p0 = make_float2((float)(d0[0] * 128 + d0[1]), (float)(d0[2] * 128 + d0[3]));
+            const float2 p1 = make_float2((float)(d1[0] * 128 + d1[1]), (float)(d1[2] * 128 + d1[3]));
+            const float2 su0 = mul2_rn(make_float2(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s0 & 0xFFFFu)),
+                                                   decode_scale<AAEDN_SCALE_F16>((uint16_t)(s0 >> 16))),
+                                       make_float2(bu.x, bu.x));
+            const float2 su1 = mul2_rn(make_float2(decode_scale<AAEDN_SCALE_F16>((uint16_t)(s1 & 0xFFFFu)),
+                                                   decode_scale<AAEDN_SCALE_F16>((uint16_t)(s1 >> 16))),
+                                       make_float2(bu.y, bu.y));
+            acc = fma2_rn(p0, su0, acc);
+            acc = fma2_rn(p1, su1, acc);
+        };
+        if (tiles == CT)
+        {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                tile(i);
         }
+        else
+        {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (4 * wj + i < tiles)
+                    tile(i);
+        }
+        float acc0 = acc.x, acc1 = acc.y;
         __syncwarp();
         if (lane == 0)
             mbar_arrive(r.empty + 8 * stage);
@@ -407,7 +445,7 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
         if (lane == 0)
         {
             __threadfence_block();
-            last = atomicAdd(cnt + (gl % GT_RC), 1u) == (unsigned)(nchunk * GT_GROUP_WARPS) - 1 ? 1u : 0u;
+            last = atomicAdd(cnt + (uint32_t)gl % GT_RC, 1u) == (unsigned)(nchunk * GT_GROUP_WARPS) - 1 ? 1u : 0u;
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last)
@@ -436,7 +474,20 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
             gemv_epilogue<1, EPI, 1>(p, tmp, cta + gl * ncta, lane, post, ecp, gl);
             __syncwarp();
             if (lane == 0)
-                cnt[gl % GT_RC] = 0u;
+                cnt[(uint32_t)gl % GT_RC] = 0u;
+        }
+        qq += GT_GROUPS;
+        stage += GT_GROUPS;
+        if (stage >= NS)
+        {
+            stage -= NS;
+            ++use;
+        }
+        c += GT_GROUPS;
+        while (c >= nchunk)
+        {
+            c -= nchunk;
+            ++gl;
         }
     }
     return !named_bar_or(1, NCT, !ok);
@@ -448,7 +499,8 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
 {
-    const int NS = p.stages > 0 ? p.stages : GT_STAGES;
+    // a multiple of GT_GROUPS, at least GT_STAGES (the host sizes shared memory so)
+    const int NS = p.stages > GT_STAGES ? p.stages / GT_GROUPS * GT_GROUPS : GT_STAGES;
     constexpr int NC = GT_CONSUMERS;
     constexpr int NCT = NC * 32;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -457,7 +509,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const Gemv
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GT_STAGE_BYTES); // full[NS], empty[NS]
     uint8_t* frag = reinterpret_cast<uint8_t*>(bars) + (size_t)NS * 16;
     float* bscale = reinterpret_cast<float*>(frag + (size_t)ntile * GT_FRAG_TILE_BYTES);
-    float* red = bscale + (size_t)ntile * 4;
+    float* red = bscale + (size_t)ntile * 8;
     float* misc = red + GT_RED_BYTES / 4; // [32, 48) per-warp sums of squares, [48, 52) zero
     float* ecache = misc + 64;
     __shared__ int s_abort_mem;

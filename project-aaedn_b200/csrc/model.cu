@@ -370,14 +370,12 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
 {
     if (tiled)
     {
-        static int max_stages = -1;
-        if (max_stages < 0)
-        {
+        static const int max_stages = [] {
+            // a multiple of the consumer groups: 4, 8 (default) or 12
             const char* e = std::getenv("AAEDN_GEMV_STAGES");
-            // 6 by default (7B, one B200: 6 stages 684.7 tok/s, 8: 660-680,
-            // 12: 651-675; deeper rings slow the operand loads that follow)
-            max_stages = e ? std::max(2, std::min(GT_MAX_STAGES, std::atoi(e))) : 6;
-        }
+            const int n = e ? std::max(GT_STAGES, std::min(GT_MAX_STAGES, std::atoi(e))) : 8;
+            return n / GT_GROUPS * GT_GROUPS;
+        }();
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
         GemvParams pp = p;
@@ -673,7 +671,7 @@ static AttnParams attn_params(const aaedn_model* m, uint32_t l, int S)
     a.state = m->state;
     a.max_len = (int)c.max_seq;
     a.max_tok = m->attn_max_tok;
-    a.page_table = m->page_table;
+    a.page_table = nullptr; // the sequence's pages are 0, 1, ... (identity table): no lookup before the K/V loads
     a.page_size = m->page_size;
     a.pstride = hd + 4; // 16-byte rows: the o-proj build reads them as float4
     return a;
@@ -1090,10 +1088,42 @@ static int layers_pass(aaedn_model* m, int n, const RowMap& rm)
         q.e.rope_sin = m->rope_sin;
         if ((rc = tc_gemm(q, st)))
             return rc;
-        attn_prefill_kernel<<<dim3(H, (n + PF_ATTN_WARPS - 1) / PF_ATTN_WARPS), PF_ATTN_WARPS * 32, 0, st>>>(
-            m->pf_q, (size_t)H * hd, L.k, L.v, rm.page_table, m->page_size, H, KV, hd, (int)rm.pos0, n,
-            1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo, rm.row_pos, rm.row_seq, rm.pt_stride);
-        AAEDN_LAUNCH_CHECK("attn_prefill_kernel");
+        if (rm.row_pos)
+        {
+            // batched decode: one query row per sequence, the decode kernel
+            // with a cluster of S splits per (kv head, row), S making about
+            // two CTAs per SM (a power of two, at most 8)
+            int S = std::max(1, std::min(8, 2 * sm_count() / std::max(1, KV * n)));
+            while (S & (S - 1))
+                S &= S - 1;
+            AttnParams a{};
+            a.q = m->pf_q;
+            a.ldq = (size_t)H * hd;
+            a.k = L.k;
+            a.v = L.v;
+            a.out = m->pf_attn;
+            a.ldo = m->kpo;
+            a.n_heads = H;
+            a.n_kv = KV;
+            a.head_dim = hd;
+            a.S = S;
+            a.scale = 1.0f / std::sqrt((float)hd); // src/transformer.cpp:198
+            a.max_len = (int)c.max_seq;
+            a.page_table = rm.page_table;
+            a.page_size = m->page_size;
+            a.row_pos = rm.row_pos;
+            a.row_seq = rm.row_seq;
+            a.pt_stride = rm.pt_stride;
+            if ((rc = attn_launch_cluster(a, dim3(KV, S, n), st, false)))
+                return rc;
+        }
+        else
+        {
+            attn_prefill_kernel<<<dim3(H, (n + PF_ATTN_WARPS - 1) / PF_ATTN_WARPS), PF_ATTN_WARPS * 32, 0, st>>>(
+                m->pf_q, (size_t)H * hd, L.k, L.v, rm.page_table, m->page_size, H, KV, hd, (int)rm.pos0, n,
+                1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo);
+            AAEDN_LAUNCH_CHECK("attn_prefill_kernel");
+        }
         if ((rc = tc_split(m->pf_attn, m->kpo, n, (int)m->kpo, m->pf_ws, st)))
             return rc;
         TcGemmArgs o = base;

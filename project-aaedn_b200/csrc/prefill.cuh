@@ -14,6 +14,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "gemm_tc.h"  // tc_kpos
 #include "gemv_q4.cuh" // block_sum
 
 namespace aaedn_dev
@@ -32,8 +33,8 @@ __global__ void pf_embed_kernel(const uint32_t* __restrict__ tokens, int n, cons
         dst[i] = src[i];
 }
 
-// One CTA per row m < M_pad: parts[q][m][k] (q = 0, 1, 2: the bf16 parts of
-// x * rms * g, src/rmsnorm.cpp:34-43); rows m >= M are zero.
+// One CTA per row m < M_pad: parts[q][m][tc_kpos(k)] (q = 0, 1, 2: the bf16
+// parts of x * rms * g, src/rmsnorm.cpp:34-43); rows m >= M are zero.
 __global__ void __launch_bounds__(256) pf_rmsnorm_split_kernel(const float* __restrict__ x, int D, int M, int M_pad,
                                                                const float* __restrict__ gain, float eps,
                                                                __nv_bfloat16* __restrict__ parts)
@@ -60,9 +61,10 @@ __global__ void __launch_bounds__(256) pf_rmsnorm_split_kernel(const float* __re
         const __nv_bfloat16 h = __float2bfloat16_rn(v);
         const float r1 = v - __bfloat162float(h);
         const __nv_bfloat16 md = __float2bfloat16_rn(r1);
-        p0[k] = h;
-        p0[k + plane] = md;
-        p0[k + 2 * plane] = __float2bfloat16_rn(r1 - __bfloat162float(md));
+        const int kp = tc_kpos(k); // the GEMM operand's K order
+        p0[kp] = h;
+        p0[kp + plane] = md;
+        p0[kp + 2 * plane] = __float2bfloat16_rn(r1 - __bfloat162float(md));
     }
 }
 
@@ -70,9 +72,8 @@ constexpr int PF_ATTN_WARPS = 4;
 
 // Causal attention of rows t < n for query head blockIdx.x: one warp per
 // row. Row t is the token at position pos0 + t of the sequence whose pages
-// page_table lists (a prefill chunk), or (row_pos, row_seq: batched decode)
-// the token at position row_pos[t] of sequence row_seq[t], whose page table
-// starts at page_table + row_seq[t] * pt_stride. Keys are taken 32 at a time,
+// page_table lists (a prefill chunk; batched decode rows use
+// attn_decode_kernel). Keys are taken 32 at a time,
 // lane j scoring key s0 + j against q (held in shared memory); the batch's
 // softmax weights then scale the V rows with lanes over the head dims; the
 // softmax is carried online across batches (running max and sum). fp32,
@@ -80,8 +81,7 @@ constexpr int PF_ATTN_WARPS = 4;
 __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
     const float* __restrict__ q, size_t ldq, const float* __restrict__ k_layer, const float* __restrict__ v_layer,
     const int* __restrict__ page_table_base, int page_size, int n_heads, int n_kv, int hd, int pos0, int n,
-    float scale, float* __restrict__ out, size_t ldo, const int* __restrict__ row_pos = nullptr,
-    const int* __restrict__ row_seq = nullptr, int pt_stride = 0)
+    float scale, float* __restrict__ out, size_t ldo)
 {
     __shared__ __align__(16) float qs[PF_ATTN_WARPS][256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
     if (t >= n)
         return;
     const int kvh = h / (n_heads / n_kv);
-    const int pos = row_pos ? row_pos[t] : pos0 + t, nkeys = pos + 1;
-    const int* page_table = row_seq ? page_table_base + (size_t)row_seq[t] * pt_stride : page_table_base;
+    const int pos = pos0 + t, nkeys = pos + 1;
+    const int* page_table = page_table_base;
     const float* qh = q + (size_t)t * ldq + (size_t)h * hd;
     for (int d = lane; d < hd; d += 32)
         qs[warp][d] = qh[d];
@@ -128,17 +128,35 @@ __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             acc[i] *= corr;
+        // the batch's V rows 8 at a time, every load of a group issued
+        // before its first use; keys in ascending order into each sum
         const int nb = min(32, nkeys - s0);
-        for (int j = 0; j < nb; ++j)
+        for (int j0 = 0; j0 < nb; j0 += 8)
         {
-            const float wj = __shfl_sync(0xffffffffu, w, j);
-            const int sj = s0 + j;
-            const int page = page_table[sj / page_size];
-            const float* vr = v_layer + (((size_t)page * n_kv + kvh) * page_size + (sj % page_size)) * hd;
+            float wj[8], vv[8][8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (i < dpl)
-                    acc[i] = fmaf(wj, vr[lane + 32 * i], acc[i]);
+            for (int u = 0; u < 8; ++u)
+            {
+                const int j = j0 + u;
+                wj[u] = __shfl_sync(0xffffffffu, w, j & 31);
+                const float* vr = nullptr;
+                if (j < nb)
+                {
+                    const int sj = s0 + j;
+                    const int page = page_table[sj / page_size];
+                    vr = v_layer + (((size_t)page * n_kv + kvh) * page_size + (sj % page_size)) * hd;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    vv[u][i] = (vr && i < dpl) ? vr[lane + 32 * i] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j0 + u < nb)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (i < dpl)
+                            acc[i] = fmaf(wj[u], vv[u][i], acc[i]);
         }
     }
     const float inv = 1.0f / lrun;

@@ -1,17 +1,20 @@
 """The arithmetic of the decode GEMV's integer engine (gemv_tiled_i8_kernel),
 restated with numpy on the CPU: the activation of each 32-element block is
-scaled to y = x * (127 / max|x|) in fp32, each y becomes the integer
+scaled to y = x * (119 / max|x|) in fp32, each y becomes the integer
 Y = rint(y * 2^21) (odd elements: rint(y * 2^17), the high nibble carries a
-factor 16), Y is split into four balanced base-128 digits, the 4-bit codes
-meet the digits in exact integer dot products (the tensor-core MMAs: each
-covers two blocks and gives all four digit sums of both), and the digit
-pairs' sums are scaled in fp32 by the lanes that hold them, digits (0, 1) at
-weight 1 and digits (2, 3) at 2^-14, then added, as the kernel does.
-This pins the engine's precision: the error of an element is below
-|w| * max|x of its block| * 1e-7 (the digits keep 2^-22 of the block's scale,
-odd elements 2^-18 of y / 16), plus fp32 accumulation; on the normally
-distributed activations of the GPU tests that is far inside their bound of
-2e-5 * sum|x * w|. No GPU."""
+factor 16). Per code byte (even element in the low nibble, odd in the high)
+the tensor-core MMA meets the raw byte lo + 16 hi with the digits of the even
+element's Y and the high nibble 16 hi with the digits of Yodd - Yeven, so
+that the sum is lo * Yeven + 16 hi * Yodd; both are split into four balanced
+base-128 digits, the dot products are exact integers (each MMA covers two
+blocks and gives all four digit sums of both), and the digit pairs' sums are
+converted to fp32 (rounded to 24 bits), scaled by the lanes that hold them,
+digits (0, 1) at weight 1 and digits (2, 3) at 2^-14, then added, as the
+kernel does. This pins the engine's precision: the error of an element is
+below |w| * max|x of its block| * 1e-7 (the digits keep 2^-21 of the block's
+scale, odd elements 2^-17 of y / 16), plus fp32 rounding of the partial sums
+and their accumulation; on the normally distributed activations of the GPU
+tests that is far inside their bound of 2e-5 * sum|x * w|. No GPU."""
 import numpy as np
 import pytest
 
@@ -37,14 +40,16 @@ def engine_dot(codes, scales, x):
         xb = x[32 * b:32 * b + 32].astype(np.float32)
         cb = codes[32 * b:32 * b + 32].astype(np.int64)
         mx = np.float32(np.abs(xb).max())
-        inv = np.float32(127.0) / mx if mx > 0 else np.float32(0)
+        inv = np.float32(119.0) / mx if mx > 0 else np.float32(0)
         y = (xb * inv).astype(np.float32)
         mult = np.where(np.arange(32) % 2 == 0, np.float32(2.0 ** 21), np.float32(2.0 ** 17)).astype(np.float32)
         Y = np.rint((y * mult).astype(np.float32)).astype(np.int64)
-        a = np.where(np.arange(32) % 2 == 0, cb, 16 * cb)  # low nibble c, high nibble 16 c
-        d0, d1, d2, d3 = _digits(Y)
-        p0, p1, q0, q1 = (int(np.dot(a, d)) for d in (d0, d1, d2, d3))
-        bsc = np.float32(mx / np.float32(127.0 * 128.0))
+        ye, yo = Y[0::2], Y[1::2]
+        raw = cb[0::2] + 16 * cb[1::2]  # the code byte as the MMA reads it
+        hi16 = 16 * cb[1::2]            # its high nibble, masked
+        de, dd = _digits(ye), _digits(yo - ye)
+        p0, p1, q0, q1 = (int(np.dot(raw, de[k]) + np.dot(hi16, dd[k])) for k in range(4))
+        bsc = np.float32(mx / np.float32(119.0 * 128.0))
         sw = np.float32(np.float16(scales[b]).astype(np.float32))
         acc_hi = np.float32(acc_hi + np.float32(sw * bsc) * np.float32(p0 * 128 + p1))
         acc_lo = np.float32(acc_lo + np.float32(sw * np.float32(bsc * np.float32(1.0 / 16384.0))) *
@@ -81,8 +86,15 @@ def test_engine_dot_error_bound(seed, dist):
 
 
 def test_digits_are_balanced_and_exact():
+    """Digits of Yeven (|y| <= 119) and of Yodd - Yeven (up to 119 * 17 / 16
+    times 2^21) fit signed bytes, and the digit sums the kernel forms
+    (c0 * 128 + c1 over a block's 16 bytes) stay inside int32."""
     rng = np.random.default_rng(9)
-    Y = rng.integers(-(127 << 21), (127 << 21) + 1, 100000).astype(np.int64)
+    lim = (119 << 21) + (119 << 17)
+    Y = np.concatenate([rng.integers(-lim, lim + 1, 100000), [lim, -lim, 119 << 21, -(119 << 21)]]).astype(np.int64)
     d0, d1, d2, d3 = _digits(Y)
     assert np.array_equal(d0 * (1 << 21) + d1 * (1 << 14) + d2 * (1 << 7) + d3, Y)
     assert np.abs(d0).max() <= 127 and max(np.abs(d).max() for d in (d1, d2, d3)) <= 64
+    c0 = 16 * 255 * 119 + 16 * 240 * 127
+    c1 = 16 * 255 * 64 + 16 * 240 * 64
+    assert c0 * 128 + c1 < 2 ** 31

@@ -132,6 +132,7 @@ def test_7b_width_two_layers_vs_oracle():
     {"AAEDN_ATTN_CLUSTER": "16"},             # clusters of 16 splits (non-portable size)
     {"AAEDN_PDL": "0", "AAEDN_L2HINT": "0"},  # plain launches, no L2 policy
     {"AAEDN_GEMV_STAGES": "12"},              # the deepest ring of the decode GEMV
+    {"AAEDN_GEMV_STAGES": "4"},               # the shallowest
 ])
 def test_launch_options_same_tokens(env, monkeypatch):
     """The model's launch options (read when it is created) change timing
