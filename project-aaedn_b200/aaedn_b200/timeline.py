@@ -48,12 +48,45 @@ def layer_table(stamps, grid, n_layers):
     return {n: {key: float(np.mean([r[key] for r in v])) / 1e3 for key in v[0]} for n, v in rows.items() if v}
 
 
+CHUNK_CTAS, CHUNKS = 8, 24  # per-chunk stamps of a tiled GEMV's first CTAs
+
+
+def chunk_view(stamps, grid, layer, events_per_cta, chunk_base, n_kv):
+    """Per GEMV of `layer`: for its first CTAs, entry / wait / ready / exit and
+    each chunk's consumer start-end; for the attention, the CTAs of kv head
+    0's splits (one cluster). us from the previous kernel's last exit."""
+    st = stamps.astype(np.int64)
+    flat = st.reshape(st.shape[0], -1)
+    lines = []
+    ka = 5 * layer + 1
+    prev = st[ka - 1, :int(grid[ka - 1]), 3].max()
+    lines.append(f"attention (layer {layer}), kv head 0: split entry wait ready exit")
+    for sp in range(int(grid[ka]) // n_kv):
+        ev = (st[ka, sp * n_kv] - prev) / 1e3
+        lines.append(f"  split {sp}: {ev[0]:.2f} {ev[1]:.2f} {ev[2]:.2f} {ev[3]:.2f}")
+    for j, name in ((0, "qkv"), (2, "o"), (3, "gate_up"), (4, "down")):
+        k = 5 * layer + j
+        g = int(grid[k])
+        if g == 0:
+            continue
+        prev = st[k - 1, :int(grid[k - 1]), 3].max()
+        lines.append(f"{name} (layer {layer}):")
+        for cta in range(min(4, g)):
+            ev = flat[k, cta * events_per_cta:cta * events_per_cta + 4] - prev
+            ch = flat[k, chunk_base + cta * 2 * CHUNKS:chunk_base + (cta + 1) * 2 * CHUNKS].reshape(CHUNKS, 2)
+            spans = " ".join(f"{(a - prev) / 1e3:.2f}-{(b - prev) / 1e3:.2f}" for a, b in ch if a > 0)
+            lines.append(f"  cta {cta}: entry {ev[0] / 1e3:.2f} wait {ev[2] / 1e3:.2f} ready {ev[1] / 1e3:.2f} "
+                         f"exit {ev[3] / 1e3:.2f} | chunks {spans}")
+    return "\n".join(lines)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--decode", type=int, default=200)
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--chunks", type=int, default=-1, help="layer whose per-chunk stamps to print")
     a = ap.parse_args(argv)
     cfg = dict(LLAMA2_7B, n_layers=a.layers)
     m = Model(cfg)
@@ -75,6 +108,8 @@ def main(argv=None):
         if n in tab:
             print(f"| {n} | " + " | ".join(f"{tab[n].get(k, float('nan')):.2f}" for k in keys) + " |")
     print(f"| layer | {sum(tab[n]['span'] for n in tab):.2f} | | | | | | |")
+    if a.chunks >= 1:
+        print(chunk_view(stamps, grid, a.chunks, 4, 160 * 4, cfg["n_kv_heads"]))
 
 
 if __name__ == "__main__":

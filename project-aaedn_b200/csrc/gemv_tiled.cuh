@@ -496,8 +496,14 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
 // The decode GEMV kernel: one producer warp streaming the CTA's chunks, 16
 // consumer warps building the integer operand together, then consuming the
 // chunks four at a time.
+// At most GT_REGS registers a thread: 17 warps x 88 leave room on the SM for
+// one attention CTA (8 warps x 64), so the kernels on either side of the
+// attention overlap with it (its loads start while the qkv GEMV drains, the
+// o GEMV's weights stream while it runs).
+constexpr int GT_REGS = 88;
+
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(GT_THREADS, 1) gemv_tiled_i8_kernel(const GemvParams p)
+__global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
 {
     // a multiple of GT_GROUPS, at least GT_STAGES (the host sizes shared memory so)
     const int NS = p.stages > GT_STAGES ? p.stages / GT_GROUPS * GT_GROUPS : GT_STAGES;

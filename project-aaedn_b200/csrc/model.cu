@@ -432,6 +432,9 @@ int set_model_kernel_attrs()
         rc = set_gemv_attrs<PRO_RMSNORM, EPI_SWIGLU>();
     if (!rc)
         rc = set_gemv_attrs<PRO_PLAIN, EPI_TP_PUSH>();
+    if (!rc && cudaFuncSetAttribute(attn_prefill_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)attn_prefill_tiled_smem_bytes()) != cudaSuccess)
+        rc = set_error(AAEDN_ECUDA, "attn_prefill_tiled_kernel smem attribute failed");
     return rc;
 }
 
@@ -1117,6 +1120,14 @@ static int layers_pass(aaedn_model* m, int n, const RowMap& rm)
             if ((rc = attn_launch_cluster(a, dim3(KV, S, n), st, false)))
                 return rc;
         }
+        else if (hd <= 128 && hd % 4 == 0 && m->page_size % PFT_K == 0)
+        {
+            attn_prefill_tiled_kernel<<<dim3(H, (n + PFT_Q - 1) / PFT_Q), PFT_WARPS * 32,
+                                        attn_prefill_tiled_smem_bytes(), st>>>(
+                m->pf_q, (size_t)H * hd, L.k, L.v, rm.page_table, m->page_size, H, KV, hd, (int)rm.pos0, n,
+                1.0f / std::sqrt((float)hd), m->pf_attn, m->kpo);
+            AAEDN_LAUNCH_CHECK("attn_prefill_tiled_kernel");
+        }
         else
         {
             attn_prefill_kernel<<<dim3(H, (n + PF_ATTN_WARPS - 1) / PF_ATTN_WARPS), PF_ATTN_WARPS * 32, 0, st>>>(
@@ -1331,8 +1342,11 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         const size_t qkv_rows = (size_t)(c.n_heads + 2 * c.n_kv_heads) * hd;
         const bool ok = m->tp_size == 1 && m->tiled && tiles_ok(qkv_rows, D) && tiles_ok(D, m->kpo) &&
                         tiles_ok(2 * F, D) && tiles_ok(D, m->kpd) && hd % 32 == 0 && hd <= 256;
+        // 1024 tokens a chunk by default: GEMMs of M = 1024 keep the tensor
+        // pipe busy (M = 2048: 58 % of the bf16 peak in the five-product
+        // form, M = 128: 32 %) for about 200 MB of chunk buffers at 7B
         const char* pe = std::getenv("AAEDN_PREFILL_ROWS");
-        const int rows = pe ? std::atoi(pe) : 256;
+        const int rows = pe ? std::atoi(pe) : 1024;
         m->pf_rows = ok && rows > 1 ? (int)std::min<uint32_t>((uint32_t)rows, c.max_seq) : 0;
         if (max_seqs)
         {

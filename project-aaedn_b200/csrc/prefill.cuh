@@ -168,6 +168,160 @@ __global__ void __launch_bounds__(PF_ATTN_WARPS * 32) attn_prefill_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Causal attention of a prefill chunk, tiled: CTA (query head h, 64 query
+// rows), 8 warps of 8 rows each; the keys come in tiles of 32 (K and V rows
+// of one page, copied with cp.async into padded shared memory, the next tile
+// in flight while this one is used), so each K/V row is read once per 64
+// query rows instead of once per row. A warp scores its 8 rows against the
+// tile with lanes over keys (q rows broadcast from shared memory), carries
+// the online softmax per row (running max warp-wide, each lane its share of
+// the running sum), then accumulates P V with lanes over head dims (4 each).
+// fp32, expf (D4); head_dim a multiple of 4, <= 128; page_size a multiple
+// of 32. out[t][h * hd + d].
+// ---------------------------------------------------------------------------
+constexpr int PFT_Q = 64, PFT_K = 32, PFT_WARPS = 8, PFT_RW = PFT_Q / PFT_WARPS, PFT_LD = 128 + 4;
+
+inline size_t attn_prefill_tiled_smem_bytes() { return ((size_t)PFT_Q * PFT_LD + 4 * PFT_K * PFT_LD + PFT_WARPS * PFT_RW * PFT_K) * 4; }
+
+__global__ void __launch_bounds__(PFT_WARPS * 32, 2) attn_prefill_tiled_kernel(
+    const float* __restrict__ q, size_t ldq, const float* __restrict__ k_layer, const float* __restrict__ v_layer,
+    const int* __restrict__ page_table, int page_size, int n_heads, int n_kv, int hd, int pos0, int n, float scale,
+    float* __restrict__ out, size_t ldo)
+{
+    extern __shared__ __align__(16) float pft[];
+    float* Qs = pft;                                  // [64][LD]
+    float* KV = Qs + PFT_Q * PFT_LD;                  // [2 buffers][K, V][32][LD]
+    float* Ps = KV + 4 * PFT_K * PFT_LD;              // [8 warps][8 rows][32]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.x, kvh = h / (n_heads / n_kv), r0 = blockIdx.y * PFT_Q;
+    const int hd4 = hd >> 2;
+    // the chunk's rows r0..: q into shared memory (rows past n are zero)
+    for (int i = tid; i < PFT_Q * hd4; i += PFT_WARPS * 32)
+    {
+        const int r = i / hd4, c = i - r * hd4;
+        const float4 v = r0 + r < n ? *reinterpret_cast<const float4*>(q + (size_t)(r0 + r) * ldq + (size_t)h * hd + 4 * c)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(Qs + r * PFT_LD + 4 * c) = v;
+    }
+    const int last_pos = pos0 + min(n, r0 + PFT_Q) - 1; // keys 0..last_pos
+    const int ntiles = last_pos / PFT_K + 1;
+    auto issue = [&](int tile, int buf) {
+        const int k0 = tile * PFT_K;
+        const int page = page_table[k0 / page_size];
+        const size_t base = (((size_t)page * n_kv + kvh) * page_size + (k0 % page_size)) * hd;
+        float* Kb = KV + (size_t)buf * 2 * PFT_K * PFT_LD;
+        float* Vb = Kb + PFT_K * PFT_LD;
+        for (int i = tid; i < PFT_K * hd4; i += PFT_WARPS * 32)
+        {
+            const int r = i / hd4, c = i - r * hd4;
+            const uint32_t ok = k0 + r <= last_pos ? 16u : 0u; // rows past the last key: zero
+            cp_async_16(Kb + r * PFT_LD + 4 * c, k_layer + base + (size_t)r * hd + 4 * c, ok);
+            cp_async_16(Vb + r * PFT_LD + 4 * c, v_layer + base + (size_t)r * hd + 4 * c, ok);
+        }
+        cp_async_commit();
+    };
+    issue(0, 0);
+    float m[PFT_RW], l[PFT_RW];
+    float4 acc[PFT_RW];
+#pragma unroll
+    for (int i = 0; i < PFT_RW; ++i)
+    {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const int wrow0 = r0 + warp * PFT_RW; // this warp's first row
+    float* Pw = Ps + warp * PFT_RW * PFT_K;
+    for (int t = 0; t < ntiles; ++t)
+    {
+        if (t + 1 < ntiles)
+        {
+            issue(t + 1, (t + 1) & 1);
+            cp_async_wait<1>();
+        }
+        else
+            cp_async_wait<0>();
+        __syncthreads();
+        const float* Kb = KV + (size_t)(t & 1) * 2 * PFT_K * PFT_LD;
+        const float* Vb = Kb + PFT_K * PFT_LD;
+        const int kpos = t * PFT_K + lane;
+        // rows of this warp that see any key of the tile (warp-uniform)
+        if (pos0 + wrow0 + PFT_RW - 1 >= t * PFT_K && wrow0 < n)
+        {
+            float sc[PFT_RW];
+#pragma unroll
+            for (int i = 0; i < PFT_RW; ++i)
+                sc[i] = 0.0f;
+            const float* kr = Kb + lane * PFT_LD;
+            const float* qw = Qs + (warp * PFT_RW) * PFT_LD;
+            for (int c = 0; c < hd4; ++c)
+            {
+                const float4 kf = *reinterpret_cast<const float4*>(kr + 4 * c);
+#pragma unroll
+                for (int i = 0; i < PFT_RW; ++i)
+                {
+                    const float4 qf = *reinterpret_cast<const float4*>(qw + i * PFT_LD + 4 * c);
+                    sc[i] = fmaf(qf.x, kf.x, sc[i]);
+                    sc[i] = fmaf(qf.y, kf.y, sc[i]);
+                    sc[i] = fmaf(qf.z, kf.z, sc[i]);
+                    sc[i] = fmaf(qf.w, kf.w, sc[i]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < PFT_RW; ++i)
+            {
+                const int rpos = pos0 + wrow0 + i;
+                const bool live = wrow0 + i < n && kpos <= rpos;
+                const float s = live ? sc[i] * scale : -INFINITY; // src/attention.cpp:36-41
+                const float bm = warp_max(s);
+                const float mn = fmaxf(m[i], bm);
+                float p = 0.0f, corr = 1.0f;
+                if (mn != -INFINITY)
+                {
+                    corr = (m[i] == -INFINITY) ? 0.0f : expf(m[i] - mn);
+                    p = live ? expf(s - mn) : 0.0f;
+                    m[i] = mn;
+                }
+                l[i] = l[i] * corr + p;
+                acc[i].x *= corr;
+                acc[i].y *= corr;
+                acc[i].z *= corr;
+                acc[i].w *= corr;
+                Pw[i * PFT_K + lane] = p;
+            }
+            __syncwarp();
+            if (lane < hd4)
+                for (int j = 0; j < PFT_K; ++j)
+                {
+                    const float4 vf = *reinterpret_cast<const float4*>(Vb + j * PFT_LD + 4 * lane);
+#pragma unroll
+                    for (int i = 0; i < PFT_RW; ++i)
+                    {
+                        const float pj = Pw[i * PFT_K + j];
+                        acc[i].x = fmaf(pj, vf.x, acc[i].x);
+                        acc[i].y = fmaf(pj, vf.y, acc[i].y);
+                        acc[i].z = fmaf(pj, vf.z, acc[i].z);
+                        acc[i].w = fmaf(pj, vf.w, acc[i].w);
+                    }
+                }
+            __syncwarp();
+        }
+        __syncthreads(); // the buffer is refilled two tiles on
+    }
+#pragma unroll
+    for (int i = 0; i < PFT_RW; ++i)
+    {
+        const float lt = warp_sum(l[i]);
+        if (wrow0 + i < n && lane < hd4)
+        {
+            const float inv = 1.0f / lt;
+            *reinterpret_cast<float4*>(out + (size_t)(wrow0 + i) * ldo + (size_t)h * hd + 4 * lane) =
+                make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // lm_head over several rows (batched decode): the final RMSNorm of each row
 // (src/transformer.cpp:230), the fp32 product with the [vocab][dim] lm_head
 // (:232-238) and each row's greedy token (argmax, ties to the lowest id).
