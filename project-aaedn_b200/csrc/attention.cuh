@@ -420,71 +420,77 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 
 // ---------------------------------------------------------------------------
 // Decode attention as clusters: the S splits of one kv head are one cluster
-// (grid (n_kv, S), cluster (1, S)), CTA rank = split.
-//   1. Before waiting for the kernel that writes q and the current K/V row,
-//      each warp requests the K and V rows of up to TB of its tokens
-//      (t0 + warp + 8 j) straight into registers; no other load precedes
-//      them (a null page table is the identity, so not even a page lookup).
-//      The position is read early and read again after the wait; if it
-//      moved (the step before had not finished advancing it) the rows are
-//      requested again.
+// (grid (n_kv, S, rows), cluster (1, S)), CTA rank = split.
+//   1. Split s takes tokens s, s + S, s + 2S, ...; warp w of it the tokens
+//      s + S (w + 8 j). The rows of its first TB tokens do not depend on the
+//      position, so each warp requests them (K and V straight into
+//      registers) before waiting for the kernel that writes q and the
+//      current K/V row: for the model's one sequence (identity page table)
+//      any token below the cache capacity, for batched rows (launched after
+//      their positions are written) below the row's length. After the wait
+//      the position bounds the tokens: rows at or past it are zeroed and
+//      masked, the current row is requested again.
 //   2. Online softmax per warp, as attn_item.
-//   3. Each warp rescales its sums to the CTA's running max, the CTA adds
-//      them in warp order: one partial (sums, max, denominator) per CTA in
-//      its shared memory.
-//   4. After a cluster barrier every CTA merges a slice of the outputs over
-//      the S partials (distributed shared memory, split order, one round of
-//      loads), then a second barrier keeps each CTA's shared memory alive
-//      until the others have read it.
+//   3. Each warp rescales its sums to the CTA's running max and the CTA adds
+//      them in warp order: one partial (sums, max, denominator) per CTA,
+//      which it writes into its slot of every cluster CTA's shared memory.
+//   4. One cluster barrier; then every CTA merges a slice of the outputs over
+//      the S partials from its own shared memory, in split order.
 // ---------------------------------------------------------------------------
+
 // MHA at head_dim <= 128: 64 registers, four CTAs per SM (a cluster then
 // needs fewer free SMs of a GPC while the kernel before drains); wider
 // groups keep their q and V sums for more heads in registers.
 constexpr int attn_decode_min_blocks(int G, int HDM) { return (G == 1 && HDM == 128) ? 4 : (G * HDM >= 1024 ? 1 : 2); }
 
-// Shared memory: wm[8][G], wl[8][G], wacc[8][G][hd], then the CTA's partial
-// [G][hd + 2] (sums, max, denominator).
-__host__ __device__ inline size_t attn_decode_smem_bytes(int G, int hd)
+// Shared memory: wm[8][G], wl[8][G], wacc[8][G][hd], then the S partials
+// [S][G][hd + 4] (sums, max, denominator; 16-byte rows).
+__host__ __device__ inline size_t attn_decode_smem_bytes(int G, int hd, int S)
 {
-    return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd + (size_t)G * (hd + 2)) * 4;
+    return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd + (size_t)S * G * (hd + 4)) * 4;
 }
 
-template <int G, int HDM>
+__device__ __forceinline__ void st_dsmem_f32(uint32_t laddr, uint32_t rank, float v)
+{
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(laddr), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+template <int G, int HDM, bool CL = true>
 __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) attn_decode_kernel(const AttnParams p)
 {
-    constexpr int NCH = HDM / 128;                // float4 slices per lane
+    constexpr int NCH = HDM / 128;                   // float4 slices per lane
     constexpr int TB = (G == 2 && NCH == 1) ? 8 : 4; // tokens per warp in flight
     extern __shared__ __align__(16) float asmem[];
     pdl_launch_dependents();
     const int kvh = blockIdx.x, split = blockIdx.y, S = (int)gridDim.y, z = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hd = p.head_dim, hd4 = hd >> 2;
-    // this row's sequence: its page table (null: the identity) and length
+    const int hd = p.head_dim, hd4 = hd >> 2, ps = hd + 4;
+    // this row's sequence: its page table (null: the identity)
     const int* pt = p.page_table && p.row_seq ? p.page_table + (size_t)p.row_seq[z] * p.pt_stride : p.page_table;
-    auto row_len = [&]() { return p.row_pos ? min(p.row_pos[z] + 1, p.max_len) : attn_len<1>(p); };
     auto row_of = [&](int t) -> size_t {
         const int page = pt ? pt[t / p.page_size] : t / p.page_size;
         return (((size_t)page * p.n_kv + kvh) * p.page_size + (t % p.page_size)) * hd;
     };
+    auto tok = [&](int j) { return split + S * (warp + ATTN_WARPS * j); }; // this warp's j-th token
     const float* qz = p.q + (size_t)z * p.ldq;
     float* outz = p.out + (size_t)z * p.ldo;
-    float* wm = asmem;                 // [8][G]
-    float* wl = wm + ATTN_WARPS * G;   // [8][G]
-    float* wacc = wl + ATTN_WARPS * G; // [8][G][hd]
-    float* cp = wacc + (size_t)ATTN_WARPS * G * hd; // [G][hd + 2]
+    float* wm = asmem;                              // [8][G]
+    float* wl = wm + ATTN_WARPS * G;                // [8][G]
+    float* wacc = wl + ATTN_WARPS * G;              // [8][G][hd]
+    float* parts = wacc + (size_t)ATTN_WARPS * G * hd; // [S][G][hd + 4]
     const int lin = split * gridDim.x + kvh;
     if (tid == 0)
         trace_mark(p.trace, lin, 0);
 
-    int L = row_len(), t0, t1;
-    attn_range(L, split, S, t0, t1);
     float4 kr[TB][NCH], vr[TB][NCH];
-    auto load = [&](int tb0, int skip) {
+    auto load = [&](int jb, int lim) {
 #pragma unroll
         for (int j = 0; j < TB; ++j)
         {
-            const int t = tb0 + ATTN_WARPS * j;
-            const bool live = t < t1 && t != skip;
+            const int t = tok(jb + j);
+            const bool live = t < lim;
             const size_t ro = live ? row_of(t) : 0;
 #pragma unroll
             for (int c = 0; c < NCH; ++c)
@@ -503,12 +509,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
             }
         }
     };
-    if (t0 + warp < t1)
-        load(t0 + warp, L - 1); // every row but the current position's
+    const int lim0 = p.row_pos ? min(p.row_pos[z] + 1, p.max_len) : p.max_len;
+    load(0, lim0);
     pdl_wait();
     if (tid == 0)
         trace_mark(p.trace, lin, 1);
-    // q, the current row and the position read again, all in flight at once
     float4 qv[G][NCH];
 #pragma unroll
     for (int gi = 0; gi < G; ++gi)
@@ -519,33 +524,34 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
             qv[gi][c] = ch < hd4 ? __ldcg(reinterpret_cast<const float4*>(qz + ((size_t)kvh * G + gi) * hd) + ch)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+    const int L = p.row_pos ? lim0 : attn_len<1>(p);
+    // rows at or past L hold no token of this sequence (zero them: masked
+    // weights times stale values must not give NaN); the current row L - 1
+    // was written by the kernel before
+#pragma unroll
+    for (int j = 0; j < TB; ++j)
     {
-        const int tcur = L - 1;
+        const int t = tok(j);
+        if (t >= L)
 #pragma unroll
-        for (int j = 0; j < TB; ++j)
-            if (t0 + warp + ATTN_WARPS * j == tcur && tcur < t1)
+            for (int c = 0; c < NCH; ++c)
             {
-                const size_t ro = row_of(tcur);
+                kr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        else if (t == L - 1)
+        {
+            const size_t ro = row_of(t);
 #pragma unroll
-                for (int c = 0; c < NCH; ++c)
+            for (int c = 0; c < NCH; ++c)
+            {
+                const int ch = lane + 32 * c;
+                if (ch < hd4)
                 {
-                    const int ch = lane + 32 * c;
-                    if (ch < hd4)
-                    {
-                        kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
-                        vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
-                    }
+                    kr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.k + ro) + ch);
+                    vr[j][c] = __ldcg(reinterpret_cast<const float4*>(p.v + ro) + ch);
                 }
             }
-        const int Lw = row_len();
-        if (Lw != L)
-        {
-            // the position was read before the step before had finished
-            // advancing it: take the range again with every row current
-            L = Lw;
-            attn_range(L, split, S, t0, t1);
-            if (t0 + warp < t1)
-                load(t0 + warp, -1);
         }
     }
     float m[G], l[G];
@@ -559,10 +565,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
         for (int c = 0; c < NCH; ++c)
             acc[gi][c] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int tb0 = t0 + warp; tb0 < t1; tb0 += ATTN_WARPS * TB)
+    for (int jb = 0; tok(jb) < L; jb += TB)
     {
-        if (tb0 != t0 + warp)
-            load(tb0, -1);
+        if (jb)
+            load(jb, L);
 #pragma unroll
         for (int gi = 0; gi < G; ++gi)
         {
@@ -590,7 +596,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
 #pragma unroll
             for (int j = 0; j < TB; ++j)
             {
-                sj[j] = (tb0 + ATTN_WARPS * j < t1) ? sj[j] * p.scale : -INFINITY; // src/attention.cpp:42
+                sj[j] = tok(jb + j) < L ? sj[j] * p.scale : -INFINITY; // src/attention.cpp:42
                 bm = fmaxf(bm, sj[j]);
             }
             const float mn = fmaxf(m[gi], bm);
@@ -610,7 +616,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
 #pragma unroll
             for (int j = 0; j < TB; ++j)
             {
-                const float e = expf(sj[j] - mn); // 0 for dead slots
+                const float e = expf(sj[j] - mn); // 0 for masked slots
                 l[gi] += e;
 #pragma unroll
                 for (int c = 0; c < NCH; ++c)
@@ -626,7 +632,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
     if (tid == 0)
         trace_mark(p.trace, lin, 2);
 
-    // 3. the CTA's partial: warps rescaled to the CTA max, added in warp order
+    // 3. the CTA's partial (warps rescaled to the CTA max, added in warp
+    // order) into slot `split` of every CTA of the cluster
     if (lane == 0)
 #pragma unroll
         for (int gi = 0; gi < G; ++gi)
@@ -650,59 +657,129 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
                 reinterpret_cast<float4*>(wacc + ((size_t)warp * G + gi) * hd)[ch] =
                     make_float4(acc[gi][c].x * f, acc[gi][c].y * f, acc[gi][c].z * f, acc[gi][c].w * f);
         }
-        if (tid == gi)
-            cp[gi * (hd + 2) + hd] = M;
     }
     __syncthreads();
-    for (int i = tid; i < G * (hd + 1); i += ATTN_THREADS)
+    for (int i = tid; i < G * (hd + 2); i += ATTN_THREADS)
     {
-        const int gi = i / (hd + 1), d = i - gi * (hd + 1);
-        float sum = 0.0f;
+        const int gi = i / (hd + 2), d = i - gi * (hd + 2);
+        float v;
         if (d < hd)
+        {
+            v = 0.0f;
             for (int w = 0; w < ATTN_WARPS; ++w)
-                sum += wacc[((size_t)w * G + gi) * hd + d];
+                v += wacc[((size_t)w * G + gi) * hd + d];
+        }
+        else if (d == hd)
+        {
+            v = -INFINITY;
+            for (int w = 0; w < ATTN_WARPS; ++w)
+                v = fmaxf(v, wm[w * G + gi]);
+        }
         else
+        {
+            v = 0.0f;
             for (int w = 0; w < ATTN_WARPS; ++w)
-                sum += wl[w * G + gi];
-        cp[gi * (hd + 2) + (d < hd ? d : hd + 1)] = sum;
+                v += wl[w * G + gi];
+        }
+        if constexpr (CL)
+        {
+            const uint32_t la = smem_addr(parts + ((size_t)split * G + gi) * ps + d);
+            for (int r = 0; r < S; ++r)
+                st_dsmem_f32(la, (uint32_t)r, v);
+        }
+        else
+            p.part[(((size_t)z * p.n_heads + kvh * G + gi) * S + split) * ps + d] = v;
     }
 
-    // 4. the cluster merge, a slice of the G * hd outputs per CTA
-    cluster_sync_all();
+    if constexpr (!CL)
     {
-        const int n = G * hd, per = (n + S - 1) / S, i = split * per + tid;
-        if (tid < per && i < n)
+        // 4'. the last CTA of this (row, kv head) merges the S partials from
+        // global memory, splits in order
+        __shared__ unsigned s_last;
+        __threadfence();
+        __syncthreads();
+        unsigned* ctr = p.counters + (size_t)z * p.n_kv + kvh;
+        if (tid == 0)
+            s_last = atomicAdd(ctr, 1u) == (unsigned)S - 1 ? 1u : 0u;
+        __syncthreads();
+        if (!s_last)
+        {
+            if (tid == 0)
+                trace_mark(p.trace, lin, 3);
+            return;
+        }
+        __threadfence();
+        for (int i = tid; i < G * hd; i += ATTN_THREADS)
         {
             const int gi = i / hd, d = i - gi * hd;
-            const uint32_t cb = smem_addr(cp + gi * (hd + 2));
-            constexpr int SM = 16;
-            float mv[SM], vv[SM], lv[SM];
-#pragma unroll
-            for (int r = 0; r < SM; ++r)
-                if (r < S)
-                {
-                    mv[r] = ld_dsmem_f32(cb + hd * 4, r);
-                    vv[r] = ld_dsmem_f32(cb + d * 4, r);
-                    lv[r] = ld_dsmem_f32(cb + (hd + 1) * 4, r);
-                }
+            const float* pb = p.part + (((size_t)z * p.n_heads + kvh * G + gi) * S) * ps;
+            // splits in batches of 8 with the loads of a batch issued together
+            constexpr int SU = 8;
             float M = -INFINITY;
+            for (int sb = 0; sb < S; sb += SU)
+            {
+                float mv[SU];
 #pragma unroll
-            for (int r = 0; r < SM; ++r)
-                if (r < S)
-                    M = fmaxf(M, mv[r]);
+                for (int u = 0; u < SU; ++u)
+                    mv[u] = sb + u < S ? __ldcg(pb + (size_t)(sb + u) * ps + hd) : -INFINITY;
+#pragma unroll
+                for (int u = 0; u < SU; ++u)
+                    M = fmaxf(M, mv[u]);
+            }
             float num = 0.0f, den = 0.0f;
+            for (int sb = 0; sb < S; sb += SU)
+            {
+                float mv[SU], vv[SU], lv[SU];
 #pragma unroll
-            for (int r = 0; r < SM; ++r)
-                if (r < S)
+                for (int u = 0; u < SU; ++u)
                 {
-                    const float w = (mv[r] == -INFINITY) ? 0.0f : expf(mv[r] - M);
-                    num = fmaf(vv[r], w, num);
-                    den = fmaf(lv[r], w, den);
+                    const bool live = sb + u < S;
+                    const float* pv = pb + (size_t)(sb + u) * ps;
+                    mv[u] = live ? __ldcg(pv + hd) : -INFINITY;
+                    vv[u] = live ? __ldcg(pv + d) : 0.0f;
+                    lv[u] = live ? __ldcg(pv + hd + 1) : 0.0f;
                 }
+#pragma unroll
+                for (int u = 0; u < SU; ++u)
+                {
+                    const float w = (mv[u] == -INFINITY) ? 0.0f : expf(mv[u] - M);
+                    num = fmaf(vv[u], w, num);
+                    den = fmaf(lv[u], w, den);
+                }
+            }
+            outz[(size_t)(kvh * G + gi) * hd + d] = den > 0.0f ? num / den : 0.0f;
+        }
+        if (tid == 0)
+        {
+            *ctr = 0u;
+            trace_mark(p.trace, lin, 3);
+        }
+        return;
+    }
+
+    // 4. one barrier (the partials written everywhere), then a slice of the
+    // outputs per CTA from its own shared memory, splits in order
+    cluster_sync_all();
+    {
+        const int n = G * hd, per = (n + S - 1) / S;
+        for (int i = split * per + tid; i < min(n, (split + 1) * per); i += ATTN_THREADS)
+        {
+            const int gi = i / hd, d = i - gi * hd;
+            float M = -INFINITY;
+            for (int r = 0; r < S; ++r)
+                M = fmaxf(M, parts[((size_t)r * G + gi) * ps + hd]);
+            float num = 0.0f, den = 0.0f;
+            for (int r = 0; r < S; ++r)
+            {
+                const float* pr = parts + ((size_t)r * G + gi) * ps;
+                const float mr = pr[hd];
+                const float w = (mr == -INFINITY) ? 0.0f : expf(mr - M);
+                num = fmaf(pr[d], w, num);
+                den = fmaf(pr[hd + 1], w, den);
+            }
             outz[(size_t)(kvh * G + gi) * hd + d] = den > 0.0f ? num / den : 0.0f;
         }
     }
-    cluster_sync_all();
     if (tid == 0)
         trace_mark(p.trace, lin, 3);
 }
@@ -719,7 +796,7 @@ inline cudaError_t attn_launch_one(const AttnParams& p, dim3 grid, size_t smem, 
 }
 
 // Shared memory of the clustered decode kernel.
-inline size_t attn_cluster_smem_bytes(int G, int hd) { return attn_decode_smem_bytes(G, hd); }
+inline size_t attn_cluster_smem_bytes(int G, int hd, int S) { return attn_decode_smem_bytes(G, hd, S); }
 
 // Decode attention as clusters of grid.y CTAs (the splits of one kv head).
 template <int G, int HDM>
@@ -728,7 +805,7 @@ inline cudaError_t attn_launch_cluster_one(const AttnParams& p, dim3 grid, cudaS
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, p.head_dim);
+    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, p.head_dim, (int)grid.y);
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -763,6 +840,36 @@ inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, 
     return AAEDN_OK;
 }
 
+// Decode attention with the splits merged through global memory by the
+// last CTA of each (row, kv head) (p.part, p.counters).
+template <int G, int HDM>
+inline cudaError_t attn_launch_global_one(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
+{
+    return launch_kernel(attn_decode_kernel<G, HDM, false>, grid, dim3(ATTN_THREADS),
+                         attn_decode_smem_bytes(G, p.head_dim, 0), st, pdl, p);
+}
+
+inline int attn_launch_global(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
+{
+    const int G = p.n_heads / p.n_kv;
+    const bool big = p.head_dim > 128;
+    if ((int)grid.y != p.S || p.S > 16)
+        return set_error(AAEDN_EINVAL, "decode attention: %u splits for %d", grid.y, p.S);
+    cudaError_t e;
+    switch (G)
+    {
+    case 1: e = big ? attn_launch_global_one<1, 256>(p, grid, st, pdl) : attn_launch_global_one<1, 128>(p, grid, st, pdl); break;
+    case 2: e = big ? attn_launch_global_one<2, 256>(p, grid, st, pdl) : attn_launch_global_one<2, 128>(p, grid, st, pdl); break;
+    case 4: e = big ? attn_launch_global_one<4, 256>(p, grid, st, pdl) : attn_launch_global_one<4, 128>(p, grid, st, pdl); break;
+    case 8: e = big ? attn_launch_global_one<8, 256>(p, grid, st, pdl) : attn_launch_global_one<8, 128>(p, grid, st, pdl); break;
+    default: return set_error(AAEDN_EUNSUPPORTED, "attention: %d query heads per kv head (1, 2, 4 or 8)", G);
+    }
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of attn_decode_kernel failed: %s", cudaGetErrorString(e));
+    count_launch();
+    return AAEDN_OK;
+}
+
 // Clusters of `S` CTAs that can be resident at once for head group G and
 // head_dim hd (0: the variant can not run here).
 template <int G, int HDM>
@@ -771,7 +878,7 @@ inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_kv, S);
     cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, hd);
+    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, hd, S);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
@@ -822,16 +929,21 @@ inline int attn_launch(const AttnParams& p, dim3 grid, size_t smem, cudaStream_t
     return AAEDN_OK;
 }
 
+// MODE 0: the API kernel; MODE 1: the model's decode kernels (clustered and
+// global-merge variants).
 template <int MODE, int G>
 inline int attn_set_attrs_g()
 {
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<MODE, G, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024));
-    AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<MODE, G, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024));
-    if constexpr (MODE == 1)
+    if constexpr (MODE == 0)
     {
-        // the clustered variant: up to 16 CTAs per cluster
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<0, G, 128>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_split_kernel<0, G, 256>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    }
+    else
+    {
+        // clusters of up to 16 CTAs
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 128>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 256>,
@@ -840,6 +952,10 @@ inline int attn_set_attrs_g()
                                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 256>,
                                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 128, false>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        AAEDN_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<G, 256, false>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     }
     return AAEDN_OK;
 }

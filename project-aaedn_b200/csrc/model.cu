@@ -837,7 +837,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
     if (mrc)
         return mrc;
     const aaedn_model_config& c = m->cfg;
-    const int D = (int)c.dim, hd = (int)c.head_dim, H = (int)c.n_heads, KV = (int)c.n_kv_heads;
+    const int D = (int)c.dim, KV = (int)c.n_kv_heads;
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l)
     {
@@ -863,10 +863,9 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         if ((rc = mark()))
             return rc;
         // --- attention
-        const size_t asmem = attn_smem_bytes(H / KV, hd, m->attn_max_tok);
         rc = !(mask & K_ATTN) ? AAEDN_OK
              : m->attn_cS     ? attn_launch_cluster(a, dim3(KV, aS), st, pdl)
-                              : attn_launch<1>(a, dim3(KV, aS), asmem, st, pdl);
+                              : attn_launch_global(a, dim3(KV, aS), st, pdl);
         if (rc)
             return rc;
         if ((rc = mark()))
@@ -1322,7 +1321,7 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         per_sm = std::max(1, std::min(4, std::atoi(e)));
     int S = std::max(1, (per_sm * sm_count() + (int)c.n_kv_heads - 1) / (int)c.n_kv_heads);
     S = std::max(1, std::min<int>(S, (int)std::max<uint32_t>(1, c.max_seq / 8)));
-    S = std::min(S, 64);
+    S = std::min(S, 16); // the decode kernel merges at most 16 splits
     m->attn_S = S;
     m->attn_max_tok = (int)((c.max_seq + S - 1) / S);
     // lm_head: one CTA per SM, each streaming one contiguous run of rows
