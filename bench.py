@@ -318,11 +318,14 @@ def prefill_report(cfg, n, ms, shards, chunk_rows):
 
 def microbench(reps=20):
     """The dequant-GEMV / GEMM microbenchmark on the block-quant format
-    (weights N(0, 0.02) quantized, activations N(0, 1) fp32) through the
-    fused_matmul entry point: shapes 4096x4096, 11008x4096, 4096x11008 at
-    M = 1 and 8 (GEMV engine; GB/s of codes + scales + activations against
-    the HBM peak) and M = 64 (tcgen05 GEMM; TFLOP/s, 2 M N K). Enough weight
-    copies rotate that every call reads HBM (more than the 126 MB of L2)."""
+    (weights N(0, 0.02) quantized, activations N(0, 1) fp32): shapes
+    4096x4096, 11008x4096, 4096x11008 at M = 1, 8 and 64, through
+    fused_matmul on the reference's row-major layout (M <= 8: the row-major
+    GEMV; M = 64: tcgen05 GEMM) and through fused_matmul_tiled on the
+    model's tile-major repacking of the same blocks (M = 1: the decode GEMV
+    engine; M = 8, 64: tcgen05 GEMM). GB/s of codes + scales + activations
+    against the HBM peak, TFLOP/s as 2 M N K. Enough weight copies rotate
+    that every call reads HBM (more than the 126 MB of L2)."""
     import torch
     import aaedn_b200 as ab
     peak, _ = measured_peaks()
@@ -348,11 +351,34 @@ def microbench(reps=20):
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / reps
             byts = gemv_bytes(N, K, M)
-            row = {"N": N, "K": K, "M": M, "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9,
+            row = {"N": N, "K": K, "M": M, "layout": "row-major", "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9,
                    "hbm_frac": byts / (ms / 1e3) / 1e9 / peak, "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12,
                    "engine": "tcgen05 GEMM" if M > 8 else "GEMV (mma.sync bf16, three activation parts)"}
             out.append(row)
         del W
+        # the same weights in the model's tile-major layout: M = 1 on the
+        # decode GEMV engine, M = 8 and 64 on the tcgen05 GEMM
+        tiled = torch.from_numpy(ab.repack_tiled(d, sc, N, K)).cuda()
+        T = [tiled.clone() for _ in range(copies)]
+        for M in (1, 8, 64):
+            x = torch.from_numpy(ab.synth_normal(78, M, M * K, std=1.0)).cuda()
+            y = torch.empty(M * N, dtype=torch.float32, device="cuda")
+            for i in range(3):
+                ab.fused_matmul_tiled(x, T[i % copies], y, M, N, K)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(reps):
+                ab.fused_matmul_tiled(x, T[i % copies], y, M, N, K)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            byts = gemv_bytes(N, K, M)
+            out.append({"N": N, "K": K, "M": M, "layout": "tile-major", "us": ms * 1e3,
+                        "gbs": byts / (ms / 1e3) / 1e9, "hbm_frac": byts / (ms / 1e3) / 1e9 / peak,
+                        "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12,
+                        "engine": "decode GEMV (integer MMA over activation digits)" if M == 1 else "tcgen05 GEMM"})
+        del T, tiled
     return out
 
 

@@ -107,6 +107,18 @@ int aaedn_cu_fused_matmul(const float* d_in, const uint8_t* d_w, const uint16_t*
                           size_t M, size_t N, size_t K, size_t lda, size_t ldb, size_t ldc, int scale_kind,
                           void* stream);
 
+/* fused_matmul on weights repacked into the tile-major layout the model
+ * streams (the same 32-code blocks and fp16 scales, reordered so that each
+ * 16-row group's K range is one run of 1152-byte tiles): M == 1 runs the
+ * decode GEMV engine, M > 1 the tcgen05 GEMM. N % 16 == 0, K % 128 == 0,
+ * K <= 32768; d_in is [M][K], d_out [M][N] (dense). The repack is host
+ * side: h_out holds aaedn_q4_tiled_bytes(N, K) bytes (codes + fp16 scales
+ * of aaedn_quantize_q4's row-major output). */
+size_t aaedn_q4_tiled_bytes(size_t N, size_t K);
+int aaedn_q4_repack_tiled(const uint8_t* h_codes, const uint16_t* h_scales, size_t N, size_t K, uint8_t* h_out);
+int aaedn_cu_fused_matmul_tiled(const float* d_in, const uint8_t* d_tiled, float* d_out, size_t M, size_t N,
+                                size_t K, void* stream);
+
 /* fp32 weights: out[m*ldc+n] = sum_k in[m*lda+k]*w[n*ldw+k] (the lm_head
  * product of src/transformer.cpp:232-238). */
 int aaedn_cu_f32_matmul(const float* d_in, const float* d_w, float* d_out, size_t M, size_t N, size_t K,

@@ -96,6 +96,9 @@ def lib():
         "aaedn_cu_dequant_4bit": ([_vp, _vp, _vp, _sz, _int, _vp], _int),
         "aaedn_cu_fused_matmul": ([_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _int, _vp], _int),
         "aaedn_cu_f32_matmul": ([_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp], _int),
+        "aaedn_q4_tiled_bytes": ([_sz, _sz], _sz),
+        "aaedn_q4_repack_tiled": ([_vp, _vp, _sz, _sz, _vp], _int),
+        "aaedn_cu_fused_matmul_tiled": ([_vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),
         "aaedn_cu_rmsnorm": ([_vp, _vp, _vp, _sz, _f32, _vp], _int),
         "aaedn_cu_rope_apply": ([_vp, _vp, _sz, _sz, _vp, _vp, _vp], _int),
         "aaedn_cu_attention": ([_vp, _vp, _vp, _vp, _sz, _vp, _sz, _sz, _f32, _vp], _int),
@@ -230,6 +233,22 @@ def fused_matmul(d_in, d_w, d_scales, d_out, M, N, K, lda=None, ldb=None, ldc=No
                  stream=None):
     check(lib().aaedn_cu_fused_matmul(_p(d_in), _p(d_w), _p(d_scales), _p(d_out), M, N, K, lda or K, ldb or K,
                                       ldc or N, scale_kind, stream))
+
+
+def repack_tiled(codes, scales, N, K):
+    """Host repack of row-major quantized weights (aaedn_quantize_q4's codes
+    and fp16 scales) into the tile-major layout of the model's engines."""
+    codes = np.ascontiguousarray(codes, np.uint8)
+    scales = np.ascontiguousarray(scales).view(np.uint16)
+    out = np.empty(lib().aaedn_q4_tiled_bytes(N, K), np.uint8)
+    check(lib().aaedn_q4_repack_tiled(_p(codes), _p(scales), N, K, _p(out)))
+    return out
+
+
+def fused_matmul_tiled(d_in, d_tiled, d_out, M, N, K, stream=None):
+    """fused_matmul on tile-major weights: M == 1 the decode GEMV engine,
+    M > 1 the tcgen05 GEMM (dense [M][K] in, [M][N] out)."""
+    check(lib().aaedn_cu_fused_matmul_tiled(_p(d_in), _p(d_tiled), _p(d_out), M, N, K, stream))
 
 
 def f32_matmul(d_in, d_w, d_out, M, N, K, stream=None):

@@ -132,8 +132,9 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t st)
     const int M_pad = (a.M + sh.bn - 1) / sh.bn * sh.bn;
     const int gx = (a.N + TC_BM - 1) / TC_BM, gy = M_pad / sh.bn;
     const int nkb = a.K / TC_BK;
-    // the paired epilogues need whole sums in the kernel: no split-K
-    const int splits = (a.epi == TC_EPI_QKV || a.epi == TC_EPI_SWIGLU) ? 1 : tc_splits(gx * gy, nkb);
+    // split-K when the tile grid leaves SMs idle (the reduction then applies
+    // the epilogue, the paired ones included)
+    const int splits = tc_splits(gx * gy, nkb);
     const int kb_per = (nkb + splits - 1) / splits;
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     __nv_bfloat16* parts = reinterpret_cast<__nv_bfloat16*>(ws);
@@ -196,7 +197,18 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t st)
     }
     if (rc)
         return rc;
-    if (splits > 1)
+    if (splits > 1 && (a.epi == TC_EPI_QKV || a.epi == TC_EPI_SWIGLU))
+    {
+        const size_t n = (size_t)a.M * (a.N / 16) * 8;
+        if (a.epi == TC_EPI_QKV)
+            tc_splitk_pair_kernel<TC_EPI_QKV><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+                partial, splits, (size_t)a.M * a.N, a.M, a.N, a.e);
+        else
+            tc_splitk_pair_kernel<TC_EPI_SWIGLU><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+                partial, splits, (size_t)a.M * a.N, a.M, a.N, a.e);
+        AAEDN_LAUNCH_CHECK("tc_splitk_pair_kernel");
+    }
+    else if (splits > 1)
     {
         const size_t n = (size_t)a.M * a.N;
         tc_splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(

@@ -212,6 +212,50 @@ __device__ __forceinline__ void tc_w_load(const TcGemmParams& p, int row, int b,
     }
 }
 
+// The paired epilogues for one activation row m: v = D[rbase + jj][m] and
+// u = D[rbase + 8 + jj][m] (jj < 8) of the 16-row group at rbase.
+//   SWIGLU: act[m][rbase / 2 + jj] = silu(v) * u (gate and up rows
+//           interleaved in 8-row chunks)
+//   QKV:    q and k rows: the rotate-half pair (i, i + hd/2) sits in rows
+//           (jj, jj + 8) of the group; RoPE at the row's position, q to
+//           qrows, k (and v, unrotated) appended to the row's page.
+template <int EPI>
+__device__ __forceinline__ void tc_pair_epilogue(const TcEpi& e, int m, int rbase, int jj, float v, float u)
+{
+    if constexpr (EPI == TC_EPI_SWIGLU)
+        e.act[(size_t)m * e.ld_act + (rbase >> 1) + jj] = __fmul_rn(silu_f(v), u); // D6
+    else
+    {
+        const int hd = e.head_dim, half = hd >> 1;
+        const bool isq = rbase < e.q_rows, isk = !isq && rbase < e.q_rows + e.kv_rows;
+        const int rel = isq ? rbase : (isk ? rbase - e.q_rows : rbase - e.q_rows - e.kv_rows);
+        const int h = rel / hd;
+        const int i = ((rel % hd) >> 4) * 8 + jj; // rope pair (i, i + half)
+        const int pos = e.row_pos ? e.row_pos[m] : e.pos0 + m;
+        const int* pt = e.row_seq ? e.page_table + (size_t)e.row_seq[m] * e.pt_stride : e.page_table;
+        const int page = pt[pos / e.page_size], slot = pos % e.page_size;
+        float* kv = nullptr;
+        if (!isq)
+            kv = (isk ? e.k_layer : e.v_layer) + (((size_t)page * e.n_kv + h) * e.page_size + slot) * hd;
+        if (isq || isk)
+        {
+            // rotate-half at the absolute position (D3, src/rope.cpp:53-54)
+            const float c = e.rope_cos[(size_t)pos * half + i], sn = e.rope_sin[(size_t)pos * half + i];
+            const float o0 = __fsub_rn(__fmul_rn(c, v), __fmul_rn(sn, u));
+            const float o1 = __fadd_rn(__fmul_rn(sn, v), __fmul_rn(c, u));
+            float* dst = isq ? e.qrows + (size_t)m * e.ldq + (size_t)h * hd : kv;
+            dst[i] = o0;
+            dst[i + half] = o1;
+        }
+        else
+        {
+            const int d = rel % hd + jj;
+            kv[d] = v;
+            kv[d + 8] = u;
+        }
+    }
+}
+
 // Epilogue of 8 activation rows (columns c0.. of the accumulator) of weight
 // row `row` (thread = TMEM lane), values v. Every lane of the warp calls it
 // (the paired epilogues exchange values between lanes r and r + 8).
@@ -246,53 +290,12 @@ __device__ __forceinline__ void tc_epilogue8(const TcGemmParams& p, float* out, 
         const int jj = row & 15, rbase = row & ~15;
         if (!live || jj >= 8)
             return;
-        const TcEpi& e = p.e;
-        if constexpr (EPI == TC_EPI_SWIGLU)
-        {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-            {
-                const int m = m_first + j;
-                if (m < p.M)
-                    e.act[(size_t)m * e.ld_act + (rbase >> 1) + jj] = __fmul_rn(silu_f(v[j]), u[j]); // D6
-            }
-        }
-        else
+        for (int j = 0; j < 8; ++j)
         {
-            const int hd = e.head_dim, half = hd >> 1;
-            const bool isq = rbase < e.q_rows, isk = !isq && rbase < e.q_rows + e.kv_rows;
-            const int rel = isq ? rbase : (isk ? rbase - e.q_rows : rbase - e.q_rows - e.kv_rows);
-            const int h = rel / hd;
-            const int i = ((rel % hd) >> 4) * 8 + jj; // rope pair (i, i + half)
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-            {
-                const int m = m_first + j;
-                if (m >= p.M)
-                    continue;
-                const int pos = e.row_pos ? e.row_pos[m] : e.pos0 + m;
-                const int* pt = e.row_seq ? e.page_table + (size_t)e.row_seq[m] * e.pt_stride : e.page_table;
-                const int page = pt[pos / e.page_size], slot = pos % e.page_size;
-                float* kv = nullptr;
-                if (!isq)
-                    kv = (isk ? e.k_layer : e.v_layer) + (((size_t)page * e.n_kv + h) * e.page_size + slot) * hd;
-                if (isq || isk)
-                {
-                    // rotate-half at the absolute position (D3, src/rope.cpp:53-54)
-                    const float c = e.rope_cos[(size_t)pos * half + i], sn = e.rope_sin[(size_t)pos * half + i];
-                    const float o0 = __fsub_rn(__fmul_rn(c, v[j]), __fmul_rn(sn, u[j]));
-                    const float o1 = __fadd_rn(__fmul_rn(sn, v[j]), __fmul_rn(c, u[j]));
-                    float* dst = isq ? e.qrows + (size_t)m * e.ldq + (size_t)h * hd : kv;
-                    dst[i] = o0;
-                    dst[i + half] = o1;
-                }
-                else
-                {
-                    const int d = rel % hd + jj;
-                    kv[d] = v[j];
-                    kv[d + 8] = u[j];
-                }
-            }
+            const int m = m_first + j;
+            if (m < p.M)
+                tc_pair_epilogue<EPI>(p.e, m, rbase, jj, v[j], u[j]);
         }
     }
 }
@@ -540,6 +543,29 @@ __global__ void tc_split_kernel(const float* __restrict__ x, size_t lda, int M, 
         w.w = pack_bf16(h[q][6], h[q][7]);
         *reinterpret_cast<uint4*>(parts + q * plane + (size_t)m * K + k) = w;
     }
+}
+
+// The split-K sum for the paired epilogues: one thread per (activation row
+// m, 16-row group, jj < 8) adds the splits of rows rbase + jj and
+// rbase + 8 + jj in order and applies the epilogue.
+template <int EPI>
+__global__ void tc_splitk_pair_kernel(const float* __restrict__ part, int splits, size_t split_stride, int M, int N,
+                                      const TcEpi e)
+{
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t per_m = (size_t)(N / 16) * 8;
+    if (i >= (size_t)M * per_m)
+        return;
+    const int m = (int)(i / per_m), r = (int)(i - (size_t)m * per_m);
+    const int rbase = (r >> 3) * 16, jj = r & 7;
+    float v = 0.0f, u = 0.0f;
+    for (int s = 0; s < splits; ++s)
+    {
+        const float* ps = part + (size_t)s * split_stride + (size_t)m * N + rbase + jj;
+        v += ps[0];
+        u += ps[8];
+    }
+    tc_pair_epilogue<EPI>(e, m, rbase, jj, v, u);
 }
 
 // out[m][n] = (accumulate ? out[m][n] : 0) + the sum over s of part[s][m][n]

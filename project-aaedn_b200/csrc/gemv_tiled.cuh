@@ -34,13 +34,13 @@ namespace aaedn_dev
 
 constexpr uint64_t GEMV_WAIT_LIMIT_NS = 2000000000ull; // 2 s: bound of every mbarrier wait
 
-constexpr int GT_CONSUMERS = 16;
-constexpr int GT_GROUPS = 4;                             // consumer groups (chunks in flight at once)
+constexpr int GT_CONSUMERS = 24;
+constexpr int GT_GROUPS = 6;                             // consumer groups (chunks in flight at once)
 constexpr int GT_GROUP_WARPS = GT_CONSUMERS / GT_GROUPS; // warps of a group
 constexpr int GT_THREADS = (GT_CONSUMERS + 1) * 32;
-// Ring stages: a multiple of the consumer groups (the consumers' waits rely
-// on it: a stage is always refilled for the group that consumed it).
-constexpr int GT_STAGES = 4;     // fewest ring stages a launch takes
+// Ring stages (any number: the producer tags each stage with the chunk it
+// holds, and a consumer waits for its chunk's tag before the parity wait).
+constexpr int GT_STAGES = 2;     // fewest ring stages a launch takes
 constexpr int GT_MAX_STAGES = 12;
 constexpr int GT_CHUNK_TILES = 16; // four tiles per warp of a group
 constexpr int GT_TILE_BYTES = 1024 + 128; // codes + scales of one tile (16 rows x 128 codes)
@@ -56,6 +56,11 @@ constexpr float GT_YMAX = 119.0f;
 constexpr int GT_RQ = 32;
 constexpr int GT_RC = 32;
 constexpr int GT_RED_BYTES = GT_RQ * GT_GROUP_WARPS * 16 * 4 + GT_RC * 4 + GT_CONSUMERS * 16 * 4;
+// The CTA's small shared words (floats): per-warp sums of squares at WSS,
+// 16 zero bytes at ZERO, flags, and the ring's stage tags at TAG.
+constexpr int GT_MISC_WSS = 0, GT_MISC_ZERO = 32, GT_MISC_FLAG = 40, GT_MISC_LAST = 41, GT_MISC_TAG = 48;
+constexpr int GT_MISC_FLOATS = 64;
+static_assert(GT_CONSUMERS <= GT_MISC_ZERO, "per-warp sums overlap the zero words");
 constexpr int GT_MAX_CHUNKS = 16; // chunks per row group: K <= 32768
 // Shared memory for the staged epilogue inputs (EpiCache): 2048 floats.
 constexpr int GT_ECACHE_FLOATS = 2048;
@@ -89,27 +94,58 @@ void repack_tiled(const uint8_t* codes, const uint16_t* scales, size_t N, size_t
 inline size_t gemv_tiled_i8_smem_bytes(int ntile, int stages = GT_STAGES)
 {
     return (size_t)stages * GT_STAGE_BYTES + (size_t)stages * 16 + (size_t)ntile * (GT_FRAG_TILE_BYTES + 32) +
-           GT_RED_BYTES + 64 * 4 + GT_ECACHE_FLOATS * 4;
+           GT_RED_BYTES + GT_MISC_FLOATS * 4 + GT_ECACHE_FLOATS * 4;
 }
 
-// The most ring stages (a multiple of GT_GROUPS, <= GT_MAX_STAGES) whose
-// shared memory fits `budget`.
+// The most ring stages (<= GT_MAX_STAGES) whose shared memory fits `budget`.
 inline int gemv_tiled_stages(int ntile, size_t budget)
 {
     int s = GT_MAX_STAGES;
     while (s > GT_STAGES && gemv_tiled_i8_smem_bytes(ntile, s) > budget)
-        s -= GT_GROUPS;
+        --s;
     return s;
 }
 
 // The shared-memory ring of a tiled GEMV CTA: stage i at ring + i * 18 KB,
-// full[i] / empty[i] mbarriers. Chunks are numbered in the order the producer
-// issues them (q); chunk q sits in stage q % ns, use q / ns.
+// full[i] / empty[i] mbarriers, tag[i] = the chunk it was last issued for.
+// Chunks are numbered in the order the producer issues them (q); chunk q
+// sits in stage q % ns, use q / ns.
 struct TiledRing
 {
-    uint32_t ring, full, empty; // shared-memory addresses
-    uint32_t ns;                // stages
+    uint32_t ring, full, empty, tag; // shared-memory addresses
+    uint32_t ns;                     // stages
 };
+
+__device__ __forceinline__ void st_shared_u32_volatile(uint32_t addr, uint32_t v)
+{
+    asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32_volatile(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// A consumer's wait for chunk qq (stage st, use `use`). The stage's previous
+// use may belong to another group and may not have landed when this group
+// arrives, so a parity bit alone could match that pending phase. Once the
+// stage is tagged qq, the producer has seen the previous use consumed (it
+// waits for that before tagging), so the stage has completed `use` or
+// `use + 1` fills, which the parity of `use` tells apart.
+__device__ __forceinline__ bool tiled_wait_chunk(const TiledRing& r, uint32_t qq, uint32_t st, uint32_t use)
+{
+    const uint32_t tag = r.tag + 4 * st;
+    if (ld_shared_u32_volatile(tag) != qq)
+    {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_shared_u32_volatile(tag) != qq)
+            if (globaltimer_ns() - t0 > GEMV_WAIT_LIMIT_NS)
+                return false;
+    }
+    return mbar_wait_bounded(r.full + 8 * st, use & 1, GEMV_WAIT_LIMIT_NS);
+}
 
 // Producer warp: issues, for every row group this CTA owns (cta, cta + ncta,
 // ...), its chunks of the tile-major matrix w ([N/16][K/128 tiles]). Returns
@@ -132,6 +168,7 @@ __device__ __forceinline__ bool tiled_produce(const uint8_t* w, int N, int K, co
                 return false;
             if (lane == 0)
             {
+                st_shared_u32_volatile(r.tag + 4 * stage, q); // the previous use is consumed
                 const uint32_t bytes = (uint32_t)tiles * GT_TILE_BYTES;
                 mbar_arrive_expect_tx(r.full + 8 * stage, bytes);
                 if (hint)
@@ -360,13 +397,7 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     for (int q = grp; q < nq; q += GT_GROUPS)
     {
         const int tiles = (c + 1) * CT <= ntile ? CT : ntile - c * CT;
-        // The ring depth is a multiple of the groups, so the stage's previous
-        // use (chunk qq - NS) was this group's own and has been consumed: the
-        // stage has completed `use` or `use + 1` fills, which the parity of
-        // `use` tells apart. (With other depths the previous use belongs to
-        // another group and may not have landed yet; a parity bit cannot
-        // tell that state from `use + 1`.)
-        if (!mbar_wait_bounded(r.full + 8 * stage, use & 1, GEMV_WAIT_LIMIT_NS) || s_abort)
+        if (!tiled_wait_chunk(r, qq, stage, use) || s_abort)
         {
             ok = false;
             s_abort = 1;
@@ -478,7 +509,7 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
         }
         qq += GT_GROUPS;
         stage += GT_GROUPS;
-        if (stage >= NS)
+        while (stage >= NS)
         {
             stage -= NS;
             ++use;
@@ -496,17 +527,15 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
 // The decode GEMV kernel: one producer warp streaming the CTA's chunks, 16
 // consumer warps building the integer operand together, then consuming the
 // chunks four at a time.
-// At most GT_REGS registers a thread: 17 warps x 88 leave room on the SM for
-// one attention CTA (8 warps x 64), so the kernels on either side of the
-// attention overlap with it (its loads start while the qkv GEMV drains, the
-// o GEMV's weights stream while it runs).
-constexpr int GT_REGS = 88;
+// At most GT_REGS registers a thread, so that 25 warps fit one CTA (the
+// consumers are latency-bound; more warps hide more of it). 80 would be
+// 64000 registers, which the launch rejects; 72 leaves headroom.
+constexpr int GT_REGS = 72;
 
 template <int PRO, int EPI>
 __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
 {
-    // a multiple of GT_GROUPS, at least GT_STAGES (the host sizes shared memory so)
-    const int NS = p.stages > GT_STAGES ? p.stages / GT_GROUPS * GT_GROUPS : GT_STAGES;
+    const int NS = p.stages > GT_STAGES ? p.stages : GT_STAGES; // the host sizes shared memory so
     constexpr int NC = GT_CONSUMERS;
     constexpr int NCT = NC * 32;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -516,8 +545,8 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
     uint8_t* frag = reinterpret_cast<uint8_t*>(bars) + (size_t)NS * 16;
     float* bscale = reinterpret_cast<float*>(frag + (size_t)ntile * GT_FRAG_TILE_BYTES);
     float* red = bscale + (size_t)ntile * 8;
-    float* misc = red + GT_RED_BYTES / 4; // [32, 48) per-warp sums of squares, [48, 52) zero
-    float* ecache = misc + 64;
+    float* misc = red + GT_RED_BYTES / 4; // GT_MISC_*: per-warp sums of squares, zeros, flags, stage tags
+    float* ecache = misc + GT_MISC_FLOATS;
     __shared__ int s_abort_mem;
     volatile int& s_abort = s_abort_mem;
 
@@ -529,6 +558,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
     r.ring = smem_addr(ring);
     r.full = smem_addr(bars);
     r.empty = r.full + NS * 8;
+    r.tag = smem_addr(misc + GT_MISC_TAG);
     r.ns = (uint32_t)NS;
 
     if (tid == 0)
@@ -537,6 +567,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
         {
             mbar_init(r.full + 8 * i, 1);
             mbar_init(r.empty + 8 * i, GT_GROUP_WARPS);
+            reinterpret_cast<unsigned*>(misc + GT_MISC_TAG)[i] = 0xFFFFFFFFu;
         }
         mbar_init_fence();
         s_abort = 0;
@@ -544,9 +575,9 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
     if (tid < GT_RC)
         reinterpret_cast<unsigned*>(red + GT_RQ * GT_GROUP_WARPS * 16)[tid] = 0u;
     if (tid < 4)
-        misc[48 + tid] = 0.0f;
+        misc[GT_MISC_ZERO + tid] = 0.0f;
     if (tid == 0)
-        reinterpret_cast<unsigned*>(misc)[60] = 0u;
+        reinterpret_cast<unsigned*>(misc)[GT_MISC_FLAG] = 0u;
     __syncthreads();
 
     if (warp == NC)
@@ -568,7 +599,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
         trace_mark(p.trace, blockIdx.x, 2);
     // epilogue inputs for shared memory: loaded into registers first, so
     // their L2 round trip overlaps the operand build's
-    constexpr int EPRE = GT_ECACHE_FLOATS / NCT; // per thread
+    constexpr int EPRE = (GT_ECACHE_FLOATS + NCT - 1) / NCT; // per thread
     float epre[EPRE];
     int n_epre = 0;
     if constexpr (EPI == EPI_RESIDUAL)
@@ -603,7 +634,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
             }
         }
     }
-    gt_build<PRO>(p, frag, bscale, misc + 32);
+    gt_build<PRO>(p, frag, bscale, misc + GT_MISC_WSS);
 #pragma unroll
     for (int j = 0; j < EPRE; ++j)
     {
@@ -622,7 +653,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
     named_bar_sync(1, NCT); // the operand and the staged inputs are complete
     if (tid == 0)
         trace_mark(p.trace, blockIdx.x, 1);
-    if (!gt_consume<PRO, EPI>(p, r, 0u, frag, bscale, misc + 32, smem_addr(misc + 48), red, ecache, blockIdx.x,
+    if (!gt_consume<PRO, EPI>(p, r, 0u, frag, bscale, misc + GT_MISC_WSS, smem_addr(misc + GT_MISC_ZERO), red, ecache, blockIdx.x,
                               gridDim.x, s_abort))
     {
         if (lane == 0 && p.state)
@@ -633,7 +664,7 @@ __global__ void __maxnreg__(GT_REGS) gemv_tiled_i8_kernel(const GemvParams p)
         // tensor parallel: the last CTA to finish copies this rank's partial
         // (complete: every CTA counted itself after a fence) into every other
         // rank's receive buffer, then raises this GEMV's epoch there
-        volatile unsigned* last = reinterpret_cast<volatile unsigned*>(misc) + 61;
+        volatile unsigned* last = reinterpret_cast<volatile unsigned*>(misc) + GT_MISC_LAST;
         __threadfence(); // every thread: its rows before the CTA counts itself
         named_bar_sync(1, NCT);
         if (tid == 0)

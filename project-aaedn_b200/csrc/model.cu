@@ -371,10 +371,8 @@ int model_gemv(const GemvParams& p, cudaStream_t st, bool pdl, bool tiled = fals
     if (tiled)
     {
         static const int max_stages = [] {
-            // a multiple of the consumer groups: 4, 8 (default) or 12
             const char* e = std::getenv("AAEDN_GEMV_STAGES");
-            const int n = e ? std::max(GT_STAGES, std::min(GT_MAX_STAGES, std::atoi(e))) : 8;
-            return n / GT_GROUPS * GT_GROUPS;
+            return e ? std::max(GT_STAGES, std::min(GT_MAX_STAGES, std::atoi(e))) : 8;
         }();
         const int groups = p.N / 16;
         const int grid = groups < sm_count() ? groups : sm_count();
@@ -435,6 +433,11 @@ int set_model_kernel_attrs()
     if (!rc && cudaFuncSetAttribute(attn_prefill_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)attn_prefill_tiled_smem_bytes()) != cudaSuccess)
         rc = set_error(AAEDN_ECUDA, "attn_prefill_tiled_kernel smem attribute failed");
+    if (!rc && (cudaFuncSetAttribute(lm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)lm_rows_smem_bytes()) != cudaSuccess ||
+                cudaFuncSetAttribute(lm_rows_few_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024) != cudaSuccess))
+        rc = set_error(AAEDN_ECUDA, "lm_rows kernel smem attributes failed");
     return rc;
 }
 
@@ -503,6 +506,9 @@ struct aaedn_model
     int *b_pos = nullptr, *b_seq = nullptr; // device [max_seqs]: the batch rows
     uint32_t *b_tokens = nullptr, *b_next = nullptr;
     float *b_logits = nullptr, *b_norm = nullptr; // [max_seqs][vocab], [max_seqs][dim]
+    float* b_pval = nullptr;                     // greedy partials [max_seqs][b_parts]
+    int* b_pidx = nullptr;
+    int b_parts = 0;
     struct Seq
     {
         bool open = false;
@@ -597,6 +603,9 @@ static size_t plan_arena(aaedn_model* m, bool carve)
         m->b_next = m->take<uint32_t>(S * 4);
         m->b_logits = m->take<float>(S * V * 4);
         m->b_norm = m->take<float>(S * D * 4);
+        m->b_parts = std::max((int)((V + LR_BN - 1) / LR_BN), 2 * sm_count());
+        m->b_pval = m->take<float>(S * (size_t)m->b_parts * 4);
+        m->b_pidx = m->take<int>(S * (size_t)m->b_parts * 4);
     }
     return align_up(m->used, 256);
 }
@@ -1558,6 +1567,72 @@ extern "C" size_t aaedn_model_arena_bytes(const aaedn_model* m) { return m ? m->
 extern "C" uint32_t aaedn_model_pos(aaedn_model* m) { return m ? m->h_pos : 0; }
 extern "C" uint32_t aaedn_model_prefill_rows(const aaedn_model* m) { return m ? (uint32_t)m->pf_rows : 0u; }
 
+// ---- fused_matmul on tile-major weights (the model's engines) ------------
+
+extern "C" size_t aaedn_q4_tiled_bytes(size_t N, size_t K) { return tiled_bytes(N, K); }
+
+extern "C" int aaedn_q4_repack_tiled(const uint8_t* h_codes, const uint16_t* h_scales, size_t N, size_t K,
+                                     uint8_t* h_out)
+{
+    if (!h_codes || !h_scales || !h_out)
+        return set_error(AAEDN_EINVAL, "aaedn_q4_repack_tiled: null buffer");
+    if (N % 16 || K % 128 || K == 0)
+        return set_error(AAEDN_EINVAL, "aaedn_q4_repack_tiled: N %% 16 and K %% 128 must be 0 (N %zu, K %zu)", N, K);
+    repack_tiled(h_codes, h_scales, N, K, h_out);
+    return AAEDN_OK;
+}
+
+extern "C" int aaedn_cu_fused_matmul_tiled(const float* d_in, const uint8_t* d_tiled, float* d_out, size_t M,
+                                           size_t N, size_t K, void* stream)
+{
+    if (M == 0 || N == 0 || K == 0)
+        return AAEDN_OK;
+    if (!d_in || !d_tiled || !d_out)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_fused_matmul_tiled: null buffer");
+    if (!tiles_ok(N, K) || M > (size_t)INT32_MAX || N > (size_t)INT32_MAX)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_fused_matmul_tiled: N %% 16, K %% 128 must be 0 and K <= 32768");
+    if ((reinterpret_cast<uintptr_t>(d_tiled) | reinterpret_cast<uintptr_t>(d_in)) & 15)
+        return set_error(AAEDN_EINVAL, "aaedn_cu_fused_matmul_tiled: buffers must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    static PerDeviceOnce attrs;
+    int rc = attrs.run([]() { return set_gemv_attrs<PRO_PLAIN, EPI_STORE>(); });
+    if (rc)
+        return rc;
+    if (M == 1)
+    {
+        // the decode GEMV engine
+        GemvParams p{};
+        p.w = d_tiled;
+        p.N = (int)N;
+        p.K = (int)K;
+        p.x = d_in;
+        p.lda = K;
+        p.y = d_out;
+        p.ldc = N;
+        p.l2_hint = 1;
+        return model_gemv<PRO_PLAIN, EPI_STORE>(p, st, false, true);
+    }
+    // more rows: the tcgen05 GEMM over the same layout
+    TcGemmArgs a{};
+    a.x = d_in;
+    a.lda = K;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.w = d_tiled;
+    a.w_layout = TC_W_TILED;
+    a.out = d_out;
+    a.ldc = N;
+    a.err = tc_api_err_word();
+    if (!a.err)
+        return set_error(AAEDN_ECUDA, "aaedn_cu_fused_matmul_tiled: error word allocation failed");
+    a.workspace_bytes = tc_gemm_workspace_bytes(a.M, a.N, a.K);
+    AAEDN_CUDA_TRY(cudaMallocAsync(&a.workspace, a.workspace_bytes, st));
+    rc = tc_gemm(a, st);
+    AAEDN_CUDA_TRY(cudaFreeAsync(a.workspace, st));
+    return rc;
+}
+
 extern "C" uint32_t aaedn_model_kernels_per_step(const aaedn_model* m)
 {
     return m ? 5u * m->cfg.n_layers + 1u : 0u;
@@ -2225,11 +2300,25 @@ static int lm_rows(aaedn_model* m, int row0, int n)
     pf_rmsnorm_rows_kernel<<<n, 256, 0, st>>>(m->pf_hidden + (size_t)row0 * D, D, m->final_norm, m->cfg.eps,
                                                m->b_norm);
     AAEDN_LAUNCH_CHECK("pf_rmsnorm_rows_kernel");
-    lm_rows_kernel<<<dim3((V + LR_TV - 1) / LR_TV, (n + LR_TM - 1) / LR_TM), 256, 0, st>>>(m->b_norm, n, D, m->lm_head,
-                                                                                         V, m->b_logits, (size_t)V);
-    AAEDN_LAUNCH_CHECK("lm_rows_kernel");
-    argmax_rows_kernel<<<n, 256, 0, st>>>(m->b_logits, (size_t)V, V, m->b_next);
-    AAEDN_LAUNCH_CHECK("argmax_rows_kernel");
+    int parts;
+    if (n <= LF_MAXM && D % 128 == 0)
+    {
+        // a few rows (a prefill's last token): stream the lm_head once
+        parts = 2 * sm_count();
+        lm_rows_few_kernel<<<parts, LF_WARPS * 32, (size_t)n * D * 4, st>>>(m->b_norm, n, D, m->lm_head, V,
+                                                                           m->b_logits, (size_t)V, m->b_pval,
+                                                                           m->b_pidx);
+        AAEDN_LAUNCH_CHECK("lm_rows_few_kernel");
+    }
+    else
+    {
+        parts = (V + LR_BN - 1) / LR_BN;
+        lm_rows_kernel<<<dim3(parts, (n + LR_BM - 1) / LR_BM), 256, lm_rows_smem_bytes(), st>>>(
+            m->b_norm, n, D, m->lm_head, V, m->b_logits, (size_t)V, m->b_pval, m->b_pidx);
+        AAEDN_LAUNCH_CHECK("lm_rows_kernel");
+    }
+    argmax_parts_kernel<<<(n + 7) / 8, 256, 0, st>>>(m->b_pval, m->b_pidx, parts, n, m->b_next);
+    AAEDN_LAUNCH_CHECK("argmax_parts_kernel");
     return AAEDN_OK;
 }
 

@@ -343,106 +343,233 @@ __global__ void __launch_bounds__(256) pf_rmsnorm_rows_kernel(const float* __res
         out[(size_t)blockIdx.x * D + k] = __fmul_rn(__fmul_rn(xr[k], rms), gain[k]);
 }
 
-constexpr int LR_TV = 64, LR_TM = 64, LR_TK = 32;
-
-// out[m * ldo + v] = sum_k x[m][k] * w[v][k] for m < M, v < V; a CTA of 256
-// threads owns 64 vocabulary rows x 64 activation rows (4 x 4 per thread),
-// K in slices of 32 staged in shared memory, k ascending in every sum.
-__global__ void __launch_bounds__(256) lm_rows_kernel(const float* __restrict__ x, int M, int D,
-                                                      const float* __restrict__ w, int V, float* __restrict__ out,
-                                                      size_t ldo)
+// Greedy-token partials: a CTA's best (value, id) per activation row over its
+// vocabulary rows, ties to the lowest id; argmax_parts_kernel takes the best
+// of a row's partials in order.
+__device__ __forceinline__ void lr_better(float& v, int& i, float ov, int oi)
 {
-    __shared__ float ws[LR_TK][LR_TV + 4];
-    __shared__ float xs[LR_TK][LR_TM + 4];
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int v0 = blockIdx.x * LR_TV, m0 = blockIdx.y * LR_TM;
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < D; k0 += LR_TK)
+    if (ov > v || (ov == v && oi < i))
     {
-        // 64 x 32 of each operand: 8 floats per thread, k fastest in memory
-        for (int i = tid; i < LR_TV * LR_TK; i += 256)
+        v = ov;
+        i = oi;
+    }
+}
+
+constexpr int LR_BM = 32, LR_BN = 128, LR_BK = 32, LR_LD = LR_BK + 4, LR_STAGES = 4;
+
+inline size_t lm_rows_smem_bytes() { return (size_t)LR_STAGES * (LR_BN + LR_BM) * LR_LD * 4; }
+
+// out[m * ldo + v] = sum_k x[m][k] * w[v][k] for m < M (<= 32 a launch row
+// tile, blockIdx.y), v < V, and the CTA's greedy partial per row into
+// part_val / part_idx [M][gridDim.x]. A CTA of 256 threads owns 128
+// vocabulary rows x 32 activation rows (4 x 4 per thread), K in slices of
+// 32 through a 4-stage cp.async ring (rows of 16-byte pieces, padded), k
+// ascending in every sum. D a multiple of 32.
+__global__ void __launch_bounds__(256, 2) lm_rows_kernel(const float* __restrict__ x, int M, int D,
+                                                         const float* __restrict__ w, int V, float* __restrict__ out,
+                                                         size_t ldo, float* __restrict__ part_val,
+                                                         int* __restrict__ part_idx)
+{
+    extern __shared__ __align__(16) float lr[];
+    const int tid = threadIdx.x, tm = tid & 7, tn = tid >> 3;
+    const int v0 = blockIdx.x * LR_BN, m0 = blockIdx.y * LR_BM;
+    auto ws = [&](int s) { return lr + (size_t)s * (LR_BN + LR_BM) * LR_LD; };
+    auto xs = [&](int s) { return ws(s) + LR_BN * LR_LD; };
+    const int nk = D / LR_BK;
+    auto issue = [&](int kb, int s) {
+        // 128 w rows and 32 x rows of 32 floats: 8 pieces of 16 bytes each
+        for (int i = tid; i < (LR_BN + LR_BM) * 8; i += 256)
         {
-            const int r = i / LR_TK, k = i % LR_TK;
-            const int v = v0 + r, m = m0 + r;
-            ws[k][r] = (v < V && k0 + k < D) ? w[(size_t)v * D + k0 + k] : 0.0f;
-            xs[k][r] = (m < M && k0 + k < D) ? x[(size_t)m * D + k0 + k] : 0.0f;
+            const int r = i >> 3, c = i & 7;
+            if (r < LR_BN)
+            {
+                const int v = v0 + r;
+                const float* src = w + (size_t)min(v, V - 1) * D + kb * LR_BK + 4 * c;
+                cp_async_16(ws(s) + r * LR_LD + 4 * c, src, v < V ? 16u : 0u);
+            }
+            else
+            {
+                const int m = m0 + r - LR_BN;
+                const float* src = x + (size_t)min(m, M - 1) * D + kb * LR_BK + 4 * c;
+                cp_async_16(xs(s) + (r - LR_BN) * LR_LD + 4 * c, src, m < M ? 16u : 0u);
+            }
         }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < LR_STAGES - 1; ++s)
+    {
+        if (s < nk)
+            issue(s, s);
+        else
+            cp_async_commit();
+    }
+    float acc[4][4] = {}; // [vocab i][row j]
+    for (int kb = 0; kb < nk; ++kb)
+    {
+        cp_async_wait<LR_STAGES - 2>();
         __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < LR_TK; ++k)
+        if (kb + LR_STAGES - 1 < nk)
+            issue(kb + LR_STAGES - 1, (kb + LR_STAGES - 1) % LR_STAGES);
+        else
+            cp_async_commit();
+        const float* W = ws(kb % LR_STAGES);
+        const float* X = xs(kb % LR_STAGES);
+#pragma unroll
+        for (int k = 0; k < LR_BK; k += 4)
         {
-            const float4 a = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
-            const float4 b = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
-            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            float4 a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                a[i] = *reinterpret_cast<const float4*>(W + (tn * 4 + i) * LR_LD + k);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                b[j] = *reinterpret_cast<const float4*>(X + (tm * 4 + j) * LR_LD + k);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                {
+                    acc[i][j] = fmaf(a[i].x, b[j].x, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].y, b[j].y, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].z, b[j].z, acc[i][j]);
+                    acc[i][j] = fmaf(a[i].w, b[j].w, acc[i][j]);
+                }
         }
-        __syncthreads();
     }
+    cp_async_wait<0>();
+    __syncthreads();
+    // logits, and each row's best over this CTA's 128 vocabulary rows
+    float* sbv = lr;                                  // [32 tn][32 rows]
+    int* sbi = reinterpret_cast<int*>(lr + 32 * LR_BM);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
     {
-        const int m = m0 + ty * 4 + j;
-        if (m >= M)
-            continue;
+        const int m = m0 + tm * 4 + j;
+        float bv = -INFINITY;
+        int bi = INT_MAX;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
         {
-            const int v = v0 + tx * 4 + i;
-            if (v < V)
+            const int v = v0 + tn * 4 + i;
+            if (v < V && m < M)
+            {
                 out[(size_t)m * ldo + v] = acc[i][j];
+                lr_better(bv, bi, acc[i][j], v);
+            }
         }
+        sbv[tn * LR_BM + tm * 4 + j] = bv;
+        sbi[tn * LR_BM + tm * 4 + j] = bi;
+    }
+    __syncthreads();
+    if (tid < LR_BM && m0 + tid < M)
+    {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int t = 0; t < 32; ++t)
+            lr_better(bv, bi, sbv[t * LR_BM + tid], sbi[t * LR_BM + tid]);
+        part_val[(size_t)(m0 + tid) * gridDim.x + blockIdx.x] = bv;
+        part_idx[(size_t)(m0 + tid) * gridDim.x + blockIdx.x] = bi;
     }
 }
 
-// next[m] = argmax_v logits[m][v] (ties to the lowest id); one CTA per row.
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ logits, size_t ld, int V,
-                                                          uint32_t* __restrict__ next)
+constexpr int LF_MAXM = 4, LF_WARPS = 8;
+
+// The same product for at most 4 activation rows (a prefill's last row):
+// every warp streams whole vocabulary rows (lanes over D, 16-byte loads)
+// against the rows held in shared memory; per-CTA greedy partials as above.
+// D a multiple of 128.
+__global__ void __launch_bounds__(LF_WARPS * 32) lm_rows_few_kernel(const float* __restrict__ x, int M, int D,
+                                                                    const float* __restrict__ w, int V,
+                                                                    float* __restrict__ out, size_t ldo,
+                                                                    float* __restrict__ part_val,
+                                                                    int* __restrict__ part_idx)
 {
-    __shared__ float sv[8];
-    __shared__ int si[8];
-    const float* l = logits + (size_t)blockIdx.x * ld;
-    float bv = -INFINITY;
-    int bi = INT_MAX;
-    for (int v = threadIdx.x; v < V; v += blockDim.x)
-        if (l[v] > bv)
+    extern __shared__ __align__(16) float xsm[]; // [M][D]
+    __shared__ float sbv[LF_WARPS][LF_MAXM];
+    __shared__ int sbi[LF_WARPS][LF_MAXM];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < M * D / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(xsm)[i] = reinterpret_cast<const float4*>(x)[i];
+    __syncthreads();
+    float bv[LF_MAXM], tmp[LF_MAXM];
+    int bi[LF_MAXM];
+#pragma unroll
+    for (int j = 0; j < LF_MAXM; ++j)
+    {
+        bv[j] = -INFINITY;
+        bi[j] = INT_MAX;
+    }
+    const int per = (V + gridDim.x - 1) / gridDim.x, v_begin = blockIdx.x * per, v_end = min(V, v_begin + per);
+    for (int v = v_begin + warp; v < v_end; v += LF_WARPS)
+    {
+        const float4* wr = reinterpret_cast<const float4*>(w + (size_t)v * D);
+#pragma unroll
+        for (int j = 0; j < LF_MAXM; ++j)
+            tmp[j] = 0.0f;
+        for (int c = lane; c < D / 4; c += 32)
         {
-            bv = l[v];
-            bi = v;
+            const float4 a = __ldcs(wr + c);
+#pragma unroll
+            for (int j = 0; j < LF_MAXM; ++j)
+                if (j < M)
+                {
+                    const float4 b = reinterpret_cast<const float4*>(xsm + (size_t)j * D)[c];
+                    tmp[j] = fmaf(a.x, b.x, tmp[j]);
+                    tmp[j] = fmaf(a.y, b.y, tmp[j]);
+                    tmp[j] = fmaf(a.z, b.z, tmp[j]);
+                    tmp[j] = fmaf(a.w, b.w, tmp[j]);
+                }
         }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-    {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi))
-        {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0)
-    {
-        sv[warp] = bv;
-        si[warp] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0)
-    {
-        bv = sv[0];
-        bi = si[0];
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] < bi))
+        for (int j = 0; j < LF_MAXM; ++j)
+            if (j < M)
             {
-                bv = sv[w];
-                bi = si[w];
+                const float s = warp_sum(tmp[j]);
+                if (lane == 0)
+                {
+                    out[(size_t)j * ldo + v] = s;
+                    lr_better(bv[j], bi[j], s, v);
+                }
             }
-        next[blockIdx.x] = bi == INT_MAX ? 0u : (uint32_t)bi;
     }
+    if (lane == 0)
+#pragma unroll
+        for (int j = 0; j < LF_MAXM; ++j)
+        {
+            sbv[warp][j] = bv[j];
+            sbi[warp][j] = bi[j];
+        }
+    __syncthreads();
+    if (tid < M)
+    {
+        float b = -INFINITY;
+        int i = INT_MAX;
+        for (int w8 = 0; w8 < LF_WARPS; ++w8)
+            lr_better(b, i, sbv[w8][tid], sbi[w8][tid]);
+        part_val[(size_t)tid * gridDim.x + blockIdx.x] = b;
+        part_idx[(size_t)tid * gridDim.x + blockIdx.x] = i;
+    }
+}
+
+// next[m] = the best of row m's n_parts partials (ties to the lowest id);
+// one warp per row.
+__global__ void __launch_bounds__(256) argmax_parts_kernel(const float* __restrict__ part_val,
+                                                           const int* __restrict__ part_idx, int n_parts, int M,
+                                                           uint32_t* __restrict__ next)
+{
+    const int m = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (m >= M)
+        return;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int c = lane; c < n_parts; c += 32)
+        lr_better(bv, bi, part_val[(size_t)m * n_parts + c], part_idx[(size_t)m * n_parts + c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        lr_better(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    if (lane == 0)
+        next[m] = bi == INT_MAX ? 0u : (uint32_t)bi;
 }
 
 } // namespace aaedn_dev

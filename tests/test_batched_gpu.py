@@ -51,7 +51,7 @@ def pair():
 
 def test_sequences_stepped_together_match_each_alone(pair):
     w, om, bm = pair
-    lens = [5, 33, 64, 70]  # page boundaries (64 tokens) on both sides
+    lens = [5, 33, 64, 70, 2, 17]  # page boundaries (64 tokens) on both sides; more than 4 rows: the tiled lm_head
     seqs, hist = [], []
     for i, n in enumerate(lens):
         s = bm.open()
@@ -114,3 +114,34 @@ def test_batched_rejects_what_it_cannot_do(pair):
     bm.close_seq(s)
     with pytest.raises(ab.AaednError):
         bm.step([s], [1])  # closed
+
+
+def test_batched_at_8b_widths_splits_the_paired_epilogues():
+    """Three sequences of the Llama-3-8B widths (2 layers, GQA 32/8, ffn
+    14336, vocab 128256) prefilled and stepped together: at so few rows the
+    qkv and gate/up GEMMs split K across CTAs, and the RoPE / K,V-append and
+    SwiGLU epilogues run in the split-K reduction. Each sequence's logits
+    and tokens match the oracle's run of that sequence alone."""
+    cfg = dict(ab.LLAMA3_8B, n_layers=2, max_seq=128)
+    w = ab.synthetic_weights(cfg, 909)
+    om = pyoracle.OracleModel(pyoracle.Oracle(), cfg, w)
+    bm = ab.BatchedModel(cfg, max_seqs=4, kv_tokens=4 * 128)
+    try:
+        bm.set_weights(w)
+        seqs, hist = [], []
+        for i, n in enumerate((3, 6, 9)):
+            s = bm.open()
+            p = ab.synth_tokens(909, i, cfg["vocab"], n)
+            _, nxt = bm.prefill(s, p)
+            seqs.append(s)
+            hist.append(list(p) + [nxt])
+        for _ in range(3):
+            logits, nxt = bm.step(seqs, [h[-1] for h in hist])
+            for i, h in enumerate(hist):
+                h.append(int(nxt[i]))
+        for i, h in enumerate(hist):
+            want = _oracle_run(om, h[:-1])
+            assert _rel_err(logits[i], want) < 1e-4, i
+            assert h[-1] == int(np.argmax(want)), i
+    finally:
+        bm.close()
