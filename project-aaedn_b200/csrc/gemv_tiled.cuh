@@ -21,9 +21,9 @@
 // conflicts).
 //
 // CTA: one producer warp (bulk copies into a ring of up to 12 stages,
-// mbarriers) + 16 consumer warps in 4 groups of 4; chunk q of the CTA's
-// stream goes to group q % 4, whose warp j takes tiles 4j..4j+3 of it, so
-// four chunks are worked on at once and a warp's four tiles give it 16
+// mbarriers) + 24 consumer warps in 6 groups of 4; chunk q of the CTA's
+// stream goes to group q % 6, whose warp j takes tiles 4j..4j+3 of it, so
+// six chunks are worked on at once and a warp's four tiles give it 16
 // independent mmas per chunk.
 #pragma once
 
@@ -193,7 +193,7 @@ __device__ __forceinline__ void tiled_drain(const TiledRing& r, uint32_t q)
 }
 
 // ---------------------------------------------------------------------------
-// The activation operand, built by the 16 consumer warps together.
+// The activation operand, built by the 24 consumer warps together.
 //
 // Work item = 8 elements (codes 8s..8s+7 of block tb of a tile); the 4 items
 // of a block sit in one lane quad, which finds the block's max with two
@@ -390,8 +390,8 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     }
     const int nq = my_groups * nchunk;
     bool ok = true;
-    // chunk q = grp, grp + 4, ...: its stage, use, row group and chunk within
-    // the row group are advanced without divisions (the ring has >= 4 stages)
+    // chunk q = grp, grp + GT_GROUPS, ...: its stage, use, row group and chunk
+    // within the row group are advanced without divisions
     uint32_t qq = q0 + (uint32_t)grp, stage = qq % NS, use = qq / NS;
     int gl = grp / nchunk, c = grp - gl * nchunk;
     for (int q = grp; q < nq; q += GT_GROUPS)
@@ -524,9 +524,9 @@ __device__ __forceinline__ bool gt_consume(const GemvParams& p, const TiledRing&
     return !named_bar_or(1, NCT, !ok);
 }
 
-// The decode GEMV kernel: one producer warp streaming the CTA's chunks, 16
+// The decode GEMV kernel: one producer warp streaming the CTA's chunks, 24
 // consumer warps building the integer operand together, then consuming the
-// chunks four at a time.
+// chunks six at a time.
 // At most GT_REGS registers a thread, so that 25 warps fit one CTA (the
 // consumers are latency-bound; more warps hide more of it). 80 would be
 // 64000 registers, which the launch rejects; 72 leaves headroom.
