@@ -70,6 +70,33 @@ int aaedn_synth_tokens(uint64_t seed, uint64_t stream_id, uint32_t vocab, uint32
  * in fp64 rounded to fp32 (the model path). */
 int aaedn_rope_table(float* h_cos, float* h_sin, size_t max_seq, size_t head_dim, double theta, int formula);
 
+/* ---- tokenizer (.abt v2; host only, no GPU needed) ----------------------- */
+/* src/tokenizer.cpp:32-158 tokenizer_load: reads an .abt v2 file (64-byte
+ * header "<8sIQI4I24s", magic "AAEDNTOK", FNV-1a 32 of the payload; the
+ * payload's string block, u32 offsets and u16 merge-rule pairs) with the
+ * reference's accept/reject decisions (AAEDN_EFORMAT when rejected). The
+ * handle owns host copies of the tables and a pair -> rule lookup table. */
+typedef struct aaedn_tokenizer aaedn_tokenizer;
+int aaedn_tokenizer_load(const char* path, aaedn_tokenizer** out);
+/* The same from a file image already in host memory. */
+int aaedn_tokenizer_from_bytes(const uint8_t* h_file, size_t n, aaedn_tokenizer** out);
+void aaedn_tokenizer_free(aaedn_tokenizer* t);
+/* h_info[5] = vocab_size, merge_count, max_token_bytes, format_version,
+ * payload_checksum (include/tokenizer.hpp:19-30). */
+int aaedn_tokenizer_info(const aaedn_tokenizer* t, uint32_t* h_info);
+/* src/tokenizer.cpp:169-239 tokenizer_encode: one id per byte of the
+ * NUL-terminated text, merged by the rules in the reference's order (merged
+ * pair = vocab_size + rule number), 32765 (BOS) first when add_bos. At most
+ * strlen(text) + add_bos ids. h_ids == NULL (cap 0): only *n_ids is set. */
+int aaedn_tokenizer_encode(const aaedn_tokenizer* t, const char* text, int add_bos, uint32_t* h_ids, size_t cap,
+                           size_t* n_ids);
+/* src/tokenizer.cpp:241-257 tokenizer_decode: the strings of the ids,
+ * concatenated (32766, 32767 and ids >= vocab_size add nothing); *n_bytes =
+ * its length, and h_text (cap > length) gets it with a NUL after it.
+ * h_text == NULL (cap 0): only *n_bytes is set. */
+int aaedn_tokenizer_decode(const aaedn_tokenizer* t, const uint32_t* h_ids, size_t n, char* h_text, size_t cap,
+                           size_t* n_bytes);
+
 /* ---- .abn model files (tools/convert_model.py:138, src/quant.cpp:31-119) -- */
 /* The 64-byte little-endian header "<8sIQI6IB15s": magic "AAEDNMDL",
  * version, payload_size, payload_checksum (FNV-1a 32 of the payload),

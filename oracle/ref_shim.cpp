@@ -11,8 +11,11 @@
 #include "quant.hpp"
 #include "rmsnorm.hpp"
 #include "rope.hpp"
+#include "tokenizer.hpp"
 
+#include <algorithm>
 #include <cstring>
+#include <string>
 #include <vector>
 
 using namespace aaedn;
@@ -85,6 +88,48 @@ int ref_quant_load(const char* path, uint64_t* num_blocks, uint32_t* version, ui
     *checksum = q.checksum;
     arena_destroy(&a);
     return ok;
+}
+
+// include/tokenizer.hpp:31-33 — loads path, then (when it loaded) encodes
+// text and decodes the ids it got. Returns 1 when the loader accepted the
+// file; info[5] = vocab_size, merge_count, max_token_bytes, format_version,
+// payload_checksum; ids / bytes capped at their capacities, counts in
+// *n_ids / *n_bytes.
+int ref_tokenizer(const char* path, const char* text, int add_bos, uint32_t* info, uint32_t* ids, size_t ids_cap,
+                  size_t* n_ids, char* bytes, size_t bytes_cap, size_t* n_bytes)
+{
+    Arena a = arena_create(size_t(64) << 20, 64);
+    Tokenizer t = tokenizer_load(&a, path);
+    info[0] = t.vocab_size;
+    info[1] = t.merge_count;
+    info[2] = t.max_token_bytes;
+    info[3] = t.format_version;
+    info[4] = t.payload_checksum;
+    const int ok = t.strings != nullptr;
+    *n_ids = 0;
+    *n_bytes = 0;
+    if (ok && text)
+    {
+        std::vector<uint32_t> v = tokenizer_encode(&t, text, add_bos != 0);
+        *n_ids = v.size();
+        std::memcpy(ids, v.data(), std::min(v.size(), ids_cap) * 4);
+        std::string d = tokenizer_decode(&t, v);
+        *n_bytes = d.size();
+        std::memcpy(bytes, d.data(), std::min(d.size(), bytes_cap));
+    }
+    arena_destroy(&a);
+    return ok;
+}
+
+// include/tokenizer.hpp:33 on given ids
+size_t ref_tokenizer_decode(const char* path, const uint32_t* ids, size_t n, char* bytes, size_t bytes_cap)
+{
+    Arena a = arena_create(size_t(64) << 20, 64);
+    Tokenizer t = tokenizer_load(&a, path);
+    std::string d = tokenizer_decode(&t, std::vector<uint32_t>(ids, ids + n));
+    std::memcpy(bytes, d.data(), std::min(d.size(), bytes_cap));
+    arena_destroy(&a);
+    return d.size();
 }
 
 } // extern "C"

@@ -96,6 +96,12 @@ def lib():
         "aaedn_cu_dequant_4bit": ([_vp, _vp, _vp, _sz, _int, _vp], _int),
         "aaedn_cu_fused_matmul": ([_vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _int, _vp], _int),
         "aaedn_cu_f32_matmul": ([_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp], _int),
+        "aaedn_tokenizer_load": ([ctypes.c_char_p, ctypes.POINTER(_vp)], _int),
+        "aaedn_tokenizer_from_bytes": ([_vp, _sz, ctypes.POINTER(_vp)], _int),
+        "aaedn_tokenizer_free": ([_vp], None),
+        "aaedn_tokenizer_info": ([_vp, _vp], _int),
+        "aaedn_tokenizer_encode": ([_vp, ctypes.c_char_p, _int, _vp, _sz, ctypes.POINTER(_sz)], _int),
+        "aaedn_tokenizer_decode": ([_vp, _vp, _sz, _vp, _sz, ctypes.POINTER(_sz)], _int),
         "aaedn_q4_tiled_bytes": ([_sz, _sz], _sz),
         "aaedn_q4_repack_tiled": ([_vp, _vp, _sz, _sz, _vp], _int),
         "aaedn_cu_fused_matmul_tiled": ([_vp, _vp, _vp, _sz, _sz, _sz, _vp], _int),

@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 INCS = ["-I" + os.path.join(ROOT, "include"), "-I" + HOST, "-I" + os.path.join(HOST, "include")]
 
 CU_SRCS = ["api.cu", "model.cu", "ffn.cu", "sample.cu", "gemm_tc.cu"]
-CPP_SRCS = ["errors.cpp", "quant_tools.cpp", "abn_file.cpp", "aaedn_api.cpp"]
+CPP_SRCS = ["errors.cpp", "quant_tools.cpp", "abn_file.cpp", "aaedn_api.cpp", "tokenizer.cpp"]
 
 
 def _deps(src):

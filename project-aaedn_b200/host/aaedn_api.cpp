@@ -32,7 +32,7 @@ namespace aaedn
 namespace
 {
 size_t align_up(size_t v, size_t a) { return a ? (v + a - 1) / a * a : v; }
-constexpr size_t kHostArenaBytes = 1 << 20; // branch and segment tables
+constexpr size_t kHostArenaBytes = 1 << 20; // least host part of an arena
 } // namespace
 
 // ---- arena (src/arena.cpp) ------------------------------------------------
@@ -46,8 +46,11 @@ Arena arena_create(size_t bytes, size_t align)
         a.capacity = bytes;
     }
     const size_t hal = align < 64 ? 64 : align;
-    a.host_base = static_cast<uint8_t*>(std::aligned_alloc(hal, align_up(kHostArenaBytes, hal)));
-    a.host_capacity = a.host_base ? kHostArenaBytes : 0;
+    // host tables (KV branch and segment tables, tokenizer tables): as large
+    // as the device part, at least 1 MB (pages are only touched when used)
+    const size_t hbytes = bytes > kHostArenaBytes ? bytes : kHostArenaBytes;
+    a.host_base = static_cast<uint8_t*>(std::aligned_alloc(hal, align_up(hbytes, hal)));
+    a.host_capacity = a.host_base ? hbytes : 0;
     return a;
 }
 

@@ -3,8 +3,9 @@
 // Same names and signatures. An Arena is one device allocation (cudaMalloc
 // at arena_create) with a bump pointer, as the reference's single
 // pre-allocated arena (src/arena.cpp:7-27); arena_alloc returns DEVICE
-// memory. Host-side tables (the KV cache's branch and segment tables) come
-// from a small host arena kept beside it (arena_alloc_host). Where the
+// memory. Host-side tables (the KV cache's branch and segment tables, the
+// tokenizer's tables) come from a host arena kept beside it (arena_alloc_host;
+// as large as the device part, at least 1 MB). Where the
 // reference asserts on overflow, arena_alloc returns nullptr and records the
 // error (aaedn_last_error()).
 #ifndef AAEDN_B200_ARENA_HPP
