@@ -60,6 +60,10 @@ struct AttnParams
     const int* row_seq;
     int pt_stride;
     size_t ldq, ldo;
+    // warps a CTA of the clustered decode kernel for one query head per kv
+    // head at head_dim <= 128 (10 or 16: more tokens in flight per split;
+    // otherwise ATTN_WARPS)
+    int warps;
 };
 
 // Shared memory: per-warp running max and sum [8][G] each, per-warp V sums
@@ -421,8 +425,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 // ---------------------------------------------------------------------------
 // Decode attention as clusters: the S splits of one kv head are one cluster
 // (grid (n_kv, S, rows), cluster (1, S)), CTA rank = split.
-//   1. Split s takes tokens s, s + S, s + 2S, ...; warp w of it the tokens
-//      s + S (w + 8 j). The rows of its first TB tokens do not depend on the
+//   1. Split s takes tokens s, s + S, s + 2S, ...; warp w of its NW warps
+//      (8, or 10 or 16 for MHA at head_dim <= 128 on request: one batch of
+//      loads then covers more context) the tokens s + S (w + NW j). The
+//      rows of its first TB tokens do not depend on the
 //      position, so each warp requests them (K and V straight into
 //      registers) before waiting for the kernel that writes q and the
 //      current K/V row: for the model's one sequence (identity page table)
@@ -438,16 +444,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 //      the S partials from its own shared memory, in split order.
 // ---------------------------------------------------------------------------
 
-// MHA at head_dim <= 128: 64 registers, four CTAs per SM (a cluster then
-// needs fewer free SMs of a GPC while the kernel before drains); wider
-// groups keep their q and V sums for more heads in registers.
-constexpr int attn_decode_min_blocks(int G, int HDM) { return (G == 1 && HDM == 128) ? 4 : (G * HDM >= 1024 ? 1 : 2); }
-
-// Shared memory: wm[8][G], wl[8][G], wacc[8][G][hd], then the S partials
-// [S][G][hd + 4] (sums, max, denominator; 16-byte rows).
-__host__ __device__ inline size_t attn_decode_smem_bytes(int G, int hd, int S)
+// MHA at head_dim <= 128: 64 registers, four CTAs of 8 warps (three of 10,
+// two of 16) per SM (a cluster then needs fewer free SMs of a GPC while the kernel
+// before drains); wider groups keep their q and V sums for more heads in
+// registers.
+constexpr int attn_decode_min_blocks(int G, int HDM, int NW = ATTN_WARPS)
 {
-    return ((size_t)2 * ATTN_WARPS * G + (size_t)ATTN_WARPS * G * hd + (size_t)S * G * (hd + 4)) * 4;
+    return NW != ATTN_WARPS ? ((G == 1 && HDM == 128) ? 32 / NW : 1)
+                            : (G == 1 && HDM == 128) ? 4 : (G * HDM >= 1024 ? 1 : 2);
+}
+
+// Shared memory: wm[NW][G], wl[NW][G], wacc[NW][G][hd] (NW warps a CTA),
+// then the S partials [S][G][hd + 4] (sums, max, denominator; 16-byte rows).
+__host__ __device__ inline size_t attn_decode_smem_bytes(int G, int hd, int S, int NW = ATTN_WARPS)
+{
+    return ((size_t)2 * NW * G + (size_t)NW * G * hd + (size_t)S * G * (hd + 4)) * 4;
 }
 
 __device__ __forceinline__ void st_dsmem_f32(uint32_t laddr, uint32_t rank, float v)
@@ -457,8 +468,8 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t laddr, uint32_t rank, floa
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
-template <int G, int HDM, bool CL = true>
-__global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) attn_decode_kernel(const AttnParams p)
+template <int G, int HDM, bool CL = true, int NW = ATTN_WARPS>
+__global__ void __launch_bounds__(NW * 32, attn_decode_min_blocks(G, HDM, NW)) attn_decode_kernel(const AttnParams p)
 {
     constexpr int NCH = HDM / 128;                   // float4 slices per lane
     constexpr int TB = (G == 2 && NCH == 1) ? 8 : 4; // tokens per warp in flight
@@ -473,13 +484,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
         const int page = pt ? pt[t / p.page_size] : t / p.page_size;
         return (((size_t)page * p.n_kv + kvh) * p.page_size + (t % p.page_size)) * hd;
     };
-    auto tok = [&](int j) { return split + S * (warp + ATTN_WARPS * j); }; // this warp's j-th token
+    auto tok = [&](int j) { return split + S * (warp + NW * j); }; // this warp's j-th token
     const float* qz = p.q + (size_t)z * p.ldq;
     float* outz = p.out + (size_t)z * p.ldo;
-    float* wm = asmem;                              // [8][G]
-    float* wl = wm + ATTN_WARPS * G;                // [8][G]
-    float* wacc = wl + ATTN_WARPS * G;              // [8][G][hd]
-    float* parts = wacc + (size_t)ATTN_WARPS * G * hd; // [S][G][hd + 4]
+    float* wm = asmem;                         // [NW][G]
+    float* wl = wm + NW * G;                   // [NW][G]
+    float* wacc = wl + NW * G;                 // [NW][G][hd]
+    float* parts = wacc + (size_t)NW * G * hd; // [S][G][hd + 4]
     const int lin = split * gridDim.x + kvh;
     if (tid == 0)
         trace_mark(p.trace, lin, 0);
@@ -644,7 +655,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
     {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < ATTN_WARPS; ++w)
+        for (int w = 0; w < NW; ++w)
             M = fmaxf(M, wm[w * G + gi]);
         const float f = (m[gi] == -INFINITY) ? 0.0f : expf(m[gi] - M);
         if (lane == 0)
@@ -659,26 +670,26 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
         }
     }
     __syncthreads();
-    for (int i = tid; i < G * (hd + 2); i += ATTN_THREADS)
+    for (int i = tid; i < G * (hd + 2); i += NW * 32)
     {
         const int gi = i / (hd + 2), d = i - gi * (hd + 2);
         float v;
         if (d < hd)
         {
             v = 0.0f;
-            for (int w = 0; w < ATTN_WARPS; ++w)
+            for (int w = 0; w < NW; ++w)
                 v += wacc[((size_t)w * G + gi) * hd + d];
         }
         else if (d == hd)
         {
             v = -INFINITY;
-            for (int w = 0; w < ATTN_WARPS; ++w)
+            for (int w = 0; w < NW; ++w)
                 v = fmaxf(v, wm[w * G + gi]);
         }
         else
         {
             v = 0.0f;
-            for (int w = 0; w < ATTN_WARPS; ++w)
+            for (int w = 0; w < NW; ++w)
                 v += wl[w * G + gi];
         }
         if constexpr (CL)
@@ -709,7 +720,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
             return;
         }
         __threadfence();
-        for (int i = tid; i < G * hd; i += ATTN_THREADS)
+        for (int i = tid; i < G * hd; i += NW * 32)
         {
             const int gi = i / hd, d = i - gi * hd;
             const float* pb = p.part + (((size_t)z * p.n_heads + kvh * G + gi) * S) * ps;
@@ -762,7 +773,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_decode_min_blocks(G, HDM)) 
     cluster_sync_all();
     {
         const int n = G * hd, per = (n + S - 1) / S;
-        for (int i = split * per + tid; i < min(n, (split + 1) * per); i += ATTN_THREADS)
+        for (int i = split * per + tid; i < min(n, (split + 1) * per); i += NW * 32)
         {
             const int gi = i / hd, d = i - gi * hd;
             float M = -INFINITY;
@@ -799,13 +810,13 @@ inline cudaError_t attn_launch_one(const AttnParams& p, dim3 grid, size_t smem, 
 inline size_t attn_cluster_smem_bytes(int G, int hd, int S) { return attn_decode_smem_bytes(G, hd, S); }
 
 // Decode attention as clusters of grid.y CTAs (the splits of one kv head).
-template <int G, int HDM>
+template <int G, int HDM, int NW = ATTN_WARPS>
 inline cudaError_t attn_launch_cluster_one(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, p.head_dim, (int)grid.y);
+    cfg.blockDim = dim3(NW * 32);
+    cfg.dynamicSmemBytes = attn_decode_smem_bytes(G, p.head_dim, (int)grid.y, NW);
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -816,7 +827,7 @@ inline cudaError_t attn_launch_cluster_one(const AttnParams& p, dim3 grid, cudaS
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<G, HDM>, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<G, HDM, true, NW>, p);
 }
 
 inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, bool pdl)
@@ -828,7 +839,12 @@ inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, 
     cudaError_t e;
     switch (G)
     {
-    case 1: e = big ? attn_launch_cluster_one<1, 256>(p, grid, st, pdl) : attn_launch_cluster_one<1, 128>(p, grid, st, pdl); break;
+    case 1:
+        e = big               ? attn_launch_cluster_one<1, 256>(p, grid, st, pdl)
+            : p.warps == 16   ? attn_launch_cluster_one<1, 128, 16>(p, grid, st, pdl)
+            : p.warps == 10   ? attn_launch_cluster_one<1, 128, 10>(p, grid, st, pdl)
+                              : attn_launch_cluster_one<1, 128>(p, grid, st, pdl);
+        break;
     case 2: e = big ? attn_launch_cluster_one<2, 256>(p, grid, st, pdl) : attn_launch_cluster_one<2, 128>(p, grid, st, pdl); break;
     case 4: e = big ? attn_launch_cluster_one<4, 256>(p, grid, st, pdl) : attn_launch_cluster_one<4, 128>(p, grid, st, pdl); break;
     case 8: e = big ? attn_launch_cluster_one<8, 256>(p, grid, st, pdl) : attn_launch_cluster_one<8, 128>(p, grid, st, pdl); break;
@@ -872,13 +888,13 @@ inline int attn_launch_global(const AttnParams& p, dim3 grid, cudaStream_t st, b
 
 // Clusters of `S` CTAs that can be resident at once for head group G and
 // head_dim hd (0: the variant can not run here).
-template <int G, int HDM>
+template <int G, int HDM, int NW = ATTN_WARPS>
 inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_kv, S);
-    cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = attn_cluster_smem_bytes(G, hd, S);
+    cfg.blockDim = dim3(NW * 32);
+    cfg.dynamicSmemBytes = attn_decode_smem_bytes(G, hd, S, NW);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
@@ -887,7 +903,7 @@ inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<G, HDM>, &cfg) != cudaSuccess)
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<G, HDM, true, NW>, &cfg) != cudaSuccess)
     {
         cudaGetLastError();
         return 0;
@@ -895,12 +911,16 @@ inline int attn_cluster_capacity_one(int S, int hd, int n_kv)
     return n;
 }
 
-inline int attn_cluster_capacity(int G, int hd, int S, int n_kv)
+inline int attn_cluster_capacity(int G, int hd, int S, int n_kv, int warps = ATTN_WARPS)
 {
     const bool big = hd > 128;
     switch (G)
     {
-    case 1: return big ? attn_cluster_capacity_one<1, 256>(S, hd, n_kv) : attn_cluster_capacity_one<1, 128>(S, hd, n_kv);
+    case 1:
+        return big            ? attn_cluster_capacity_one<1, 256>(S, hd, n_kv)
+               : warps == 16  ? attn_cluster_capacity_one<1, 128, 16>(S, hd, n_kv)
+               : warps == 10  ? attn_cluster_capacity_one<1, 128, 10>(S, hd, n_kv)
+                              : attn_cluster_capacity_one<1, 128>(S, hd, n_kv);
     case 2: return big ? attn_cluster_capacity_one<2, 256>(S, hd, n_kv) : attn_cluster_capacity_one<2, 128>(S, hd, n_kv);
     case 4: return big ? attn_cluster_capacity_one<4, 256>(S, hd, n_kv) : attn_cluster_capacity_one<4, 128>(S, hd, n_kv);
     case 8: return big ? attn_cluster_capacity_one<8, 256>(S, hd, n_kv) : attn_cluster_capacity_one<8, 128>(S, hd, n_kv);

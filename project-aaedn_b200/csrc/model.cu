@@ -466,6 +466,7 @@ struct aaedn_model
     int page_size = 64, n_pages = 0;
     int attn_S = 1, attn_max_tok = 1;
     int attn_cS = 0; // splits of the clustered decode attention (0: splits merged through global memory)
+    int attn_warps = ATTN_WARPS; // warps a CTA of the clustered decode attention (MHA, head_dim <= 128)
     int lm_ctas = 1, lm_rows = 8, lm_stages = 8, lm_consumers = 8;
     cudaGraphExec_t graph_exec = nullptr;
     uint32_t kernels_per_step = 0;
@@ -686,6 +687,7 @@ static AttnParams attn_params(const aaedn_model* m, uint32_t l, int S)
     a.page_table = nullptr; // the sequence's pages are 0, 1, ... (identity table): no lookup before the K/V loads
     a.page_size = m->page_size;
     a.pstride = hd + 4; // 16-byte rows: the o-proj build reads them as float4
+    a.warps = m->attn_warps;
     return a;
 }
 
@@ -1439,6 +1441,16 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         const int G = (int)(c.n_heads / c.n_kv_heads);
         if (Sc >= 2 && attn_cluster_capacity(G, (int)c.head_dim, Sc, (int)c.n_kv_heads) >= 1)
             m->attn_cS = Sc;
+        // more warps a CTA for MHA at head_dim <= 128, so one batch of K/V
+        // loads covers more context (10 by default: three CTAs per SM;
+        // AAEDN_ATTN_WARPS=8 or 16), only when every kv head's cluster can be
+        // resident at once. 7B, one B200: 8 warps 682 tok/s, 10 warps 685-690,
+        // 16 warps 620 (late clusters)
+        const char* we = std::getenv("AAEDN_ATTN_WARPS");
+        const int nw = we ? std::atoi(we) : 10;
+        if (m->attn_cS && (nw == 10 || nw == 16) && G == 1 && c.head_dim <= 128 &&
+            attn_cluster_capacity(G, (int)c.head_dim, Sc, (int)c.n_kv_heads, nw) >= (int)c.n_kv_heads)
+            m->attn_warps = nw;
     }
     rc = set_model_kernel_attrs();
     if (rc)
