@@ -808,7 +808,7 @@ static LmParams lm_params(const aaedn_model* m)
 }
 
 // hidden += the sum of the ranks' partials in buffer buf (o: 0, down: 1)
-static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool signal)
+static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool signal, bool pdl)
 {
     if (!m->tp_ready)
         return set_error(AAEDN_ESTATE, "tensor parallel model: aaedn_model_tp_connect was not called");
@@ -822,8 +822,10 @@ static int tp_reduce(aaedn_model* m, cudaStream_t st, int buf, int phase, bool s
     rp.epoch = m->tp_epoch;
     rp.state = m->state;
     const int blocks = std::max(1, std::min(32, (int)(m->cfg.dim + 255) / 256));
-    tp_reduce_kernel<<<blocks, 256, 0, st>>>(rp);
-    AAEDN_LAUNCH_CHECK("tp_reduce_kernel");
+    cudaError_t e = launch_kernel(tp_reduce_kernel, dim3(blocks), dim3(256), 0, st, pdl, rp);
+    if (e != cudaSuccess)
+        return set_error(AAEDN_ECUDA, "launch of tp_reduce_kernel failed: %s", cudaGetErrorString(e));
+    count_launch();
     return AAEDN_OK;
 }
 
@@ -887,7 +889,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         {
             rc = !(mask & K_O) ? AAEDN_OK : model_gemv<PRO_PLAIN, EPI_TP_PUSH>(o, st, pdl, L.to);
             if (!rc && (mask & K_O))
-                rc = tp_reduce(m, st, 0, 2 * (int)l, false);
+                rc = tp_reduce(m, st, 0, 2 * (int)l, false, pdl);
         }
         else
             rc = !(mask & K_O) ? AAEDN_OK : model_gemv<PRO_PLAIN, EPI_RESIDUAL>(o, st, pdl, L.to);
@@ -906,7 +908,7 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
         {
             rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_TP_PUSH>(dn, st, pdl, L.td) : AAEDN_OK;
             if (!rc && (mask & K_DOWN))
-                rc = tp_reduce(m, st, 1, 2 * (int)l + 1, false);
+                rc = tp_reduce(m, st, 1, 2 * (int)l + 1, false, pdl);
         }
         else
             rc = (mask & K_DOWN) ? model_gemv<PRO_PLAIN, EPI_RESIDUAL>(dn, st, pdl, L.td) : AAEDN_OK;
@@ -940,8 +942,10 @@ static int enqueue_step(aaedn_model* m, cudaStream_t st, bool debug, const std::
             ap.state = m->state;
             ap.out_tokens = m->out_tokens;
             ap.max_seq = (int)c.max_seq;
-            tp_argmax_kernel<<<1, 256, 0, st>>>(ap);
-            AAEDN_LAUNCH_CHECK("tp_argmax_kernel");
+            cudaError_t ea = launch_kernel(tp_argmax_kernel, dim3(1), dim3(256), 0, st, pdl, ap);
+            if (ea != cudaSuccess)
+                return set_error(AAEDN_ECUDA, "launch of tp_argmax_kernel failed: %s", cudaGetErrorString(ea));
+            count_launch();
         }
     }
     if (m->tp_size > 1)

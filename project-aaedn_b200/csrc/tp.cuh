@@ -43,11 +43,16 @@ struct TpReduceParams
 };
 
 // hidden[i] += sum over ranks (in rank order) of part[rank][buf][i]. Launched
-// right after the GEMV that wrote this rank's partial (stream order: that
-// kernel has finished). Block 0 signals; every block waits for all flags.
+// right after the GEMV that wrote this rank's partial (as its programmatic
+// dependent: the launch wait returns once that kernel has finished). Block 0
+// signals; every block waits for all flags.
 __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p)
 {
     __shared__ int s_ok;
+    // launched as a programmatic dependent of the GEMV that wrote this rank's
+    // partial: everything below waits for that kernel
+    pdl_launch_dependents();
+    pdl_wait();
     const unsigned E = *p.epoch + (unsigned)p.phase + 1u;
     if (threadIdx.x == 0)
     {
@@ -97,6 +102,8 @@ __global__ void __launch_bounds__(256) tp_argmax_kernel(const TpArgmaxParams p)
 {
     __shared__ float s_v[8];
     __shared__ int s_i[8];
+    pdl_launch_dependents();
+    pdl_wait(); // the lm_head kernel's per-CTA results
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned E = *p.epoch + (unsigned)p.phase + 1u;
     float v = -INFINITY;
