@@ -485,18 +485,20 @@ def run_ours(args):
     pos1 = model.pos
 
     # ---- end to end through the reference-facing call (host token in, host
-    # logits out, host argmax), E steps
-    logits = model.logits()
+    # logits out, host argmax), E steps; the token and the logits live in
+    # pinned host buffers
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, pin_memory=True).numpy()
+    logits[:] = model.logits()
+    tok = torch.empty(1, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    tok = np.empty(1, np.uint32)
     for _ in range(E):
         # tensor parallel: each rank holds a vocabulary slice of the logits;
         # the ranks' argmax exchange already chose the token on the device
         tok[0] = model.next_token() if tp else int(np.argmax(logits))
-        logits = model.forward(tok)
+        model.forward(tok, out=logits)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()

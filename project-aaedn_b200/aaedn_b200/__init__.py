@@ -496,9 +496,17 @@ class Model:
     def reset(self):
         check(lib().aaedn_model_reset(self.h))
 
-    def forward(self, tokens, want_logits=True):
+    def forward(self, tokens, want_logits=True, out=None):
+        """transformer_forward: the logits of the last token (out: a host
+        float32 array of vocab entries to fill, e.g. pinned memory; else a
+        new array)."""
         t = np.ascontiguousarray(tokens, np.uint32).reshape(-1)
-        logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        if out is not None:
+            if out.dtype != np.float32 or out.size != self.cfg["vocab"] or not out.flags["C_CONTIGUOUS"]:
+                raise ValueError("out must be a contiguous float32 array of vocab entries")
+            logits = out
+        else:
+            logits = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
         check(lib().aaedn_model_forward(self.h, _p(t), t.size, _p(logits)))
         return logits
 

@@ -428,12 +428,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 //   1. Split s takes tokens s, s + S, s + 2S, ...; warp w of its NW warps
 //      (8, or 10 or 16 for MHA at head_dim <= 128 on request: one batch of
 //      loads then covers more context) the tokens s + S (w + NW j). The
-//      rows of its first TB tokens do not depend on the
-//      position, so each warp requests them (K and V straight into
+//      rows of its first TB tokens (earlier positions) do not depend on the
+//      kernel before, so each warp requests them (K and V straight into
 //      registers) before waiting for the kernel that writes q and the
 //      current K/V row: for the model's one sequence (identity page table)
-//      any token below the cache capacity, for batched rows (launched after
-//      their positions are written) below the row's length. After the wait
+//      those below the position read before the wait plus two (it may be
+//      one step behind), for batched rows (launched after their positions
+//      are written) those below the row's length. After the wait
 //      the position bounds the tokens: rows at or past it are zeroed and
 //      masked, the current row is requested again.
 //   2. Online softmax per warp, as attn_item.
@@ -520,7 +521,13 @@ __global__ void __launch_bounds__(NW * 32, attn_decode_min_blocks(G, HDM, NW)) a
             }
         }
     };
-    const int lim0 = p.row_pos ? min(p.row_pos[z] + 1, p.max_len) : p.max_len;
+    // rows requested before the wait: below the row's length (batched rows are
+    // launched after their positions are written), or, for the one sequence,
+    // up to the position as it stands before the wait plus one: the kernel
+    // that advances it may not have finished yet, and it moves by one a step
+    // (the exact length bounds the tokens after the wait)
+    const int lim0 = p.row_pos ? min(p.row_pos[z] + 1, p.max_len)
+                               : min((int)*reinterpret_cast<const volatile uint32_t*>(&p.state->pos) + 2, p.max_len);
     load(0, lim0);
     pdl_wait();
     if (tid == 0)
@@ -538,7 +545,9 @@ __global__ void __launch_bounds__(NW * 32, attn_decode_min_blocks(G, HDM, NW)) a
     const int L = p.row_pos ? lim0 : attn_len<1>(p);
     // rows at or past L hold no token of this sequence (zero them: masked
     // weights times stale values must not give NaN); the current row L - 1
-    // was written by the kernel before
+    // was written by the kernel before, and rows at or past the bound of the
+    // requests before the wait (a position read more than a step behind)
+    // were not requested
 #pragma unroll
     for (int j = 0; j < TB; ++j)
     {
@@ -550,7 +559,7 @@ __global__ void __launch_bounds__(NW * 32, attn_decode_min_blocks(G, HDM, NW)) a
                 kr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
                 vr[j][c] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-        else if (t == L - 1)
+        else if (t == L - 1 || t >= lim0)
         {
             const size_t ro = row_of(t);
 #pragma unroll
