@@ -61,7 +61,7 @@ struct AttnParams
     int pt_stride;
     size_t ldq, ldo;
     // warps a CTA of the clustered decode kernel for one query head per kv
-    // head at head_dim <= 128 (10 or 16: more tokens in flight per split;
+    // head at head_dim <= 128 (10: more tokens in flight per split;
     // otherwise ATTN_WARPS)
     int warps;
 };
@@ -426,8 +426,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 // Decode attention as clusters: the S splits of one kv head are one cluster
 // (grid (n_kv, S, rows), cluster (1, S)), CTA rank = split.
 //   1. Split s takes tokens s, s + S, s + 2S, ...; warp w of its NW warps
-//      (8, or 10 or 16 for MHA at head_dim <= 128 on request: one batch of
-//      loads then covers more context) the tokens s + S (w + NW j). The
+//      (8, or 10 for MHA at head_dim <= 128: one batch of loads then covers
+//      more context) the tokens s + S (w + NW j). The
 //      rows of its first TB tokens (earlier positions) do not depend on the
 //      kernel before, so each warp requests them (K and V straight into
 //      registers) before waiting for the kernel that writes q and the
@@ -445,8 +445,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, attn_min_blocks(G, HDM)) attn_sp
 //      the S partials from its own shared memory, in split order.
 // ---------------------------------------------------------------------------
 
-// MHA at head_dim <= 128: 64 registers, four CTAs of 8 warps (three of 10,
-// two of 16) per SM (a cluster then needs fewer free SMs of a GPC while the kernel
+// MHA at head_dim <= 128: 64 registers, four CTAs of 8 warps (three of 10)
+// per SM (a cluster then needs fewer free SMs of a GPC while the kernel
 // before drains); wider groups keep their q and V sums for more heads in
 // registers.
 constexpr int attn_decode_min_blocks(int G, int HDM, int NW = ATTN_WARPS)
@@ -850,7 +850,6 @@ inline int attn_launch_cluster(const AttnParams& p, dim3 grid, cudaStream_t st, 
     {
     case 1:
         e = big               ? attn_launch_cluster_one<1, 256>(p, grid, st, pdl)
-            : p.warps == 16   ? attn_launch_cluster_one<1, 128, 16>(p, grid, st, pdl)
             : p.warps == 10   ? attn_launch_cluster_one<1, 128, 10>(p, grid, st, pdl)
                               : attn_launch_cluster_one<1, 128>(p, grid, st, pdl);
         break;
@@ -927,7 +926,6 @@ inline int attn_cluster_capacity(int G, int hd, int S, int n_kv, int warps = ATT
     {
     case 1:
         return big            ? attn_cluster_capacity_one<1, 256>(S, hd, n_kv)
-               : warps == 16  ? attn_cluster_capacity_one<1, 128, 16>(S, hd, n_kv)
                : warps == 10  ? attn_cluster_capacity_one<1, 128, 10>(S, hd, n_kv)
                               : attn_cluster_capacity_one<1, 128>(S, hd, n_kv);
     case 2: return big ? attn_cluster_capacity_one<2, 256>(S, hd, n_kv) : attn_cluster_capacity_one<2, 128>(S, hd, n_kv);

@@ -1446,13 +1446,13 @@ static int create_impl(const aaedn_model_config* cfg, uint32_t tp_rank, uint32_t
         if (Sc >= 2 && attn_cluster_capacity(G, (int)c.head_dim, Sc, (int)c.n_kv_heads) >= 1)
             m->attn_cS = Sc;
         // more warps a CTA for MHA at head_dim <= 128, so one batch of K/V
-        // loads covers more context (10 by default: three CTAs per SM;
-        // AAEDN_ATTN_WARPS=8 or 16), only when every kv head's cluster can be
-        // resident at once. 7B, one B200: 8 warps 682 tok/s, 10 warps 685-690,
-        // 16 warps 620 (late clusters)
+        // loads covers more context (10: three CTAs per SM; AAEDN_ATTN_WARPS=8
+        // keeps 8), only when every kv head's cluster can be resident at once.
+        // 7B, one B200: 8 warps 682 tok/s, 10 warps 685-690 (16 warps, two
+        // CTAs per SM: 620, clusters placed late)
         const char* we = std::getenv("AAEDN_ATTN_WARPS");
         const int nw = we ? std::atoi(we) : 10;
-        if (m->attn_cS && (nw == 10 || nw == 16) && G == 1 && c.head_dim <= 128 &&
+        if (m->attn_cS && nw == 10 && G == 1 && c.head_dim <= 128 &&
             attn_cluster_capacity(G, (int)c.head_dim, Sc, (int)c.n_kv_heads, nw) >= (int)c.n_kv_heads)
             m->attn_warps = nw;
     }

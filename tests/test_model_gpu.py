@@ -135,7 +135,6 @@ def test_7b_width_two_layers_vs_oracle():
     {"AAEDN_GEMV_STAGES": "4"},               # the shallowest
     {"AAEDN_ATTN_WARPS": "8"},                # decode attention CTAs of 8 warps
     {"AAEDN_ATTN_WARPS": "10"},               # of 10 warps
-    {"AAEDN_ATTN_WARPS": "16"},               # of 16 warps (where all clusters fit at once)
 ])
 def test_launch_options_same_tokens(env, monkeypatch):
     """The model's launch options (read when it is created) change timing
