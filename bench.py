@@ -67,7 +67,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=512)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="end-to-end steps (default: --steps, over the timed region's positions)")
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -423,8 +424,8 @@ def run_ours(args):
 
     cfg = model_cfg(args)
     K, W = args.steps, max(3, args.warmup)
-    E, P = args.e2e_steps, args.profile_steps
-    if args.prompt + W + K + E + P + 2 > cfg["max_seq"]:
+    E, P = (args.e2e_steps if args.e2e_steps is not None else K), args.profile_steps
+    if args.prompt + W + max(K, E) + P + 2 > cfg["max_seq"]:
         raise SystemExit(f"steps+warmup too large for ctx {cfg['max_seq']}")
 
     tp = world > 1 and args.mode == "tp"
@@ -485,8 +486,14 @@ def run_ours(args):
     pos1 = model.pos
 
     # ---- end to end through the reference-facing call (host token in, host
-    # logits out, host argmax), E steps; the token and the logits live in
-    # pinned host buffers
+    # logits out, host argmax), E steps from the timed region's first
+    # position (the sequence restarted: the same prompt and warm-up steps,
+    # untimed); the token and the logits live in pinned host buffers
+    model.reset()
+    model.forward(prompt, want_logits=False)
+    model.decode_steps(W)
+    torch.cuda.synchronize()
+    assert model.pos == pos0
     logits = torch.empty(cfg["vocab"], dtype=torch.float32, pin_memory=True).numpy()
     logits[:] = model.logits()
     tok = torch.empty(1, dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
@@ -590,7 +597,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": (4 * ab.tp_plan(cfg, rank, world)["vocab"] + 4) if tp else 4 * cfg["vocab"],
                     "call": ("aaedn_model_forward (transformer_forward, this rank's logits slice) + the "
                              "device's next token" if tp else
-                             "aaedn_model_forward (transformer_forward) + host argmax")},
+                             "aaedn_model_forward (transformer_forward) + host argmax"),
+                    "steps": E, "positions": [pos0, pos0 + E]},
             "gpu_launches": int(launches),
             "clocks": clk,
         }
