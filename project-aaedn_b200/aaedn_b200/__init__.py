@@ -341,6 +341,9 @@ LLAMA2_7B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=32, head_dim=128,
                  max_seq=4096, rope_theta=10000.0, eps=1e-6)
 LLAMA3_8B = dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=14336, vocab=128256,
                  max_seq=4096, rope_theta=500000.0, eps=1e-6)
+# the 70B shape of the batched-branch workload (64 query / 8 KV heads, ctx 8192)
+LLAMA_70B = dict(dim=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672, vocab=128256,
+                 max_seq=8192, rope_theta=500000.0, eps=1e-6)
 
 LAYER_MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
 

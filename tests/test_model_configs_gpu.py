@@ -6,7 +6,8 @@ activations far from N(0, 1).
   tests/golden/llama2_7b_seed1234.npz by tests/golden/make_model_fixtures.py
   (the oracle needs tens of minutes for this decode on a few cores).
 * The Llama-3-8B widths (vocab 128256, ffn 14336, 32 query / 8 KV heads,
-  theta 500000) with two layers, against the oracle directly.
+  theta 500000) and the 70B widths (dim 8192, ffn 28672, 64 query / 8 KV
+  heads) with two layers, against the oracle directly.
 * Hidden states with per-block outliers (one element 10^4 times its block,
   and blocks that are zero but for one value) through both GEMV engines:
   the decode model's integer engine (activation digits scaled per 32-element
@@ -59,6 +60,22 @@ def test_llama3_8b_widths_two_layers_vs_oracle():
     with ab.Model(cfg) as gm:
         gm.set_weights(w)
         got = gm.generate(prompt, 64)
+        np.testing.assert_array_equal(got, want)
+        assert _rel_err(gm.logits(), wl) < 1e-4
+
+
+def test_70b_widths_two_layers_vs_oracle():
+    """The 70B shape's widths (dim 8192, 64 query / 8 KV heads, ffn 28672,
+    vocab 128256: eight query heads per KV head, the down GEMV's K = 28672
+    near the engine's 32768 bound) with two layers, against the oracle."""
+    cfg = dict(ab.LLAMA_70B, n_layers=2, max_seq=64)
+    w = ab.synthetic_weights(cfg, 7070)
+    om = pyoracle.OracleModel(pyoracle.Oracle(), cfg, w)
+    prompt = ab.synth_tokens(7070, 0, cfg["vocab"], 5)
+    want, wl = om.generate(prompt, 16)
+    with ab.Model(cfg) as gm:
+        gm.set_weights(w)
+        got = gm.generate(prompt, 16)
         np.testing.assert_array_equal(got, want)
         assert _rel_err(gm.logits(), wl) < 1e-4
 
