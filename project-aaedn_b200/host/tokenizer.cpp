@@ -27,9 +27,11 @@
 // the same check decides), and entries with equal rule numbers leave the
 // queue in the order of the standard library's binary heap, so the queue is
 // a std::priority_queue ordered by rule number, as in the reference. What
-// differs is the rule lookup: the reference scans every rule for every pair;
-// here a hash table from the pair to its lowest rule number, built once per
-// loaded tokenizer, answers in O(1).
+// differs is the cost, not the result: the reference scans every rule for
+// every pair and erases from a vector (O(n) a merge); here a hash table from
+// the pair to its lowest rule number, built once per loaded tokenizer,
+// answers in O(1), and the sequence is a linked list of byte slots with a
+// Fenwick tree that finds the k-th present token in O(log n).
 //
 // Decode (src/tokenizer.cpp:241-257): ids 32766 (EOS) and 32767 (PAD) and
 // ids >= vocab_size contribute nothing, every other id its string. One
@@ -194,13 +196,71 @@ struct Merge
     bool operator<(const Merge& o) const { return rule > o.rule; }
 };
 
+// The token sequence during encode. The queue's positions count the tokens
+// present now (an erasure shifts every later one down by one), so a token
+// keeps the slot of its first byte, merged-away slots leave a linked list of
+// present slots, and a Fenwick tree over the slots finds the slot of the
+// k-th present token in O(log n): O((n + merges) log n) for a text of n
+// bytes, where erasing from a vector (the reference) costs O(n) a merge.
+class TokenSeq
+{
+  public:
+    explicit TokenSeq(const unsigned char* text, size_t n)
+        : val_(n), prev_(n), next_(n), bit_(n + 1), n_(n), present_(n)
+    {
+        for (size_t i = 0; i < n; ++i)
+        {
+            val_[i] = text[i];
+            prev_[i] = (int64_t)i - 1;
+            next_[i] = i + 1 < n ? (int64_t)i + 1 : -1;
+        }
+        for (size_t i = 1; i <= n; ++i) // every slot present: bit[i] = lowbit(i)
+            bit_[i] = (uint32_t)(i & (~i + 1));
+        top_ = 1;
+        while (top_ * 2 <= n)
+            top_ *= 2;
+    }
+    size_t size() const { return present_; }
+    uint32_t& val(int64_t slot) { return val_[(size_t)slot]; }
+    int64_t prev(int64_t slot) const { return prev_[(size_t)slot]; }
+    int64_t next(int64_t slot) const { return next_[(size_t)slot]; }
+    // slot of the k-th present token (k < size())
+    int64_t slot_of(size_t k) const
+    {
+        size_t pos = 0, rem = k + 1;
+        for (size_t step = top_; step; step >>= 1)
+            if (pos + step <= n_ && bit_[pos + step] < rem)
+            {
+                pos += step;
+                rem -= bit_[pos];
+            }
+        return (int64_t)pos; // the last prefix with fewer than k + 1 present: 0-based slot pos
+    }
+    void erase(int64_t slot)
+    {
+        for (size_t i = (size_t)slot + 1; i <= n_; i += i & (~i + 1))
+            --bit_[i];
+        const int64_t p = prev_[(size_t)slot], q = next_[(size_t)slot];
+        if (p >= 0)
+            next_[(size_t)p] = q;
+        if (q >= 0)
+            prev_[(size_t)q] = p;
+        --present_;
+    }
+
+  private:
+    std::vector<uint32_t> val_;
+    std::vector<int64_t> prev_, next_;
+    std::vector<uint32_t> bit_;
+    size_t n_, present_, top_;
+};
+
 // Byte-level BPE over a rule table (see the file comment).
 std::vector<uint32_t> encode_core(const std::unordered_map<uint32_t, uint32_t>& rule, uint32_t vocab_size,
                                   const char* text, bool add_bos)
 {
-    std::vector<uint32_t> tok;
-    for (const unsigned char* c = reinterpret_cast<const unsigned char*>(text); *c; ++c)
-        tok.push_back(*c);
+    const size_t n = std::strlen(text);
+    TokenSeq seq(reinterpret_cast<const unsigned char*>(text), n);
     // the rule for tokens (x, y), or false (ids above 16 bits match none)
     auto find = [&](uint32_t x, uint32_t y, uint32_t& m) {
         if ((x | y) > 0xFFFFu)
@@ -213,26 +273,41 @@ std::vector<uint32_t> encode_core(const std::unordered_map<uint32_t, uint32_t>& 
     };
     std::priority_queue<Merge> q;
     uint32_t m;
-    for (size_t i = 0; i + 1 < tok.size(); ++i)
-        if (find(tok[i], tok[i + 1], m))
-            q.push({m, (uint32_t)i, (uint16_t)tok[i], (uint16_t)tok[i + 1]});
+    for (size_t i = 0; i + 1 < n; ++i) // every slot is present: slot i is position i
+        if (find(seq.val((int64_t)i), seq.val((int64_t)i + 1), m))
+            q.push({m, (uint32_t)i, (uint16_t)seq.val((int64_t)i), (uint16_t)seq.val((int64_t)i + 1)});
     while (!q.empty())
     {
         const Merge top = q.top();
         q.pop();
-        const size_t i = top.pos;
-        if (i + 1 >= tok.size() || tok[i] != top.a || tok[i + 1] != top.b)
+        const size_t p = top.pos;
+        if (p + 1 >= seq.size())
+            continue;
+        const int64_t i = seq.slot_of(p), j = seq.next(i);
+        if (seq.val(i) != top.a || seq.val(j) != top.b)
             continue; // stale: the pair is gone or something else sits here now
-        tok[i] = vocab_size + top.rule;
-        tok.erase(tok.begin() + (ptrdiff_t)i + 1);
-        if (i > 0 && find(tok[i - 1], tok[i], m))
-            q.push({m, (uint32_t)(i - 1), (uint16_t)tok[i - 1], (uint16_t)tok[i]});
-        if (i + 1 < tok.size() && find(tok[i], tok[i + 1], m))
-            q.push({m, (uint32_t)i, (uint16_t)tok[i], (uint16_t)tok[i + 1]});
+        seq.val(i) = vocab_size + top.rule;
+        seq.erase(j);
+        if (p > 0)
+        {
+            const int64_t h = seq.prev(i);
+            if (find(seq.val(h), seq.val(i), m))
+                q.push({m, (uint32_t)(p - 1), (uint16_t)seq.val(h), (uint16_t)seq.val(i)});
+        }
+        if (p + 1 < seq.size())
+        {
+            const int64_t k = seq.next(i);
+            if (find(seq.val(i), seq.val(k), m))
+                q.push({m, (uint32_t)p, (uint16_t)seq.val(i), (uint16_t)seq.val(k)});
+        }
     }
+    std::vector<uint32_t> out;
+    out.reserve(seq.size() + (add_bos ? 1 : 0));
     if (add_bos)
-        tok.insert(tok.begin(), kBos);
-    return tok;
+        out.push_back(kBos);
+    for (int64_t s = n ? 0 : -1; s >= 0; s = seq.next(s)) // slot 0 is never merged away
+        out.push_back(seq.val(s));
+    return out;
 }
 
 // The strings of ids, concatenated (see the file comment). `strings` ends in

@@ -208,6 +208,79 @@ def test_library_matches_compiled_reference_fuzz(tmp_path):
             assert t.decode(got) == buf.raw[:nb.value]
 
 
+@pytest.mark.skipif(not os.path.exists(REF_SO), reason="oracle/_ref (the reference compiled here) is not built")
+def test_long_text_matches_compiled_reference(tmp_path):
+    """A 40 KB text (tens of thousands of merges, many of them chained and
+    tied) against the reference compiled from source."""
+    lib = ctypes.CDLL(REF_SO)
+    sz = ctypes.c_size_t
+    lib.ref_tokenizer.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                  sz, ctypes.POINTER(sz), ctypes.c_void_p, sz, ctypes.POINTER(sz)]
+    lib.ref_tokenizer.restype = ctypes.c_int
+    rng = np.random.default_rng(11)
+    tokens, merges = _random_tokenizer(rng, 250)
+    alpha = b"abcde "
+    merges = [(x, y) for x in alpha for y in alpha] + merges  # every byte pair has a rule
+    p = str(tmp_path / "t.abt")
+    with open(p, "wb") as f:
+        f.write(abt_bytes(tokens, merges))
+    text = bytes(b"abcde "[int(k)] for k in rng.integers(0, 6, 40000))
+    ids = np.zeros(len(text) + 2, np.uint32)
+    buf = ctypes.create_string_buffer(8 * len(text))
+    info = np.zeros(5, np.uint32)
+    ni, nb = sz(), sz()
+    assert lib.ref_tokenizer(p.encode(), text, 1, info.ctypes.data, ids.ctypes.data, ids.size, ctypes.byref(ni),
+                             buf, len(buf), ctypes.byref(nb)) == 1
+    got = Tokenizer(path=p).encode(text, add_bos=True)
+    assert len(text) + 1 - got.size > 500  # a thousand merges (most queued entries go stale as positions shift)
+    np.testing.assert_array_equal(got, ids[:ni.value])
+
+
+def _chain_tokenizer(k):
+    """Byte tokens and the chain (a, a) -> X0, (X0, a) -> X1, ...: a run of
+    'a' merges over and over near its start."""
+    toks = [bytes([i]) for i in range(256)]
+    return toks, [(97, 97)] + [(256 + i, 97) for i in range(k - 1)]
+
+
+def test_encode_scales_to_megabytes():
+    """Encode is O((n + merges) log n): a 1 MB run of one byte under a
+    30000-rule chain (hundreds of thousands of merges near the start, where
+    erasing from a vector, as the reference does, moves the whole tail each
+    time) stays well under a few seconds."""
+    import time
+    t = Tokenizer(data=abt_bytes(*_chain_tokenizer(30000)))
+    text = b"a" * (1 << 20)
+    t0 = time.perf_counter()
+    ids = t.encode(text)
+    dt = time.perf_counter() - t0
+    assert len(text) - ids.size > 100000, ids.size
+    assert dt < 10.0, dt
+
+
+@pytest.mark.skipif(not os.path.exists(REF_SO), reason="oracle/_ref (the reference compiled here) is not built")
+def test_merge_chain_matches_compiled_reference(tmp_path):
+    """The chained merges of a 20 KB run of one byte against the reference."""
+    lib = ctypes.CDLL(REF_SO)
+    sz = ctypes.c_size_t
+    lib.ref_tokenizer.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                  sz, ctypes.POINTER(sz), ctypes.c_void_p, sz, ctypes.POINTER(sz)]
+    lib.ref_tokenizer.restype = ctypes.c_int
+    p = str(tmp_path / "chain.abt")
+    with open(p, "wb") as f:
+        f.write(abt_bytes(*_chain_tokenizer(3000)))
+    text = b"a" * 20000
+    ids = np.zeros(len(text) + 2, np.uint32)
+    buf = ctypes.create_string_buffer(8 * len(text))
+    info = np.zeros(5, np.uint32)
+    ni, nb = sz(), sz()
+    assert lib.ref_tokenizer(p.encode(), text, 0, info.ctypes.data, ids.ctypes.data, ids.size, ctypes.byref(ni),
+                             buf, len(buf), ctypes.byref(nb)) == 1
+    got = Tokenizer(path=p).encode(text)
+    assert len(text) - got.size > 5000
+    np.testing.assert_array_equal(got, ids[:ni.value])
+
+
 CPP = r'''
 #include <cstdio>
 #include <cstring>
