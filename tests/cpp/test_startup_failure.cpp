@@ -71,7 +71,7 @@ int main(int argc, char** argv)
     aaedn::QuantBlock none = aaedn::quant_load(&arena, (dir + "/missing.abn").c_str());
     CHECK(zeroed(none));
 
-    // the reader's verdicts and error codes
+    // the reader's decisions and error codes
     aaedn_abn_header h{};
     CHECK(aaedn_abn_read_header(bad_magic.c_str(), &h) == AAEDN_EFORMAT);
     CHECK(std::strstr(aaedn_last_error(), "magic") != nullptr);

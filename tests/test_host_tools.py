@@ -96,7 +96,7 @@ def _abn(hidden=64, version=2, magic=b"AAEDNMDL", corrupt=False, truncate=0, siz
 @pytest.mark.parametrize("case", ["valid", "magic", "version", "size", "checksum", "short", "header"])
 def test_abn_reader_matches_oracle(oracle, tmp_path, case):
     """quant_load's checks (src/quant.cpp:50-111) in the host reader, and the
-    oracle's restatement of them, give the same verdict."""
+    oracle's restatement of them, give the same decision."""
     kw = {"valid": {}, "magic": {"magic": b"AAEDNXXX"}, "version": {"version": 3}, "size": {"size_delta": 2},
           "checksum": {"corrupt": True}, "short": {"truncate": 3}, "header": {"truncate": 10 ** 6}}[case]
     blob, codes, scales = _abn(**kw) if case != "header" else (_abn()[0][:40], None, None)
